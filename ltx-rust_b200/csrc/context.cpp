@@ -1,0 +1,83 @@
+// ltx_ctx: device, stream, last-error text, device timeout flag, scratch.
+#include <cstring>
+#include <new>
+
+#include "internal.hpp"
+
+namespace ltx {
+
+int ensure_scratch(ltx_ctx *ctx, size_t bytes) {
+    if (ctx->scratch_bytes >= bytes) return LTX_OK;
+    if (ctx->scratch) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(ctx->scratch);
+        ctx->scratch = nullptr;
+        ctx->scratch_bytes = 0;
+    }
+    cudaError_t e = cudaMalloc(&ctx->scratch, bytes);
+    if (e != cudaSuccess) return fail(ctx, LTX_ERR_OOM, "scratch allocation of %zu bytes: %s", bytes, cudaGetErrorString(e));
+    ctx->scratch_bytes = bytes;
+    return LTX_OK;
+}
+
+}  // namespace ltx
+
+extern "C" int ltx_ctx_create(int device, void *stream, ltx_ctx **out) {
+    if (!out) return LTX_ERR_INVALID_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return LTX_ERR_CUDA;
+    ltx_ctx *ctx = new (std::nothrow) ltx_ctx();
+    if (!ctx) return LTX_ERR_OOM;
+    ctx->device = device;
+    if (cudaSetDevice(device) != cudaSuccess) {
+        delete ctx;
+        return LTX_ERR_CUDA;
+    }
+    cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+    if (stream) {
+        ctx->stream = static_cast<cudaStream_t>(stream);
+    } else {
+        if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {
+            delete ctx;
+            return LTX_ERR_CUDA;
+        }
+        ctx->own_stream = true;
+    }
+    if (cudaMalloc(&ctx->timeout_flag, sizeof(int)) != cudaSuccess ||
+        cudaMemsetAsync(ctx->timeout_flag, 0, sizeof(int), ctx->stream) != cudaSuccess) {
+        if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+        delete ctx;
+        return LTX_ERR_CUDA;
+    }
+    *out = ctx;
+    return LTX_OK;
+}
+
+extern "C" void ltx_ctx_destroy(ltx_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->timeout_flag) cudaFree(ctx->timeout_flag);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+extern "C" const char *ltx_last_error(const ltx_ctx *ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
+
+extern "C" void *ltx_ctx_stream(const ltx_ctx *ctx) { return ctx ? static_cast<void *>(ctx->stream) : nullptr; }
+
+extern "C" int ltx_ctx_synchronize(ltx_ctx *ctx) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return ltx::cuda_fail(ctx, e, "cudaStreamSynchronize");
+    int flag = 0;
+    e = cudaMemcpy(&flag, ctx->timeout_flag, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return ltx::cuda_fail(ctx, e, "reading the timeout flag");
+    if (flag) {
+        cudaMemset(ctx->timeout_flag, 0, sizeof(int));
+        return ltx::fail(ctx, LTX_ERR_TIMEOUT, "a device-side wait gave up (code %d)", flag);
+    }
+    return LTX_OK;
+}

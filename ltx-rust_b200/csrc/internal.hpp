@@ -1,0 +1,66 @@
+// Host-side internals shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/ltx_b200.h"
+
+struct ltx_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    std::string last_error;
+    // Device word that kernels set when a bounded wait gives up (a code, 0 = fine).
+    int *timeout_flag = nullptr;
+    int sm_count = 0;
+    // Scratch buffer grown on demand and reused by later calls on this context.
+    void *scratch = nullptr;
+    size_t scratch_bytes = 0;
+};
+
+namespace ltx {
+
+inline int fail(ltx_ctx *ctx, int code, const char *fmt, ...) {
+    if (ctx) {
+        char buf[1024];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof buf, fmt, ap);
+        va_end(ap);
+        ctx->last_error = buf;
+    }
+    return code;
+}
+
+inline int cuda_fail(ltx_ctx *ctx, cudaError_t e, const char *what) {
+    return fail(ctx, LTX_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Makes sure ctx->scratch holds at least `bytes`; returns a status.
+int ensure_scratch(ltx_ctx *ctx, size_t bytes);
+
+inline size_t dtype_size(int dt) {
+    switch (dt) {
+    case LTX_F32: return 4;
+    case LTX_F16:
+    case LTX_BF16: return 2;
+    case LTX_F8_E4M3:
+    case LTX_F8_E5M2: return 1;
+    default: return 0;
+    }
+}
+
+}  // namespace ltx
+
+#define LTX_CUDA_TRY(ctx, call)                                          \
+    do {                                                                 \
+        cudaError_t _e = (call);                                         \
+        if (_e != cudaSuccess) return ltx::cuda_fail((ctx), _e, #call);  \
+    } while (0)

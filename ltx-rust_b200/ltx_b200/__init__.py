@@ -1,0 +1,112 @@
+"""ctypes binding of libltx_b200.so (the C ABI in include/ltx_b200.h).
+
+This is the thin layer a Python caller (the tests, bench.py) uses; it mirrors
+the names of the reference crates' entry points it wraps.  The compute path is
+entirely in the shared library; when the library cannot be loaded every call
+raises (there is no CPU fallback).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libltx_b200.so")
+
+LTX_F32, LTX_F16, LTX_BF16, LTX_F8_E4M3, LTX_F8_E5M2 = 0, 1, 2, 3, 4
+MAX_DELTAS = 8
+
+STATUS = {
+    0: "OK", 1: "INVALID_ARG", 2: "SHAPE", 3: "DTYPE", 4: "MISSING_KEY", 5: "DUPLICATE_KEY",
+    6: "LORA_RANK", 7: "NO_LORA_MATCHES", 8: "IO", 9: "FORMAT", 10: "CONFIG", 11: "SIGMA",
+    12: "SCHEDULE", 13: "CUDA", 14: "NCCL", 15: "TIMEOUT", 16: "OOM", 17: "UNSUPPORTED",
+    18: "MISSING_CONFIG", 19: "NEGATIVE_CONTEXT",
+}
+
+
+class LtxError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"ltx_b200 error {STATUS.get(code, code)}: {msg}")
+        self.code = code
+        self.kind = STATUS.get(code, str(code))
+
+
+class LoraDelta(ctypes.Structure):
+    _fields_ = [("a_dev", ctypes.c_void_p), ("b_dev", ctypes.c_void_p), ("rank", ctypes.c_int32),
+                ("a_dtype", ctypes.c_int32), ("b_dtype", ctypes.c_int32), ("coeff", ctypes.c_float)]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads the library (raising if it is missing: there is no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: run `python ltx-rust_b200/build.py` first")
+    L = ctypes.CDLL(LIB_PATH)
+    V, I, F, P, I64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_int64
+    sig = {
+        "ltx_ctx_create": (I, [I, V, ctypes.POINTER(V)]),
+        "ltx_ctx_destroy": (None, [V]),
+        "ltx_last_error": (ctypes.c_char_p, [V]),
+        "ltx_ctx_stream": (V, [V]),
+        "ltx_ctx_synchronize": (I, [V]),
+        "ltx_lora_coeff": (F, [F, F, ctypes.c_int32]),
+        "ltx_dequant_merge": (I, [V, P, ctypes.c_int32, ctypes.c_int32, F, I64, I64,
+                                  ctypes.POINTER(LoraDelta), ctypes.c_int32, P, ctypes.c_int32]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+class Context:
+    """An ltx_ctx bound to a CUDA device and stream (default: torch's current stream)."""
+
+    def __init__(self, device: int = 0, stream: int | None = None):
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream(device).cuda_stream
+        self.h = ctypes.c_void_p()
+        rc = lib().ltx_ctx_create(device, ctypes.c_void_p(stream), ctypes.byref(self.h))
+        if rc != 0:
+            raise LtxError(rc, f"ltx_ctx_create(device={device})")
+
+    def check(self, rc: int, what: str):
+        if rc != 0:
+            msg = lib().ltx_last_error(self.h)
+            raise LtxError(rc, f"{what}: {msg.decode() if msg else ''}")
+
+    def synchronize(self):
+        self.check(lib().ltx_ctx_synchronize(self.h), "synchronize")
+
+    def close(self):
+        if self.h:
+            lib().ltx_ctx_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ── ltx-weights ──────────────────────────────────────────────────────────
+    def dequant_merge(self, w_ptr: int, w_dtype: int, has_scale: bool, scale: float, out_features: int,
+                      in_features: int, deltas, dst_ptr: int, dst_dtype: int):
+        """WeightStore::read body on device pointers (ltx_dequant_merge)."""
+        n = len(deltas)
+        arr = (LoraDelta * max(n, 1))(*[LoraDelta(*d) for d in deltas])
+        self.check(lib().ltx_dequant_merge(self.h, ctypes.c_void_p(w_ptr), w_dtype, int(has_scale), scale,
+                                           out_features, in_features, arr, n, ctypes.c_void_p(dst_ptr),
+                                           dst_dtype), "ltx_dequant_merge")
+
+
+def lora_coeff(strength: float, alpha: float, rank: int) -> float:
+    return lib().ltx_lora_coeff(strength, alpha, rank)
