@@ -65,9 +65,10 @@ typedef struct ltx_ctx ltx_ctx;
 
 /* ── context ──────────────────────────────────────────────────────────────── */
 
-/* Creates a context on CUDA device `device`.  `stream` is a cudaStream_t (NULL
- * = a new non-blocking stream owned by the context).  No reference
- * counterpart: the reference picks its device through Burn's `B::Device`. */
+/* Creates a context on CUDA device `device` that enqueues on `stream` (a
+ * cudaStream_t owned by the caller; NULL = the CUDA default stream).  No
+ * reference counterpart: the reference picks its device through Burn's
+ * `B::Device`. */
 int ltx_ctx_create(int device, void *stream, ltx_ctx **out);
 void ltx_ctx_destroy(ltx_ctx *ctx);
 /* Message of the last failed call on this context ("" if none). */
@@ -115,6 +116,30 @@ int ltx_dequant_merge(ltx_ctx *ctx, const void *w_dev, int32_t w_dtype, int32_t 
                       float scale, int64_t out_features, int64_t in_features,
                       const ltx_lora_delta *deltas, int32_t n_deltas, void *dst_dev,
                       int32_t dst_dtype);
+
+/* ── ltx-dit: building blocks ─────────────────────────────────────────────── */
+
+/* Epilogues of ltx_gemm_bf16. */
+typedef enum {
+    LTX_EPI_BF16 = 0,       /* out(bf16) = acc + bias                                  */
+    LTX_EPI_GELU_BF16 = 1,  /* out(bf16) = gelu_tanh(acc + bias)  (feed_forward.rs:38-42) */
+    LTX_EPI_F32 = 2,        /* out(f32)  = acc + bias                                  */
+    LTX_EPI_RESID = 3       /* out(f32) += (acc + bias) * gate[gate_idx[row]][col]
+                               (block.rs:138, :152; gate NULL = no gate, block.rs:148) */
+} ltx_epilogue;
+
+/* out = epilogue(A[m,k] . W[n,k]^T) on the tensor cores (tcgen05, bf16 in,
+ * f32 accumulate).  Replaces Burn `Linear::forward` (y = x W^T + b) for the
+ * DiT's projections (attention.rs:150-152, :194; feed_forward.rs:38-42;
+ * model.rs:187, :254).  A and W are bf16 row-major with leading dimensions
+ * lda/ldw in elements (multiples of 8; 16-byte aligned base pointers).
+ * `bias_dev` is f32 [n] or NULL.  For LTX_EPI_RESID, `gate_dev` is f32
+ * [U, ld_gate] and `gate_idx_dev` int32 [m] selects the gate row per output
+ * row (NULL = row 0).  Enqueued on the context stream. */
+int ltx_gemm_bf16(ltx_ctx *ctx, const void *a_dev, int64_t lda, const void *w_dev, int64_t ldw,
+                  int32_t m, int32_t n, int32_t k, int32_t epilogue, const float *bias_dev,
+                  void *out_dev, int64_t ldo, const float *gate_dev, const int32_t *gate_idx_dev,
+                  int64_t ld_gate);
 
 #ifdef __cplusplus
 }

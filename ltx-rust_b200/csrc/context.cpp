@@ -35,15 +35,9 @@ extern "C" int ltx_ctx_create(int device, void *stream, ltx_ctx **out) {
         return LTX_ERR_CUDA;
     }
     cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
-    if (stream) {
-        ctx->stream = static_cast<cudaStream_t>(stream);
-    } else {
-        if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {
-            delete ctx;
-            return LTX_ERR_CUDA;
-        }
-        ctx->own_stream = true;
-    }
+    // The caller's stream; NULL is the CUDA default (legacy) stream, which is
+    // also what PyTorch and most hosts enqueue on by default.
+    ctx->stream = static_cast<cudaStream_t>(stream);
     if (cudaMalloc(&ctx->timeout_flag, sizeof(int)) != cudaSuccess ||
         cudaMemsetAsync(ctx->timeout_flag, 0, sizeof(int), ctx->stream) != cudaSuccess) {
         if (ctx->own_stream) cudaStreamDestroy(ctx->stream);

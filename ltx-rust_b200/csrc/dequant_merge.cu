@@ -105,123 +105,224 @@ __global__ void dequant_only_scalar_kernel(MergeParams p, int64_t n) {
 }
 
 // ── delta path: FP32-FMA-bound tiled kernel ──────────────────────────────────
+//
+// All deltas' (c, a) pairs form ONE chain: for delta d, rank step r,
+// v = fma(coeff_d * B_d[o][r], A_d[r][i], v).  A pre-pass writes the chain as
+// f32 into scratch — a32[k][cols_p] and ct[k][rows_p] (ct transposed so a
+// CTA's rows are contiguous for each k) — zero-padded to the tile grid, so
+// the main kernel stages it with unconditional 16-byte cp.async copies.
 
 constexpr int kWarps = 8;
 constexpr int kRowsPerWarp = 16;
 constexpr int kTileRows = kWarps * kRowsPerWarp;  // 128
-constexpr int kTileCols = 256;                     // 32 lanes x 8 columns
-constexpr int kRChunk = 32;                        // rank steps staged per pass
+constexpr int kTileCols = 256;                     // per lane: 4 cols at lane*4, 4 at 128+lane*4
+constexpr int kRChunk = 32;                        // chain steps per stage
 
 struct MergeSmem {
-    float a[kRChunk][kTileCols];        // A[r][col], decoded          32 KB
-    float c[kRChunk][kTileRows];        // coeff * B[row][r]            16 KB
+    float a[2][kRChunk][kTileCols];    // A chain rows                      64 KB
+    float2 c[2][kRChunk][kTileRows];   // {c, c} = coeff*B, paired for FFMA2 64 KB
+    uint8_t w8[kTileRows][kTileCols];  // FP8 base tile                      32 KB
 };
 
+struct ChainMap {
+    int n;                      // deltas
+    int start[LTX_MAX_DELTAS];  // first chain index of each delta
+};
+
+__global__ void merge_prepass_kernel(MergeParams p, ChainMap cm, int ktot, float *a32, float2 *ct, int64_t cols_p,
+                                     int64_t rows_p) {
+    const int64_t na = (int64_t)ktot * cols_p, nc = (int64_t)ktot * rows_p;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nc; i += stride) {
+        const bool is_a = i < na;
+        const int64_t j = is_a ? i : i - na;
+        const int k = (int)(j / (is_a ? cols_p : rows_p));
+        const int64_t x = j % (is_a ? cols_p : rows_p);
+        int d = 0;
+        while (d + 1 < cm.n && k >= cm.start[d + 1]) ++d;
+        const DeltaDev &dl = p.d[d];
+        const int r = k - cm.start[d];
+        if (is_a) {
+            a32[j] = x < p.cols ? load_as_f32(dl.a, dl.a_dt, (int64_t)r * p.cols + x) : 0.f;
+        } else {
+            // store.rs:786: coeff = self.scale * b_value (one f32 rounding)
+            const float c = x < p.rows ? __fmul_rn(dl.coeff, load_as_f32(dl.b, dl.b_dt, x * dl.rank + r)) : 0.f;
+            ct[j] = make_float2(c, c);
+        }
+    }
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int WDT>
+__device__ __forceinline__ float base_t(const MergeParams &p, int64_t idx) {
+    float v = load_as_f32(p.w, WDT, idx);
+    return p.fp8_scaled ? __fmaf_rn(p.scale, v, 0.0f) : v;
+}
+
 template <int WDT, bool OUT_BF16>
-__global__ void __launch_bounds__(kWarps * 32, 1) dequant_merge_kernel(MergeParams p) {
+__global__ void __launch_bounds__(kWarps * 32, 1)
+    dequant_merge_kernel(MergeParams p, const float *__restrict__ a32, const float2 *__restrict__ ct, int ktot,
+                         int64_t cols_p, int64_t rows_p, int base_vec) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     MergeSmem &s = *reinterpret_cast<MergeSmem *>(smem_raw);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t row0 = (int64_t)blockIdx.y * kTileRows;
     const int64_t col0 = (int64_t)blockIdx.x * kTileCols;
-    const int64_t my_row = row0 + warp * kRowsPerWarp;
-    const int64_t my_col = col0 + lane * 8;
-    const bool full_cols = my_col + 8 <= p.cols;
+    const int nchunks = (ktot + kRChunk - 1) / kRChunk;
 
-    // acc[i][j/2] holds columns (2j, 2j+1) of row i as a float2 for FFMA2.
+    auto issue = [&](int chunk, int buf) {
+        const int k0 = chunk * kRChunk;
+        // A: kRChunk rows x 256 floats = 2048 16-byte pieces; C: kRChunk x 128 = 1024 pieces.
+        for (int q = threadIdx.x; q < kRChunk * kTileCols / 4; q += blockDim.x) {
+            const int r = q / (kTileCols / 4), c4 = q % (kTileCols / 4);
+            const int k = min(k0 + r, ktot - 1);   // rows past the chain end are never read
+            cp_async16(&s.a[buf][r][c4 * 4], a32 + (int64_t)k * cols_p + col0 + c4 * 4);
+        }
+        for (int q = threadIdx.x; q < kRChunk * kTileRows / 2; q += blockDim.x) {
+            const int r = q / (kTileRows / 2), c2 = q % (kTileRows / 2);
+            const int k = min(k0 + r, ktot - 1);
+            cp_async16(&s.c[buf][r][c2 * 2], ct + (int64_t)k * rows_p + row0 + c2 * 2);
+        }
+    };
+    // Group 0: the FP8 base tile (full, aligned tiles only) and chain chunk 0.
+    if (base_vec) {
+        for (int q = threadIdx.x; q < kTileRows * kTileCols / 16; q += blockDim.x) {
+            const int rr = q / (kTileCols / 16), c16 = q % (kTileCols / 16);
+            cp_async16(&s.w8[rr][c16 * 16],
+                       static_cast<const uint8_t *>(p.w) + (row0 + rr) * p.cols + col0 + c16 * 16);
+        }
+    }
+    issue(0, 0);
+    cp_async_commit();
+
     float2 acc[kRowsPerWarp][4];
+    const int64_t cseg[2] = {col0 + lane * 4, col0 + 128 + lane * 4};
+    if (base_vec) {
+        // FP8 only: decode the staged base tile.
+        if (nchunks > 1) issue(1, 1);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < kRowsPerWarp; ++i) {
+            const int rr = warp * kRowsPerWarp + i;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t w4 = *reinterpret_cast<const uint32_t *>(&s.w8[rr][h * 128 + lane * 4]);
+                float x[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t b = (w4 >> (8 * e)) & 0xFFu;
+                    x[e] = WDT == LTX_F8_E4M3 ? dec_e4m3(b) : dec_e5m2(b);
+                    if (p.fp8_scaled) x[e] = __fmaf_rn(p.scale, x[e], 0.0f);
+                }
+                acc[i][2 * h] = make_float2(x[0], x[1]);
+                acc[i][2 * h + 1] = make_float2(x[2], x[3]);
+            }
+        }
+    } else
 #pragma unroll
     for (int i = 0; i < kRowsPerWarp; ++i) {
-        const int64_t r = my_row + i;
+        const int64_t r = row0 + warp * kRowsPerWarp + i;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            float x0 = 0.f, x1 = 0.f;
+        for (int h = 0; h < 2; ++h) {
+            float x[4] = {0.f, 0.f, 0.f, 0.f};
             if (r < p.rows) {
-                const int64_t base = r * p.cols + my_col + 2 * j;
-                if (full_cols || my_col + 2 * j < p.cols) x0 = base_value(p, base);
-                if (full_cols || my_col + 2 * j + 1 < p.cols) x1 = base_value(p, base + 1);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (cseg[h] + e < p.cols) x[e] = base_t<WDT>(p, r * p.cols + cseg[h] + e);
             }
-            acc[i][j] = make_float2(x0, x1);
+            acc[i][2 * h] = make_float2(x[0], x[1]);
+            acc[i][2 * h + 1] = make_float2(x[2], x[3]);
         }
     }
 
-    for (int d = 0; d < p.n_deltas; ++d) {
-        const DeltaDev dl = p.d[d];
-        for (int rc = 0; rc < dl.rank; rc += kRChunk) {
-            const int nr = min(kRChunk, dl.rank - rc);
-            __syncthreads();
-            // Stage A[rc .. rc+nr)[col0 .. col0+256) and coeff*B[row0 .. +128)[rc .. rc+nr).
-            for (int idx = threadIdx.x; idx < kRChunk * kTileCols; idx += blockDim.x) {
-                const int r = idx / kTileCols, cc = idx % kTileCols;
-                const int64_t gc = col0 + cc;
-                s.a[r][cc] = (r < nr && gc < p.cols) ? load_as_f32(dl.a, dl.a_dt, (int64_t)(rc + r) * p.cols + gc) : 0.f;
-            }
-            for (int idx = threadIdx.x; idx < kRChunk * kTileRows; idx += blockDim.x) {
-                const int rr = idx % kTileRows, r = idx / kTileRows;
-                const int64_t gr = row0 + rr;
-                // store.rs:786: coeff = self.scale * b_value (one f32 rounding)
-                s.c[r][rr] = (r < nr && gr < p.rows)
-                                 ? __fmul_rn(dl.coeff, load_as_f32(dl.b, dl.b_dt, gr * dl.rank + rc + r))
-                                 : 0.f;
-            }
-            __syncthreads();
-            for (int r = 0; r < nr; ++r) {
-                const float4 a0 = *reinterpret_cast<const float4 *>(&s.a[r][lane * 8]);
-                const float4 a1 = *reinterpret_cast<const float4 *>(&s.a[r][lane * 8 + 4]);
-                const float2 av[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y),
-                                      make_float2(a1.z, a1.w)};
-                float cv[kRowsPerWarp];
-#pragma unroll
-                for (int q = 0; q < kRowsPerWarp / 4; ++q) {
-                    const float4 c4 = *reinterpret_cast<const float4 *>(&s.c[r][warp * kRowsPerWarp + 4 * q]);
-                    cv[4 * q] = c4.x;
-                    cv[4 * q + 1] = c4.y;
-                    cv[4 * q + 2] = c4.z;
-                    cv[4 * q + 3] = c4.w;
-                }
-#pragma unroll
-                for (int i = 0; i < kRowsPerWarp; ++i) {
-                    const float2 c2 = make_float2(cv[i], cv[i]);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) acc[i][j] = __ffma2_rn(c2, av[j], acc[i][j]);
-                }
-            }
-        }
-    }
-
-#pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
-        const int64_t r = my_row + i;
-        if (r >= p.rows) continue;
-        const int64_t base = r * p.cols + my_col;
-        if (p.dst_aligned16 && full_cols && ((base & 7) == 0)) {
-            if constexpr (OUT_BF16) {
-                uint32_t o[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    __nv_bfloat162 h = __floats2bfloat162_rn(acc[i][j].x, acc[i][j].y);
-                    o[j] = *reinterpret_cast<uint32_t *>(&h);
-                }
-                __stcs(reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.dst) + base),
-                       make_uint4(o[0], o[1], o[2], o[3]));
+    for (int ch = 0; ch < nchunks; ++ch) {
+        const int buf = ch & 1;
+        // With base_vec, chunk ch+1 was issued one step earlier (chunk 1 in the prologue).
+        if (!base_vec) {
+            if (ch + 1 < nchunks) {
+                issue(ch + 1, buf ^ 1);
+                cp_async_commit();
+                cp_async_wait<1>();
             } else {
-                float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.dst) + base);
-                __stcs(dst, make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y));
-                __stcs(dst + 1, make_float4(acc[i][2].x, acc[i][2].y, acc[i][3].x, acc[i][3].y));
+                cp_async_wait<0>();
             }
         } else {
+            // chunk ch is in the oldest outstanding group; chunk ch+1 (if any) in the newer one.
+            if (ch + 1 < nchunks) cp_async_wait<1>(); else cp_async_wait<0>();
+        }
+        __syncthreads();
+        const int nr = min(kRChunk, ktot - ch * kRChunk);
+        for (int r = 0; r < nr; ++r) {
+            const float4 a0 = *reinterpret_cast<const float4 *>(&s.a[buf][r][lane * 4]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&s.a[buf][r][128 + lane * 4]);
+            const float2 av[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y),
+                                  make_float2(a1.z, a1.w)};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                if (my_col + 2 * j < p.cols) store_out(p, base + 2 * j, acc[i][j].x);
-                if (my_col + 2 * j + 1 < p.cols) store_out(p, base + 2 * j + 1, acc[i][j].y);
+            for (int q = 0; q < kRowsPerWarp / 2; ++q) {
+                const float4 cc = *reinterpret_cast<const float4 *>(&s.c[buf][r][warp * kRowsPerWarp + 2 * q]);
+                const float2 c0 = make_float2(cc.x, cc.y), c1 = make_float2(cc.z, cc.w);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    acc[2 * q][j] = __ffma2_rn(c0, av[j], acc[2 * q][j]);
+                    acc[2 * q + 1][j] = __ffma2_rn(c1, av[j], acc[2 * q + 1][j]);
+                }
+            }
+        }
+        __syncthreads();   // buffer `buf` is refilled below
+        if (base_vec && ch + 2 < nchunks) {
+            issue(ch + 2, buf);
+            cp_async_commit();
+        }
+    }
+
+#pragma unroll
+    for (int i = 0; i < kRowsPerWarp; ++i) {
+        const int64_t r = row0 + warp * kRowsPerWarp + i;
+        if (r >= p.rows) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int64_t base = r * p.cols + cseg[h];
+            const float2 v0 = acc[i][2 * h], v1 = acc[i][2 * h + 1];
+            if (p.dst_aligned16 && cseg[h] + 4 <= p.cols && (base & 3) == 0) {
+                if constexpr (OUT_BF16) {
+                    __nv_bfloat162 h0 = __floats2bfloat162_rn(v0.x, v0.y), h1 = __floats2bfloat162_rn(v1.x, v1.y);
+                    __stcs(reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(p.dst) + base),
+                           make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1)));
+                } else {
+                    __stcs(reinterpret_cast<float4 *>(static_cast<float *>(p.dst) + base),
+                           make_float4(v0.x, v0.y, v1.x, v1.y));
+                }
+            } else {
+                const float vv[4] = {v0.x, v0.y, v1.x, v1.y};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (cseg[h] + e < p.cols) store_out(p, base + e, vv[e]);
             }
         }
     }
 }
 
+// Bytes of chain scratch the delta path needs for this call (0 without deltas).
+size_t merge_scratch_bytes(const MergeParams &p) {
+    if (p.n_deltas == 0) return 0;
+    int64_t ktot = 0;
+    for (int d = 0; d < p.n_deltas; ++d) ktot += p.d[d].rank;
+    const int64_t cols_p = (p.cols + kTileCols - 1) / kTileCols * kTileCols;
+    const int64_t rows_p = (p.rows + kTileRows - 1) / kTileRows * kTileRows;
+    return (size_t)(ktot * (cols_p + 2 * rows_p)) * sizeof(float);
+}
+
 template <int WDT>
-cudaError_t launch_merge(const MergeParams &p, cudaStream_t st, int sms) {
+cudaError_t launch_merge(const MergeParams &p, cudaStream_t st, int sms, void *scratch) {
     const size_t smem = sizeof(MergeSmem);
     const int64_t n = p.rows * p.cols;
     if (p.n_deltas == 0) {
@@ -239,17 +340,36 @@ cudaError_t launch_merge(const MergeParams &p, cudaStream_t st, int sms) {
             dequant_only_kernel<WDT, false><<<grid, 256, 0, st>>>(p, n);
         return cudaGetLastError();
     }
-    dim3 grid((unsigned)((p.cols + kTileCols - 1) / kTileCols), (unsigned)((p.rows + kTileRows - 1) / kTileRows));
+    // Chain scratch: a32[ktot][cols_p] + ct[ktot][rows_p], f32, zero padded.
+    ChainMap cm{};
+    cm.n = p.n_deltas;
+    int ktot = 0;
+    for (int d = 0; d < p.n_deltas; ++d) {
+        cm.start[d] = ktot;
+        ktot += p.d[d].rank;
+    }
+    const int64_t cols_p = (p.cols + kTileCols - 1) / kTileCols * kTileCols;
+    const int64_t rows_p = (p.rows + kTileRows - 1) / kTileRows * kTileRows;
+    float *a32 = static_cast<float *>(scratch);
+    float2 *ctp = reinterpret_cast<float2 *>(a32 + (int64_t)ktot * cols_p);
+    const int base_vec = (WDT == LTX_F8_E4M3 || WDT == LTX_F8_E5M2) && p.cols % kTileCols == 0 &&
+                         p.rows % kTileRows == 0 && (uintptr_t)p.w % 16 == 0;
+    {
+        const int64_t work = (int64_t)ktot * (cols_p + rows_p);
+        const int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sms * 16);
+        merge_prepass_kernel<<<grid, 256, 0, st>>>(p, cm, ktot, a32, ctp, cols_p, rows_p);
+    }
+    dim3 grid((unsigned)(cols_p / kTileCols), (unsigned)(rows_p / kTileRows));
     if (p.dst_bf16) {
         auto k = dequant_merge_kernel<WDT, true>;
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        k<<<grid, kWarps * 32, smem, st>>>(p);
+        k<<<grid, kWarps * 32, smem, st>>>(p, a32, ctp, ktot, cols_p, rows_p, base_vec);
     } else {
         auto k = dequant_merge_kernel<WDT, false>;
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        k<<<grid, kWarps * 32, smem, st>>>(p);
+        k<<<grid, kWarps * 32, smem, st>>>(p, a32, ctp, ktot, cols_p, rows_p, base_vec);
     }
     return cudaGetLastError();
 }
@@ -286,13 +406,18 @@ int dequant_merge(ltx_ctx *ctx, cudaStream_t stream, const void *w, int w_dt, in
     p.dst = dst;
     p.dst_bf16 = dst_dt == LTX_BF16;
     p.dst_aligned16 = ((uintptr_t)dst % 16) == 0;
+    const size_t need = merge_scratch_bytes(p);
+    if (need) {
+        int rc = ensure_scratch(ctx, need);
+        if (rc != LTX_OK) return rc;
+    }
     cudaError_t e;
     switch (w_dt) {
-    case LTX_F32: e = launch_merge<LTX_F32>(p, stream, ctx->sm_count); break;
-    case LTX_F16: e = launch_merge<LTX_F16>(p, stream, ctx->sm_count); break;
-    case LTX_BF16: e = launch_merge<LTX_BF16>(p, stream, ctx->sm_count); break;
-    case LTX_F8_E4M3: e = launch_merge<LTX_F8_E4M3>(p, stream, ctx->sm_count); break;
-    default: e = launch_merge<LTX_F8_E5M2>(p, stream, ctx->sm_count); break;
+    case LTX_F32: e = launch_merge<LTX_F32>(p, stream, ctx->sm_count, ctx->scratch); break;
+    case LTX_F16: e = launch_merge<LTX_F16>(p, stream, ctx->sm_count, ctx->scratch); break;
+    case LTX_BF16: e = launch_merge<LTX_BF16>(p, stream, ctx->sm_count, ctx->scratch); break;
+    case LTX_F8_E4M3: e = launch_merge<LTX_F8_E4M3>(p, stream, ctx->sm_count, ctx->scratch); break;
+    default: e = launch_merge<LTX_F8_E5M2>(p, stream, ctx->sm_count, ctx->scratch); break;
     }
     if (e != cudaSuccess) return cuda_fail(ctx, e, "dequant_merge launch");
     return LTX_OK;

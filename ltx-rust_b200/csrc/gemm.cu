@@ -1,0 +1,351 @@
+// K2: C[M,N] = A[M,K] . W[N,K]^T on the 5th-generation tensor cores, with
+// the DiT's linear-layer epilogues fused.  Replaces Burn `Linear::forward`
+// for every projection of the block (crates/ltx-dit/src/attention.rs:150-152,
+// :194, feed_forward.rs:38-42, model.rs:187, :254, adaln.rs:84-88, :130-142).
+//
+// Design (sm_100a, one CTA per SM, persistent):
+//   warp 0      TMA producer: 128x64 A tile + BNx64 W tile per stage,
+//               128-byte swizzle, STAGES-deep ring of mbarriers.
+//   warp 1      one thread issues tcgen05.mma (M=128, N=BN, K=16) x 4 per
+//               stage into a TMEM accumulator; tcgen05.commit frees the stage.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (one row per
+//               thread), fused bias / GELU(tanh) / gated residual, store.
+//   Two TMEM accumulators (2 x BN columns) let the epilogue of tile i run
+//   under the mainloop of tile i+1.  Tiles are walked in groups of 16
+//   M-blocks so the A panel and the W panel of concurrent tiles stay in L2.
+// No TMA multicast anywhere: each CTA loads its own tiles from local HBM.
+#include <cuda.h>
+
+#include "device_common.cuh"
+#include "internal.hpp"
+
+namespace ltx {
+
+enum GemmEpilogue : int {
+    EPI_BF16 = 0,        // out_bf16 = acc + bias
+    EPI_GELU_BF16 = 1,   // out_bf16 = gelu_tanh(acc + bias)
+    EPI_F32 = 2,         // out_f32 = acc + bias
+    EPI_RESID = 3,       // x_f32 += (acc + bias) * gate[gidx[row]][col]   (gate optional)
+};
+
+struct GemmParams {
+    int M, N, K;
+    const float *bias;      // [N] or null
+    void *out;              // bf16 / f32 [M, ldo]
+    int64_t ldo;
+    const float *gate;      // [U, ld_gate] or null (EPI_RESID)
+    const int *gate_idx;    // [M] row -> gate row (EPI_RESID, null = row 0)
+    int64_t ld_gate;
+    int *timeout_flag;
+};
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+constexpr int kGroupM = 16;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;  // power of two >= 32
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+};
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))  (feed_forward.rs:31-32)
+    const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+    return 0.5f * x * (1.0f + tanhf(u));
+}
+
+__device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, int &mb, int &nb) {
+    const int per_group = kGroupM * n_blocks;
+    const int g = t / per_group;
+    const int first_m = g * kGroupM;
+    const int gm = min(kGroupM, m_blocks - first_m);
+    const int r = t - g * per_group;
+    mb = first_m + r % gm;
+    nb = r / gm;
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    using C = GemmCfg<BN>;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *sA = smem;
+    unsigned char *sB = smem + C::STAGES * C::A_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+    uint64_t *empty = full + C::STAGES;
+    uint64_t *tfull = empty + C::STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m_blocks = (p.M + BM - 1) / BM, n_blocks = (p.N + BN - 1) / BN;
+    const int num_tiles = m_blocks * n_blocks;
+    const int k_blocks = (p.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    bool aborted = false;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            tma_prefetch_desc(&tmA);
+            tma_prefetch_desc(&tmB);
+            uint32_t it = 0;
+            for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
+                int mb, nb;
+                tile_coords(t, m_blocks, n_blocks, mb, nb);
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % C::STAGES;
+                    const uint32_t ph = (it / C::STAGES) & 1;
+                    if (!mbar_wait(&empty[s], ph ^ 1, p.timeout_flag, 101, &aborted)) break;
+                    mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+                    tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * BK, mb * BM);
+                    tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * BK, nb * BN);
+                }
+            }
+            if (aborted) {
+                // Let the copies already issued land before the CTA exits.
+                bool a2 = false;
+                for (uint32_t j = it > (uint32_t)C::STAGES ? it - C::STAGES : 0; j < it; ++j)
+                    mbar_wait(&full[j % C::STAGES], (j / C::STAGES) & 1, nullptr, 0, &a2);
+            }
+        }
+    } else if (warp == 1) {
+        if (elect_one()) {
+            constexpr uint32_t idesc = idesc_f16(BM, BN, true);
+            uint32_t it = 0, tile_i = 0;
+            for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tile_i) {
+                const uint32_t acc = tile_i & 1, aph = (tile_i >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], aph ^ 1, p.timeout_flag, 102, &aborted)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                    const int s = it % C::STAGES;
+                    const uint32_t ph = (it / C::STAGES) & 1;
+                    if (!mbar_wait(&full[s], ph, p.timeout_flag, 103, &aborted)) break;
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
+                    const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t ad = sdesc_sw128(a_addr + kk * 32, 16, 1024);
+                        const uint64_t bd = sdesc_sw128(b_addr + kk * 32, 16, 1024);
+                        umma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (aborted) break;
+                umma_commit(&tfull[acc]);
+            }
+        }
+    } else {
+        // Epilogue warps 2..5 own TMEM lane quadrant (warp % 4).
+        const int quad = warp & 3;
+        uint32_t tile_i = 0;
+        for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tile_i) {
+            int mb, nb;
+            tile_coords(t, m_blocks, n_blocks, mb, nb);
+            const uint32_t acc = tile_i & 1, aph = (tile_i >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], aph, p.timeout_flag, 104, &aborted)) break;
+            tc_fence_after();
+            const int row = mb * BM + quad * 32 + lane;
+            const bool row_ok = row < p.M;
+            const float *gate_row = nullptr;
+            if (EPI == EPI_RESID && p.gate) gate_row = p.gate + (int64_t)(p.gate_idx && row_ok ? p.gate_idx[row] : 0) * p.ld_gate;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
+                tmem_ld_wait();
+                const int col0 = nb * BN + c * 32;
+                if (!row_ok || col0 >= p.N) continue;
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                const bool full_cols = col0 + 32 <= p.N;
+                if (p.bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (full_cols || col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
+                }
+                if constexpr (EPI == EPI_BF16 || EPI == EPI_GELU_BF16) {
+                    if constexpr (EPI == EPI_GELU_BF16) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+                    }
+                    __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + (int64_t)row * p.ldo + col0;
+                    if (full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                __nv_bfloat162 h = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+                                w[e] = *reinterpret_cast<uint32_t *>(&h);
+                            }
+                            *reinterpret_cast<uint4 *>(o + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.N) o[j] = __float2bfloat16_rn(v[j]);
+                    }
+                } else if constexpr (EPI == EPI_F32) {
+                    float *o = static_cast<float *>(p.out) + (int64_t)row * p.ldo + col0;
+                    if (full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            *reinterpret_cast<float4 *>(o + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.N) o[j] = v[j];
+                    }
+                } else {  // EPI_RESID
+                    float *o = static_cast<float *>(p.out) + (int64_t)row * p.ldo + col0;
+                    if (full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            float4 x = *reinterpret_cast<float4 *>(o + 4 * q);
+                            float g[4] = {1.f, 1.f, 1.f, 1.f};
+                            if (gate_row) {
+                                const float4 g4 = __ldg(reinterpret_cast<const float4 *>(gate_row + col0 + 4 * q));
+                                g[0] = g4.x; g[1] = g4.y; g[2] = g4.z; g[3] = g4.w;
+                            }
+                            x.x += v[4 * q] * g[0];
+                            x.y += v[4 * q + 1] * g[1];
+                            x.z += v[4 * q + 2] * g[2];
+                            x.w += v[4 * q + 3] * g[3];
+                            *reinterpret_cast<float4 *>(o + 4 * q) = x;
+                        }
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < p.N) o[j] += v[j] * (gate_row ? gate_row[col0 + j] : 1.f);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// ── host side ────────────────────────────────────────────────────────────────
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] with leading dimension ld (elements), box {64, box_rows}.
+bool make_tmap_bf16(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+cudaError_t launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int sms, cudaStream_t st) {
+    using C = GemmCfg<BN>;
+    auto k = gemm_kernel<BN, EPI>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e != cudaSuccess) return e;
+    const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+    const int grid = std::min(tiles, sms);
+    k<<<grid, kThreads, C::SMEM, st>>>(ta, tb, p);
+    return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t dispatch_epi(int epi, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int sms,
+                         cudaStream_t st) {
+    switch (epi) {
+    case EPI_BF16: return launch_gemm<BN, EPI_BF16>(ta, tb, p, sms, st);
+    case EPI_GELU_BF16: return launch_gemm<BN, EPI_GELU_BF16>(ta, tb, p, sms, st);
+    case EPI_F32: return launch_gemm<BN, EPI_F32>(ta, tb, p, sms, st);
+    default: return launch_gemm<BN, EPI_RESID>(ta, tb, p, sms, st);
+    }
+}
+
+}  // namespace
+
+// Enqueues out = epilogue(A[M,K] . W[N,K]^T).  A and W are bf16 row-major
+// with leading dimensions lda/ldw (elements, multiples of 8, 16-byte aligned bases).
+int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
+              int K, int epi, const float *bias, void *out, int64_t ldo, const float *gate, const int *gate_idx,
+              int64_t ld_gate) {
+    if (!A || !W || !out) return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: null pointer");
+    if (M <= 0 || N <= 0 || K <= 0) return fail(ctx, LTX_ERR_SHAPE, "gemm: empty shape %d x %d x %d", M, N, K);
+    if (lda % 8 || ldw % 8 || lda < K || ldw < K || ((uintptr_t)A & 15) || ((uintptr_t)W & 15))
+        return fail(ctx, LTX_ERR_SHAPE, "gemm: operands need 16-byte aligned rows (lda %lld ldw %lld)", (long long)lda,
+                    (long long)ldw);
+    if (epi < EPI_BF16 || epi > EPI_RESID) return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: bad epilogue %d", epi);
+    const int BN = N <= 128 ? 128 : 256;
+    CUtensorMap ta, tb;
+    if (!make_tmap_bf16(&ta, A, M, K, lda, BM) || !make_tmap_bf16(&tb, W, N, K, ldw, BN))
+        return fail(ctx, LTX_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed");
+    GemmParams p{M, N, K, bias, out, ldo, gate, gate_idx, ld_gate, ctx->timeout_flag};
+    cudaError_t e = BN == 128 ? dispatch_epi<128>(epi, ta, tb, p, ctx->sm_count, st)
+                              : dispatch_epi<256>(epi, ta, tb, p, ctx->sm_count, st);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm launch");
+    return LTX_OK;
+}
+
+}  // namespace ltx
+
+extern "C" int ltx_gemm_bf16(ltx_ctx *ctx, const void *a_dev, int64_t lda, const void *w_dev, int64_t ldw, int32_t m,
+                             int32_t n, int32_t k, int32_t epilogue, const float *bias_dev, void *out_dev, int64_t ldo,
+                             const float *gate_dev, const int32_t *gate_idx_dev, int64_t ld_gate) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    return ltx::gemm_bf16(ctx, ctx->stream, a_dev, lda, w_dev, ldw, m, n, k, epilogue, bias_dev, out_dev, ldo, gate_dev,
+                          gate_idx_dev, ld_gate);
+}

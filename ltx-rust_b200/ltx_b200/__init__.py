@@ -57,6 +57,8 @@ def lib() -> ctypes.CDLL:
         "ltx_lora_coeff": (F, [F, F, ctypes.c_int32]),
         "ltx_dequant_merge": (I, [V, P, ctypes.c_int32, ctypes.c_int32, F, I64, I64,
                                   ctypes.POINTER(LoraDelta), ctypes.c_int32, P, ctypes.c_int32]),
+        "ltx_gemm_bf16": (I, [V, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                              P, P, I64, P, P, I64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -106,6 +108,22 @@ class Context:
         self.check(lib().ltx_dequant_merge(self.h, ctypes.c_void_p(w_ptr), w_dtype, int(has_scale), scale,
                                            out_features, in_features, arr, n, ctypes.c_void_p(dst_ptr),
                                            dst_dtype), "ltx_dequant_merge")
+
+
+EPI_BF16, EPI_GELU_BF16, EPI_F32, EPI_RESID = 0, 1, 2, 3
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t if isinstance(t, int) else t.data_ptr())
+
+
+def gemm(ctx: "Context", a, w, out, epilogue=EPI_BF16, bias=None, gate=None, gate_idx=None):
+    """out = epilogue(a @ w.T) with torch CUDA tensors (a [M,K] bf16, w [N,K] bf16)."""
+    M, K = a.shape
+    N = w.shape[0]
+    ctx.check(lib().ltx_gemm_bf16(ctx.h, _ptr(a), a.stride(0), _ptr(w), w.stride(0), M, N, K, epilogue,
+                                  _ptr(bias), _ptr(out), out.stride(0), _ptr(gate), _ptr(gate_idx),
+                                  gate.stride(0) if gate is not None else 0), "ltx_gemm_bf16")
 
 
 def lora_coeff(strength: float, alpha: float, rank: int) -> float:
