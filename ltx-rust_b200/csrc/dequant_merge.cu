@@ -115,13 +115,13 @@ __global__ void dequant_only_scalar_kernel(MergeParams p, int64_t n) {
 constexpr int kWarps = 8;
 constexpr int kRowsPerWarp = 16;
 constexpr int kTileRows = kWarps * kRowsPerWarp;  // 128
-constexpr int kTileCols = 256;                     // per lane: 4 cols at lane*4, 4 at 128+lane*4
-constexpr int kRChunk = 32;                        // chain steps per stage
+constexpr int kTileCols = 128;                     // per lane: 4 columns at lane*4
+constexpr int kRChunk = 16;                        // chain steps per stage
 
 struct MergeSmem {
-    float a[2][kRChunk][kTileCols];    // A chain rows                      64 KB
-    float2 c[2][kRChunk][kTileRows];   // {c, c} = coeff*B, paired for FFMA2 64 KB
-    uint8_t w8[kTileRows][kTileCols];  // FP8 base tile                      32 KB
+    float a[2][kRChunk][kTileCols];    // A chain rows                       16 KB
+    float2 c[2][kRChunk][kTileRows];   // {c, c} = coeff*B, paired for FFMA2  32 KB
+    uint8_t w8[kTileRows][kTileCols];  // FP8 base tile                       16 KB
 };
 
 struct ChainMap {
@@ -166,7 +166,7 @@ __device__ __forceinline__ float base_t(const MergeParams &p, int64_t idx) {
 }
 
 template <int WDT, bool OUT_BF16>
-__global__ void __launch_bounds__(kWarps * 32, 1)
+__global__ void __launch_bounds__(kWarps * 32, 2)
     dequant_merge_kernel(MergeParams p, const float *__restrict__ a32, const float2 *__restrict__ ct, int ktot,
                          int64_t cols_p, int64_t rows_p, int base_vec) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -202,8 +202,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     issue(0, 0);
     cp_async_commit();
 
-    float2 acc[kRowsPerWarp][4];
-    const int64_t cseg[2] = {col0 + lane * 4, col0 + 128 + lane * 4};
+    float2 acc[kRowsPerWarp][2];
+    const int64_t mycol = col0 + lane * 4;
     if (base_vec) {
         // FP8 only: decode the staged base tile.
         if (nchunks > 1) issue(1, 1);
@@ -213,35 +213,29 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 #pragma unroll
         for (int i = 0; i < kRowsPerWarp; ++i) {
             const int rr = warp * kRowsPerWarp + i;
+            const uint32_t w4 = *reinterpret_cast<const uint32_t *>(&s.w8[rr][lane * 4]);
+            float x[4];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint32_t w4 = *reinterpret_cast<const uint32_t *>(&s.w8[rr][h * 128 + lane * 4]);
-                float x[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const uint32_t b = (w4 >> (8 * e)) & 0xFFu;
-                    x[e] = WDT == LTX_F8_E4M3 ? dec_e4m3(b) : dec_e5m2(b);
-                    if (p.fp8_scaled) x[e] = __fmaf_rn(p.scale, x[e], 0.0f);
-                }
-                acc[i][2 * h] = make_float2(x[0], x[1]);
-                acc[i][2 * h + 1] = make_float2(x[2], x[3]);
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t b = (w4 >> (8 * e)) & 0xFFu;
+                x[e] = WDT == LTX_F8_E4M3 ? dec_e4m3(b) : dec_e5m2(b);
+                if (p.fp8_scaled) x[e] = __fmaf_rn(p.scale, x[e], 0.0f);
             }
+            acc[i][0] = make_float2(x[0], x[1]);
+            acc[i][1] = make_float2(x[2], x[3]);
         }
     } else
 #pragma unroll
     for (int i = 0; i < kRowsPerWarp; ++i) {
         const int64_t r = row0 + warp * kRowsPerWarp + i;
+        float x[4] = {0.f, 0.f, 0.f, 0.f};
+        if (r < p.rows) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            float x[4] = {0.f, 0.f, 0.f, 0.f};
-            if (r < p.rows) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    if (cseg[h] + e < p.cols) x[e] = base_t<WDT>(p, r * p.cols + cseg[h] + e);
-            }
-            acc[i][2 * h] = make_float2(x[0], x[1]);
-            acc[i][2 * h + 1] = make_float2(x[2], x[3]);
+            for (int e = 0; e < 4; ++e)
+                if (mycol + e < p.cols) x[e] = base_t<WDT>(p, r * p.cols + mycol + e);
         }
+        acc[i][0] = make_float2(x[0], x[1]);
+        acc[i][1] = make_float2(x[2], x[3]);
     }
 
     for (int ch = 0; ch < nchunks; ++ch) {
@@ -261,21 +255,24 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         }
         __syncthreads();
         const int nr = min(kRChunk, ktot - ch * kRChunk);
-        for (int r = 0; r < nr; ++r) {
-            const float4 a0 = *reinterpret_cast<const float4 *>(&s.a[buf][r][lane * 4]);
-            const float4 a1 = *reinterpret_cast<const float4 *>(&s.a[buf][r][128 + lane * 4]);
-            const float2 av[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y),
-                                  make_float2(a1.z, a1.w)};
+        auto step = [&](int r) {
+            const float4 a4 = *reinterpret_cast<const float4 *>(&s.a[buf][r][lane * 4]);
+            const float2 a01 = make_float2(a4.x, a4.y), a23 = make_float2(a4.z, a4.w);
 #pragma unroll
             for (int q = 0; q < kRowsPerWarp / 2; ++q) {
                 const float4 cc = *reinterpret_cast<const float4 *>(&s.c[buf][r][warp * kRowsPerWarp + 2 * q]);
                 const float2 c0 = make_float2(cc.x, cc.y), c1 = make_float2(cc.z, cc.w);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    acc[2 * q][j] = __ffma2_rn(c0, av[j], acc[2 * q][j]);
-                    acc[2 * q + 1][j] = __ffma2_rn(c1, av[j], acc[2 * q + 1][j]);
-                }
+                acc[2 * q][0] = __ffma2_rn(c0, a01, acc[2 * q][0]);
+                acc[2 * q][1] = __ffma2_rn(c0, a23, acc[2 * q][1]);
+                acc[2 * q + 1][0] = __ffma2_rn(c1, a01, acc[2 * q + 1][0]);
+                acc[2 * q + 1][1] = __ffma2_rn(c1, a23, acc[2 * q + 1][1]);
             }
+        };
+        if (nr == kRChunk) {
+#pragma unroll 4
+            for (int r = 0; r < kRChunk; ++r) step(r);
+        } else {
+            for (int r = 0; r < nr; ++r) step(r);
         }
         __syncthreads();   // buffer `buf` is refilled below
         if (base_vec && ch + 2 < nchunks) {
@@ -288,25 +285,22 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     for (int i = 0; i < kRowsPerWarp; ++i) {
         const int64_t r = row0 + warp * kRowsPerWarp + i;
         if (r >= p.rows) continue;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int64_t base = r * p.cols + cseg[h];
-            const float2 v0 = acc[i][2 * h], v1 = acc[i][2 * h + 1];
-            if (p.dst_aligned16 && cseg[h] + 4 <= p.cols && (base & 3) == 0) {
-                if constexpr (OUT_BF16) {
-                    __nv_bfloat162 h0 = __floats2bfloat162_rn(v0.x, v0.y), h1 = __floats2bfloat162_rn(v1.x, v1.y);
-                    __stcs(reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(p.dst) + base),
-                           make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1)));
-                } else {
-                    __stcs(reinterpret_cast<float4 *>(static_cast<float *>(p.dst) + base),
-                           make_float4(v0.x, v0.y, v1.x, v1.y));
-                }
+        const int64_t base = r * p.cols + mycol;
+        const float2 v0 = acc[i][0], v1 = acc[i][1];
+        if (p.dst_aligned16 && mycol + 4 <= p.cols && (base & 3) == 0) {
+            if constexpr (OUT_BF16) {
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(v0.x, v0.y), h1 = __floats2bfloat162_rn(v1.x, v1.y);
+                __stcs(reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(p.dst) + base),
+                       make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1)));
             } else {
-                const float vv[4] = {v0.x, v0.y, v1.x, v1.y};
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    if (cseg[h] + e < p.cols) store_out(p, base + e, vv[e]);
+                __stcs(reinterpret_cast<float4 *>(static_cast<float *>(p.dst) + base),
+                       make_float4(v0.x, v0.y, v1.x, v1.y));
             }
+        } else {
+            const float vv[4] = {v0.x, v0.y, v1.x, v1.y};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (mycol + e < p.cols) store_out(p, base + e, vv[e]);
         }
     }
 }

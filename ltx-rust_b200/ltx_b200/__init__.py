@@ -59,6 +59,8 @@ def lib() -> ctypes.CDLL:
                                   ctypes.POINTER(LoraDelta), ctypes.c_int32, P, ctypes.c_int32]),
         "ltx_gemm_bf16": (I, [V, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                               P, P, I64, P, P, I64]),
+        "ltx_attention_fwd": (I, [V, P, I64, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                  ctypes.c_int32, ctypes.c_int32, F, P, I64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -124,6 +126,13 @@ def gemm(ctx: "Context", a, w, out, epilogue=EPI_BF16, bias=None, gate=None, gat
     ctx.check(lib().ltx_gemm_bf16(ctx.h, _ptr(a), a.stride(0), _ptr(w), w.stride(0), M, N, K, epilogue,
                                   _ptr(bias), _ptr(out), out.stride(0), _ptr(gate), _ptr(gate_idx),
                                   gate.stride(0) if gate is not None else 0), "ltx_gemm_bf16")
+
+
+def attention(ctx: "Context", q, k, v, out, batch, heads, tq, tk, scale, head_dim=128):
+    """out = softmax(q k^T * scale) v; q/k/v/out token-major bf16 CUDA tensors (row stride = stride(0))."""
+    ctx.check(lib().ltx_attention_fwd(ctx.h, _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0),
+                                      batch, heads, tq, tk, head_dim, scale, _ptr(out), out.stride(0)),
+              "ltx_attention_fwd")
 
 
 def lora_coeff(strength: float, alpha: float, rank: int) -> float:
