@@ -153,6 +153,96 @@ int ltx_attention_fwd(ltx_ctx *ctx, const void *q_dev, int64_t ldq, const void *
                       const void *v_dev, int64_t ldv, int32_t batch, int32_t heads, int32_t tq,
                       int32_t tk, int32_t head_dim, float scale, void *out_dev, int64_t ldo);
 
+/* ── ltx-weights: the weight store ─────────────────────────────────────────── */
+
+typedef struct ltx_store ltx_store;
+
+/* Key maps applied at open (crates/ltx-weights/src/key_map.rs:90-111). */
+#define LTX_KEYMAP_IDENTITY 0     /* KeyMap::identity: names as stored              */
+#define LTX_KEYMAP_TRANSFORMER 1  /* KeyMap::transformer: keep and strip
+                                     `model.diffusion_model.`                       */
+
+/* WeightStore::open (store.rs:124-208): memory-maps the safetensors files,
+ * renames keys, rejects duplicates (LTX_ERR_DUPLICATE_KEY) and hides the
+ * `{key}_scale` siblings of FP8 tensors.  __metadata__ is merged, first file
+ * wins. */
+int ltx_store_open(ltx_ctx *ctx, const char *const *paths, int32_t n_paths, int32_t keymap,
+                   ltx_store **out);
+void ltx_store_destroy(ltx_store *store);
+/* WeightStore::merge_lora (store.rs:542-640): pairs `P.lora_A.weight` /
+ * `P.lora_B.weight` with `P.weight`, checks ranks and shapes, alpha defaults
+ * to the rank, coeff = ltx_lora_coeff(strength, alpha, rank).  The factors
+ * are kept on the device and applied in order by every later read.
+ * LTX_ERR_NO_LORA_MATCHES when nothing matched but something was unmatched. */
+int ltx_store_merge_lora(ltx_store *store, const char *lora_path, float strength, int32_t *n_matched,
+                         int32_t *n_unmatched);
+/* WeightStore::contains / keys (store.rs:443-455): 1 if visible, else 0. */
+int ltx_store_contains(const ltx_store *store, const char *key);
+int32_t ltx_store_num_keys(const ltx_store *store);
+const char *ltx_store_key(const ltx_store *store, int32_t index);
+/* WeightStore::shape (store.rs:462-467); dtype receives the ltx_dtype or -1. */
+int ltx_store_shape(ltx_store *store, const char *key, int64_t *dims, int32_t max_dims, int32_t *ndim,
+                    int32_t *dtype);
+/* WeightStore::metadata / config (store.rs:425-441): copies the string value
+ * (NUL-terminated, truncated to buf_len); *needed = full length + 1. */
+int ltx_store_metadata(const ltx_store *store, const char *key, char *buf, size_t buf_len, size_t *needed);
+/* WeightStore::read (store.rs:479-521) into device memory: decode, FP8 scale,
+ * merged LoRA deltas, as F32 (bit-exact with the reference) or BF16 (its
+ * round-to-nearest-even).  Enqueued on the context stream. */
+int ltx_store_read(ltx_store *store, const char *key, int32_t dst_dtype, void *dst_dev, size_t dst_bytes);
+
+/* ── ltx-dit: the video transformer ───────────────────────────────────────── */
+
+typedef struct ltx_model ltx_model;
+
+/* VideoTransformer::load (load.rs:61-107) from a store; `config_json` NULL =
+ * the store's __metadata__["config"] (bare or under "transformer"), parsed
+ * and validated like DiTConfig::from_json (config.rs:176-231).  Linear
+ * weights are read through the dequant+merge kernel into bf16; Q|K|V and
+ * K|V projections are fused at load.  LTX_ERR_MISSING_KEY / LTX_ERR_SHAPE
+ * mirror DitError::Weight. */
+int ltx_model_load(ltx_ctx *ctx, ltx_store *store, const char *config_json, ltx_model **out);
+/* A random-init model of the given config, built the way an FP8 LTX
+ * checkpoint is loaded: every linear weight drawn N(0, 0.02) on the device,
+ * quantised to float8_e4m3fn with scale amax/448, and merged with a rank
+ * `lora_rank` bf16 LoRA (N(0, 0.01), alpha = rank, `lora_strength`) by the
+ * dequant+merge kernel.  No reference counterpart (the reference tests use
+ * tiny random-init fixtures). */
+int ltx_model_init_random(ltx_ctx *ctx, const char *config_json, uint64_t seed, int32_t lora_rank,
+                          float lora_strength, ltx_model **out);
+void ltx_model_destroy(ltx_model *model);
+/* Device bytes held by the model's weights. */
+int64_t ltx_model_weight_bytes(const ltx_model *model);
+/* VideoTransformer::forward (model.rs:169-255) with context_mask and
+ * self_attn_mask None (as alpha_gen calls it): latent [B,T,in], timesteps
+ * [B,T], positions [B,3,T,2], context [B,S,cross_dim] -> out [B,T,out], all
+ * f32 device buffers.  Synchronises once to read the timesteps (the adaLN
+ * path runs on the distinct values only). */
+int ltx_model_forward(ltx_model *model, ltx_ctx *ctx, const float *latent_dev, const float *timesteps_dev,
+                      const float *positions_dev, const float *context_dev, int32_t batch, int32_t tokens,
+                      int32_t context_tokens, float *out_dev);
+
+/* ── ltx-sampler: one guided Euler step ────────────────────────────────────── */
+
+/* One iteration of euler_denoising_loop (loop_.rs:93-149) around the DiT:
+ *   t = mask * sigma per token (guidance.rs:114)
+ *   v_c, v_u = DiT(latent, t, positions, ctx_cond / ctx_uncond)  — one batch-2
+ *              forward when cfg_scale != 1 (guidance.rs:58-60, :126, :147)
+ *   x0 = latent - t * v  (velocity -> x0; the reference has no such adapter,
+ *                         this is upstream LTX-2's X0 rule)
+ *   pred = x0_c + (cfg-1)(x0_c - x0_u), rescaled by
+ *          rescale*std(x0_c)/std(pred) + (1-rescale)  (guidance.rs:149-165)
+ *   x0' = x0*m + clean*(1-m); latent += ((latent - x0')/sigma)(sigma_next - sigma)
+ *                                                      (loop_.rs:37-65)
+ * latent_dev [T, C] is updated in place.  mask_host (optional, T floats)
+ * avoids a device read of mask_dev.  LTX_ERR_SIGMA / LTX_ERR_NEGATIVE_CONTEXT
+ * as SamplerError::InvalidSigma / MissingNegativeContext. */
+int ltx_denoise_step(ltx_model *model, ltx_ctx *ctx, float *latent_dev, const float *clean_dev,
+                     const float *mask_host, const float *mask_dev, const float *positions_dev,
+                     const float *ctx_cond_dev, const float *ctx_uncond_dev, int32_t tokens,
+                     int32_t context_tokens, float sigma, float sigma_next, float cfg_scale,
+                     float rescale_scale);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,7 @@ extern "C" void ltx_ctx_destroy(ltx_ctx *ctx) {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->work) cudaFree(ctx->work);
     if (ctx->timeout_flag) cudaFree(ctx->timeout_flag);
     if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
     delete ctx;

@@ -15,6 +15,7 @@
 //                   rounding of every element is the reference's.
 #include "device_common.cuh"
 #include "internal.hpp"
+#include "kernels.hpp"
 
 namespace ltx {
 namespace {

@@ -1,0 +1,477 @@
+// The DiT's memory-bound kernels (K4 norms/modulation, K5 timestep path,
+// RoPE tables, head gating) and the sampler update (K6: CFG + rescale +
+// post-process + Euler).  Each cites the reference code it replaces.
+#include "device_common.cuh"
+#include "internal.hpp"
+#include "kernels.hpp"
+
+namespace ltx {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// Block-wide sum over blockDim.x (a multiple of 32, <= 1024) threads, fixed order.
+__device__ float block_sum(float v, float *red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+    if (warp == 0) {
+        t = lane < nw ? red[lane] : 0.f;
+        t = warp_sum(t);
+        if (lane == 0) red[32] = t;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+// ── RoPE tables (rope.rs:46-167) ─────────────────────────────────────────────
+
+// positions [B, 3, T, 2] -> cos/sin [B*T, width]:
+//   split:       width = inner/2, entry pad + g*3 + p, pad = inner/2 - 3*grid
+//   interleaved: width = inner,   entries pad + 2*(g*3+p) + {0,1}, pad = inner - 6*grid
+// with angle = (((s+e)/2)/max_p * 2 - 1) * freq[g] (or s/max_p without the
+// mid-point grid), padding entries cos 1 / sin 0.
+__global__ void rope_table_kernel(const float *pos, int B, int T, const float *freq, int grid, float mp0, float mp1,
+                                  float mp2, int use_mid, int interleaved, int width, float *cos_out, float *sin_out) {
+    const int64_t total = (int64_t)B * T * width;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t bt = i / width;
+        const int e = (int)(i % width);
+        const int b = (int)(bt / T), t = (int)(bt % T);
+        const int used = interleaved ? 6 * grid : 3 * grid;
+        const int pad = width - used;
+        float c = 1.f, s = 0.f;
+        if (e >= pad) {
+            const int idx = interleaved ? (e - pad) >> 1 : (e - pad);
+            const int g = idx / 3, ax = idx % 3;
+            const float *pp = pos + (((int64_t)b * 3 + ax) * T + t) * 2;
+            const float mp = ax == 0 ? mp0 : (ax == 1 ? mp1 : mp2);
+            const float frac = use_mid ? __fdiv_rn(__fdiv_rn(__fadd_rn(pp[0], pp[1]), 2.0f), mp) : __fdiv_rn(pp[0], mp);
+            const float fm = __fadd_rn(__fmul_rn(frac, 2.0f), -1.0f);
+            const float ang = __fmul_rn(fm, freq[g]);
+            sincosf(ang, &s, &c);
+        }
+        cos_out[i] = c;
+        sin_out[i] = s;
+    }
+}
+
+// ── norms + adaLN modulation (norm.rs:23-53, block.rs:131-132, :150-151, model.rs:237-253) ──
+
+// One block per row.  mode 0: y = x / sqrt(mean(x^2)+eps)
+//                     mode 1: y = rms(x) * (1 + scale) + shift
+//                     mode 2: y = layer_norm(x) * (1 + scale) + shift
+// shift/scale rows come from a modulation table tab[u][k][D] (u = idx[row]).
+__global__ void norm_mod_kernel(const float *x, int64_t ldx, int rows, int D, float eps, int mode, const float *tab,
+                                int tab_coeff, const int *idx, int k_shift, __nv_bfloat16 *out, int64_t ldo) {
+    __shared__ float red[33];
+    const int row = blockIdx.x;
+    if (row >= rows) return;
+    const float *xr = x + (int64_t)row * ldx;
+    float mean = 0.f;
+    if (mode == 2) {
+        float s = 0.f;
+        for (int c = threadIdx.x; c < D; c += blockDim.x) s += xr[c];
+        mean = block_sum(s, red) / (float)D;
+    }
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
+        const float v = xr[c] - mean;
+        ss += v * v;
+    }
+    const float denom = sqrtf(block_sum(ss, red) / (float)D + eps);
+    const float *shift = nullptr, *scale = nullptr;
+    if (mode != 0) {
+        const int u = idx ? idx[row] : 0;
+        shift = tab + ((int64_t)u * tab_coeff + k_shift) * D;
+        scale = shift + D;
+    }
+    __nv_bfloat16 *o = out + (int64_t)row * ldo;
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
+        float y = (xr[c] - mean) / denom;
+        if (mode != 0) y = y * (scale[c] + 1.0f) + shift[c];
+        o[c] = __float2bfloat16_rn(y);
+    }
+}
+
+// Modulation tables for all blocks at once:
+//   tab[l][u][k][c] = sst_l[k][c] + mod[u][k*D + c]   (block.rs:164-198)
+// and the output head table
+//   otab[u][k][c] = sst_out[k][c] + emb[u][c]         (model.rs:237-245)
+__global__ void ada_tables_kernel(const float *const *sst, int L, int coeff, const float *mod, const float *sst_out,
+                                  const float *emb, int U, int D, float *tab, float *otab) {
+    const int64_t per_block = (int64_t)U * coeff * D;
+    const int64_t total = per_block * L + (int64_t)U * 2 * D;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        if (i < per_block * L) {
+            const int l = (int)(i / per_block);
+            const int64_t r = i % per_block;
+            const int u = (int)(r / ((int64_t)coeff * D));
+            const int64_t kc = r % ((int64_t)coeff * D);
+            tab[i] = sst[l][kc] + mod[(int64_t)u * coeff * D + kc];
+        } else {
+            const int64_t r = i - per_block * L;
+            const int u = (int)(r / (2 * D));
+            const int64_t kc = r % (2 * D);
+            otab[r] = sst_out[kc] + emb[(int64_t)u * D + kc % D];
+        }
+    }
+}
+
+// ── Q/K RMSNorm(gamma) over the full inner dim + split/interleaved RoPE ──────
+// (attention.rs:154-160 with Burn RmsNorm, rope.rs:231-257 / :269-293).
+// In place on bf16 rows [rows, D] (leading dimension ld).  One block per row.
+__global__ void qk_norm_rope_kernel(__nv_bfloat16 *buf, int64_t ld, int rows, int D, int H, float eps,
+                                    const float *gamma, const float *cos_t, const float *sin_t, int interleaved) {
+    extern __shared__ float row_s[];
+    __shared__ float red[33];
+    const int row = blockIdx.x;
+    if (row >= rows) return;
+    __nv_bfloat16 *xr = buf + (int64_t)row * ld;
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
+        const float v = __bfloat162float(xr[c]);
+        row_s[c] = v;
+        ss += v * v;
+    }
+    const float denom = sqrtf(block_sum(ss, red) / (float)D + eps);
+    for (int c = threadIdx.x; c < D; c += blockDim.x) row_s[c] = row_s[c] / denom * gamma[c];
+    __syncthreads();
+    if (!cos_t) {
+        for (int c = threadIdx.x; c < D; c += blockDim.x) xr[c] = __float2bfloat16_rn(row_s[c]);
+        return;
+    }
+    if (!interleaved) {
+        const int d = D / H, half = d / 2, width = D / 2;
+        const float *cr = cos_t + (int64_t)row * width, *sr = sin_t + (int64_t)row * width;
+        for (int i = threadIdx.x; i < width; i += blockDim.x) {
+            const int h = i / half, j = i % half;
+            const float x1 = row_s[h * d + j], x2 = row_s[h * d + half + j];
+            const float c = cr[i], s = sr[i];
+            xr[h * d + j] = __float2bfloat16_rn(c * x1 - s * x2);
+            xr[h * d + half + j] = __float2bfloat16_rn(s * x1 + c * x2);
+        }
+    } else {
+        const float *cr = cos_t + (int64_t)row * D, *sr = sin_t + (int64_t)row * D;
+        for (int c = threadIdx.x; c < D; c += blockDim.x) {
+            const float rot = (c & 1) ? row_s[c - 1] : -row_s[c + 1];
+            xr[c] = __float2bfloat16_rn(row_s[c] * cr[c] + rot * sr[c]);
+        }
+    }
+}
+
+// ── timestep path (adaln.rs:43-142, model.rs:196-206) ────────────────────────
+
+__global__ void sinusoid_kernel(const float *ts, int U, float ts_mult, const float *freq, float *out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= U * 128) return;
+    const int u = i / 128, f = i % 128;
+    const float ang = __fmul_rn(__fmul_rn(ts[u], ts_mult), freq[f]);
+    float s, c;
+    sincosf(ang, &s, &c);
+    out[u * 256 + f] = c;
+    out[u * 256 + 128 + f] = s;
+}
+
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+
+// out[u][n] = bias[n] + sum_k f(x[u][k]) W[n][k], f = SiLU or identity; f32
+// weights and accumulation (the timestep MLP and adaLN projection run on the
+// few distinct timesteps only).  One warp per output column, U <= 4 rows per pass.
+__global__ void small_linear_kernel(const float *x, int U, int K, const float *W, const float *bias, int N, int silu_in,
+                                    float *out) {
+    extern __shared__ float xs[];   // [4][K]
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    for (int u0 = 0; u0 < U; u0 += 4) {
+        const int nu = min(4, U - u0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < nu * K; i += blockDim.x) {
+            const float v = x[(int64_t)(u0 + i / K) * K + i % K];
+            xs[i] = silu_in ? silu(v) : v;
+        }
+        __syncthreads();
+        if (warp < N) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            const float *w = W + (int64_t)warp * K;
+            for (int k = lane; k < K; k += 32) {
+                const float wv = w[k];
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+                    if (r < nu) acc[r] += wv * xs[r * K + k];
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const float s = warp_sum(acc[r]);
+                if (lane == 0 && r < nu) out[(int64_t)(u0 + r) * N + warp] = s + (bias ? bias[warp] : 0.f);
+            }
+        }
+    }
+}
+
+// ── small elementwise helpers ────────────────────────────────────────────────
+
+__global__ void f32_to_bf16_kernel(const float *in, int64_t n, __nv_bfloat16 *out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = __float2bfloat16_rn(in[i]);
+}
+
+// ctx' = ctx * (1 + pst[1]) + pst[0], bf16 out (block.rs:217-223, cross-attention AdaLN flag path).
+__global__ void ctx_mod_kernel(const float *ctx, int64_t n, int D, const float *pst, __nv_bfloat16 *out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % D);
+        out[i] = __float2bfloat16_rn(ctx[i] * (pst[D + c] + 1.0f) + pst[c]);
+    }
+}
+
+// out[row][h*d + c] *= 2 * sigmoid(logit[row][h])   (attention.rs:180-189)
+__global__ void head_gate_kernel(__nv_bfloat16 *o, int64_t ldo, const float *logits, int64_t ldl, int rows, int H,
+                                 int d) {
+    const int64_t total = (int64_t)rows * H * d;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int row = (int)(i / (H * d));
+        const int hc = (int)(i % (H * d));
+        const float g = 2.0f / (1.0f + expf(-logits[(int64_t)row * ldl + hc / d]));
+        __nv_bfloat16 *p = o + (int64_t)row * ldo + hc;
+        *p = __float2bfloat16_rn(__bfloat162float(*p) * g);
+    }
+}
+
+// ── generic attention for head dims other than 128 (small configs only) ──────
+// One block per (batch, head, query row); scores staged in shared memory.
+__global__ void attn_generic_kernel(const __nv_bfloat16 *q, int64_t ldq, const __nv_bfloat16 *k, int64_t ldk,
+                                    const __nv_bfloat16 *v, int64_t ldv, int B, int H, int Tq, int Tk, int d,
+                                    float scale, __nv_bfloat16 *out, int64_t ldo) {
+    extern __shared__ float sm[];   // [d] q row, then [Tk] scores
+    __shared__ float red[33];
+    const int t = blockIdx.x % Tq, h = (blockIdx.x / Tq) % H, b = blockIdx.x / (Tq * H);
+    float *qs = sm, *sc = sm + d;
+    const __nv_bfloat16 *qr = q + ((int64_t)b * Tq + t) * ldq + h * d;
+    for (int c = threadIdx.x; c < d; c += blockDim.x) qs[c] = __bfloat162float(qr[c]);
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < Tk; j += blockDim.x) {
+        const __nv_bfloat16 *kr = k + ((int64_t)b * Tk + j) * ldk + h * d;
+        float s = 0.f;
+        for (int c = 0; c < d; ++c) s += qs[c] * __bfloat162float(kr[c]);
+        s *= scale;
+        sc[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    // block max
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = -INFINITY;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+        red[32] = m;
+    }
+    __syncthreads();
+    const float m = red[32];
+    __syncthreads();
+    float sum = 0.f;
+    for (int j = threadIdx.x; j < Tk; j += blockDim.x) {
+        const float p = expf(sc[j] - m);
+        sc[j] = p;
+        sum += p;
+    }
+    const float l = block_sum(sum, red);
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+        float acc = 0.f;
+        for (int j = 0; j < Tk; ++j) acc += sc[j] * __bfloat162float(v[((int64_t)b * Tk + j) * ldv + h * d + c]);
+        out[((int64_t)b * Tq + t) * ldo + h * d + c] = __float2bfloat16_rn(acc / l);
+    }
+}
+
+// ── K6: CFG + rescale + post-process + Euler (guidance.rs:149-165, loop_.rs:37-65) ──
+//
+// x0_c = x - t*v_c, x0_u = x - t*v_u  (velocity -> x0 per token, t = mask*sigma)
+// pred = x0_c + (g-1)(x0_c - x0_u);  factor = r*std(x0_c)/std(pred) + (1-r)
+// x0   = pred*factor;  x0' = x0*m + clean*(1-m);  x += ((x - x0')/sigma)*(sigma_next - sigma)
+// Stats: per-block f64 partial sums (sum, sumsq) of x0_c and pred in a fixed
+// order, then one block folds them — deterministic for a given grid.
+
+constexpr int kStatBlocks = 256;
+
+__global__ void cfg_stats_kernel(const float *x, const float *vc, const float *vu, const float *tok_t, int T, int C,
+                                 float g, double *partial) {
+    __shared__ double red[4][32];
+    double s[4] = {0, 0, 0, 0};
+    const int64_t n = (int64_t)T * C;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float t = tok_t[i / C];
+        const float xc = x[i] - t * vc[i];
+        const float xu = x[i] - t * vu[i];
+        const float pr = xc + (g - 1.0f) * (xc - xu);
+        s[0] += xc;
+        s[1] += (double)xc * xc;
+        s[2] += pr;
+        s[3] += (double)pr * pr;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        double v = s[q];
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+        if (lane == 0) red[q][warp] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < 4) {
+        double v = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += red[threadIdx.x][w];
+        partial[blockIdx.x * 4 + threadIdx.x] = v;
+    }
+}
+
+__global__ void cfg_euler_apply_kernel(float *x, const float *vc, const float *vu, const float *tok_t, const float *mask,
+                                       const float *clean, int T, int C, float g, float rescale, int use_cfg,
+                                       const double *partial, int nparts, float sigma, float sigma_next) {
+    __shared__ float factor_s;
+    if (threadIdx.x == 0) {
+        float factor = 1.0f;
+        if (use_cfg && fabsf(rescale) >= 1e-6f) {
+            double s[4] = {0, 0, 0, 0};
+            for (int b = 0; b < nparts; ++b)
+                for (int q = 0; q < 4; ++q) s[q] += partial[b * 4 + q];
+            const double n = (double)T * C;
+            const double mc = s[0] / n, mp = s[2] / n;
+            const double vc_ = s[1] / n - mc * mc, vp = s[3] / n - mp * mp;
+            const double sc = sqrt(fmax(vc_, 0.0) + 1e-8), sp = sqrt(fmax(vp, 0.0) + 1e-8);
+            factor = (float)(rescale * (sc / sp) + (1.0 - rescale));
+        }
+        factor_s = factor;
+    }
+    __syncthreads();
+    const float factor = factor_s;
+    const float dt = sigma_next - sigma;
+    const int64_t n = (int64_t)T * C;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t tok = i / C;
+        const float t = tok_t[tok];
+        const float xi = x[i];
+        const float xc = xi - t * vc[i];
+        float x0 = xc;
+        if (use_cfg) {
+            const float xu = xi - t * vu[i];
+            x0 = (xc + (g - 1.0f) * (xc - xu)) * factor;
+        }
+        const float m = mask[tok];
+        const float x0a = x0 * m + clean[i] * (1.0f - m);
+        const float vel = (xi - x0a) / sigma;
+        x[i] = xi + vel * dt;
+    }
+}
+
+}  // namespace
+
+// ── launchers (kernels.hpp) ──────────────────────────────────────────────────
+
+static int grid_for(int64_t n, int sms, int per_sm = 8) {
+    return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * per_sm));
+}
+
+cudaError_t rope_table(cudaStream_t st, int sms, const float *pos, int B, int T, const float *freq, int grid,
+                       const float max_pos[3], bool use_mid, bool interleaved, int width, float *cos_out,
+                       float *sin_out) {
+    rope_table_kernel<<<grid_for((int64_t)B * T * width, sms), 256, 0, st>>>(
+        pos, B, T, freq, grid, max_pos[0], max_pos[1], max_pos[2], use_mid, interleaved, width, cos_out, sin_out);
+    return cudaGetLastError();
+}
+
+cudaError_t norm_mod(cudaStream_t st, const float *x, int64_t ldx, int rows, int D, float eps, int mode,
+                     const float *tab, int tab_coeff, const int *idx, int k_shift, __nv_bfloat16 *out, int64_t ldo) {
+    if (rows <= 0) return cudaSuccess;
+    norm_mod_kernel<<<rows, 256, 0, st>>>(x, ldx, rows, D, eps, mode, tab, tab_coeff, idx, k_shift, out, ldo);
+    return cudaGetLastError();
+}
+
+cudaError_t ada_tables(cudaStream_t st, int sms, const float *const *sst_dev, int L, int coeff, const float *mod,
+                       const float *sst_out, const float *emb, int U, int D, float *tab, float *otab) {
+    const int64_t total = (int64_t)L * U * coeff * D + (int64_t)U * 2 * D;
+    ada_tables_kernel<<<grid_for(total, sms), 256, 0, st>>>(sst_dev, L, coeff, mod, sst_out, emb, U, D, tab, otab);
+    return cudaGetLastError();
+}
+
+cudaError_t qk_norm_rope(cudaStream_t st, __nv_bfloat16 *buf, int64_t ld, int rows, int D, int H, float eps,
+                         const float *gamma, const float *cos_t, const float *sin_t, bool interleaved) {
+    if (rows <= 0) return cudaSuccess;
+    const size_t smem = (size_t)D * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(qk_norm_rope_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    qk_norm_rope_kernel<<<rows, 256, smem, st>>>(buf, ld, rows, D, H, eps, gamma, cos_t, sin_t, interleaved);
+    return cudaGetLastError();
+}
+
+cudaError_t sinusoid(cudaStream_t st, const float *ts, int U, float ts_mult, const float *freq, float *out) {
+    sinusoid_kernel<<<(U * 128 + 127) / 128, 128, 0, st>>>(ts, U, ts_mult, freq, out);
+    return cudaGetLastError();
+}
+
+cudaError_t small_linear(cudaStream_t st, const float *x, int U, int K, const float *W, const float *bias, int N,
+                         bool silu_in, float *out) {
+    const size_t smem = (size_t)4 * K * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(small_linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    const int warps_per_block = 8;
+    small_linear_kernel<<<(N + warps_per_block - 1) / warps_per_block, warps_per_block * 32, smem, st>>>(
+        x, U, K, W, bias, N, silu_in, out);
+    return cudaGetLastError();
+}
+
+cudaError_t f32_to_bf16(cudaStream_t st, int sms, const float *in, int64_t n, __nv_bfloat16 *out) {
+    f32_to_bf16_kernel<<<grid_for(n, sms), 256, 0, st>>>(in, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t ctx_mod(cudaStream_t st, int sms, const float *ctx, int64_t n, int D, const float *pst, __nv_bfloat16 *out) {
+    ctx_mod_kernel<<<grid_for(n, sms), 256, 0, st>>>(ctx, n, D, pst, out);
+    return cudaGetLastError();
+}
+
+cudaError_t head_gate(cudaStream_t st, int sms, __nv_bfloat16 *o, int64_t ldo, const float *logits, int64_t ldl,
+                      int rows, int H, int d) {
+    head_gate_kernel<<<grid_for((int64_t)rows * H * d, sms), 256, 0, st>>>(o, ldo, logits, ldl, rows, H, d);
+    return cudaGetLastError();
+}
+
+cudaError_t attention_generic(cudaStream_t st, const __nv_bfloat16 *q, int64_t ldq, const __nv_bfloat16 *k, int64_t ldk,
+                              const __nv_bfloat16 *v, int64_t ldv, int B, int H, int Tq, int Tk, int d, float scale,
+                              __nv_bfloat16 *out, int64_t ldo) {
+    const size_t smem = (size_t)(d + Tk) * sizeof(float);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(attn_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    attn_generic_kernel<<<B * H * Tq, 128, smem, st>>>(q, ldq, k, ldk, v, ldv, B, H, Tq, Tk, d, scale, out, ldo);
+    return cudaGetLastError();
+}
+
+size_t cfg_scratch_bytes() { return (size_t)kStatBlocks * 4 * sizeof(double); }
+
+cudaError_t cfg_euler(cudaStream_t st, int sms, float *x, const float *vc, const float *vu, const float *tok_t,
+                      const float *mask, const float *clean, int T, int C, float g, float rescale, bool use_cfg,
+                      double *partial, float sigma, float sigma_next) {
+    if (use_cfg) {
+        cfg_stats_kernel<<<kStatBlocks, 256, 0, st>>>(x, vc, vu, tok_t, T, C, g, partial);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    // The apply kernel folds the partials in every block (256 x 4 doubles, cheap) before updating.
+    cfg_euler_apply_kernel<<<grid_for((int64_t)T * C, sms, 4), 256, 0, st>>>(
+        x, vc, vu, tok_t, mask, clean, T, C, g, rescale, use_cfg, partial, kStatBlocks, sigma, sigma_next);
+    return cudaGetLastError();
+}
+
+}  // namespace ltx

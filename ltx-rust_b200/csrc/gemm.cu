@@ -18,6 +18,7 @@
 
 #include "device_common.cuh"
 #include "internal.hpp"
+#include "kernels.hpp"
 
 namespace ltx {
 

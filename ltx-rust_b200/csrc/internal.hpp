@@ -23,6 +23,9 @@ struct ltx_ctx {
     // Scratch buffer grown on demand and reused by later calls on this context.
     void *scratch = nullptr;
     size_t scratch_bytes = 0;
+    // Forward/step workspace (activations), grown on demand and reused.
+    void *work = nullptr;
+    size_t work_bytes = 0;
 };
 
 namespace ltx {

@@ -1,0 +1,49 @@
+// Internal launchers shared between the kernels and the host-side model code.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "internal.hpp"
+
+namespace ltx {
+
+// dequant_merge.cu
+int dequant_merge(ltx_ctx *ctx, cudaStream_t stream, const void *w, int w_dt, int has_scale, float scale, int64_t rows,
+                  int64_t cols, const ltx_lora_delta *deltas, int n_deltas, void *dst, int dst_dt);
+
+// gemm.cu (epilogue codes = ltx_epilogue)
+int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
+              int K, int epi, const float *bias, void *out, int64_t ldo, const float *gate, const int *gate_idx,
+              int64_t ld_gate);
+
+// attention.cu (head_dim 128)
+int attention_fwd(ltx_ctx *ctx, cudaStream_t st, const void *q, int64_t ldq, const void *k, int64_t ldk, const void *v,
+                  int64_t ldv, int B, int H, int Tq, int Tk, float scale, void *out, int64_t ldo);
+
+// dit_kernels.cu
+cudaError_t rope_table(cudaStream_t st, int sms, const float *pos, int B, int T, const float *freq, int grid,
+                       const float max_pos[3], bool use_mid, bool interleaved, int width, float *cos_out,
+                       float *sin_out);
+cudaError_t norm_mod(cudaStream_t st, const float *x, int64_t ldx, int rows, int D, float eps, int mode,
+                     const float *tab, int tab_coeff, const int *idx, int k_shift, __nv_bfloat16 *out, int64_t ldo);
+cudaError_t ada_tables(cudaStream_t st, int sms, const float *const *sst_dev, int L, int coeff, const float *mod,
+                       const float *sst_out, const float *emb, int U, int D, float *tab, float *otab);
+cudaError_t qk_norm_rope(cudaStream_t st, __nv_bfloat16 *buf, int64_t ld, int rows, int D, int H, float eps,
+                         const float *gamma, const float *cos_t, const float *sin_t, bool interleaved);
+cudaError_t sinusoid(cudaStream_t st, const float *ts, int U, float ts_mult, const float *freq, float *out);
+cudaError_t small_linear(cudaStream_t st, const float *x, int U, int K, const float *W, const float *bias, int N,
+                         bool silu_in, float *out);
+cudaError_t f32_to_bf16(cudaStream_t st, int sms, const float *in, int64_t n, __nv_bfloat16 *out);
+cudaError_t ctx_mod(cudaStream_t st, int sms, const float *ctx, int64_t n, int D, const float *pst, __nv_bfloat16 *out);
+cudaError_t head_gate(cudaStream_t st, int sms, __nv_bfloat16 *o, int64_t ldo, const float *logits, int64_t ldl,
+                      int rows, int H, int d);
+cudaError_t attention_generic(cudaStream_t st, const __nv_bfloat16 *q, int64_t ldq, const __nv_bfloat16 *k, int64_t ldk,
+                              const __nv_bfloat16 *v, int64_t ldv, int B, int H, int Tq, int Tk, int d, float scale,
+                              __nv_bfloat16 *out, int64_t ldo);
+size_t cfg_scratch_bytes();
+cudaError_t cfg_euler(cudaStream_t st, int sms, float *x, const float *vc, const float *vu, const float *tok_t,
+                      const float *mask, const float *clean, int T, int C, float g, float rescale, bool use_cfg,
+                      double *partial, float sigma, float sigma_next);
+
+}  // namespace ltx

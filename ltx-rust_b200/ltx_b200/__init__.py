@@ -61,6 +61,24 @@ def lib() -> ctypes.CDLL:
                               P, P, I64, P, P, I64]),
         "ltx_attention_fwd": (I, [V, P, I64, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                   ctypes.c_int32, ctypes.c_int32, F, P, I64]),
+        "ltx_store_open": (I, [V, ctypes.POINTER(ctypes.c_char_p), ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(V)]),
+        "ltx_store_destroy": (None, [V]),
+        "ltx_store_merge_lora": (I, [V, ctypes.c_char_p, F, ctypes.POINTER(ctypes.c_int32),
+                                     ctypes.POINTER(ctypes.c_int32)]),
+        "ltx_store_contains": (I, [V, ctypes.c_char_p]),
+        "ltx_store_num_keys": (ctypes.c_int32, [V]),
+        "ltx_store_key": (ctypes.c_char_p, [V, ctypes.c_int32]),
+        "ltx_store_shape": (I, [V, ctypes.c_char_p, ctypes.POINTER(I64), ctypes.c_int32,
+                                ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),
+        "ltx_store_metadata": (I, [V, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t,
+                                   ctypes.POINTER(ctypes.c_size_t)]),
+        "ltx_store_read": (I, [V, ctypes.c_char_p, ctypes.c_int32, P, ctypes.c_size_t]),
+        "ltx_model_load": (I, [V, V, ctypes.c_char_p, ctypes.POINTER(V)]),
+        "ltx_model_init_random": (I, [V, ctypes.c_char_p, ctypes.c_uint64, ctypes.c_int32, F, ctypes.POINTER(V)]),
+        "ltx_model_destroy": (None, [V]),
+        "ltx_model_weight_bytes": (I64, [V]),
+        "ltx_model_forward": (I, [V, V, P, P, P, P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, P]),
+        "ltx_denoise_step": (I, [V, V, P, P, P, P, P, P, P, ctypes.c_int32, ctypes.c_int32, F, F, F, F]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -133,6 +151,121 @@ def attention(ctx: "Context", q, k, v, out, batch, heads, tq, tk, scale, head_di
     ctx.check(lib().ltx_attention_fwd(ctx.h, _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0),
                                       batch, heads, tq, tk, head_dim, scale, _ptr(out), out.stride(0)),
               "ltx_attention_fwd")
+
+
+KEYMAP_IDENTITY, KEYMAP_TRANSFORMER = 0, 1
+
+
+class WeightStore:
+    """ltx-weights WeightStore over the C ABI (ltx_store_*); reads land in device memory."""
+
+    def __init__(self, ctx: Context, paths, keymap=KEYMAP_IDENTITY):
+        self.ctx = ctx
+        self.h = ctypes.c_void_p()
+        arr = (ctypes.c_char_p * len(paths))(*[p.encode() for p in paths])
+        ctx.check(lib().ltx_store_open(ctx.h, arr, len(paths), keymap, ctypes.byref(self.h)), "ltx_store_open")
+
+    def merge_lora(self, path: str, strength: float):
+        m, u = ctypes.c_int32(), ctypes.c_int32()
+        self.ctx.check(lib().ltx_store_merge_lora(self.h, path.encode(), strength, ctypes.byref(m), ctypes.byref(u)),
+                       "ltx_store_merge_lora")
+        return m.value, u.value
+
+    def contains(self, key):
+        return bool(lib().ltx_store_contains(self.h, key.encode()))
+
+    def keys(self):
+        return [lib().ltx_store_key(self.h, i).decode() for i in range(lib().ltx_store_num_keys(self.h))]
+
+    def shape(self, key):
+        dims = (ctypes.c_int64 * 8)()
+        nd, dt = ctypes.c_int32(), ctypes.c_int32()
+        self.ctx.check(lib().ltx_store_shape(self.h, key.encode(), dims, 8, ctypes.byref(nd), ctypes.byref(dt)),
+                       "ltx_store_shape")
+        return [dims[i] for i in range(nd.value)]
+
+    def metadata(self, key):
+        need = ctypes.c_size_t()
+        rc = lib().ltx_store_metadata(self.h, key.encode(), None, 0, ctypes.byref(need))
+        if rc != 0:
+            raise LtxError(rc, f"metadata {key!r}")
+        buf = ctypes.create_string_buffer(need.value)
+        lib().ltx_store_metadata(self.h, key.encode(), buf, need.value, None)
+        return buf.value.decode()
+
+    def read(self, key, dtype=LTX_F32):
+        """Returns a torch CUDA tensor (f32 or bf16) with the stored shape."""
+        import torch
+        shape = self.shape(key)
+        t = torch.empty(shape, dtype=torch.float32 if dtype == LTX_F32 else torch.bfloat16, device="cuda")
+        self.ctx.check(lib().ltx_store_read(self.h, key.encode(), dtype, _ptr(t), t.numel() * t.element_size()),
+                       "ltx_store_read")
+        return t
+
+    def close(self):
+        if self.h:
+            lib().ltx_store_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class VideoTransformer:
+    """ltx-dit VideoTransformer over the C ABI (ltx_model_*)."""
+
+    def __init__(self, ctx: Context, handle):
+        self.ctx, self.h = ctx, handle
+
+    @staticmethod
+    def load(ctx: Context, store: WeightStore, config_json: str | None = None):
+        h = ctypes.c_void_p()
+        ctx.check(lib().ltx_model_load(ctx.h, store.h, config_json.encode() if config_json else None, ctypes.byref(h)),
+                  "ltx_model_load")
+        return VideoTransformer(ctx, h)
+
+    @staticmethod
+    def init_random(ctx: Context, config_json: str, seed=0, lora_rank=64, lora_strength=1.0):
+        h = ctypes.c_void_p()
+        ctx.check(lib().ltx_model_init_random(ctx.h, config_json.encode(), seed, lora_rank, lora_strength,
+                                              ctypes.byref(h)), "ltx_model_init_random")
+        return VideoTransformer(ctx, h)
+
+    def weight_bytes(self):
+        return lib().ltx_model_weight_bytes(self.h)
+
+    def forward(self, latent, timesteps, positions, context, out):
+        """latent [B,T,in], timesteps [B,T], positions [B,3,T,2], context [B,S,Dc] -> out [B,T,out] (f32 CUDA)."""
+        B, T, _ = latent.shape
+        S = context.shape[1]
+        self.ctx.check(lib().ltx_model_forward(self.h, self.ctx.h, _ptr(latent), _ptr(timesteps), _ptr(positions),
+                                               _ptr(context), B, T, S, _ptr(out)), "ltx_model_forward")
+
+    def denoise_step(self, latent, clean, mask, positions, ctx_cond, ctx_uncond, sigma, sigma_next, cfg_scale=1.0,
+                     rescale_scale=0.7, mask_host=None):
+        """One guided Euler step in place on latent [T, C] (ltx_denoise_step)."""
+        T = latent.shape[0]
+        S = ctx_cond.shape[0]
+        mh = None
+        if mask_host is not None:
+            mh = mask_host.ctypes.data_as(ctypes.c_void_p)
+        self.ctx.check(lib().ltx_denoise_step(self.h, self.ctx.h, _ptr(latent), _ptr(clean), mh, _ptr(mask),
+                                              _ptr(positions), _ptr(ctx_cond), _ptr(ctx_uncond), T, S, sigma,
+                                              sigma_next, cfg_scale, rescale_scale), "ltx_denoise_step")
+
+    def close(self):
+        if self.h:
+            lib().ltx_model_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def lora_coeff(strength: float, alpha: float, rank: int) -> float:

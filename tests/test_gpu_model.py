@@ -1,0 +1,260 @@
+"""The weight store, the DiT forward and the guided Euler step through the C ABI,
+against the CPU oracle.
+
+Bars: store reads bit-exact (f32) with the oracle; DiT outputs and step
+latents within rel-L2 1e-2 (the bf16 bar of the north star) of the f32
+oracle, which is itself pinned to the reference fixtures at atol 1e-4 /
+rtol 1e-3 (tests/test_oracle_pinning.py).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import dit, sampler
+from oracle.weight_store import KeyMap, LoraFile, WeightStore as OracleStore
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    import ltx_b200
+    return ltx_b200.Context(0)
+
+
+def rel_l2(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+# ── store ─────────────────────────────────────────────────────────────────────
+
+def test_store_reads_match_oracle(ctx):
+    import ltx_b200
+    for files, km, lora in [(["fp8_e4m3fn_parity.safetensors"], 0, None),
+                            (["lora_parity_base.safetensors"], 0, ("lora_parity_lora.safetensors", 0.75)),
+                            (["transformer_keymap_fixture.safetensors"], 1, None),
+                            (["dit_parity.safetensors"], 0, None)]:
+        paths = [os.path.join(GOLD, f) for f in files]
+        st = ltx_b200.WeightStore(ctx, paths, km)
+        os_ = OracleStore(paths, KeyMap.transformer() if km else KeyMap.identity())
+        if lora:
+            m, u = st.merge_lora(os.path.join(GOLD, lora[0]), lora[1])
+            rep = os_.merge_lora(LoraFile(os.path.join(GOLD, lora[0])), lora[1])
+            assert m == len(rep.matched_keys) and u == len(rep.unmatched_lora_keys)
+        assert sorted(st.keys()) == sorted(os_.keys())
+        for k in os_.keys():
+            got = st.read(k).cpu().numpy()
+            exp = os_.read(k)
+            assert got.shape == tuple(exp.shape)
+            nan = np.isnan(exp)
+            assert (np.isnan(got) == nan).all()
+            assert (got[~nan].view(np.uint32) == exp[~nan].view(np.uint32)).all(), k
+
+
+def test_store_errors(ctx, tmp_path):
+    import ltx_b200
+    from oracle.weight_store import write_safetensors
+    f32b = lambda v: np.asarray(v, np.float32).tobytes()
+    p1 = str(tmp_path / "a.st")
+    write_safetensors(p1, {"x": ("F32", [1], f32b([0])), "w": ("I32", [2], np.array([1, 2], np.int32).tobytes())})
+    st = ltx_b200.WeightStore(ctx, [p1])
+    with pytest.raises(ltx_b200.LtxError) as e:
+        st.read("nope")
+    assert e.value.kind == "MISSING_KEY"
+    with pytest.raises(ltx_b200.LtxError) as e:
+        st.read("w")
+    assert e.value.kind == "DTYPE"
+    with pytest.raises(ltx_b200.LtxError) as e:
+        ltx_b200.WeightStore(ctx, [p1, p1])
+    assert e.value.kind == "DUPLICATE_KEY"
+    with pytest.raises(ltx_b200.LtxError) as e:
+        st.metadata("config")
+    assert e.value.kind == "MISSING_CONFIG"
+    lp = str(tmp_path / "l.st")
+    write_safetensors(lp, {"absent.lora_A.weight": ("F32", [1, 1], f32b([1])),
+                           "absent.lora_B.weight": ("F32", [1, 1], f32b([1]))})
+    with pytest.raises(ltx_b200.LtxError) as e:
+        st.merge_lora(lp, 1.0)
+    assert e.value.kind == "NO_LORA_MATCHES"
+    bp = str(tmp_path / "b.st")
+    write_safetensors(bp, {"layer.weight": ("F32", [2, 3], f32b([0] * 6))})
+    lb = str(tmp_path / "lb.st")
+    write_safetensors(lb, {"layer.lora_A.weight": ("F32", [1, 3], f32b([1, 2, 3])),
+                           "layer.lora_B.weight": ("F32", [4, 1], f32b([0] * 4))})
+    with pytest.raises(ltx_b200.LtxError) as e:
+        ltx_b200.WeightStore(ctx, [bp]).merge_lora(lb, 1.0)
+    assert e.value.kind == "SHAPE"
+
+
+# ── DiT fixtures (tiny, head_dim 8: generic attention path) ──────────────────
+
+@pytest.mark.parametrize("name", ["dit_parity.safetensors", "dit_parity_gated_adaln.safetensors"])
+def test_dit_fixture_forward(ctx, name):
+    import ltx_b200
+    path = os.path.join(GOLD, name)
+    st = ltx_b200.WeightStore(ctx, [path])
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    o = OracleStore([path], KeyMap.identity())
+    inp = {k: torch.from_numpy(o.read("input." + k)).cuda() for k in ("latent", "timesteps", "positions", "context")}
+    exp = o.read("output")
+    out = torch.empty(exp.shape, dtype=torch.float32, device="cuda")
+    model.forward(inp["latent"], inp["timesteps"], inp["positions"], inp["context"], out)
+    ctx.synchronize()
+    got = out.cpu().numpy()
+    err = rel_l2(got, exp)
+    print(f"\n{name}: rel-L2 {err:.2e}, max abs {np.abs(got - exp).max():.2e}")
+    assert err < 1e-2
+
+
+def test_model_load_errors(ctx):
+    import ltx_b200
+    path = os.path.join(GOLD, "dit_parity.safetensors")
+    st = ltx_b200.WeightStore(ctx, [path])
+    cfg = json.loads(st.metadata("config"))
+    bad = dict(cfg, num_layers=3)
+    with pytest.raises(ltx_b200.LtxError) as e:
+        ltx_b200.VideoTransformer.load(ctx, st, json.dumps(bad))
+    assert e.value.kind == "MISSING_KEY"
+    bad = dict(cfg, attention_head_dim=16)
+    with pytest.raises(ltx_b200.LtxError) as e:
+        ltx_b200.VideoTransformer.load(ctx, st, json.dumps(bad))
+    assert e.value.kind == "SHAPE"
+    bad = dict(cfg, apply_gated_attention=True)
+    with pytest.raises(ltx_b200.LtxError) as e:
+        ltx_b200.VideoTransformer.load(ctx, st, json.dumps(bad))
+    assert e.value.kind == "MISSING_KEY"
+    bad = dict(cfg, cross_attention_adaln=True, use_prompt_adaln_single=True)
+    with pytest.raises(ltx_b200.LtxError) as e:
+        ltx_b200.VideoTransformer.load(ctx, st, json.dumps(bad))
+    assert e.value.kind == "CONFIG"
+
+
+# ── mid-size FP8 + LoRA checkpoint (head_dim 128: tensor-core kernels) ───────
+
+@pytest.fixture(scope="module")
+def mid_ckpt(tmp_path_factory):
+    from dit_checkpoint import small_config, write_checkpoint, write_lora
+    d = tmp_path_factory.mktemp("ckpt")
+    cfg = small_config(heads=2, head_dim=128, layers=2)
+    ck, lo = str(d / "dit.safetensors"), str(d / "lora.safetensors")
+    write_checkpoint(ck, cfg, seed=3)
+    write_lora(lo, cfg, rank=16, alpha=8.0, seed=4)
+    o = OracleStore([ck], KeyMap.transformer())
+    o.merge_lora(LoraFile(lo), 0.9)
+    params = dit.load_params({k: o.read(k) for k in o.keys()})
+    return cfg, ck, lo, params
+
+
+def make_inputs(cfg, F=4, Hh=8, W=8, S=77, seed=0):
+    rng = np.random.default_rng(seed)
+    T = 2 * F * Hh * W
+    pos = np.concatenate([sampler.target_positions(F, Hh, W), sampler.reference_positions(F, Hh, W)], axis=2)
+    lat = rng.standard_normal((1, T, cfg["in_channels"])).astype(np.float32)
+    ts = np.concatenate([np.full(T // 2, 0.7, np.float32), np.zeros(T // 2, np.float32)])[None]
+    ctxt = rng.standard_normal((1, S, cfg["cross_attention_dim"])).astype(np.float32)
+    return lat, ts, pos, ctxt
+
+
+def test_mid_model_forward(ctx, mid_ckpt):
+    import ltx_b200
+    cfg, ck, lo, params = mid_ckpt
+    st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+    st.merge_lora(lo, 0.9)
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    lat, ts, pos, ctxt = make_inputs(cfg)
+    out = torch.empty(lat.shape, dtype=torch.float32, device="cuda")
+    model.forward(*(torch.from_numpy(a).cuda() for a in (lat, ts, pos, ctxt)), out)
+    ctx.synchronize()
+    c = dit.DiTConfig.from_json(cfg)
+    with torch.no_grad():
+        exp = dit.model_forward(params, c, *(torch.from_numpy(a) for a in (lat, ts, pos, ctxt))).numpy()
+    err = rel_l2(out.cpu().numpy(), exp)
+    print(f"\nmid model forward rel-L2 {err:.2e}")
+    assert err < 1e-2
+
+
+def test_mid_model_batch2_matches_batch1(ctx, mid_ckpt):
+    """CFG batching: the two rows of a batch-2 forward equal two batch-1 forwards."""
+    import ltx_b200
+    cfg, ck, lo, _ = mid_ckpt
+    st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    lat, ts, pos, c1 = make_inputs(cfg, seed=1)
+    c2 = np.random.default_rng(9).standard_normal(c1.shape).astype(np.float32)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    o2 = torch.empty((2,) + lat.shape[1:], dtype=torch.float32, device="cuda")
+    model.forward(dev(np.concatenate([lat, lat])), dev(np.concatenate([ts, ts])), dev(np.concatenate([pos, pos])),
+                  dev(np.concatenate([c1, c2])), o2)
+    outs = []
+    for c in (c1, c2):
+        o = torch.empty(lat.shape, dtype=torch.float32, device="cuda")
+        model.forward(dev(lat), dev(ts), dev(pos), dev(c), o)
+        outs.append(o)
+    ctx.synchronize()
+    for b in range(2):
+        assert rel_l2(o2[b].cpu().numpy(), outs[b][0].cpu().numpy()) < 1e-3
+
+
+def test_mid_model_denoise_step(ctx, mid_ckpt):
+    import ltx_b200
+    cfg, ck, lo, params = mid_ckpt
+    st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+    st.merge_lora(lo, 0.9)
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    F, Hh, W, S = 4, 8, 8, 64
+    rng = np.random.default_rng(5)
+    C, Tt = cfg["in_channels"], F * Hh * W
+    init = sampler.LatentState(rng.standard_normal((1, Tt, C)).astype(np.float32), np.ones((1, Tt, 1), np.float32),
+                               sampler.target_positions(F, Hh, W), np.zeros((1, Tt, C), np.float32))
+    ref = rng.standard_normal((1, C, F, Hh, W)).astype(np.float32)
+    state = sampler.apply_reference(init, ref, strength=1.0)
+    cc = rng.standard_normal((1, S, cfg["cross_attention_dim"])).astype(np.float32)
+    cu = rng.standard_normal((1, S, cfg["cross_attention_dim"])).astype(np.float32)
+    sig = sampler.scheduler_execute(8, Tt)
+    s0, s1 = float(sig[1]), float(sig[2])
+    c = dit.DiTConfig.from_json(cfg)
+
+    def model_x0(latent, ts, pos, ctx_):
+        with torch.no_grad():
+            v = dit.model_forward(params, c, torch.from_numpy(latent), torch.from_numpy(ts), torch.from_numpy(pos),
+                                  torch.from_numpy(ctx_)).numpy()
+        return sampler.velocity_to_x0(latent, ts, v)
+
+    exp = sampler.euler_loop([s0, s1], state, state.latent.shape[1], model_x0, cc, cu, cfg_scale=3.0,
+                             rescale_scale=0.7).latent[0]
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+    lat = dev(state.latent[0])
+    model.denoise_step(lat, dev(state.clean_latent[0]), dev(state.denoise_mask[0, :, 0]), dev(state.positions),
+                       dev(cc[0]), dev(cu[0]), s0, s1, 3.0, 0.7)
+    ctx.synchronize()
+    got = lat.cpu().numpy()
+    delta_err = rel_l2(got - state.latent[0], exp - state.latent[0])
+    print(f"\ndenoise step: latent rel-L2 {rel_l2(got, exp):.2e}, update rel-L2 {delta_err:.2e}")
+    assert rel_l2(got, exp) < 1e-2 and delta_err < 1e-2
+    # reference tokens (mask 0) keep x0' = clean: x_next = x + ((x - clean)/s0)(s1 - s0)
+    Tr = state.latent.shape[1] // 2
+    x, cl = state.latent[0, Tr:], state.clean_latent[0, Tr:]
+    np.testing.assert_allclose(got[Tr:], x + (x - cl) / np.float32(s0) * np.float32(s1 - s0), rtol=1e-5, atol=1e-5)
+
+
+def test_denoise_step_errors(ctx, mid_ckpt):
+    import ltx_b200
+    cfg, ck, lo, _ = mid_ckpt
+    st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    T, C = 64, cfg["in_channels"]
+    z = torch.zeros(T, C, device="cuda")
+    m = torch.ones(T, device="cuda")
+    pos = torch.from_numpy(sampler.target_positions(1, 8, 8)).cuda()
+    cc = torch.zeros(8, cfg["cross_attention_dim"], device="cuda")
+    with pytest.raises(ltx_b200.LtxError) as e:
+        model.denoise_step(z, z, m, pos, cc, None, 0.0, 0.0, 1.0)
+    assert e.value.kind == "SIGMA"
+    with pytest.raises(ltx_b200.LtxError) as e:
+        model.denoise_step(z, z, m, pos, cc, None, 0.5, 0.2, 3.0)
+    assert e.value.kind == "NEGATIVE_CONTEXT"
