@@ -7,8 +7,18 @@ rank per GPU; each rank processes its own independent units (weak scaling,
 no collective on the data path) and the step time is the max over ranks.
 
 Workloads:
+  denoise_step   config 4 (default): one Euler/CFG denoising step of the
+                 48-block 22B-class DiT (D 4096, 32x128 heads, FFN 16384) on
+                 T = 12288 tokens (16x24x16 target latent + same-size IC
+                 reference), 1024 context tokens, guidance 3.0 (CFG batch 2:
+                 cond / uncond contexts), rescale 0.7.  Random-init FP8 e4m3
+                 weights merged with a rank-64 LoRA on the device at load.
+                 metric tokens/s = 12288 / step time; at N GPUs each rank
+                 denoises its own temporal chunk (config 5's chunk-parallel
+                 axis: independent chunks, no collective), value = N*12288/t.
   dequant_merge  config 1: FP8 e4m3 [4096,4096] (+scale) + rank-64 bf16 LoRA
-                 -> bf16 [4096,4096], metric GB/s of algorithmic bytes.
+                 -> bf16 [4096,4096], metric GB/s of algorithmic bytes; also
+                 reported as the `dequant_merge` object of the step line.
 
 `--impl reference` times the reference algorithm's CPU restatement (the
 reference is a Rust workspace that cannot be built here) on the host cores,
@@ -18,6 +28,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import numpy as np
 import os
 import statistics
 import subprocess
@@ -204,6 +215,208 @@ def run_dequant_merge(args, rank, ws, device):
     return res
 
 
+# ── workload: denoise_step (config 4) ────────────────────────────────────────
+
+CFG4 = {"transformer": {"num_attention_heads": 32, "attention_head_dim": 128, "in_channels": 128,
+                        "out_channels": 128, "num_layers": 48, "cross_attention_dim": 4096, "norm_eps": 1e-6,
+                        "positional_embedding_theta": 10000.0, "positional_embedding_max_pos": [20, 2048, 2048],
+                        "timestep_scale_multiplier": 1000, "use_middle_indices_grid": True, "rope_type": "split",
+                        "apply_gated_attention": False, "cross_attention_adaln": False,
+                        "use_prompt_adaln_single": True, "ff_bias": False, "use_keyframes_abs_pos_embedding": False,
+                        "caption_proj_before_connector": True}}
+LAT_F, LAT_H, LAT_W = 16, 24, 16            # latent [1,128,16,24,16]
+T_TARGET = LAT_F * LAT_H * LAT_W             # 6144
+T_TOTAL = 2 * T_TARGET                       # + IC reference tokens
+S_CTX, D, FF = 1024, 4096, 16384
+
+
+def step_flops(layers=48, T=T_TOTAL, S=S_CTX, B=2):
+    """Matmul FLOPs of one CFG step (8.521 TF/block/pass + head)."""
+    gemm = 2 * T * D * (3 * D + D + D + D + 2 * FF) + 2 * S * D * 2 * D
+    attn = 4 * T * T * D + 4 * T * S * D
+    head = 2 * T * 128 * D + 2 * T * D * 128
+    return B * (layers * (gemm + attn) + head), B * layers * gemm, B * layers * attn
+
+
+def make_step_inputs(F, H, W, S, Dc, seed):
+    """Config-4 sampler state through the product API: target latent N(0,1) with
+    the IC reference appended (VideoReferenceCondition::apply_to,
+    conditioning.rs:63-106: zeros in the noisy latent, clean reference tokens,
+    mask 1 - strength = 0), positions from make_target/reference_positions,
+    cond/uncond contexts N(0,1), sigmas from LTX2Scheduler::execute(8, 6144)."""
+    import ltx_b200
+    rng = np.random.default_rng(seed)
+    Tt, C = F * H * W, 128
+    ref_tokens = rng.standard_normal((Tt, C), dtype=np.float32)
+    latent = np.concatenate([rng.standard_normal((Tt, C), dtype=np.float32), np.zeros((Tt, C), np.float32)])
+    clean = np.concatenate([np.zeros((Tt, C), np.float32), ref_tokens])
+    mask = np.concatenate([np.ones(Tt, np.float32), np.zeros(Tt, np.float32)])
+    pos = np.concatenate([ltx_b200.target_positions(F, H, W), ltx_b200.reference_positions(F, H, W)], axis=2)
+    return {"latent": latent, "clean": clean, "mask": mask, "positions": pos,
+            "ctx_cond": rng.standard_normal((S, Dc), dtype=np.float32),
+            "ctx_uncond": rng.standard_normal((S, Dc), dtype=np.float32),
+            "sigmas": ltx_b200.scheduler_execute(8, Tt)}
+
+
+def run_denoise_step(args, rank, ws, device):
+    import numpy as np
+    import torch
+    import ltx_b200
+    torch.cuda.set_device(device)
+    ctx = ltx_b200.Context(device)
+    t0 = time.time()
+    model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(CFG4), seed=7 + rank, lora_rank=64,
+                                                  lora_strength=1.0)
+    ctx.synchronize()
+    load_s = time.time() - t0
+    inp = make_step_inputs(LAT_F, LAT_H, LAT_W, S_CTX, D, seed=100 + rank)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+    lat0 = inp["latent"]
+    lat, clean, mask = dev(lat0), dev(inp["clean"]), dev(inp["mask"])
+    pos, cc, cu = dev(inp["positions"]), dev(inp["ctx_cond"]), dev(inp["ctx_uncond"])
+    mask_h = np.ascontiguousarray(inp["mask"], np.float32)
+    sig = inp["sigmas"]
+
+    def step(i):
+        s0, s1 = float(sig[i % (len(sig) - 1)]), float(sig[i % (len(sig) - 1) + 1])
+        if s1 <= 0:
+            s1 = 0.0
+        model.denoise_step(lat, clean, mask, pos, cc, cu, s0, s1, 3.0, 0.7, mask_host=mask_h)
+
+    for i in range(args.warmup):
+        step(i)
+    ctx.synchronize()
+    stream = torch.cuda.current_stream()
+    barrier(ws)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+    ctx.synchronize()
+    barrier(ws)
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps, ws)
+    # e2e through the C ABI from host buffers: pinned latent in, new latent out, each step
+    lat_h = torch.from_numpy(np.ascontiguousarray(lat0, np.float32)).pin_memory()
+    out_h = torch.empty_like(lat_h).pin_memory()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(1, min(args.steps, 3))
+    barrier(ws)
+    torch.cuda.synchronize()
+    s2.record(stream)
+    for i in range(n_e2e):
+        lat.copy_(lat_h, non_blocking=True)
+        step(i)
+        out_h.copy_(lat, non_blocking=True)
+    e2.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / n_e2e, ws)
+    ok = bool(torch.isfinite(out_h).all())
+    # dominant kernel timed alone: FFN-in GEMM (GELU epilogue) at the step's shape
+    M, N, K = 2 * T_TOTAL, FF, D
+    a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+    o = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    for _ in range(3):
+        ltx_b200.gemm(ctx, a, w, o, ltx_b200.EPI_GELU_BF16)
+    gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gs.record(stream)
+    for _ in range(10):
+        ltx_b200.gemm(ctx, a, w, o, ltx_b200.EPI_GELU_BF16)
+    ge.record(stream)
+    torch.cuda.synchronize()
+    gemm_ms = gs.elapsed_time(ge) / 10
+    del a, w, o
+    peaks, src = measured_peaks()
+    total, gemm_f, attn_f = step_flops()
+    gemm_tf = 2.0 * M * N * K / (gemm_ms * 1e-3) / 1e12
+    res = {
+        "metric": "DiT denoise-step tokens/s (config 4: 48 blocks, T=12288, CFG batch 2 + Euler)",
+        "value": ws * T_TOTAL / (ms * 1e-3),
+        "unit": "tokens/s",
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "dtype": "bf16 (tensor-core GEMM/attention inputs; f32 accumulate, residual and sampler)",
+        "config": {"workload": "denoise_step_config4", "layers": 48, "hidden": D, "heads": 32, "head_dim": 128,
+                   "ffn": FF, "tokens": T_TOTAL, "latent": [1, 128, LAT_F, LAT_H, LAT_W], "ic_reference": True,
+                   "context_tokens": S_CTX, "cfg_batch": 2, "guidance": 3.0, "rescale": 0.7,
+                   "weights": "random-init fp8 e4m3 per-tensor scale + rank-64 LoRA merged on device",
+                   "parallelism": f"chunk-parallel x{ws} (one independent chunk per GPU)",
+                   "l2": "inputs and weights exceed L2 (25.8 GB bf16 weights streamed per step)",
+                   "step_tflop": total / 1e12, "model_load_s": load_s},
+        "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMM, FFN-in + GELU (M=24576, N=16384, K=4096)",
+                     "achieved": gemm_tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": gemm_tf / peaks["bf16_tflops"], "traffic": None, "peak_source": src,
+                     "algorithmic_flops_per_launch": 2.0 * M * N * K,
+                     "step_tflops_achieved": total / (ms * 1e-3) / 1e12,
+                     "step_frac_of_sustained": total / (ms * 1e-3) / 1e12 / peaks.get("bf16_tflops_sustained",
+                                                                                      peaks["bf16_tflops"])},
+        "e2e": {"value": ws * T_TOTAL / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": lat_h.numel() * 4, "d2h_bytes_per_step": out_h.numel() * 4},
+        "gpu_launches": args.steps * launches_per_step(48),
+        "clocks": clk.summary(),
+        "finite_output": ok,
+    }
+    model.close()
+    ctx.close()
+    return res
+
+
+def launches_per_step(L):
+    """Kernels one ltx_denoise_step enqueues (counted from model.cpp's forward):
+    head 9 (convert, patchify GEMM, sinusoid, 3 small linears, tables, RoPE, ctx
+    convert), per block 16 (3 norms, 6 GEMMs, 3 QK-norm, 2 attention + 2 spare
+    for the cross K/V norm and q norm counted above), output 2, sampler 2."""
+    return 9 + L * 15 + 2 + 2
+
+
+def cpu_baseline_step(blocks=1, threads=None):
+    """The torch-f32 oracle (oracle/dit.py) on the host cores: one full-size
+    block for the CFG batch 2 (T=12288, S=1024, D=4096), extrapolated x48 +
+    the output head to the step.  Sample = `blocks` block forward(s)."""
+    import torch
+    from oracle import dit
+    dit.SDPA_Q_CHUNK = 256
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    cfg = dit.DiTConfig(num_layers=1)
+    p = {}
+    pre = "transformer_blocks.0."
+    shapes = {"attn1.to_q": (D, D), "attn1.to_k": (D, D), "attn1.to_v": (D, D), "attn1.to_out.0": (D, D),
+              "attn2.to_q": (D, D), "attn2.to_k": (D, D), "attn2.to_v": (D, D), "attn2.to_out.0": (D, D),
+              "ff.net.0.proj": (FF, D), "ff.net.2": (D, FF)}
+    for k, (o, i) in shapes.items():
+        p[pre + k + ".weight"] = torch.randn(o, i, generator=g) * 0.02
+        if "ff." not in k:
+            p[pre + k + ".bias"] = torch.zeros(o)
+    for a in ("attn1.", "attn2."):
+        p[pre + a + "q_norm.weight"] = torch.ones(D)
+        p[pre + a + "k_norm.weight"] = torch.ones(D)
+    p[pre + "scale_shift_table"] = torch.randn(6, D, generator=g) * 0.02
+    B = 2
+    x = torch.randn(B, T_TOTAL, D, generator=g)
+    ctx = torch.randn(B, S_CTX, D, generator=g)
+    mod = torch.randn(B, T_TOTAL, 6 * D, generator=g) * 0.02
+    from oracle import sampler as osam
+    pos = torch.from_numpy(np.concatenate([osam.target_positions(LAT_F, LAT_H, LAT_W, B),
+                                           osam.reference_positions(LAT_F, LAT_H, LAT_W, B)], axis=2))
+    pe = dit.precompute_freqs_cis(pos, cfg)
+    t0 = time.time()
+    with torch.no_grad():
+        for _ in range(blocks):
+            dit.block_forward(p, 0, cfg, x, ctx, mod, pe)
+    per_block = (time.time() - t0) / blocks
+    step_s = per_block * 48
+    return {"value": T_TOTAL / step_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{blocks} full-size block forward(s) (CFG batch 2, T=12288, S=1024) on the torch-f32 "
+                      f"oracle: {per_block:.1f} s/block, extrapolated x48 blocks (output head excluded)"}
+
+
 def cpu_baseline_dequant(seconds=5.0, threads=None):
     """The oracle (CPU restatement of store.rs:479-521 + 767-793) on all host cores."""
     from oracle.weight_store import LowRankDelta, decode_to_f32, read_raw
@@ -245,15 +458,30 @@ def max_over_ranks(x, ws):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="dequant_merge")
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="denoise_step", choices=["denoise_step", "dequant_merge"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=5.0)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_env()
 
+    if args.impl == "reference" and args.workload == "denoise_step":
+        if rank != 0:
+            return
+        base = cpu_baseline_step(blocks=1)
+        res = {"impl": "reference", "metric": "DiT denoise-step tokens/s (config 4: 48 blocks, T=12288, CFG batch 2 + Euler)",
+               "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": T_TOTAL / base["value"] * 1e3,
+               "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+               "data": "synthetic (random-init weights, N(0,1) activations)",
+               "config": {"workload": "denoise_step_config4"}, "cpu_baseline": base,
+               "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+               "note": "CPU restatement of the reference (oracle/dit.py, torch f32): the Rust reference cannot be "
+                       "built here; one block timed and extrapolated to the 48-block step"}
+        print(json.dumps(res))
+        return
     if args.impl == "reference":
         if rank != 0:
             return
@@ -275,12 +503,25 @@ def main():
         from datetime import timedelta
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    res = run_dequant_merge(args, rank, ws, local)
-    if rank == 0:
-        res.update({"n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
-                    "data": "synthetic (seeded N(0,0.02) weight, N(0,0.01) LoRA)"})
-        res["cpu_baseline"] = cpu_baseline_dequant(seconds=args.cpu_seconds) if ws == 1 else None
-        print(json.dumps(res))
+    if args.workload == "dequant_merge":
+        res = run_dequant_merge(args, rank, ws, local)
+        if rank == 0:
+            res.update({"n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
+                        "data": "synthetic (seeded N(0,0.02) weight, N(0,0.01) LoRA)"})
+            res["cpu_baseline"] = cpu_baseline_dequant(seconds=args.cpu_seconds) if ws == 1 else None
+            print(json.dumps(res))
+    else:
+        res = run_denoise_step(args, rank, ws, local)
+        dq_args = argparse.Namespace(steps=20, warmup=5)
+        dq = run_dequant_merge(dq_args, rank, ws, local)
+        if rank == 0:
+            res.update({"n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
+                        "data": "synthetic (random-init FP8+LoRA weights, N(0,1) latent/reference/contexts)"})
+            res["dequant_merge"] = {k: dq[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "e2e")}
+            if ws == 1 and args.cpu_seconds > 0:
+                res["cpu_baseline"] = cpu_baseline_step(blocks=1)
+                res["dequant_merge"]["cpu_baseline"] = cpu_baseline_dequant(seconds=min(args.cpu_seconds, 3.0))
+            print(json.dumps(res))
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -243,6 +243,30 @@ int ltx_denoise_step(ltx_model *model, ltx_ctx *ctx, float *latent_dev, const fl
                      int32_t context_tokens, float sigma, float sigma_next, float cfg_scale,
                      float rescale_scale);
 
+/* LTX2Scheduler::execute (crates/ltx-sampler/src/scheduler.rs:67-125): writes
+ * steps + 1 sigmas with the reference's f32 operations (bit-exact).  Defaults
+ * of SchedulerConfig: max_shift 2.05, base_shift 0.95, stretch 1, terminal 0.1.
+ * Host-only; needs no context or GPU. */
+int ltx_scheduler_execute(int32_t steps, uint64_t num_tokens, float max_shift, float base_shift,
+                          int32_t stretch, float terminal, float *sigmas_out);
+/* make_target_positions (patchifier.rs:101-118): [batch, 3, F*H*W, 2] f32
+ * pixel/time bounds with the causal fix, into host memory (bit-exact).
+ * LTX-2 scale factors are (8, 32, 32).  Host-only. */
+int ltx_target_positions(uint32_t frames, uint32_t height, uint32_t width, uint32_t batch, uint32_t scale_t,
+                         uint32_t scale_h, uint32_t scale_w, float fps, float *out_host);
+/* make_reference_positions (patchifier.rs:131-161) for IC-LoRA reference
+ * tokens, into host memory (bit-exact).  Host-only. */
+int ltx_reference_positions(uint32_t frames, uint32_t height, uint32_t width, uint32_t batch,
+                            uint32_t first_latent_frame, uint32_t scale_t, uint32_t scale_h, uint32_t scale_w,
+                            float fps, uint32_t temporal_scale_factor, uint32_t downscale_factor,
+                            float *out_host);
+/* patchify / unpatchify (patchifier.rs:50-89), patch size 1, on the device:
+ * [B, C, F, H, W] <-> [B, F*H*W, C] f32. */
+int ltx_patchify(ltx_ctx *ctx, const float *latent_dev, int32_t batch, int32_t channels, int32_t frames,
+                 int32_t height, int32_t width, float *tokens_dev);
+int ltx_unpatchify(ltx_ctx *ctx, const float *tokens_dev, int32_t batch, int32_t channels, int32_t frames,
+                   int32_t height, int32_t width, float *latent_dev);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,7 +25,7 @@ NVCC = os.path.join(CUDA, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
                      "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]
-CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-Wall", "-Wextra", "-I" + os.path.join(CUDA, "include"),
+CXX_FLAGS = ["-O3", "-std=c++17", "-ffp-contract=off", "-fPIC", "-Wall", "-Wextra", "-I" + os.path.join(CUDA, "include"),
              "-I" + os.path.join(ROOT, "include")]
 
 

@@ -1,4 +1,5 @@
 // ltx_ctx: device, stream, last-error text, device timeout flag, scratch.
+#include <algorithm>
 #include <cstring>
 #include <new>
 
@@ -20,6 +21,25 @@ int ensure_scratch(ltx_ctx *ctx, size_t bytes) {
     return LTX_OK;
 }
 
+int upload(ltx_ctx *ctx, void *dst_dev, const void *src_host, size_t bytes) {
+    if (bytes == 0) return LTX_OK;
+    // The staging buffer is reused: the previous upload must have left it.
+    LTX_CUDA_TRY(ctx, cudaEventSynchronize(ctx->upload_done));
+    if (ctx->pinned_bytes < bytes) {
+        if (ctx->pinned) cudaFreeHost(ctx->pinned);
+        ctx->pinned = nullptr;
+        ctx->pinned_bytes = 0;
+        const size_t want = std::max<size_t>(bytes, 1 << 20);
+        if (cudaHostAlloc(&ctx->pinned, want, cudaHostAllocDefault) != cudaSuccess)
+            return fail(ctx, LTX_ERR_OOM, "pinned staging of %zu bytes", want);
+        ctx->pinned_bytes = want;
+    }
+    memcpy(ctx->pinned, src_host, bytes);
+    LTX_CUDA_TRY(ctx, cudaMemcpyAsync(dst_dev, ctx->pinned, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    LTX_CUDA_TRY(ctx, cudaEventRecord(ctx->upload_done, ctx->stream));
+    return LTX_OK;
+}
+
 }  // namespace ltx
 
 extern "C" int ltx_ctx_create(int device, void *stream, ltx_ctx **out) {
@@ -38,7 +58,8 @@ extern "C" int ltx_ctx_create(int device, void *stream, ltx_ctx **out) {
     // The caller's stream; NULL is the CUDA default (legacy) stream, which is
     // also what PyTorch and most hosts enqueue on by default.
     ctx->stream = static_cast<cudaStream_t>(stream);
-    if (cudaMalloc(&ctx->timeout_flag, sizeof(int)) != cudaSuccess ||
+    if (cudaEventCreateWithFlags(&ctx->upload_done, cudaEventDisableTiming) != cudaSuccess ||
+        cudaMalloc(&ctx->timeout_flag, sizeof(int)) != cudaSuccess ||
         cudaMemsetAsync(ctx->timeout_flag, 0, sizeof(int), ctx->stream) != cudaSuccess) {
         if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
         delete ctx;
@@ -54,6 +75,8 @@ extern "C" void ltx_ctx_destroy(ltx_ctx *ctx) {
     cudaStreamSynchronize(ctx->stream);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->work) cudaFree(ctx->work);
+    if (ctx->pinned) cudaFreeHost(ctx->pinned);
+    if (ctx->upload_done) cudaEventDestroy(ctx->upload_done);
     if (ctx->timeout_flag) cudaFree(ctx->timeout_flag);
     if (ctx->own_stream) cudaStreamDestroy(ctx->stream);
     delete ctx;

@@ -6,6 +6,11 @@
 #include "kernels.hpp"
 
 namespace ltx {
+
+static int grid_for(int64_t n, int sms, int per_sm = 8) {
+    return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * per_sm));
+}
+
 namespace {
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -369,13 +374,31 @@ __global__ void cfg_euler_apply_kernel(float *x, const float *vc, const float *v
     }
 }
 
+// patchify (patchifier.rs:50-60): [B, C, T] -> [B, T, C], T = F*H*W (patch size 1);
+// unpatchify the inverse.  Pure index permutation (bit-exact).
+__global__ void permute_ct_kernel(const float *in, float *out, int B, int C, int64_t T, int to_tokens) {
+    const int64_t n = (int64_t)B * C * T;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / ((int64_t)C * T), r = i % ((int64_t)C * T);
+        if (to_tokens) {   // i indexes the token layout [b][t][c]
+            const int64_t t = r / C, c = r % C;
+            out[i] = in[(b * C + c) * T + t];
+        } else {           // i indexes the latent layout [b][c][t]
+            const int64_t c = r / T, t = r % T;
+            out[i] = in[(b * T + t) * C + c];
+        }
+    }
+}
+
 }  // namespace
+
+cudaError_t permute_ct(cudaStream_t st, int sms, const float *in, float *out, int B, int C, int64_t T, bool to_tokens) {
+    permute_ct_kernel<<<grid_for((int64_t)B * C * T, sms), 256, 0, st>>>(in, out, B, C, T, to_tokens);
+    return cudaGetLastError();
+}
 
 // ── launchers (kernels.hpp) ──────────────────────────────────────────────────
 
-static int grid_for(int64_t n, int sms, int per_sm = 8) {
-    return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * per_sm));
-}
 
 cudaError_t rope_table(cudaStream_t st, int sms, const float *pos, int B, int T, const float *freq, int grid,
                        const float max_pos[3], bool use_mid, bool interleaved, int width, float *cos_out,
@@ -475,3 +498,21 @@ cudaError_t cfg_euler(cudaStream_t st, int sms, float *x, const float *vc, const
 }
 
 }  // namespace ltx
+
+extern "C" int ltx_patchify(ltx_ctx *ctx, const float *latent_dev, int32_t batch, int32_t channels, int32_t frames,
+                            int32_t height, int32_t width, float *tokens_dev) {
+    if (!ctx || !latent_dev || !tokens_dev || batch < 0 || channels < 0 || frames < 0 || height < 0 || width < 0)
+        return ctx ? ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_patchify: bad arguments") : LTX_ERR_INVALID_ARG;
+    cudaError_t e = ltx::permute_ct(ctx->stream, ctx->sm_count, latent_dev, tokens_dev, batch, channels,
+                                    (int64_t)frames * height * width, true);
+    return e == cudaSuccess ? LTX_OK : ltx::cuda_fail(ctx, e, "ltx_patchify");
+}
+
+extern "C" int ltx_unpatchify(ltx_ctx *ctx, const float *tokens_dev, int32_t batch, int32_t channels, int32_t frames,
+                              int32_t height, int32_t width, float *latent_dev) {
+    if (!ctx || !latent_dev || !tokens_dev || batch < 0 || channels < 0 || frames < 0 || height < 0 || width < 0)
+        return ctx ? ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_unpatchify: bad arguments") : LTX_ERR_INVALID_ARG;
+    cudaError_t e = ltx::permute_ct(ctx->stream, ctx->sm_count, tokens_dev, latent_dev, batch, channels,
+                                    (int64_t)frames * height * width, false);
+    return e == cudaSuccess ? LTX_OK : ltx::cuda_fail(ctx, e, "ltx_unpatchify");
+}

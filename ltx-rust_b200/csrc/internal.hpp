@@ -26,6 +26,11 @@ struct ltx_ctx {
     // Forward/step workspace (activations), grown on demand and reused.
     void *work = nullptr;
     size_t work_bytes = 0;
+    // Pinned host staging for the small per-call uploads (timestep index),
+    // so they do not serialise the host with the stream.
+    void *pinned = nullptr;
+    size_t pinned_bytes = 0;
+    cudaEvent_t upload_done = nullptr;
 };
 
 namespace ltx {
@@ -48,6 +53,9 @@ inline int cuda_fail(ltx_ctx *ctx, cudaError_t e, const char *what) {
 
 // Makes sure ctx->scratch holds at least `bytes`; returns a status.
 int ensure_scratch(ltx_ctx *ctx, size_t bytes);
+// Copies host bytes to the device through the context's pinned staging
+// buffer (waits for the previous upload from that buffer to finish first).
+int upload(ltx_ctx *ctx, void *dst_dev, const void *src_host, size_t bytes);
 
 inline size_t dtype_size(int dt) {
     switch (dt) {

@@ -512,8 +512,17 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         w = carve_work(static_cast<char *>(ctx->work), c, rows, crow, U, c.layers);
     }
     if (work_out) *work_out = w;
-    CU(cudaMemcpyAsync(w.ts_u, uniq.data(), U * 4, cudaMemcpyHostToDevice, st));
-    CU(cudaMemcpyAsync(w.idx, idx.data(), rows * 4, cudaMemcpyHostToDevice, st));
+    {
+        // one pinned upload: distinct timesteps then the per-token index
+        std::vector<char> blob((size_t)U * 4 + (size_t)rows * 4);
+        memcpy(blob.data(), uniq.data(), (size_t)U * 4);
+        memcpy(blob.data() + (size_t)U * 4, idx.data(), (size_t)rows * 4);
+        TRY(ensure_scratch(ctx, blob.size()));
+        TRY(upload(ctx, ctx->scratch, blob.data(), blob.size()));
+        CU(cudaMemcpyAsync(w.ts_u, ctx->scratch, (size_t)U * 4, cudaMemcpyDeviceToDevice, st));
+        CU(cudaMemcpyAsync(w.idx, static_cast<char *>(ctx->scratch) + (size_t)U * 4, (size_t)rows * 4,
+                           cudaMemcpyDeviceToDevice, st));
+    }
 
     // patch embedding (model.rs:187): f32 latent -> bf16 -> tensor-core GEMM, f32 out
     CU(f32_to_bf16(st, sms, latent, rows * c.in_ch, w.latb));
@@ -712,7 +721,7 @@ extern "C" int ltx_denoise_step(ltx_model *m, ltx_ctx *ctx, float *latent_dev, c
     }
     TRY(forward_impl(m, ctx, lat2, ts, pos2, ctx2, B, T, S, vel, &w));
     // per-token t for the velocity -> x0 adapter: x0 = x - t * v
-    CU(cudaMemcpyAsync(w.tok_t, ts.data(), (size_t)T * 4, cudaMemcpyHostToDevice, st));
+    TRY(upload(ctx, w.tok_t, ts.data(), (size_t)T * 4));
     CU(cfg_euler(st, ctx->sm_count, latent_dev, vel, use_cfg ? vel + (int64_t)T * C : vel, w.tok_t, mask_dev, clean_dev,
                  T, C, cfg_scale, rescale_scale, use_cfg, w.partial, sigma, sigma_next));
     (void)D;

@@ -79,6 +79,11 @@ def lib() -> ctypes.CDLL:
         "ltx_model_weight_bytes": (I64, [V]),
         "ltx_model_forward": (I, [V, V, P, P, P, P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, P]),
         "ltx_denoise_step": (I, [V, V, P, P, P, P, P, P, P, ctypes.c_int32, ctypes.c_int32, F, F, F, F]),
+        "ltx_scheduler_execute": (I, [ctypes.c_int32, ctypes.c_uint64, F, F, ctypes.c_int32, F, P]),
+        "ltx_target_positions": (I, [ctypes.c_uint32] * 7 + [F, P]),
+        "ltx_reference_positions": (I, [ctypes.c_uint32] * 8 + [F, ctypes.c_uint32, ctypes.c_uint32, P]),
+        "ltx_patchify": (I, [V, P] + [ctypes.c_int32] * 5 + [P]),
+        "ltx_unpatchify": (I, [V, P] + [ctypes.c_int32] * 5 + [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -266,6 +271,49 @@ class VideoTransformer:
             self.close()
         except Exception:
             pass
+
+
+def scheduler_execute(steps, num_tokens, max_shift=2.05, base_shift=0.95, stretch=True, terminal=0.1):
+    """LTX2Scheduler::execute -> list of steps+1 f32 sigmas (host, no GPU needed)."""
+    import numpy as np
+    out = np.empty(steps + 1, np.float32)
+    rc = lib().ltx_scheduler_execute(steps, num_tokens, max_shift, base_shift, int(stretch), terminal,
+                                     out.ctypes.data_as(ctypes.c_void_p))
+    if rc:
+        raise LtxError(rc, "ltx_scheduler_execute")
+    return out
+
+
+def target_positions(frames, height, width, batch=1, scale=(8, 32, 32), fps=24.0):
+    """make_target_positions -> np.float32 [batch, 3, F*H*W, 2] (host, no GPU needed)."""
+    import numpy as np
+    out = np.empty((batch, 3, frames * height * width, 2), np.float32)
+    rc = lib().ltx_target_positions(frames, height, width, batch, *scale, fps, out.ctypes.data_as(ctypes.c_void_p))
+    if rc:
+        raise LtxError(rc, "ltx_target_positions")
+    return out
+
+
+def reference_positions(frames, height, width, batch=1, first_latent_frame=0, scale=(8, 32, 32), fps=24.0,
+                        temporal_scale_factor=1, downscale_factor=1):
+    """make_reference_positions -> np.float32 [batch, 3, F*H*W, 2] (host, no GPU needed)."""
+    import numpy as np
+    out = np.empty((batch, 3, frames * height * width, 2), np.float32)
+    rc = lib().ltx_reference_positions(frames, height, width, batch, first_latent_frame, *scale, fps,
+                                       temporal_scale_factor, downscale_factor, out.ctypes.data_as(ctypes.c_void_p))
+    if rc:
+        raise LtxError(rc, "ltx_reference_positions")
+    return out
+
+
+def patchify(ctx: "Context", latent5, tokens):
+    B, C, F, H, W = latent5.shape
+    ctx.check(lib().ltx_patchify(ctx.h, _ptr(latent5), B, C, F, H, W, _ptr(tokens)), "ltx_patchify")
+
+
+def unpatchify(ctx: "Context", tokens, latent5):
+    B, C, F, H, W = latent5.shape
+    ctx.check(lib().ltx_unpatchify(ctx.h, _ptr(tokens), B, C, F, H, W, _ptr(latent5)), "ltx_unpatchify")
 
 
 def lora_coeff(strength: float, alpha: float, rank: int) -> float:

@@ -216,10 +216,14 @@ def attention(p, pre, cfg: DiTConfig, x, context=None, pe=None, mask=None):
     return linear(out, p[pre + "to_out.0.weight"], p.get(pre + "to_out.0.bias"))
 
 
-def sdpa(q, k, v, scale, mask=None, q_chunk=2048):
+SDPA_Q_CHUNK = 2048   # rows of scores materialised at once (memory bound for full-size runs)
+
+
+def sdpa(q, k, v, scale, mask=None, q_chunk=None):
     """softmax(q k^T * scale + mask) v; rows are processed in query chunks,
     which is the reference's own chunked_sdp_attention (attention.rs:252-285):
     identical per-row results, bounded memory."""
+    q_chunk = q_chunk or SDPA_Q_CHUNK
     outs = []
     for s in range(0, q.shape[2], q_chunk):
         sc = (q[:, :, s:s + q_chunk] @ k.transpose(2, 3)) * scale
