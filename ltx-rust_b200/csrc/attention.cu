@@ -14,10 +14,13 @@
 //                                                      B = V_j MN-major)
 //            QK_{j+1} is issued before PV_j, so the tensor core computes the
 //            next scores while the softmax warps work on the current ones.
-//   warps 2-5  one query row per thread: row max and exp2 over S_j read from
-//            TMEM, P_j (bf16) written to smem in the 128B-swizzled K-major
-//            layout the MMA reads, O kept in registers and updated with
-//            PV_{j-1} one tile late (O = O*exp2(m_o - m) + PV).
+//   warps 2-9  two threads per query row (warps w and w+4 share a TMEM lane
+//            quadrant; each takes 64 of the 128 score / output columns):
+//            row max exchanged through shared memory (named barrier), exp2
+//            two-at-a-time (ex2.approx.f16x2), P_j (bf16) written to smem in
+//            the 128B-swizzled K-major layout the MMA reads (each half-thread
+//            writes one whole 64-key swizzle atom), O half kept in registers
+//            and updated with PV_{j-1} one tile late (O = O*exp2(m_o - m) + PV).
 // All waits are bounded (2 s) and report LTX_ERR_TIMEOUT through the flag.
 #include <cuda.h>
 
@@ -40,7 +43,8 @@ namespace {
 constexpr int D = 128;
 constexpr int BQ = 128, BKV = 128;
 constexpr int KV_STAGES = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kSoftmaxWarps = 8;
 constexpr int TILE_BYTES = 128 * D * 2;   // 32 KB: 128 rows x 128 bf16 (two 64-col swizzle atoms)
 constexpr int HALF_BYTES = 128 * 64 * 2;  // 16 KB: one atom column block
 
@@ -50,7 +54,8 @@ struct AttnSmemLayout {
     static constexpr int K = P + TILE_BYTES;
     static constexpr int V = K + KV_STAGES * TILE_BYTES;
     static constexpr int BAR = V + KV_STAGES * TILE_BYTES;
-    static constexpr int BYTES = BAR + 256;
+    static constexpr int RED = BAR + 256;                   // [2 parity][2 half][128 rows] f32
+    static constexpr int BYTES = RED + 2 * 2 * 128 * 4;
 };
 constexpr size_t kAttnSmem = AttnSmemLayout::BYTES + 1024;
 
@@ -71,6 +76,18 @@ __device__ __forceinline__ float ex2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+
+// exp2 of two values with one MUFU op: f32 -> f16x2 -> ex2.approx.f16x2 -> f32.
+// (P is rounded to bf16 for the MMA afterwards, so the f16 step costs nothing.)
+__device__ __forceinline__ float2 ex2x2(float a, float b) {
+    uint32_t in, out;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(b), "f"(a));
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(out) : "r"(in));
+    __half2 h = *reinterpret_cast<__half2 *>(&out);
+    return __half22float2(h);
+}
+
+__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -110,11 +127,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_empty[i], 4);
+            mbar_init(&s_empty[i], kSoftmaxWarps);
             mbar_init(&pv_full[i], 1);
-            mbar_init(&pv_empty[i], 4);
+            mbar_init(&pv_empty[i], kSoftmaxWarps);
         }
-        mbar_init(p_full, 4);
+        mbar_init(p_full, kSoftmaxWarps);
         mbar_init(p_empty, 1);
         fence_barrier_init();
     }
@@ -202,17 +219,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // Softmax / output warps: thread owns query row quad*32 + lane of the tile.
+        // Softmax / output warps 2..9: row quad*32 + lane, column half `hf` (64 of 128).
         const int quad = warp & 3;
+        const int hf = (warp - 2) >> 2;
         const int row_in_tile = quad * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        float o[D];
+        float *red = reinterpret_cast<float *>(smem + AttnSmemLayout::RED);   // [2][2][128]
+        float o[D / 2];
 #pragma unroll
-        for (int c = 0; c < D; ++c) o[c] = 0.f;
+        for (int c = 0; c < D / 2; ++c) o[c] = 0.f;
         float m = -INFINITY, l = 0.f, m_o = -INFINITY;
         float m_hist[2] = {-INFINITY, -INFINITY};   // max used for P_j, by j % 2
         // P smem: row r, 16-byte chunk c of atom a at a*16K + r*128 + ((c ^ (r&7)) * 16).
-        unsigned char *p_row = sP + row_in_tile * 128;
+        // This thread writes atom `hf` of its row (keys hf*64 .. hf*64+63).
+        unsigned char *p_row = sP + hf * HALF_BYTES + row_in_tile * 128;
         const int sw = row_in_tile & 7;
 
         auto fold_pv = [&](int j) -> bool {
@@ -222,9 +242,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float alpha = ex2(m_o - mj);   // 0 on the first fold (m_o = -inf)
             m_o = mj;
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + lane_base + 256 + (j & 1) * 128 + c * 32, r);
+                tmem_ld_32x32b_x32(tmem + lane_base + 256 + (j & 1) * 128 + hf * 64 + c * 32, r);
                 tmem_ld_wait();
 #pragma unroll
                 for (int e = 0; e < 32; ++e) o[c * 32 + e] = o[c * 32 + e] * alpha + __uint_as_float(r[e]);
@@ -235,34 +255,44 @@ __global__ void __launch_bounds__(kThreads, 1)
             return true;
         };
 
-        for (int j = 0; j < n_kv && !aborted; ++j) {
-            if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.timeout_flag, 209, &aborted)) break;
-            tc_fence_after();
-            const uint32_t s_tmem = tmem + lane_base + (j & 1) * 128;
-            const int kv0 = j * BKV;
-            // pass 1: row max of the scaled scores
+        // Every softmax thread calls softmax_bar() exactly n_kv + 1 times, also
+        // after a timed-out wait (it then skips the work, not the barrier), so
+        // the named barrier can never be left waiting.
+        for (int j = 0; j < n_kv; ++j) {
+            const bool live = mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.timeout_flag, 209, &aborted);
+            if (live) tc_fence_after();
+            const uint32_t s_tmem = tmem + lane_base + (j & 1) * 128 + hf * 64;
+            const int kv0 = j * BKV + hf * 64;
+            // pass 1: row max of this half, then combine the two halves of the row
             float mx = -INFINITY;
+            if (live) {
 #pragma unroll
-            for (int c = 0; c < BKV / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(s_tmem + c * 32, r);
-                tmem_ld_wait();
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(s_tmem + c * 32, r);
+                    tmem_ld_wait();
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const float x = (kv0 + c * 32 + e < p.Tk) ? __uint_as_float(r[e]) * p.scale_log2 : -INFINITY;
-                    mx = fmaxf(mx, x);
+                    for (int e = 0; e < 32; ++e) {
+                        const float x = (kv0 + c * 32 + e < p.Tk) ? __uint_as_float(r[e]) * p.scale_log2 : -INFINITY;
+                        mx = fmaxf(mx, x);
+                    }
                 }
             }
+            float *rj = red + (j & 1) * 256;
+            rj[hf * 128 + row_in_tile] = mx;
+            softmax_bar();
+            if (!live || aborted) continue;
+            mx = fmaxf(rj[row_in_tile], rj[128 + row_in_tile]);
             const float m_new = fmaxf(m, mx);
             const float corr = ex2(m - m_new);
             m = m_new;
             m_hist[j & 1] = m_new;
             // P_j overwrites P_{j-1}: wait until PV_{j-1} has read it.
-            if (j > 0 && !mbar_wait(p_empty, (j - 1) & 1, p.timeout_flag, 210, &aborted)) break;
-            // pass 2: P = exp2(x - m), row sum, bf16 P into smem
+            if (j > 0 && !mbar_wait(p_empty, (j - 1) & 1, p.timeout_flag, 210, &aborted)) continue;
+            // pass 2: P = exp2(x - m), partial row sum, bf16 P into smem
             float sum = 0.f;
 #pragma unroll
-            for (int c = 0; c < BKV / 32; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(s_tmem + c * 32, r);
                 tmem_ld_wait();
@@ -270,18 +300,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
                     const bool ok0 = kv0 + c * 32 + e < p.Tk, ok1 = kv0 + c * 32 + e + 1 < p.Tk;
-                    const float p0 = ok0 ? ex2(__uint_as_float(r[e]) * p.scale_log2 - m_new) : 0.f;
-                    const float p1 = ok1 ? ex2(__uint_as_float(r[e + 1]) * p.scale_log2 - m_new) : 0.f;
-                    sum += p0 + p1;
-                    __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
+                    const float x0 = ok0 ? fmaf(__uint_as_float(r[e]), p.scale_log2, -m_new) : -INFINITY;
+                    const float x1 = ok1 ? fmaf(__uint_as_float(r[e + 1]), p.scale_log2, -m_new) : -INFINITY;
+                    const float2 pe = ex2x2(x0, x1);
+                    sum += pe.x + pe.y;
+                    __nv_bfloat162 hv = __floats2bfloat162_rn(pe.x, pe.y);
                     pk[e >> 1] = *reinterpret_cast<uint32_t *>(&hv);
                 }
-                // columns c*32 .. c*32+31 = atom (c>>1), chunks (c&1)*4 .. +3
-                unsigned char *atom = p_row + (c >> 1) * HALF_BYTES;
+                // keys c*32 .. c*32+31 of this atom = chunks c*4 .. c*4+3
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const int chunk = (c & 1) * 4 + q;
-                    *reinterpret_cast<uint4 *>(atom + ((chunk ^ sw) << 4)) =
+                    const int chunk = c * 4 + q;
+                    *reinterpret_cast<uint4 *>(p_row + ((chunk ^ sw) << 4)) =
                         make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
                 }
             }
@@ -293,16 +323,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&s_empty[j & 1]);
                 mbar_arrive(p_full);
             }
-            if (j > 0 && !fold_pv(j - 1)) break;
+            if (j > 0) fold_pv(j - 1);
         }
         if (!aborted) fold_pv(n_kv - 1);
+        // combine the two partial row sums in the buffer the last max exchange did not use
+        float *rl = red + (n_kv & 1) * 256;
+        rl[hf * 128 + row_in_tile] = l;
+        softmax_bar();
+        const float l_row = rl[row_in_tile] + rl[128 + row_in_tile];
         if (!aborted) {
             const int q_row = qt * BQ + row_in_tile;
             if (q_row < p.Tq) {
-                const float inv = 1.f / l;
-                __nv_bfloat16 *dst = p.out + ((int64_t)b * p.Tq + q_row) * p.ldo + h * D;
+                const float inv = 1.f / l_row;
+                __nv_bfloat16 *dst = p.out + ((int64_t)b * p.Tq + q_row) * p.ldo + h * D + hf * 64;
 #pragma unroll
-                for (int c = 0; c < D; c += 8) {
+                for (int c = 0; c < D / 2; c += 8) {
                     uint32_t w[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {

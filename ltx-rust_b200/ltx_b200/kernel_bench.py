@@ -81,7 +81,8 @@ def main():
     ctx.synchronize()
     ms = _time(fn, a.iters)
     ctx.synchronize()
-    print(f"{a.kernel}: {ms:.4f} ms  {flops / ms / 1e9:.1f} {unit}")
+    rate = flops / ms / (1e6 if unit == "GB/s" else 1e9)
+    print(f"{a.kernel}: {ms:.4f} ms  {rate:.1f} {unit}")
 
 
 if __name__ == "__main__":
