@@ -117,6 +117,30 @@ int ltx_dequant_merge(ltx_ctx *ctx, const void *w_dev, int32_t w_dtype, int32_t 
                       const ltx_lora_delta *deltas, int32_t n_deltas, void *dst_dev,
                       int32_t dst_dtype);
 
+/* Maximum chain scratch, in bytes, that ltx_dequant_merge_noalloc can use. */
+#define LTX_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* ltx_dequant_merge for callers that cannot allocate device memory — code
+ * inside a memory pool or host framework that owns every device allocation,
+ * or a process that must not call cudaMalloc after start-up.  No counterpart
+ * in the reference (its merge runs on the host).  Same arguments and the same
+ * bit-exact result as ltx_dequant_merge, except that it needs no ltx_ctx
+ * (creating one allocates): `stream` is a cudaStream_t (NULL = default
+ * stream) on the current device, and a failure message is written to
+ * `errbuf` (may be NULL).  It calls no cudaMalloc/cudaFree: the merge's chain
+ * scratch (4 * total rank * (round_up(in,128) + 2*round_up(out,128)) bytes)
+ * lives in one LTX_NOALLOC_SCRATCH_BYTES file-scope device array that every
+ * GPU loading the library holds until exit; larger merges return
+ * LTX_ERR_UNSUPPORTED before enqueuing anything.  All calls on a device share
+ * that array, so calls whose GPU work overlaps (e.g. on two streams) race on
+ * it.  The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) and caches it; make that first call before any
+ * stream capture. */
+int ltx_dequant_merge_noalloc(void *stream, const void *w_dev, int32_t w_dtype, int32_t has_scale,
+                              float scale, int64_t out_features, int64_t in_features,
+                              const ltx_lora_delta *deltas, int32_t n_deltas, void *dst_dev,
+                              int32_t dst_dtype, char *errbuf, size_t errbuf_len);
+
 /* ── ltx-dit: building blocks ─────────────────────────────────────────────── */
 
 /* Epilogues of ltx_gemm_bf16. */

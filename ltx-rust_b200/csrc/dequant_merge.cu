@@ -13,6 +13,10 @@
 //                   16 x 8 register tile, issuing packed FFMA2 (two
 //                   independent IEEE fma.rn per instruction), so the
 //                   rounding of every element is the reference's.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
 #include "device_common.cuh"
 #include "internal.hpp"
 #include "kernels.hpp"
@@ -431,4 +435,149 @@ extern "C" int ltx_dequant_merge(ltx_ctx *ctx, const void *w_dev, int32_t w_dtyp
     if (!ctx) return LTX_ERR_INVALID_ARG;
     return ltx::dequant_merge(ctx, ctx->stream, w_dev, w_dtype, has_scale, scale, out_features, in_features, deltas,
                               n_deltas, dst_dev, dst_dtype);
+}
+
+// ── allocation-free entry point ──────────────────────────────────────────────
+//
+// For callers that cannot call cudaMalloc: code running inside a memory pool
+// or a host framework that owns every device allocation, or a process that
+// must not allocate after start-up (a real-time pipeline, or a sandbox whose
+// device allocator is closed).  Those callers bring their own input and output
+// buffers; the only extra device memory the merge needs is its chain scratch
+// (all stacked LoRA deltas' A rows and coeff*B columns as f32, zero-padded to
+// the tile grid), which here lives in one fixed file-scope device array
+// instead of a cudaMalloc'd buffer.
+//
+//   * Size: kNoAllocScratchBytes (16 MiB) on every GPU that loads this
+//     library, held until the process exits.  A call needs
+//       4 * (sum of ranks) * (round_up(in, 128) + 2 * round_up(out, 128)) bytes;
+//     rank 64 fits every weight of the 22B DiT (the largest, the 24576 x 4096
+//     adaLN projection, needs 13.6 MB).  Larger calls are rejected with
+//     LTX_ERR_UNSUPPORTED before anything is enqueued.
+//   * Sharing: every call on a device uses the same array.  The kernels write
+//     every scratch element they later read, so nothing has to start at zero,
+//     but two calls whose work overlaps on the GPU (different streams, or the
+//     same array used from two host threads with no ordering) race on it.
+//   * Set-up: the first call on each device resolves the array's device
+//     address with cudaGetSymbolAddress (with that device current) and caches
+//     it.  Make that first call before any stream capture.
+namespace ltx {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) unsigned char g_merge_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void *g_scratch_addr[kMaxDevices] = {};
+
+void set_err(char *buf, size_t len, const char *fmt, ...) {
+    if (!buf || !len) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, len, fmt, ap);
+    va_end(ap);
+}
+
+}  // namespace
+}  // namespace ltx
+
+extern "C" int ltx_dequant_merge_noalloc(void *stream, const void *w_dev, int32_t w_dtype, int32_t has_scale,
+                                         float scale, int64_t out_features, int64_t in_features,
+                                         const ltx_lora_delta *deltas, int32_t n_deltas, void *dst_dev,
+                                         int32_t dst_dtype, char *errbuf, size_t errbuf_len) {
+    using namespace ltx;
+    if (errbuf && errbuf_len) errbuf[0] = 0;
+    if (!w_dev || !dst_dev) {
+        set_err(errbuf, errbuf_len, "dequant_merge_noalloc: null pointer");
+        return LTX_ERR_INVALID_ARG;
+    }
+    if (out_features < 0 || in_features < 0) {
+        set_err(errbuf, errbuf_len, "dequant_merge_noalloc: negative shape");
+        return LTX_ERR_SHAPE;
+    }
+    if (w_dtype < LTX_F32 || w_dtype > LTX_F8_E5M2) {
+        set_err(errbuf, errbuf_len, "dequant_merge_noalloc: bad weight dtype %d", w_dtype);
+        return LTX_ERR_DTYPE;
+    }
+    if (dst_dtype != LTX_F32 && dst_dtype != LTX_BF16) {
+        set_err(errbuf, errbuf_len, "dequant_merge_noalloc: output dtype must be F32 or BF16");
+        return LTX_ERR_DTYPE;
+    }
+    if (n_deltas < 0 || n_deltas > LTX_MAX_DELTAS || (n_deltas > 0 && !deltas)) {
+        set_err(errbuf, errbuf_len, "dequant_merge_noalloc: bad delta count %d", n_deltas);
+        return LTX_ERR_INVALID_ARG;
+    }
+    if (out_features * in_features == 0) return LTX_OK;
+    MergeParams p{};
+    p.w = w_dev;
+    p.w_dt = w_dtype;
+    p.fp8_scaled = (w_dtype == LTX_F8_E4M3 || w_dtype == LTX_F8_E5M2) && has_scale;
+    p.scale = scale;
+    p.rows = out_features;
+    p.cols = in_features;
+    p.n_deltas = n_deltas;
+    for (int i = 0; i < n_deltas; ++i) {
+        const ltx_lora_delta &d = deltas[i];
+        if (!d.a_dev || !d.b_dev || d.rank <= 0) {
+            set_err(errbuf, errbuf_len, "dequant_merge_noalloc: delta %d has rank %d or a null factor", i, d.rank);
+            return LTX_ERR_SHAPE;
+        }
+        if (d.a_dtype < LTX_F32 || d.a_dtype > LTX_F8_E5M2 || d.b_dtype < LTX_F32 || d.b_dtype > LTX_F8_E5M2) {
+            set_err(errbuf, errbuf_len, "dequant_merge_noalloc: delta %d has an unsupported dtype", i);
+            return LTX_ERR_DTYPE;
+        }
+        p.d[i] = DeltaDev{d.a_dev, d.b_dev, d.rank, d.a_dtype, d.b_dtype, d.coeff};
+    }
+    p.dst = dst_dev;
+    p.dst_bf16 = dst_dtype == LTX_BF16;
+    p.dst_aligned16 = ((uintptr_t)dst_dev % 16) == 0;
+    const size_t need = merge_scratch_bytes(p);
+    if (need > kNoAllocScratchBytes) {
+        set_err(errbuf, errbuf_len,
+                "dequant_merge_noalloc: this merge needs %zu bytes of scratch; the allocation-free entry point has "
+                "%zu (4 * total rank * (round_up(in,128) + 2*round_up(out,128)))",
+                need, kNoAllocScratchBytes);
+        return LTX_ERR_UNSUPPORTED;
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        set_err(errbuf, errbuf_len, "dequant_merge_noalloc: no usable current device");
+        return LTX_ERR_CUDA;
+    }
+    void *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_scratch_mu);
+        if (!g_scratch_addr[dev]) {
+            // A host-side stand-in names the array here; the device address
+            // comes from the runtime, with `dev` current.
+            e = cudaGetSymbolAddress(&g_scratch_addr[dev], g_merge_scratch);
+            if (e != cudaSuccess) {
+                g_scratch_addr[dev] = nullptr;
+                set_err(errbuf, errbuf_len, "dequant_merge_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+                return LTX_ERR_CUDA;
+            }
+        }
+        scratch = g_scratch_addr[dev];
+    }
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) {
+        set_err(errbuf, errbuf_len, "dequant_merge_noalloc: %s", cudaGetErrorString(e));
+        return LTX_ERR_CUDA;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (w_dtype) {
+    case LTX_F32: e = launch_merge<LTX_F32>(p, st, sms, scratch); break;
+    case LTX_F16: e = launch_merge<LTX_F16>(p, st, sms, scratch); break;
+    case LTX_BF16: e = launch_merge<LTX_BF16>(p, st, sms, scratch); break;
+    case LTX_F8_E4M3: e = launch_merge<LTX_F8_E4M3>(p, st, sms, scratch); break;
+    default: e = launch_merge<LTX_F8_E5M2>(p, st, sms, scratch); break;
+    }
+    if (e != cudaSuccess) {
+        set_err(errbuf, errbuf_len, "dequant_merge_noalloc launch: %s", cudaGetErrorString(e));
+        return LTX_ERR_CUDA;
+    }
+    return LTX_OK;
 }

@@ -84,6 +84,9 @@ def lib() -> ctypes.CDLL:
         "ltx_reference_positions": (I, [ctypes.c_uint32] * 8 + [F, ctypes.c_uint32, ctypes.c_uint32, P]),
         "ltx_patchify": (I, [V, P] + [ctypes.c_int32] * 5 + [P]),
         "ltx_unpatchify": (I, [V, P] + [ctypes.c_int32] * 5 + [P]),
+        "ltx_dequant_merge_noalloc": (I, [V, P, ctypes.c_int32, ctypes.c_int32, F, I64, I64,
+                                          ctypes.POINTER(LoraDelta), ctypes.c_int32, P, ctypes.c_int32,
+                                          ctypes.c_char_p, ctypes.c_size_t]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -314,6 +317,23 @@ def patchify(ctx: "Context", latent5, tokens):
 def unpatchify(ctx: "Context", tokens, latent5):
     B, C, F, H, W = latent5.shape
     ctx.check(lib().ltx_unpatchify(ctx.h, _ptr(tokens), B, C, F, H, W, _ptr(latent5)), "ltx_unpatchify")
+
+
+NOALLOC_SCRATCH_BYTES = 16 << 20
+
+
+def dequant_merge_noalloc(stream: int, w_ptr: int, w_dtype: int, has_scale: bool, scale: float, out_features: int,
+                          in_features: int, deltas, dst_ptr: int, dst_dtype: int):
+    """ltx_dequant_merge_noalloc: the same merge without allocating device memory
+    (for callers that cannot call cudaMalloc); raises LtxError with the library's message."""
+    n = len(deltas)
+    arr = (LoraDelta * max(n, 1))(*[LoraDelta(*d) for d in deltas])
+    err = ctypes.create_string_buffer(512)
+    rc = lib().ltx_dequant_merge_noalloc(ctypes.c_void_p(stream), ctypes.c_void_p(w_ptr), w_dtype, int(has_scale),
+                                         scale, out_features, in_features, arr, n, ctypes.c_void_p(dst_ptr),
+                                         dst_dtype, err, len(err))
+    if rc != 0:
+        raise LtxError(rc, err.value.decode())
 
 
 def lora_coeff(strength: float, alpha: float, rank: int) -> float:
