@@ -168,14 +168,15 @@ int ltx_gemm_bf16(ltx_ctx *ctx, const void *a_dev, int64_t lda, const void *w_de
 /* out = softmax(q k^T * scale) v per batch and head, without materialising
  * the scores (flash attention on tcgen05; scores and P.V accumulate in TMEM).
  * Replaces sdp_attention / chunked_sdp_attention (attention.rs:228-285,
- * mask = None as in alpha_gen).  q/k/v/out are bf16, token-major: row
- * b*T + t, head h in columns [h*head_dim, (h+1)*head_dim), leading
- * dimensions in elements (multiples of 8, 16-byte aligned bases).  q has
- * tq rows per batch, k/v tk rows.  head_dim must be 128
+ * mask = None as in alpha_gen).  q/k/out are bf16, v is bf16 or f16
+ * (`v_dtype`; with f16 the probabilities P are kept in f16 too), all
+ * token-major: row b*T + t, head h in columns [h*head_dim, (h+1)*head_dim),
+ * leading dimensions in elements (multiples of 8, 16-byte aligned bases).
+ * q has tq rows per batch, k/v tk rows.  head_dim must be 128
  * (LTX_ERR_UNSUPPORTED otherwise). */
 int ltx_attention_fwd(ltx_ctx *ctx, const void *q_dev, int64_t ldq, const void *k_dev, int64_t ldk,
-                      const void *v_dev, int64_t ldv, int32_t batch, int32_t heads, int32_t tq,
-                      int32_t tk, int32_t head_dim, float scale, void *out_dev, int64_t ldo);
+                      const void *v_dev, int64_t ldv, int32_t v_dtype, int32_t batch, int32_t heads,
+                      int32_t tq, int32_t tk, int32_t head_dim, float scale, void *out_dev, int64_t ldo);
 
 /* ── ltx-weights: the weight store ─────────────────────────────────────────── */
 

@@ -89,6 +89,8 @@ __device__ __forceinline__ float2 ex2x2(float a, float b) {
 
 __device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+// VF16: V (and so P) are f16; otherwise bf16.  Q and K are always bf16.
+template <bool VF16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, AttnParams p) {
@@ -177,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         if (elect_one()) {
             constexpr uint32_t idesc_qk = idesc_f16(BQ, BKV, true, false);
-            constexpr uint32_t idesc_pv = idesc_f16(BQ, D, true, true);   // B = V, MN-major
+            constexpr uint32_t idesc_pv = idesc_f16(BQ, D, !VF16, true);   // B = V, MN-major
             const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
             auto issue_pv = [&](int j) -> bool {
                 const int s = j % KV_STAGES;
@@ -225,9 +227,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row_in_tile = quad * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         float *red = reinterpret_cast<float *>(smem + AttnSmemLayout::RED);   // [2][2][128]
-        float o[D / 2];
+        float2 o[D / 4];   // this thread's 64 output columns as pairs
 #pragma unroll
-        for (int c = 0; c < D / 2; ++c) o[c] = 0.f;
+        for (int c = 0; c < D / 4; ++c) o[c] = make_float2(0.f, 0.f);
         float m = -INFINITY, l = 0.f, m_o = -INFINITY;
         float m_hist[2] = {-INFINITY, -INFINITY};   // max used for P_j, by j % 2
         // P smem: row r, 16-byte chunk c of atom a at a*16K + r*128 + ((c ^ (r&7)) * 16).
@@ -240,14 +242,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const float mj = m_hist[j & 1];
             const float alpha = ex2(m_o - mj);   // 0 on the first fold (m_o = -inf)
+            const float2 a2 = make_float2(alpha, alpha);
             m_o = mj;
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(tmem + lane_base + 256 + (j & 1) * 128 + hf * 64, r0);
+            tmem_ld_32x32b_x32(tmem + lane_base + 256 + (j & 1) * 128 + hf * 64 + 32, r1);
+            tmem_ld_wait();
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + lane_base + 256 + (j & 1) * 128 + hf * 64 + c * 32, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 32; ++e) o[c * 32 + e] = o[c * 32 + e] * alpha + __uint_as_float(r[e]);
+            for (int e = 0; e < 16; ++e) {
+                o[e] = __ffma2_rn(o[e], a2, make_float2(__uint_as_float(r0[2 * e]), __uint_as_float(r0[2 * e + 1])));
+                o[16 + e] = __ffma2_rn(o[16 + e], a2, make_float2(__uint_as_float(r1[2 * e]), __uint_as_float(r1[2 * e + 1])));
             }
             tc_fence_before();
             __syncwarp();
@@ -258,25 +262,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Every softmax thread calls softmax_bar() exactly n_kv + 1 times, also
         // after a timed-out wait (it then skips the work, not the barrier), so
         // the named barrier can never be left waiting.
+        const float2 sl2 = make_float2(p.scale_log2, p.scale_log2);
         for (int j = 0; j < n_kv; ++j) {
             const bool live = mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.timeout_flag, 209, &aborted);
-            if (live) tc_fence_after();
-            const uint32_t s_tmem = tmem + lane_base + (j & 1) * 128 + hf * 64;
             const int kv0 = j * BKV + hf * 64;
-            // pass 1: row max of this half, then combine the two halves of the row
+            const bool ragged = kv0 + 64 > p.Tk;   // only the last tile can be
+            float sv[64];
             float mx = -INFINITY;
             if (live) {
+                tc_fence_after();
+                const uint32_t s_tmem = tmem + lane_base + (j & 1) * 128 + hf * 64;
+                uint32_t r0[32], r1[32];
+                tmem_ld_32x32b_x32(s_tmem, r0);
+                tmem_ld_32x32b_x32(s_tmem + 32, r1);
+                tmem_ld_wait();
+                // the scores are in registers: hand the TMEM buffer back to the MMA warp
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_empty[j & 1]);
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(s_tmem + c * 32, r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        const float x = (kv0 + c * 32 + e < p.Tk) ? __uint_as_float(r[e]) * p.scale_log2 : -INFINITY;
-                        mx = fmaxf(mx, x);
-                    }
+                for (int e = 0; e < 32; ++e) {
+                    sv[e] = __uint_as_float(r0[e]);
+                    sv[32 + e] = __uint_as_float(r1[e]);
                 }
+                if (ragged) {
+#pragma unroll
+                    for (int e = 0; e < 64; ++e)
+                        if (kv0 + e >= p.Tk) sv[e] = -INFINITY;
+                }
+#pragma unroll
+                for (int e = 0; e < 64; ++e) mx = fmaxf(mx, sv[e]);
+                mx *= p.scale_log2;   // scale > 0: max(s * scale) = scale * max(s)
             }
             float *rj = red + (j & 1) * 256;
             rj[hf * 128 + row_in_tile] = mx;
@@ -289,40 +305,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             m_hist[j & 1] = m_new;
             // P_j overwrites P_{j-1}: wait until PV_{j-1} has read it.
             if (j > 0 && !mbar_wait(p_empty, (j - 1) & 1, p.timeout_flag, 210, &aborted)) continue;
-            // pass 2: P = exp2(x - m), partial row sum, bf16 P into smem
-            float sum = 0.f;
+            // P = exp2(s * scale - m): two per MUFU op (ex2.approx.f16x2), partial row sum in f32.
+            const float2 nm2 = make_float2(-m_new, -m_new);
+            float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(s_tmem + c * 32, r);
-                tmem_ld_wait();
-                uint32_t pk[16];
+            for (int q = 0; q < 8; ++q) {   // 8 chunks of 8 keys = one 16-byte smem store each
+                uint32_t pk[4];
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const bool ok0 = kv0 + c * 32 + e < p.Tk, ok1 = kv0 + c * 32 + e + 1 < p.Tk;
-                    const float x0 = ok0 ? fmaf(__uint_as_float(r[e]), p.scale_log2, -m_new) : -INFINITY;
-                    const float x1 = ok1 ? fmaf(__uint_as_float(r[e + 1]), p.scale_log2, -m_new) : -INFINITY;
-                    const float2 pe = ex2x2(x0, x1);
-                    sum += pe.x + pe.y;
-                    __nv_bfloat162 hv = __floats2bfloat162_rn(pe.x, pe.y);
-                    pk[e >> 1] = *reinterpret_cast<uint32_t *>(&hv);
+                for (int t = 0; t < 4; ++t) {
+                    const int e = q * 8 + 2 * t;
+                    const float2 x = __ffma2_rn(make_float2(sv[e], sv[e + 1]), sl2, nm2);
+                    uint32_t in, out;
+                    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(x.y), "f"(x.x));
+                    asm("ex2.approx.f16x2 %0, %1;" : "=r"(out) : "r"(in));
+                    const float2 pf = __half22float2(*reinterpret_cast<__half2 *>(&out));
+                    sum2 = __fadd2_rn(sum2, pf);
+                    if constexpr (VF16) {
+                        pk[t] = out;
+                    } else {
+                        __nv_bfloat162 hv = __floats2bfloat162_rn(pf.x, pf.y);
+                        pk[t] = *reinterpret_cast<uint32_t *>(&hv);
+                    }
                 }
-                // keys c*32 .. c*32+31 of this atom = chunks c*4 .. c*4+3
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int chunk = c * 4 + q;
-                    *reinterpret_cast<uint4 *>(p_row + ((chunk ^ sw) << 4)) =
-                        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-                }
+                *reinterpret_cast<uint4 *>(p_row + ((q ^ sw) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
-            l = l * corr + sum;
-            tc_fence_before();
+            l = l * corr + (sum2.x + sum2.y);
             fence_proxy_async_smem();   // P (generic-proxy writes) -> visible to the tensor core
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&s_empty[j & 1]);
-                mbar_arrive(p_full);
-            }
+            if (lane == 0) mbar_arrive(p_full);
             if (j > 0) fold_pv(j - 1);
         }
         if (!aborted) fold_pv(n_kv - 1);
@@ -337,14 +347,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float inv = 1.f / l_row;
                 __nv_bfloat16 *dst = p.out + ((int64_t)b * p.Tq + q_row) * p.ldo + h * D + hf * 64;
 #pragma unroll
-                for (int c = 0; c < D / 2; c += 8) {
+                for (int c = 0; c < D / 4; c += 4) {
                     uint32_t w[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        __nv_bfloat162 hv = __floats2bfloat162_rn(o[c + 2 * e] * inv, o[c + 2 * e + 1] * inv);
+                        __nv_bfloat162 hv = __floats2bfloat162_rn(o[c + e].x * inv, o[c + e].y * inv);
                         w[e] = *reinterpret_cast<uint32_t *>(&hv);
                     }
-                    *reinterpret_cast<uint4 *>(dst + c) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4 *>(dst + 2 * c) = make_uint4(w[0], w[1], w[2], w[3]);
                 }
             }
         }
@@ -376,14 +386,15 @@ EncodeTiledFn encode_fn_attn() {
 }
 
 // [B, T, cols] bf16 view: base pointer, row stride ld (elements), box {64, 128, 1}.
-bool make_tmap_3d(CUtensorMap *m, const void *ptr, int B, int T, int cols, int64_t ld) {
+bool make_tmap_3d(CUtensorMap *m, const void *ptr, int B, int T, int cols, int64_t ld, bool f16 = false) {
     EncodeTiledFn fn = encode_fn_attn();
     if (!fn) return false;
     cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)T, (cuuint64_t)B};
     cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(ld * 2 * T)};
     cuuint32_t box[3] = {64, 128, 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+    return fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(ptr),
+              dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -395,7 +406,7 @@ bool make_tmap_3d(CUtensorMap *m, const void *ptr, int B, int T, int cols, int64
 // columns [h*128, h*128+128).  Requirements: head_dim 128, ld % 8 == 0,
 // 16-byte aligned bases.
 int attention_fwd(ltx_ctx *ctx, cudaStream_t st, const void *q, int64_t ldq, const void *k, int64_t ldk, const void *v,
-                  int64_t ldv, int B, int H, int Tq, int Tk, float scale, void *out, int64_t ldo) {
+                  int64_t ldv, int B, int H, int Tq, int Tk, float scale, void *out, int64_t ldo, bool v_f16) {
     if (!q || !k || !v || !out) return fail(ctx, LTX_ERR_INVALID_ARG, "attention: null pointer");
     if (B <= 0 || H <= 0 || Tq <= 0 || Tk <= 0) return fail(ctx, LTX_ERR_SHAPE, "attention: empty shape");
     if (ldq % 8 || ldk % 8 || ldv % 8 || ldo % 8 || ((uintptr_t)q & 15) || ((uintptr_t)k & 15) || ((uintptr_t)v & 15) ||
@@ -403,13 +414,14 @@ int attention_fwd(ltx_ctx *ctx, cudaStream_t st, const void *q, int64_t ldq, con
         return fail(ctx, LTX_ERR_SHAPE, "attention: rows must be 16-byte aligned");
     CUtensorMap tq, tk, tv;
     if (!make_tmap_3d(&tq, q, B, Tq, H * D, ldq) || !make_tmap_3d(&tk, k, B, Tk, H * D, ldk) ||
-        !make_tmap_3d(&tv, v, B, Tk, H * D, ldv))
+        !make_tmap_3d(&tv, v, B, Tk, H * D, ldv, v_f16))
         return fail(ctx, LTX_ERR_CUDA, "attention: cuTensorMapEncodeTiled failed");
     AttnParams p{B, H, Tq, Tk, scale * 1.4426950408889634f, static_cast<__nv_bfloat16 *>(out), ldo, ctx->timeout_flag};
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem);
+    auto kern = v_f16 ? attn_fwd_kernel<true> : attn_fwd_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
     const int grid = B * H * ((Tq + BQ - 1) / BQ);
-    attn_fwd_kernel<<<grid, kThreads, kAttnSmem, st>>>(tq, tk, tv, p);
+    kern<<<grid, kThreads, kAttnSmem, st>>>(tq, tk, tv, p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "attention launch");
     return LTX_OK;
@@ -418,10 +430,11 @@ int attention_fwd(ltx_ctx *ctx, cudaStream_t st, const void *q, int64_t ldq, con
 }  // namespace ltx
 
 extern "C" int ltx_attention_fwd(ltx_ctx *ctx, const void *q_dev, int64_t ldq, const void *k_dev, int64_t ldk,
-                                 const void *v_dev, int64_t ldv, int32_t batch, int32_t heads, int32_t tq, int32_t tk,
-                                 int32_t head_dim, float scale, void *out_dev, int64_t ldo) {
+                                 const void *v_dev, int64_t ldv, int32_t v_dtype, int32_t batch, int32_t heads,
+                                 int32_t tq, int32_t tk, int32_t head_dim, float scale, void *out_dev, int64_t ldo) {
     if (!ctx) return LTX_ERR_INVALID_ARG;
     if (head_dim != 128) return ltx::fail(ctx, LTX_ERR_UNSUPPORTED, "attention: head_dim %d (only 128)", head_dim);
+    if (v_dtype != LTX_BF16 && v_dtype != LTX_F16) return ltx::fail(ctx, LTX_ERR_DTYPE, "attention: V must be BF16 or F16");
     return ltx::attention_fwd(ctx, ctx->stream, q_dev, ldq, k_dev, ldk, v_dev, ldv, batch, heads, tq, tk, scale,
-                              out_dev, ldo);
+                              out_dev, ldo, v_dtype == LTX_F16);
 }

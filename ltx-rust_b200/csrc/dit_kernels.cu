@@ -390,7 +390,189 @@ __global__ void permute_ct_kernel(const float *in, float *out, int B, int C, int
     }
 }
 
+// ── warp-per-row variants for the production shapes (D a multiple of 128) ───
+
+__device__ __forceinline__ float warp_sum_all(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// norm_mod with one warp per row and the row held in registers: lane l owns
+// float4 columns l*4 + 128*i, i < NV (NV = D/128).  Same modes as norm_mod_kernel.
+template <int NV>
+__global__ void __launch_bounds__(256) norm_mod_warp_kernel(const float *x, int64_t ldx, int rows, float eps, int mode,
+                                                            const float *tab, int tab_coeff, const int *idx,
+                                                            int k_shift, __nv_bfloat16 *out, int64_t ldo) {
+    constexpr int D = NV * 128;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)row * ldx);
+    float4 v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = __ldcs(xr + lane + 32 * i);
+    float mean = 0.f;
+    if (mode == 2) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        mean = warp_sum_all(s) / (float)D;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        v[i].x -= mean; v[i].y -= mean; v[i].z -= mean; v[i].w -= mean;
+        ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
+    const float denom = sqrtf(warp_sum_all(ss) / (float)D + eps);
+    const float4 *sh = nullptr, *sc = nullptr;
+    if (mode != 0) {
+        const int u = idx ? idx[row] : 0;
+        const float *shift = tab + ((int64_t)u * tab_coeff + k_shift) * D;
+        sh = reinterpret_cast<const float4 *>(shift);
+        sc = reinterpret_cast<const float4 *>(shift + D);
+    }
+    uint2 *o = reinterpret_cast<uint2 *>(out + (int64_t)row * ldo);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        float a = v[i].x / denom, b = v[i].y / denom, c = v[i].z / denom, d = v[i].w / denom;
+        if (mode != 0) {
+            const float4 s4 = __ldg(sc + lane + 32 * i), h4 = __ldg(sh + lane + 32 * i);
+            a = a * (s4.x + 1.0f) + h4.x;
+            b = b * (s4.y + 1.0f) + h4.y;
+            c = c * (s4.z + 1.0f) + h4.z;
+            d = d * (s4.w + 1.0f) + h4.w;
+        }
+        __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+        o[lane + 32 * i] = make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+    }
+}
+
+// RMSNorm(gamma) over a bf16 row in place (no RoPE), warp per row; lane l owns
+// 8-element groups l*8 + 256*i, i < NG (NG = D/256).
+template <int NG>
+__global__ void __launch_bounds__(256) rmsnorm_gamma_warp_kernel(__nv_bfloat16 *buf, int64_t ld, int rows, float eps,
+                                                                 const float *gamma) {
+    constexpr int D = NG * 256;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    uint4 *xr = reinterpret_cast<uint4 *>(buf + (int64_t)row * ld);
+    float f[NG][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NG; ++i) {
+        const uint4 u = xr[lane + 32 * i];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[e]));
+            f[i][2 * e] = t.x;
+            f[i][2 * e + 1] = t.y;
+            ss += t.x * t.x + t.y * t.y;
+        }
+    }
+    const float denom = sqrtf(warp_sum_all(ss) / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < NG; ++i) {
+        const float4 *g4 = reinterpret_cast<const float4 *>(gamma + (lane + 32 * i) * 8);
+        const float4 ga = __ldg(g4), gb = __ldg(g4 + 1);
+        const float g[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(f[i][2 * e] / denom * g[2 * e], f[i][2 * e + 1] / denom * g[2 * e + 1]);
+            w[e] = *reinterpret_cast<uint32_t *>(&h);
+        }
+        xr[lane + 32 * i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// Self-attention Q and K of one token, in place: RMSNorm(gamma) over the full
+// inner dim for each, then split RoPE with the angles computed here from the
+// token's positions (the same f32 operations as rope_table_kernel), so no
+// cos/sin table is read.  Head dim 128, H = D/128 heads, warp per token; lane l
+// owns pairs j = 2l, 2l+1 of every head (columns h*128 + {2l, 2l+1} and
+// h*128 + 64 + {2l, 2l+1}).
+template <int H>
+__global__ void __launch_bounds__(256) qk_norm_rope_fused_kernel(__nv_bfloat16 *q, __nv_bfloat16 *k, int64_t ld,
+                                                                 int rows, int T, float eps, const float *gq,
+                                                                 const float *gk, const float *pos, const float *freq,
+                                                                 int grid, float mp0, float mp1, float mp2,
+                                                                 int use_mid) {
+    constexpr int D = H * 128;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    uint32_t *qr = reinterpret_cast<uint32_t *>(q + (int64_t)row * ld);
+    uint32_t *kr = reinterpret_cast<uint32_t *>(k + (int64_t)row * ld);
+    // word index of pair (2l, 2l+1) in head h: h*64 + l (first half), h*64 + 32 + l (second half).
+    // Phase 1 streams the row for the two sums of squares; phase 2 re-reads it
+    // (L1-resident, 16 KB per warp) to normalise, rotate and store.
+    float sq = 0.f, sk = 0.f;
+#pragma unroll 8
+    for (int w = lane; w < D / 2; w += 32) {
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qr[w]));
+        const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[w]));
+        sq += a.x * a.x + a.y * a.y;
+        sk += c.x * c.x + c.y * c.y;
+    }
+    const float dq = sqrtf(warp_sum_all(sq) / (float)D + eps);
+    const float dk = sqrtf(warp_sum_all(sk) / (float)D + eps);
+    // normalised position per axis for this token (rope.rs:90-98)
+    const int b = row / T, t = row % T;
+    float fm[3];
+#pragma unroll
+    for (int ax = 0; ax < 3; ++ax) {
+        const float *pp = pos + (((int64_t)b * 3 + ax) * T + t) * 2;
+        const float mp = ax == 0 ? mp0 : (ax == 1 ? mp1 : mp2);
+        const float frac = use_mid ? __fdiv_rn(__fdiv_rn(__fadd_rn(pp[0], pp[1]), 2.0f), mp) : __fdiv_rn(pp[0], mp);
+        fm[ax] = __fadd_rn(__fmul_rn(frac, 2.0f), -1.0f);
+    }
+    const int pad = D / 2 - 3 * grid;
+#pragma unroll 4
+    for (int h = 0; h < H; ++h) {
+        const float2 qa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qr[h * 64 + lane]));
+        const float2 qb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qr[h * 64 + 32 + lane]));
+        const float2 ka = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[h * 64 + lane]));
+        const float2 kb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[h * 64 + 32 + lane]));
+        float c[2], s[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int entry = h * 64 + 2 * lane + e;   // index into the [D/2] cos/sin row
+            c[e] = 1.f;
+            s[e] = 0.f;
+            if (entry >= pad) {
+                const int idx = entry - pad, g = idx / 3, ax = idx % 3;
+                sincosf(__fmul_rn(fm[ax], __ldg(freq + g)), &s[e], &c[e]);
+            }
+        }
+        const int col = h * 128 + 2 * lane;
+        const float q1x = qa.x / dq * __ldg(gq + col), q1y = qa.y / dq * __ldg(gq + col + 1);
+        const float q2x = qb.x / dq * __ldg(gq + col + 64), q2y = qb.y / dq * __ldg(gq + col + 65);
+        const float k1x = ka.x / dk * __ldg(gk + col), k1y = ka.y / dk * __ldg(gk + col + 1);
+        const float k2x = kb.x / dk * __ldg(gk + col + 64), k2y = kb.y / dk * __ldg(gk + col + 65);
+        __nv_bfloat162 o;
+        o = __floats2bfloat162_rn(c[0] * q1x - s[0] * q2x, c[1] * q1y - s[1] * q2y);
+        qr[h * 64 + lane] = *reinterpret_cast<uint32_t *>(&o);
+        o = __floats2bfloat162_rn(s[0] * q1x + c[0] * q2x, s[1] * q1y + c[1] * q2y);
+        qr[h * 64 + 32 + lane] = *reinterpret_cast<uint32_t *>(&o);
+        o = __floats2bfloat162_rn(c[0] * k1x - s[0] * k2x, c[1] * k1y - s[1] * k2y);
+        kr[h * 64 + lane] = *reinterpret_cast<uint32_t *>(&o);
+        o = __floats2bfloat162_rn(s[0] * k1x + c[0] * k2x, s[1] * k1y + c[1] * k2y);
+        kr[h * 64 + 32 + lane] = *reinterpret_cast<uint32_t *>(&o);
+    }
+}
+
 }  // namespace
+
+bool qk_norm_rope_fused(cudaStream_t st, __nv_bfloat16 *q, __nv_bfloat16 *k, int64_t ld, int rows, int T, int D,
+                        float eps, const float *gq, const float *gk, const float *pos, const float *freq, int grid,
+                        const float max_pos[3], bool use_mid, cudaError_t *err) {
+    if (D != 4096 || (ld % 2) || ((uintptr_t)q & 3) || ((uintptr_t)k & 3)) return false;
+    qk_norm_rope_fused_kernel<32><<<(rows + 7) / 8, 256, 0, st>>>(q, k, ld, rows, T, eps, gq, gk, pos, freq, grid,
+                                                                   max_pos[0], max_pos[1], max_pos[2], use_mid);
+    *err = cudaGetLastError();
+    return true;
+}
 
 cudaError_t permute_ct(cudaStream_t st, int sms, const float *in, float *out, int B, int C, int64_t T, bool to_tokens) {
     permute_ct_kernel<<<grid_for((int64_t)B * C * T, sms), 256, 0, st>>>(in, out, B, C, T, to_tokens);
@@ -411,6 +593,13 @@ cudaError_t rope_table(cudaStream_t st, int sms, const float *pos, int B, int T,
 cudaError_t norm_mod(cudaStream_t st, const float *x, int64_t ldx, int rows, int D, float eps, int mode,
                      const float *tab, int tab_coeff, const int *idx, int k_shift, __nv_bfloat16 *out, int64_t ldo) {
     if (rows <= 0) return cudaSuccess;
+    const bool vec = ldx % 4 == 0 && ldo % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 7) == 0 &&
+                     (!tab || ((uintptr_t)tab & 15) == 0);
+    if (vec && D == 4096) {
+        norm_mod_warp_kernel<32><<<(rows + 7) / 8, 256, 0, st>>>(x, ldx, rows, eps, mode, tab, tab_coeff, idx, k_shift,
+                                                                  out, ldo);
+        return cudaGetLastError();
+    }
     norm_mod_kernel<<<rows, 256, 0, st>>>(x, ldx, rows, D, eps, mode, tab, tab_coeff, idx, k_shift, out, ldo);
     return cudaGetLastError();
 }
@@ -425,6 +614,10 @@ cudaError_t ada_tables(cudaStream_t st, int sms, const float *const *sst_dev, in
 cudaError_t qk_norm_rope(cudaStream_t st, __nv_bfloat16 *buf, int64_t ld, int rows, int D, int H, float eps,
                          const float *gamma, const float *cos_t, const float *sin_t, bool interleaved) {
     if (rows <= 0) return cudaSuccess;
+    if (!cos_t && D == 4096 && ld % 8 == 0 && ((uintptr_t)buf & 15) == 0 && ((uintptr_t)gamma & 15) == 0) {
+        rmsnorm_gamma_warp_kernel<16><<<(rows + 7) / 8, 256, 0, st>>>(buf, ld, rows, eps, gamma);
+        return cudaGetLastError();
+    }
     const size_t smem = (size_t)D * sizeof(float);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(qk_norm_rope_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

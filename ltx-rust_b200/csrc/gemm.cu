@@ -38,6 +38,7 @@ struct GemmParams {
     const int *gate_idx;    // [M] row -> gate row (EPI_RESID, null = row 0)
     int64_t ld_gate;
     int *timeout_flag;
+    int f16_from_col;       // EPI_BF16: columns >= this are written as f16 (N = none)
 };
 
 namespace {
@@ -200,20 +201,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
                     }
                     __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + (int64_t)row * p.ldo + col0;
+                    // 32-column chunks never straddle f16_from_col (a multiple of 32 when used).
+                    const bool as_f16 = EPI == EPI_BF16 && col0 >= p.f16_from_col;
                     if (full_cols && ((reinterpret_cast<uintptr_t>(o) & 15) == 0)) {
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             uint32_t w[4];
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
-                                __nv_bfloat162 h = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
-                                w[e] = *reinterpret_cast<uint32_t *>(&h);
+                                if (as_f16) {
+                                    __half2 h = __floats2half2_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+                                    w[e] = *reinterpret_cast<uint32_t *>(&h);
+                                } else {
+                                    __nv_bfloat162 h = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+                                    w[e] = *reinterpret_cast<uint32_t *>(&h);
+                                }
                             }
                             *reinterpret_cast<uint4 *>(o + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
                         }
                     } else {
                         for (int j = 0; j < 32; ++j)
-                            if (col0 + j < p.N) o[j] = __float2bfloat16_rn(v[j]);
+                            if (col0 + j < p.N) {
+                                if (as_f16)
+                                    reinterpret_cast<__half *>(o)[j] = __float2half_rn(v[j]);
+                                else
+                                    o[j] = __float2bfloat16_rn(v[j]);
+                            }
                     }
                 } else if constexpr (EPI == EPI_F32) {
                     float *o = static_cast<float *>(p.out) + (int64_t)row * p.ldo + col0;
@@ -323,7 +336,7 @@ cudaError_t dispatch_epi(int epi, const CUtensorMap &ta, const CUtensorMap &tb, 
 // with leading dimensions lda/ldw (elements, multiples of 8, 16-byte aligned bases).
 int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
               int K, int epi, const float *bias, void *out, int64_t ldo, const float *gate, const int *gate_idx,
-              int64_t ld_gate) {
+              int64_t ld_gate, int f16_from_col) {
     if (!A || !W || !out) return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: null pointer");
     if (M <= 0 || N <= 0 || K <= 0) return fail(ctx, LTX_ERR_SHAPE, "gemm: empty shape %d x %d x %d", M, N, K);
     if (lda % 8 || ldw % 8 || lda < K || ldw < K || ((uintptr_t)A & 15) || ((uintptr_t)W & 15))
@@ -334,7 +347,10 @@ int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const v
     CUtensorMap ta, tb;
     if (!make_tmap_bf16(&ta, A, M, K, lda, BM) || !make_tmap_bf16(&tb, W, N, K, ldw, BN))
         return fail(ctx, LTX_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed");
-    GemmParams p{M, N, K, bias, out, ldo, gate, gate_idx, ld_gate, ctx->timeout_flag};
+    if (f16_from_col < 0 || f16_from_col > N) f16_from_col = N;
+    if (f16_from_col < N && (epi != EPI_BF16 || f16_from_col % 32))
+        return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: f16 columns need the bf16 epilogue and a multiple of 32");
+    GemmParams p{M, N, K, bias, out, ldo, gate, gate_idx, ld_gate, ctx->timeout_flag, f16_from_col};
     cudaError_t e = BN == 128 ? dispatch_epi<128>(epi, ta, tb, p, ctx->sm_count, st)
                               : dispatch_epi<256>(epi, ta, tb, p, ctx->sm_count, st);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm launch");
@@ -348,5 +364,5 @@ extern "C" int ltx_gemm_bf16(ltx_ctx *ctx, const void *a_dev, int64_t lda, const
                              const float *gate_dev, const int32_t *gate_idx_dev, int64_t ld_gate) {
     if (!ctx) return LTX_ERR_INVALID_ARG;
     return ltx::gemm_bf16(ctx, ctx->stream, a_dev, lda, w_dev, ldw, m, n, k, epilogue, bias_dev, out_dev, ldo, gate_dev,
-                          gate_idx_dev, ld_gate);
+                          gate_idx_dev, ld_gate, n);
 }

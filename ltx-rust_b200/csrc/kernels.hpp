@@ -15,11 +15,11 @@ int dequant_merge(ltx_ctx *ctx, cudaStream_t stream, const void *w, int w_dt, in
 // gemm.cu (epilogue codes = ltx_epilogue)
 int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
               int K, int epi, const float *bias, void *out, int64_t ldo, const float *gate, const int *gate_idx,
-              int64_t ld_gate);
+              int64_t ld_gate, int f16_from_col = 1 << 30);
 
 // attention.cu (head_dim 128)
 int attention_fwd(ltx_ctx *ctx, cudaStream_t st, const void *q, int64_t ldq, const void *k, int64_t ldk, const void *v,
-                  int64_t ldv, int B, int H, int Tq, int Tk, float scale, void *out, int64_t ldo);
+                  int64_t ldv, int B, int H, int Tq, int Tk, float scale, void *out, int64_t ldo, bool v_f16);
 
 // dit_kernels.cu
 cudaError_t rope_table(cudaStream_t st, int sms, const float *pos, int B, int T, const float *freq, int grid,
@@ -41,6 +41,11 @@ cudaError_t head_gate(cudaStream_t st, int sms, __nv_bfloat16 *o, int64_t ldo, c
 cudaError_t attention_generic(cudaStream_t st, const __nv_bfloat16 *q, int64_t ldq, const __nv_bfloat16 *k, int64_t ldk,
                               const __nv_bfloat16 *v, int64_t ldv, int B, int H, int Tq, int Tk, int d, float scale,
                               __nv_bfloat16 *out, int64_t ldo);
+// Fused self-attention Q/K RMSNorm(gamma) + split RoPE with in-register angles; returns
+// false (nothing launched) when the shape is not the specialised one (D 4096, head dim 128).
+bool qk_norm_rope_fused(cudaStream_t st, __nv_bfloat16 *q, __nv_bfloat16 *k, int64_t ld, int rows, int T, int D,
+                        float eps, const float *gq, const float *gk, const float *pos, const float *freq, int grid,
+                        const float max_pos[3], bool use_mid, cudaError_t *err);
 cudaError_t permute_ct(cudaStream_t st, int sms, const float *in, float *out, int B, int C, int64_t T, bool to_tokens);
 size_t cfg_scratch_bytes();
 cudaError_t cfg_euler(cudaStream_t st, int sms, float *x, const float *vc, const float *vu, const float *tok_t,

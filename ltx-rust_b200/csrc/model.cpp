@@ -537,13 +537,18 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
     // RoPE tables (rope.rs:46-167)
     const float mp[3] = {(float)c.max_pos[0], (float)c.max_pos[1], (float)c.max_pos[2]};
     const int width = c.interleaved ? (int)D : (int)(D / 2);
-    CU(rope_table(st, sms, positions, B, T, m->rope_freq, m->rope_grid, mp, c.use_mid, c.interleaved, width, w.cos, w.sin));
+    // The fused Q/K kernel computes RoPE angles in registers for the production
+    // shape (D 4096, head dim 128, split RoPE); other shapes use the tables.
+    const bool fused_qk = D == 4096 && d == 128 && !c.interleaved;
+    if (!fused_qk)
+        CU(rope_table(st, sms, positions, B, T, m->rope_freq, m->rope_grid, mp, c.use_mid, c.interleaved, width, w.cos,
+                      w.sin));
     if (!c.cross_adaln) CU(f32_to_bf16(st, sms, context, crow * Dc, w.ctxb));
 
     const float scale = 1.0f / sqrtf((float)d);
     auto attend = [&](const __nv_bfloat16 *q, int64_t ldq, const __nv_bfloat16 *k, int64_t ldk, const __nv_bfloat16 *v,
                       int64_t ldv, int Tk) -> int {
-        if (d == 128) return attention_fwd(ctx, st, q, ldq, k, ldk, v, ldv, B, (int)H, T, Tk, scale, w.att, D);
+        if (d == 128) return attention_fwd(ctx, st, q, ldq, k, ldk, v, ldv, B, (int)H, T, Tk, scale, w.att, D, true);
         CU(attention_generic(st, q, ldq, k, ldk, v, ldv, B, (int)H, T, Tk, (int)d, scale, w.att, D));
         return LTX_OK;
     };
@@ -552,10 +557,19 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         const float *tab = w.tab + (int64_t)l * U * K * D;
         // self-attention: x += attn(mod(rms(x))) * gate_msa
         CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 0, w.xn, D));
+        // V columns come out as f16: the attention keeps P in f16 for the P.V MMA
+        const int vcol = d == 128 ? (int)(2 * D) : (int)(3 * D);
         TRY(gemm_bf16(ctx, st, w.xn, D, b.qkv, D, (int)rows, (int)(3 * D), (int)D, LTX_EPI_BF16, b.qkv_b, w.qkv,
-                      3 * D, nullptr, nullptr, 0));
-        CU(qk_norm_rope(st, w.qkv, 3 * D, (int)rows, (int)D, (int)H, c.eps, b.qn, w.cos, w.sin, c.interleaved));
-        CU(qk_norm_rope(st, w.qkv + D, 3 * D, (int)rows, (int)D, (int)H, c.eps, b.kn, w.cos, w.sin, c.interleaved));
+                      3 * D, nullptr, nullptr, 0, vcol));
+        if (fused_qk) {
+            cudaError_t qe = cudaSuccess;
+            qk_norm_rope_fused(st, w.qkv, w.qkv + D, 3 * D, (int)rows, T, (int)D, c.eps, b.qn, b.kn, positions,
+                               m->rope_freq, m->rope_grid, mp, c.use_mid, &qe);
+            CU(qe);
+        } else {
+            CU(qk_norm_rope(st, w.qkv, 3 * D, (int)rows, (int)D, (int)H, c.eps, b.qn, w.cos, w.sin, c.interleaved));
+            CU(qk_norm_rope(st, w.qkv + D, 3 * D, (int)rows, (int)D, (int)H, c.eps, b.kn, w.cos, w.sin, c.interleaved));
+        }
         TRY(attend(w.qkv, 3 * D, w.qkv + D, 3 * D, w.qkv + 2 * D, 3 * D, T));
         if (c.gated) {
             TRY(gemm_bf16(ctx, st, w.xn, D, b.g1, D, (int)rows, (int)H, (int)D, LTX_EPI_F32, b.g1_b, w.glog, H, nullptr,
@@ -574,7 +588,7 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         CU(qk_norm_rope(st, w.q2, D, (int)rows, (int)D, (int)H, c.eps, b.qn2, nullptr, nullptr, false));
         if (c.cross_adaln) CU(ctx_mod(st, sms, context, crow * Dc, (int)Dc, b.pst, w.ctxb));
         TRY(gemm_bf16(ctx, st, w.ctxb, Dc, b.kv2, Dc, (int)crow, (int)(2 * D), (int)Dc, LTX_EPI_BF16, b.kv2_b, w.kv2,
-                      2 * D, nullptr, nullptr, 0));
+                      2 * D, nullptr, nullptr, 0, d == 128 ? (int)D : (int)(2 * D)));
         CU(qk_norm_rope(st, w.kv2, 2 * D, (int)crow, (int)D, (int)H, c.eps, b.kn2, nullptr, nullptr, false));
         TRY(attend(w.q2, D, w.kv2, 2 * D, w.kv2 + D, 2 * D, S));
         if (c.gated) {

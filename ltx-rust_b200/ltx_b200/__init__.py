@@ -60,7 +60,7 @@ def lib() -> ctypes.CDLL:
         "ltx_gemm_bf16": (I, [V, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                               P, P, I64, P, P, I64]),
         "ltx_attention_fwd": (I, [V, P, I64, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
-                                  ctypes.c_int32, ctypes.c_int32, F, P, I64]),
+                                  ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, F, P, I64]),
         "ltx_store_open": (I, [V, ctypes.POINTER(ctypes.c_char_p), ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(V)]),
         "ltx_store_destroy": (None, [V]),
         "ltx_store_merge_lora": (I, [V, ctypes.c_char_p, F, ctypes.POINTER(ctypes.c_int32),
@@ -155,8 +155,10 @@ def gemm(ctx: "Context", a, w, out, epilogue=EPI_BF16, bias=None, gate=None, gat
 
 
 def attention(ctx: "Context", q, k, v, out, batch, heads, tq, tk, scale, head_dim=128):
-    """out = softmax(q k^T * scale) v; q/k/v/out token-major bf16 CUDA tensors (row stride = stride(0))."""
-    ctx.check(lib().ltx_attention_fwd(ctx.h, _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0),
+    """out = softmax(q k^T * scale) v; q/k/out token-major bf16 CUDA tensors, v bf16 or f16 (row stride = stride(0))."""
+    import torch
+    vdt = LTX_F16 if v.dtype == torch.float16 else LTX_BF16
+    ctx.check(lib().ltx_attention_fwd(ctx.h, _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(v), v.stride(0), vdt,
                                       batch, heads, tq, tk, head_dim, scale, _ptr(out), out.stride(0)),
               "ltx_attention_fwd")
 

@@ -51,7 +51,7 @@ def main():
         Tk = a.Tk or a.T
         q = torch.randn(a.B * a.T, a.H * 128, device="cuda", generator=g).to(torch.bfloat16)
         k = torch.randn(a.B * Tk, a.H * 128, device="cuda", generator=g).to(torch.bfloat16)
-        v = torch.randn(a.B * Tk, a.H * 128, device="cuda", generator=g).to(torch.bfloat16)
+        v = torch.randn(a.B * Tk, a.H * 128, device="cuda", generator=g).to(torch.float16)
         o = torch.empty_like(q)
         fn = lambda: ltx_b200.attention(ctx, q, k, v, o, a.B, a.H, a.T, Tk, 1 / math.sqrt(128))
         flops = 4.0 * a.B * a.H * a.T * Tk * 128

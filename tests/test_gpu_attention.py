@@ -33,14 +33,15 @@ def rel_l2(a, b):
     return float((a.double() - b.double()).norm() / b.double().norm())
 
 
+@pytest.mark.parametrize("vdt", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("B,H,Tq,Tk", [(1, 1, 128, 128), (2, 2, 256, 384), (2, 3, 200, 300), (1, 2, 1, 5),
                                        (2, 4, 1024, 77), (1, 2, 384, 1024), (2, 1, 130, 129)])
-def test_attention_small(ctx, B, H, Tq, Tk):
+def test_attention_small(ctx, B, H, Tq, Tk, vdt):
     import ltx_b200
     g = torch.Generator(device="cuda").manual_seed(B * 1000 + H * 100 + Tq + Tk)
     q = torch.randn(B * Tq, H * 128, device="cuda", generator=g).to(torch.bfloat16)
     k = torch.randn(B * Tk, H * 128, device="cuda", generator=g).to(torch.bfloat16)
-    v = torch.randn(B * Tk, H * 128, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B * Tk, H * 128, device="cuda", generator=g).to(vdt)
     out = torch.zeros(B * Tq, H * 128, device="cuda", dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(128)
     ltx_b200.attention(ctx, q, k, v, out, B, H, Tq, Tk, scale)
@@ -70,7 +71,7 @@ def test_attention_full_size(ctx):
     g = torch.Generator(device="cuda").manual_seed(11)
     q = torch.randn(B * T, H * 128, device="cuda", generator=g).to(torch.bfloat16)
     k = torch.randn(B * T, H * 128, device="cuda", generator=g).to(torch.bfloat16)
-    v = torch.randn(B * T, H * 128, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B * T, H * 128, device="cuda", generator=g).to(torch.float16)
     out = torch.zeros(B * T, H * 128, device="cuda", dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(128)
     ltx_b200.attention(ctx, q, k, v, out, B, H, T, T, scale)
@@ -88,7 +89,7 @@ def test_attention_full_size(ctx):
     ctx.synchronize()
     ms = s.elapsed_time(e) / 3
     flops = 4.0 * B * H * T * T * 128
-    qt, kt, vt = (x.view(B, T, H, 128).transpose(1, 2) for x in (q, k, v))
+    qt, kt, vt = (x.view(B, T, H, 128).transpose(1, 2) for x in (q, k, v.to(torch.bfloat16)))
     torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)
     s.record()
     for _ in range(3):

@@ -258,3 +258,28 @@ def test_denoise_step_errors(ctx, mid_ckpt):
     with pytest.raises(ltx_b200.LtxError) as e:
         model.denoise_step(z, z, m, pos, cc, None, 0.5, 0.2, 3.0)
     assert e.value.kind == "NEGATIVE_CONTEXT"
+
+
+def test_wide_model_forward(ctx, tmp_path):
+    """D = 4096, 32 heads x 128 (the 22B block width): exercises the warp-per-row
+    norms and the fused Q/K RMSNorm + in-register RoPE path."""
+    import ltx_b200
+    from dit_checkpoint import small_config, write_checkpoint
+    cfg = small_config(heads=32, head_dim=128, layers=1)
+    ck = str(tmp_path / "wide.safetensors")
+    write_checkpoint(ck, cfg, seed=11)
+    st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    lat, ts, pos, ctxt = make_inputs(cfg, F=2, Hh=8, W=8, S=64, seed=3)
+    out = torch.empty(lat.shape, dtype=torch.float32, device="cuda")
+    model.forward(*(torch.from_numpy(a).cuda() for a in (lat, ts, pos, ctxt)), out)
+    ctx.synchronize()
+    model.close()
+    st.close()
+    o = OracleStore([ck], KeyMap.transformer())
+    params = dit.load_params({k: o.read(k, n_threads=os.cpu_count() or 1) for k in o.keys()})
+    with torch.no_grad():
+        exp = dit.model_forward(params, dit.DiTConfig.from_json(cfg), *(torch.from_numpy(a) for a in (lat, ts, pos, ctxt))).numpy()
+    err = rel_l2(out.cpu().numpy(), exp)
+    print(f"\nwide model forward rel-L2 {err:.2e}")
+    assert err < 1e-2
