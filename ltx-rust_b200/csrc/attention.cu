@@ -2,25 +2,28 @@
 //
 // Replaces sdp_attention (crates/ltx-dit/src/attention.rs:228-242), which
 // materialises softmax(Q K^T * scale) V as a full [B, H, Tq, Tk] f32 matrix;
-// here the scores live only in TMEM.  Head dim 128, bf16 Q/K/V, f32
-// accumulation, non-causal, optional key padding mask for a ragged last tile.
+// here the scores live only in TMEM.  Head dim 128, bf16 Q/K, bf16 or f16 V,
+// f32 accumulation, non-causal, key padding mask for a ragged last tile.
 //
-// One CTA per (batch, head, 128-query tile), 6 warps:
-//   warp 0   TMA: Q once, then K_j / V_j into a 2-stage ring (3-D tensor
-//            maps {H*128, T, B}, so a tile never reads the next batch).
-//   warp 1   one thread issues tcgen05.mma:
-//              S_j  = Q K_j^T        -> TMEM S[j%2]   (A,B K-major)
-//              PV_j = P_j V_j        -> TMEM PV[j%2]  (A = P from smem,
-//                                                      B = V_j MN-major)
-//            QK_{j+1} is issued before PV_j, so the tensor core computes the
-//            next scores while the softmax warps work on the current ones.
-//   warps 2-9  two threads per query row (warps w and w+4 share a TMEM lane
-//            quadrant; each takes 64 of the 128 score / output columns):
-//            row max exchanged through shared memory (named barrier), exp2
-//            two-at-a-time (ex2.approx.f16x2), P_j (bf16) written to smem in
-//            the 128B-swizzled K-major layout the MMA reads (each half-thread
-//            writes one whole 64-key swizzle atom), O half kept in registers
-//            and updated with PV_{j-1} one tile late (O = O*exp2(m_o - m) + PV).
+// One CTA per (batch, head, 256 queries) = two 128-row query tiles A and B
+// that share every K/V tile (half the L2->SM traffic of one tile per CTA).
+// 10 warps:
+//   warp 0     TMA: Q_A and Q_B once, then K_0, V_0, K_1, V_1, ... through a
+//              3-slot ring of 32 KB tiles (3-D tensor maps {H*128, T, B}, so
+//              a tile never reads the next batch).
+//   warp 1     one thread issues tcgen05.mma in the order
+//                QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) ...
+//              S_X = Q_X K_j^T -> TMEM S_X; O_X += P_X V_j -> TMEM O_X
+//              (P from smem, V as an MN-major B operand), so tile A's
+//              softmax runs under tile B's MMAs and vice versa.
+//   warps 2-5  softmax of tile A, warps 6-9 of tile B: one query row per
+//              thread; the row's 128 scores are read from TMEM into
+//              registers, max and exp2 (two per MUFU op, ex2.approx.f16x2),
+//              P (f16 or bf16) written to smem in the 128B-swizzled K-major
+//              layout.  O stays in TMEM; it is rescaled in place (tcgen05.ld/
+//              st) only when a row max grows by more than kRescaleLog2 over
+//              the max P is taken against — safe because the scores of tile
+//              j are ready only after the P.V of tile j-1 has completed.
 // All waits are bounded (2 s) and report LTX_ERR_TIMEOUT through the flag.
 #include <cuda.h>
 
@@ -42,22 +45,21 @@ namespace {
 
 constexpr int D = 128;
 constexpr int BQ = 128, BKV = 128;
-constexpr int KV_STAGES = 2;
+constexpr int kRing = 3;                  // K/V tile slots
 constexpr int kThreads = 320;
-constexpr int kSoftmaxWarps = 8;
-constexpr int TILE_BYTES = 128 * D * 2;   // 32 KB: 128 rows x 128 bf16 (two 64-col swizzle atoms)
+constexpr int TILE_BYTES = 128 * D * 2;   // 32 KB: 128 rows x 128 16-bit values (two 64-col swizzle atoms)
 constexpr int HALF_BYTES = 128 * 64 * 2;  // 16 KB: one atom column block
+constexpr float kRescaleLog2 = 8.0f;      // O is rescaled when a row max grows by more than 2^8
 
 struct AttnSmemLayout {
-    static constexpr int Q = 0;
-    static constexpr int P = Q + TILE_BYTES;
-    static constexpr int K = P + TILE_BYTES;
-    static constexpr int V = K + KV_STAGES * TILE_BYTES;
-    static constexpr int BAR = V + KV_STAGES * TILE_BYTES;
-    static constexpr int RED = BAR + 256;                   // [2 parity][2 half][128 rows] f32
-    static constexpr int BYTES = RED + 2 * 2 * 128 * 4;
+    static constexpr int Q = 0;                         // Q_A, Q_B
+    static constexpr int P = Q + 2 * TILE_BYTES;        // P_A, P_B
+    static constexpr int RING = P + 2 * TILE_BYTES;     // kRing K/V slots
+    static constexpr int BAR = RING + kRing * TILE_BYTES;
+    static constexpr int BYTES = BAR + 128;
 };
 constexpr size_t kAttnSmem = AttnSmemLayout::BYTES + 1024;
+static_assert(kAttnSmem <= 232448, "attention smem exceeds the per-CTA limit");
 
 __device__ __forceinline__ void tma_load_3d(void *smem_dst, const void *tmap, uint64_t *bar, int x, int y, int z) {
     asm volatile(
@@ -77,17 +79,17 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// exp2 of two values with one MUFU op: f32 -> f16x2 -> ex2.approx.f16x2 -> f32.
-// (P is rounded to bf16 for the MMA afterwards, so the f16 step costs nothing.)
-__device__ __forceinline__ float2 ex2x2(float a, float b) {
-    uint32_t in, out;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(b), "f"(a));
-    asm("ex2.approx.f16x2 %0, %1;" : "=r"(out) : "r"(in));
-    __half2 h = *reinterpret_cast<__half2 *>(&out);
-    return __half22float2(h);
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
 }
-
-__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // VF16: V (and so P) are f16; otherwise bf16.  Q and K are always bf16.
 template <bool VF16>
@@ -98,23 +100,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *sQ = smem + AttnSmemLayout::Q;
     unsigned char *sP = smem + AttnSmemLayout::P;
-    unsigned char *sK = smem + AttnSmemLayout::K;
-    unsigned char *sV = smem + AttnSmemLayout::V;
+    unsigned char *sRing = smem + AttnSmemLayout::RING;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + AttnSmemLayout::BAR);
     uint64_t *q_full = bars + 0;
-    uint64_t *k_full = bars + 1;            // [KV_STAGES]
-    uint64_t *v_full = bars + 3;            // [KV_STAGES]
-    uint64_t *kv_empty = bars + 5;          // [KV_STAGES]
-    uint64_t *s_full = bars + 7;            // [2]
-    uint64_t *s_empty = bars + 9;           // [2]
-    uint64_t *p_full = bars + 11;
-    uint64_t *p_empty = bars + 12;
-    uint64_t *pv_full = bars + 13;          // [2]
-    uint64_t *pv_empty = bars + 15;         // [2]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 17);
+    uint64_t *slot_full = bars + 1;         // [kRing]
+    uint64_t *slot_empty = bars + 4;        // [kRing]
+    uint64_t *s_full = bars + 7;            // [2]  tile A, B
+    uint64_t *p_full = bars + 9;            // [2]
+    uint64_t *pv_done = bars + 11;          // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 13);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q_tiles = (p.Tq + BQ - 1) / BQ;
+    const int q_tiles = (p.Tq + 2 * BQ - 1) / (2 * BQ);
     const int qt = blockIdx.x % q_tiles;
     const int h = (blockIdx.x / q_tiles) % p.H;
     const int b = blockIdx.x / (q_tiles * p.H);
@@ -122,19 +119,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < KV_STAGES; ++s) {
-            mbar_init(&k_full[s], 1);
-            mbar_init(&v_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+        for (int s = 0; s < kRing; ++s) {
+            mbar_init(&slot_full[s], 1);
+            mbar_init(&slot_empty[s], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_empty[i], kSoftmaxWarps);
-            mbar_init(&pv_full[i], 1);
-            mbar_init(&pv_empty[i], kSoftmaxWarps);
+            mbar_init(&p_full[i], 4);
+            mbar_init(&pv_done[i], 1);
         }
-        mbar_init(p_full, kSoftmaxWarps);
-        mbar_init(p_empty, 1);
         fence_barrier_init();
     }
     if (warp == 0) {
@@ -144,7 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem = *tmem_slot;   // S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
     bool aborted = false;
 
     if (warp == 0) {
@@ -152,209 +145,207 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmQ);
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
-            mbar_arrive_expect_tx(q_full, TILE_BYTES);
-            tma_load_3d(sQ, &tmQ, q_full, h * D, qt * BQ, b);
-            tma_load_3d(sQ + HALF_BYTES, &tmQ, q_full, h * D + 64, qt * BQ, b);
+            mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+            for (int t = 0; t < 2; ++t) {
+                tma_load_3d(sQ + t * TILE_BYTES, &tmQ, q_full, h * D, qt * 2 * BQ + t * BQ, b);
+                tma_load_3d(sQ + t * TILE_BYTES + HALF_BYTES, &tmQ, q_full, h * D + 64, qt * 2 * BQ + t * BQ, b);
+            }
+            // load sequence: s = 2j -> K_j, s = 2j + 1 -> V_j, slot s % kRing
             int issued = 0;
-            for (int j = 0; j < n_kv && !aborted; ++j, ++issued) {
-                const int s = j % KV_STAGES;
-                const uint32_t ph = (j / KV_STAGES) & 1;
-                if (!mbar_wait(&kv_empty[s], ph ^ 1, p.timeout_flag, 201, &aborted)) break;
-                unsigned char *k_dst = sK + s * TILE_BYTES, *v_dst = sV + s * TILE_BYTES;
-                mbar_arrive_expect_tx(&k_full[s], TILE_BYTES);
-                tma_load_3d(k_dst, &tmK, &k_full[s], h * D, j * BKV, b);
-                tma_load_3d(k_dst + HALF_BYTES, &tmK, &k_full[s], h * D + 64, j * BKV, b);
-                mbar_arrive_expect_tx(&v_full[s], TILE_BYTES);
-                tma_load_3d(v_dst, &tmV, &v_full[s], h * D, j * BKV, b);
-                tma_load_3d(v_dst + HALF_BYTES, &tmV, &v_full[s], h * D + 64, j * BKV, b);
+            for (int s = 0; s < 2 * n_kv && !aborted; ++s, ++issued) {
+                const int slot = s % kRing;
+                if (!mbar_wait(&slot_empty[slot], ((s / kRing) & 1) ^ 1, p.timeout_flag, 201, &aborted)) break;
+                unsigned char *dst = sRing + slot * TILE_BYTES;
+                const void *tm = (s & 1) ? &tmV : &tmK;
+                const int j = s >> 1;
+                mbar_arrive_expect_tx(&slot_full[slot], TILE_BYTES);
+                tma_load_3d(dst, tm, &slot_full[slot], h * D, j * BKV, b);
+                tma_load_3d(dst + HALF_BYTES, tm, &slot_full[slot], h * D + 64, j * BKV, b);
             }
             // Wait for every copy this thread started before the CTA can exit.
             bool a2 = false;
             mbar_wait(q_full, 0, nullptr, 0, &a2);
-            for (int j = issued > KV_STAGES ? issued - KV_STAGES : 0; j < issued; ++j) {
-                mbar_wait(&k_full[j % KV_STAGES], (j / KV_STAGES) & 1, nullptr, 0, &a2);
-                mbar_wait(&v_full[j % KV_STAGES], (j / KV_STAGES) & 1, nullptr, 0, &a2);
-            }
+            for (int s = issued > kRing ? issued - kRing : 0; s < issued; ++s)
+                mbar_wait(&slot_full[s % kRing], (s / kRing) & 1, nullptr, 0, &a2);
         }
     } else if (warp == 1) {
         if (elect_one()) {
             constexpr uint32_t idesc_qk = idesc_f16(BQ, BKV, true, false);
             constexpr uint32_t idesc_pv = idesc_f16(BQ, D, !VF16, true);   // B = V, MN-major
             const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
-            auto issue_pv = [&](int j) -> bool {
-                const int s = j % KV_STAGES;
-                if (!mbar_wait(p_full, j & 1, p.timeout_flag, 202, &aborted)) return false;
-                if (!mbar_wait(&v_full[s], (j / KV_STAGES) & 1, p.timeout_flag, 203, &aborted)) return false;
-                if (!mbar_wait(&pv_empty[j & 1], ((j >> 1) & 1) ^ 1, p.timeout_flag, 204, &aborted)) return false;
-                tc_fence_after();
-                const uint32_t v_addr = smem_u32(sV + s * TILE_BYTES);
-                const uint32_t d_tmem = tmem + 256 + (j & 1) * 128;
+            auto slot_of = [](int s) { return s % kRing; };
+            auto wait_slot = [&](int s, int code) {
+                return mbar_wait(&slot_full[slot_of(s)], (s / kRing) & 1, p.timeout_flag, code, &aborted);
+            };
+            auto issue_qk = [&](int t, int j) {   // S_t = Q_t K_j^T
+                const uint32_t k_addr = smem_u32(sRing + slot_of(2 * j) * TILE_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+                    umma_f16_ss(tmem + t * 128, sdesc_sw128(q_addr + t * TILE_BYTES + off, 16, 1024),
+                                sdesc_sw128(k_addr + off, 16, 1024), idesc_qk, kk ? 1u : 0u);
+                }
+                umma_commit(&s_full[t]);
+            };
+            auto issue_pv = [&](int t, int j) {   // O_t (+)= P_t V_j
+                const uint32_t v_addr = smem_u32(sRing + slot_of(2 * j + 1) * TILE_BYTES);
+                const uint32_t pa = p_addr + t * TILE_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < BKV / 16; ++kk) {
-                    const uint64_t ad = sdesc_sw128(p_addr + (kk >> 2) * HALF_BYTES + (kk & 3) * 32, 16, 1024);
+                    const uint64_t ad = sdesc_sw128(pa + (kk >> 2) * HALF_BYTES + (kk & 3) * 32, 16, 1024);
                     const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, HALF_BYTES, 1024);
-                    umma_f16_ss(d_tmem, ad, bd, idesc_pv, kk ? 1u : 0u);
+                    umma_f16_ss(tmem + 256 + t * 128, ad, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                umma_commit(&pv_full[j & 1]);
-                umma_commit(&kv_empty[s]);
-                umma_commit(p_empty);
-                return true;
+                umma_commit(&pv_done[t]);
             };
-            if (mbar_wait(q_full, 0, p.timeout_flag, 205, &aborted)) {
-                for (int j = 0; j < n_kv; ++j) {
-                    const int s = j % KV_STAGES;
-                    if (!mbar_wait(&k_full[s], (j / KV_STAGES) & 1, p.timeout_flag, 206, &aborted)) break;
-                    if (!mbar_wait(&s_empty[j & 1], ((j >> 1) & 1) ^ 1, p.timeout_flag, 207, &aborted)) break;
-                    tc_fence_after();
-                    const uint32_t k_addr = smem_u32(sK + s * TILE_BYTES);
-                    const uint32_t d_tmem = tmem + (j & 1) * 128;
-#pragma unroll
-                    for (int kk = 0; kk < D / 16; ++kk) {
-                        const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-                        umma_f16_ss(d_tmem, sdesc_sw128(q_addr + off, 16, 1024), sdesc_sw128(k_addr + off, 16, 1024),
-                                    idesc_qk, kk ? 1u : 0u);
+            bool ok = mbar_wait(q_full, 0, p.timeout_flag, 205, &aborted) && wait_slot(0, 206);
+            if (ok) {
+                tc_fence_after();
+                issue_qk(0, 0);
+                issue_qk(1, 0);
+                umma_commit(&slot_empty[slot_of(0)]);   // K_0 read by both
+            }
+            for (int j = 0; ok && j < n_kv; ++j) {
+                // V_j, then per tile: PV_t(j) once P_t(j) is ready, then QK_t(j+1)
+                if (!wait_slot(2 * j + 1, 207)) break;
+                const bool next = j + 1 < n_kv;
+                if (next && !wait_slot(2 * j + 2, 208)) break;
+                for (int t = 0; t < 2; ++t) {
+                    if (!mbar_wait(&p_full[t], j & 1, p.timeout_flag, 209 + t, &aborted)) {
+                        ok = false;
+                        break;
                     }
-                    umma_commit(&s_full[j & 1]);
-                    if (j > 0 && !issue_pv(j - 1)) break;
+                    tc_fence_after();
+                    issue_pv(t, j);
+                    if (next) issue_qk(t, j + 1);
                 }
-                if (!aborted) issue_pv(n_kv - 1);
+                if (!ok) break;
+                umma_commit(&slot_empty[slot_of(2 * j + 1)]);        // V_j read by both PVs
+                if (next) umma_commit(&slot_empty[slot_of(2 * j + 2)]);   // K_{j+1} read by both QKs
             }
         }
     } else {
-        // Softmax / output warps 2..9: row quad*32 + lane, column half `hf` (64 of 128).
+        // Softmax warps: tile t = 0 (warps 2-5) or 1 (warps 6-9), row quad*32 + lane.
+        const int t = (warp - 2) >> 2;
         const int quad = warp & 3;
-        const int hf = (warp - 2) >> 2;
         const int row_in_tile = quad * 32 + lane;
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-        float *red = reinterpret_cast<float *>(smem + AttnSmemLayout::RED);   // [2][2][128]
-        float2 o[D / 4];   // this thread's 64 output columns as pairs
-#pragma unroll
-        for (int c = 0; c < D / 4; ++c) o[c] = make_float2(0.f, 0.f);
-        float m = -INFINITY, l = 0.f, m_o = -INFINITY;
-        float m_hist[2] = {-INFINITY, -INFINITY};   // max used for P_j, by j % 2
-        // P smem: row r, 16-byte chunk c of atom a at a*16K + r*128 + ((c ^ (r&7)) * 16).
-        // This thread writes atom `hf` of its row (keys hf*64 .. hf*64+63).
-        unsigned char *p_row = sP + hf * HALF_BYTES + row_in_tile * 128;
+        const uint32_t s_tmem = tmem + lane_base + t * 128;
+        const uint32_t o_tmem = tmem + lane_base + 256 + t * 128;
+        unsigned char *p_row = sP + t * TILE_BYTES + row_in_tile * 128;
         const int sw = row_in_tile & 7;
-
-        auto fold_pv = [&](int j) -> bool {
-            if (!mbar_wait(&pv_full[j & 1], (j >> 1) & 1, p.timeout_flag, 208, &aborted)) return false;
-            tc_fence_after();
-            const float mj = m_hist[j & 1];
-            const float alpha = ex2(m_o - mj);   // 0 on the first fold (m_o = -inf)
-            const float2 a2 = make_float2(alpha, alpha);
-            m_o = mj;
-            uint32_t r0[32], r1[32];
-            tmem_ld_32x32b_x32(tmem + lane_base + 256 + (j & 1) * 128 + hf * 64, r0);
-            tmem_ld_32x32b_x32(tmem + lane_base + 256 + (j & 1) * 128 + hf * 64 + 32, r1);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                o[e] = __ffma2_rn(o[e], a2, make_float2(__uint_as_float(r0[2 * e]), __uint_as_float(r0[2 * e + 1])));
-                o[16 + e] = __ffma2_rn(o[16 + e], a2, make_float2(__uint_as_float(r1[2 * e]), __uint_as_float(r1[2 * e + 1])));
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&pv_empty[j & 1]);
-            return true;
-        };
-
-        // Every softmax thread calls softmax_bar() exactly n_kv + 1 times, also
-        // after a timed-out wait (it then skips the work, not the barrier), so
-        // the named barrier can never be left waiting.
         const float2 sl2 = make_float2(p.scale_log2, p.scale_log2);
-        for (int j = 0; j < n_kv; ++j) {
-            const bool live = mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.timeout_flag, 209, &aborted);
-            const int kv0 = j * BKV + hf * 64;
-            const bool ragged = kv0 + 64 > p.Tk;   // only the last tile can be
-            float sv[64];
+        float m_ref = -INFINITY;   // the max P is taken against
+        float l = 0.f;
+        for (int j = 0; j < n_kv && !aborted; ++j) {
+            if (!mbar_wait(&s_full[t], j & 1, p.timeout_flag, 211, &aborted)) break;
+            tc_fence_after();
+            const int kv0 = j * BKV;
+            const bool ragged = kv0 + BKV > p.Tk;   // only the last tile can be
+            // pass 1: row max over the 128 scores (read from TMEM in 32-column chunks)
             float mx = -INFINITY;
-            if (live) {
-                tc_fence_after();
-                const uint32_t s_tmem = tmem + lane_base + (j & 1) * 128 + hf * 64;
-                uint32_t r0[32], r1[32];
-                tmem_ld_32x32b_x32(s_tmem, r0);
-                tmem_ld_32x32b_x32(s_tmem + 32, r1);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(s_tmem + c * 32, r);
                 tmem_ld_wait();
-                // the scores are in registers: hand the TMEM buffer back to the MMA warp
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_empty[j & 1]);
 #pragma unroll
                 for (int e = 0; e < 32; ++e) {
-                    sv[e] = __uint_as_float(r0[e]);
-                    sv[32 + e] = __uint_as_float(r1[e]);
+                    const float v = (ragged && kv0 + c * 32 + e >= p.Tk) ? -INFINITY : __uint_as_float(r[e]);
+                    mx = fmaxf(mx, v);
                 }
-                if (ragged) {
-#pragma unroll
-                    for (int e = 0; e < 64; ++e)
-                        if (kv0 + e >= p.Tk) sv[e] = -INFINITY;
-                }
-#pragma unroll
-                for (int e = 0; e < 64; ++e) mx = fmaxf(mx, sv[e]);
-                mx *= p.scale_log2;   // scale > 0: max(s * scale) = scale * max(s)
             }
-            float *rj = red + (j & 1) * 256;
-            rj[hf * 128 + row_in_tile] = mx;
-            softmax_bar();
-            if (!live || aborted) continue;
-            mx = fmaxf(rj[row_in_tile], rj[128 + row_in_tile]);
-            const float m_new = fmaxf(m, mx);
-            const float corr = ex2(m - m_new);
-            m = m_new;
-            m_hist[j & 1] = m_new;
-            // P_j overwrites P_{j-1}: wait until PV_{j-1} has read it.
-            if (j > 0 && !mbar_wait(p_empty, (j - 1) & 1, p.timeout_flag, 210, &aborted)) continue;
-            // P = exp2(s * scale - m): two per MUFU op (ex2.approx.f16x2), partial row sum in f32.
-            const float2 nm2 = make_float2(-m_new, -m_new);
+            mx *= p.scale_log2;   // scale > 0: max(s * scale) = scale * max(s)
+            if (mx > m_ref + kRescaleLog2) {
+                // O_t and l are relative to m_ref; move them to mx.  P.V of the
+                // previous tile has completed (its commit preceded this S).
+                const float alpha = ex2(m_ref - mx);   // 0 when m_ref = -inf
+                if (j > 0) {
+                    const float2 a2 = make_float2(alpha, alpha);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(o_tmem + c * 32, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            const float2 v = __fmul2_rn(make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), a2);
+                            r[2 * e] = __float_as_uint(v.x);
+                            r[2 * e + 1] = __float_as_uint(v.y);
+                        }
+                        tmem_st_32x32b_x32(o_tmem + c * 32, r);
+                    }
+                    tmem_st_wait();
+                }
+                l *= alpha;
+                m_ref = mx;
+            }
+            // pass 2: P = exp2(s * scale - m_ref) (<= 2^kRescaleLog2), two per MUFU op; row sum in f32.
+            const float2 nm2 = make_float2(-m_ref, -m_ref);
             float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {   // 8 chunks of 8 keys = one 16-byte smem store each
-                uint32_t pk[4];
+            for (int c = 0; c < 4; ++c) {           // keys c*32 .. c*32+31: atom c>>1, chunks (c&1)*4 ..
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(s_tmem + c * 32, r);
+                tmem_ld_wait();
+                if (ragged) {
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int e = q * 8 + 2 * t;
-                    const float2 x = __ffma2_rn(make_float2(sv[e], sv[e + 1]), sl2, nm2);
-                    uint32_t in, out;
-                    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(x.y), "f"(x.x));
-                    asm("ex2.approx.f16x2 %0, %1;" : "=r"(out) : "r"(in));
-                    const float2 pf = __half22float2(*reinterpret_cast<__half2 *>(&out));
-                    sum2 = __fadd2_rn(sum2, pf);
-                    if constexpr (VF16) {
-                        pk[t] = out;
-                    } else {
-                        __nv_bfloat162 hv = __floats2bfloat162_rn(pf.x, pf.y);
-                        pk[t] = *reinterpret_cast<uint32_t *>(&hv);
-                    }
+                    for (int e = 0; e < 32; ++e)
+                        if (kv0 + c * 32 + e >= p.Tk) r[e] = __float_as_uint(-INFINITY);
                 }
-                *reinterpret_cast<uint4 *>(p_row + ((q ^ sw) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                unsigned char *atom = p_row + (c >> 1) * HALF_BYTES;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {      // 16-byte chunk: 8 keys
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int e = q * 8 + 2 * u;
+                        const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sl2, nm2);
+                        uint32_t in, out;
+                        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(x.y), "f"(x.x));
+                        asm("ex2.approx.f16x2 %0, %1;" : "=r"(out) : "r"(in));
+                        const float2 pf = __half22float2(*reinterpret_cast<__half2 *>(&out));
+                        sum2 = __fadd2_rn(sum2, pf);
+                        if constexpr (VF16) {
+                            pk[u] = out;
+                        } else {
+                            __nv_bfloat162 hv = __floats2bfloat162_rn(pf.x, pf.y);
+                            pk[u] = *reinterpret_cast<uint32_t *>(&hv);
+                        }
+                    }
+                    const int chunk = (c & 1) * 4 + q;
+                    *reinterpret_cast<uint4 *>(atom + ((chunk ^ sw) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
             }
-            l = l * corr + (sum2.x + sum2.y);
+            l += sum2.x + sum2.y;
+            tc_fence_before();
             fence_proxy_async_smem();   // P (generic-proxy writes) -> visible to the tensor core
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
-            if (j > 0) fold_pv(j - 1);
+            if (lane == 0) mbar_arrive(&p_full[t]);
         }
-        if (!aborted) fold_pv(n_kv - 1);
-        // combine the two partial row sums in the buffer the last max exchange did not use
-        float *rl = red + (n_kv & 1) * 256;
-        rl[hf * 128 + row_in_tile] = l;
-        softmax_bar();
-        const float l_row = rl[row_in_tile] + rl[128 + row_in_tile];
-        if (!aborted) {
-            const int q_row = qt * BQ + row_in_tile;
-            if (q_row < p.Tq) {
-                const float inv = 1.f / l_row;
-                __nv_bfloat16 *dst = p.out + ((int64_t)b * p.Tq + q_row) * p.ldo + h * D + hf * 64;
+        // O_t is final once the last P.V has completed.
+        if (!aborted && mbar_wait(&pv_done[t], (n_kv - 1) & 1, p.timeout_flag, 212, &aborted)) {
+            tc_fence_after();
+            const int q_row = qt * 2 * BQ + t * BQ + row_in_tile;
+            const float inv = 1.f / l;
+            __nv_bfloat16 *dst = p.out + ((int64_t)b * p.Tq + q_row) * p.ldo + h * D;
 #pragma unroll
-                for (int c = 0; c < D / 4; c += 4) {
-                    uint32_t w[4];
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(o_tmem + c * 32, r);
+                tmem_ld_wait();
+                if (q_row < p.Tq) {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        __nv_bfloat162 hv = __floats2bfloat162_rn(o[c + e].x * inv, o[c + e].y * inv);
-                        w[e] = *reinterpret_cast<uint32_t *>(&hv);
+                    for (int g = 0; g < 4; ++g) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            __nv_bfloat162 hv = __floats2bfloat162_rn(__uint_as_float(r[g * 8 + 2 * e]) * inv,
+                                                                      __uint_as_float(r[g * 8 + 2 * e + 1]) * inv);
+                            w[e] = *reinterpret_cast<uint32_t *>(&hv);
+                        }
+                        *reinterpret_cast<uint4 *>(dst + c * 32 + g * 8) = make_uint4(w[0], w[1], w[2], w[3]);
                     }
-                    *reinterpret_cast<uint4 *>(dst + 2 * c) = make_uint4(w[0], w[1], w[2], w[3]);
                 }
             }
         }
@@ -420,7 +411,7 @@ int attention_fwd(ltx_ctx *ctx, cudaStream_t st, const void *q, int64_t ldq, con
     auto kern = v_f16 ? attn_fwd_kernel<true> : attn_fwd_kernel<false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttnSmem);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "attention smem attribute");
-    const int grid = B * H * ((Tq + BQ - 1) / BQ);
+    const int grid = B * H * ((Tq + 2 * BQ - 1) / (2 * BQ));
     kern<<<grid, kThreads, kAttnSmem, st>>>(tq, tk, tv, p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(ctx, e, "attention launch");
