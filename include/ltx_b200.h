@@ -49,7 +49,8 @@ typedef enum {
     LTX_ERR_OOM = 16,             /* device or host allocation failed                       */
     LTX_ERR_UNSUPPORTED = 17,     /* a configuration this build does not implement          */
     LTX_ERR_MISSING_CONFIG = 18,  /* WeightError::MissingConfig                             */
-    LTX_ERR_NEGATIVE_CONTEXT = 19 /* SamplerError::MissingNegativeContext                   */
+    LTX_ERR_NEGATIVE_CONTEXT = 19, /* SamplerError::MissingNegativeContext                  */
+    LTX_ERR_CHUNK_PLAN = 20       /* ChunkError (crates/ltx-chunk/src/error.rs)             */
 } ltx_status;
 
 /* Element types, named after the safetensors dtype strings. */
@@ -73,6 +74,9 @@ int ltx_ctx_create(int device, void *stream, ltx_ctx **out);
 void ltx_ctx_destroy(ltx_ctx *ctx);
 /* Message of the last failed call on this context ("" if none). */
 const char *ltx_last_error(const ltx_ctx *ctx);
+/* Message of the last failed host-only call (one taking no context, e.g.
+ * ltx_chunk_plan) on the calling thread ("" if none). */
+const char *ltx_host_last_error(void);
 /* The cudaStream_t the context enqueues on. */
 void *ltx_ctx_stream(const ltx_ctx *ctx);
 /* Blocks until the context's stream is idle, then reports any device-side
@@ -291,6 +295,47 @@ int ltx_patchify(ltx_ctx *ctx, const float *latent_dev, int32_t batch, int32_t c
                  int32_t height, int32_t width, float *tokens_dev);
 int ltx_unpatchify(ltx_ctx *ctx, const float *tokens_dev, int32_t batch, int32_t channels, int32_t frames,
                    int32_t height, int32_t width, float *latent_dev);
+
+/* ---- temporal chunks (crates/ltx-chunk) ---------------------------------- */
+
+/* ltx_chunk::plan::Chunk (crates/ltx-chunk/src/plan.rs:24-35): frames
+ * [start, end) of the clip, and the frames shared with the previous chunk. */
+typedef struct {
+    uint32_t start;
+    uint32_t end;
+    uint32_t real_overlap;
+} ltx_chunk;
+
+/* ltx_chunk::plan::plan (plan.rs:56-160): overlapping windows of chunk_len
+ * (8k+1) frames, stride chunk_len - overlap, the last one anchored to the
+ * clip's end.  Writes at most max_chunks entries and the count to *n_chunks
+ * (the count is written even when max_chunks is too small, which returns
+ * LTX_ERR_INVALID_ARG).  Errors (LTX_ERR_CHUNK_PLAN) mirror ChunkError:
+ * ZeroTotal, ChunkLenNotOnGrid, OverlapNotSmallerThanChunkLen,
+ * OverlapNotMultipleOf8, StrideSmallerThanOverlap; ltx_host_last_error()
+ * names the variant.  Host-only. */
+int ltx_chunk_plan(uint32_t total, uint32_t chunk_len, uint32_t overlap, ltx_chunk *chunks_out,
+                   int32_t max_chunks, int32_t *n_chunks);
+/* crossfade_weight (crates/ltx-chunk/src/blend.rs:49-56): f32 of the f64
+ * smoothstep(offset / overlap_len); 1 when overlap_len is 0.  Host-only. */
+float ltx_crossfade_weight(uint32_t offset, uint32_t overlap_len);
+/* One seam of Blender::finish_chunk (blend.rs:176-182, 284-298) on the
+ * device: for frame i < overlap_frames and every value j of the frame,
+ *   w = crossfade_weight(i, overlap_frames),
+ *   dst[i][j] = fma(w, incoming[i][j], (1 - w) * outgoing[i][j])   (f32),
+ * bit-exact with the reference.  Frames are frame_values contiguous f32 (a
+ * pixel frame, or a latent frame of H*W tokens x C channels).  dst may alias
+ * incoming or outgoing. */
+int ltx_seam_blend(ltx_ctx *ctx, const float *outgoing_dev, const float *incoming_dev, uint32_t overlap_frames,
+                   int64_t frame_values, float *dst_dev);
+/* The whole clip as the reference's streaming Blender emits it (blend.rs
+ * finish_chunk / flush, driven as in ltx-pipeline/src/lib.rs:270-353), on
+ * the device: chunk_dev[n] holds chunks[n]'s (end - start) frames; dst_dev
+ * receives chunks[n_chunks-1].end frames.  Frames covered by one chunk are
+ * copied, seam frames are blended as ltx_seam_blend.  chunk_dev is a host
+ * array of device pointers; the plan must be one ltx_chunk_plan produced. */
+int ltx_chunk_assemble(ltx_ctx *ctx, const float *const *chunk_dev, const ltx_chunk *chunks, int32_t n_chunks,
+                       int64_t frame_values, float *dst_dev);
 
 #ifdef __cplusplus
 }

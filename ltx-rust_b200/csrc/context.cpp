@@ -84,6 +84,8 @@ extern "C" void ltx_ctx_destroy(ltx_ctx *ctx) {
 
 extern "C" const char *ltx_last_error(const ltx_ctx *ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
 
+extern "C" const char *ltx_host_last_error(void) { return ltx::host_error().c_str(); }
+
 extern "C" void *ltx_ctx_stream(const ltx_ctx *ctx) { return ctx ? static_cast<void *>(ctx->stream) : nullptr; }
 
 extern "C" int ltx_ctx_synchronize(ltx_ctx *ctx) {

@@ -57,6 +57,21 @@ int ensure_scratch(ltx_ctx *ctx, size_t bytes);
 // buffer (waits for the previous upload from that buffer to finish first).
 int upload(ltx_ctx *ctx, void *dst_dev, const void *src_host, size_t bytes);
 
+// Message of the last failed host-only call (no context) on this thread.
+inline std::string &host_error() {
+    static thread_local std::string msg;
+    return msg;
+}
+inline int host_fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    host_error() = buf;
+    return code;
+}
+
 inline size_t dtype_size(int dt) {
     switch (dt) {
     case LTX_F32: return 4;

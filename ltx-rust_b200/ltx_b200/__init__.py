@@ -20,7 +20,7 @@ STATUS = {
     0: "OK", 1: "INVALID_ARG", 2: "SHAPE", 3: "DTYPE", 4: "MISSING_KEY", 5: "DUPLICATE_KEY",
     6: "LORA_RANK", 7: "NO_LORA_MATCHES", 8: "IO", 9: "FORMAT", 10: "CONFIG", 11: "SIGMA",
     12: "SCHEDULE", 13: "CUDA", 14: "NCCL", 15: "TIMEOUT", 16: "OOM", 17: "UNSUPPORTED",
-    18: "MISSING_CONFIG", 19: "NEGATIVE_CONTEXT",
+    18: "MISSING_CONFIG", 19: "NEGATIVE_CONTEXT", 20: "CHUNK_PLAN",
 }
 
 
@@ -34,6 +34,14 @@ class LtxError(RuntimeError):
 class LoraDelta(ctypes.Structure):
     _fields_ = [("a_dev", ctypes.c_void_p), ("b_dev", ctypes.c_void_p), ("rank", ctypes.c_int32),
                 ("a_dtype", ctypes.c_int32), ("b_dtype", ctypes.c_int32), ("coeff", ctypes.c_float)]
+
+
+class Chunk(ctypes.Structure):
+    """ltx_chunk (plan::Chunk): frames [start, end) and the overlap with the previous chunk."""
+    _fields_ = [("start", ctypes.c_uint32), ("end", ctypes.c_uint32), ("real_overlap", ctypes.c_uint32)]
+
+    def as_tuple(self):
+        return (self.start, self.end, self.real_overlap)
 
 
 _lib = None
@@ -84,6 +92,12 @@ def lib() -> ctypes.CDLL:
         "ltx_reference_positions": (I, [ctypes.c_uint32] * 8 + [F, ctypes.c_uint32, ctypes.c_uint32, P]),
         "ltx_patchify": (I, [V, P] + [ctypes.c_int32] * 5 + [P]),
         "ltx_unpatchify": (I, [V, P] + [ctypes.c_int32] * 5 + [P]),
+        "ltx_host_last_error": (ctypes.c_char_p, []),
+        "ltx_chunk_plan": (I, [ctypes.c_uint32] * 3 + [ctypes.POINTER(Chunk), ctypes.c_int32,
+                                                        ctypes.POINTER(ctypes.c_int32)]),
+        "ltx_crossfade_weight": (F, [ctypes.c_uint32, ctypes.c_uint32]),
+        "ltx_seam_blend": (I, [V, P, P, ctypes.c_uint32, I64, P]),
+        "ltx_chunk_assemble": (I, [V, ctypes.POINTER(P), ctypes.POINTER(Chunk), ctypes.c_int32, I64, P]),
         "ltx_dequant_merge_noalloc": (I, [V, P, ctypes.c_int32, ctypes.c_int32, F, I64, I64,
                                           ctypes.POINTER(LoraDelta), ctypes.c_int32, P, ctypes.c_int32,
                                           ctypes.c_char_p, ctypes.c_size_t]),
@@ -340,3 +354,38 @@ def dequant_merge_noalloc(stream: int, w_ptr: int, w_dtype: int, has_scale: bool
 
 def lora_coeff(strength: float, alpha: float, rank: int) -> float:
     return lib().ltx_lora_coeff(strength, alpha, rank)
+
+
+# ── temporal chunks (crates/ltx-chunk) ─────────────────────────────────────────
+
+def chunk_plan(total: int, chunk_len: int, overlap: int):
+    """plan::plan -> [(start, end, real_overlap), ...] (host, no GPU needed).
+    Raises LtxError(kind "CHUNK_PLAN") naming the ChunkError variant."""
+    n = ctypes.c_int32(0)
+    cap = max(1, total // max(1, chunk_len - overlap) + 2)
+    arr = (Chunk * cap)()
+    rc = lib().ltx_chunk_plan(total, chunk_len, overlap, arr, cap, ctypes.byref(n))
+    if rc:
+        raise LtxError(rc, lib().ltx_host_last_error().decode())
+    return [arr[i].as_tuple() for i in range(n.value)]
+
+
+def crossfade_weight(offset: int, overlap_len: int) -> float:
+    """blend::crossfade_weight (host)."""
+    return lib().ltx_crossfade_weight(offset, overlap_len)
+
+
+def seam_blend(ctx: "Context", outgoing, incoming, dst):
+    """Blends overlap frames on the device: tensors [frames, ...] f32 (dst may be incoming)."""
+    frames = outgoing.shape[0]
+    fv = outgoing.numel() // max(frames, 1)
+    ctx.check(lib().ltx_seam_blend(ctx.h, _ptr(outgoing), _ptr(incoming), frames, fv, _ptr(dst)), "ltx_seam_blend")
+
+
+def chunk_assemble(ctx: "Context", chunk_tensors, chunks, dst):
+    """The clip the reference's Blender emits, from per-chunk device tensors [len_n, ...] f32."""
+    n = len(chunks)
+    ptrs = (ctypes.c_void_p * n)(*[_ptr(t) for t in chunk_tensors])
+    arr = (Chunk * n)(*[Chunk(*c) for c in chunks])
+    fv = dst.numel() // max(dst.shape[0], 1)
+    ctx.check(lib().ltx_chunk_assemble(ctx.h, ptrs, arr, n, fv, _ptr(dst)), "ltx_chunk_assemble")

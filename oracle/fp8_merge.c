@@ -184,3 +184,14 @@ float oracle_fmaf(float a, float b, float c) { return fmaf(a, b, c); }
 
 /* f32 exp as Rust's f32::exp (libm expf, correctly rounded in glibc). */
 float oracle_expf(float x) { return expf(x); }
+
+/* Blender::blend_with_pending (crates/ltx-chunk/src/blend.rs:284-298) over n
+ * values: w_old = 1 - w_new, out = w_new.mul_add(new, w_old * old), f32 with
+ * the two roundings of the reference (no contraction: -ffp-contract=off). */
+void oracle_crossfade_blend(const float *old_v, const float *new_v, float w_new, long long n, float *out) {
+    const float w_old = 1.0f - w_new;
+    for (long long i = 0; i < n; ++i) {
+        const float a = w_old * old_v[i];
+        out[i] = fmaf(w_new, new_v[i], a);
+    }
+}

@@ -61,6 +61,9 @@ def lib() -> ctypes.CDLL:
             getattr(L, name).restype = ctypes.c_float
             getattr(L, name).argtypes = [ctypes.c_float] * 3
         L.oracle_expf.restype = ctypes.c_float
+        L.oracle_crossfade_blend.restype = None
+        L.oracle_crossfade_blend.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_longlong,
+                                             ctypes.c_void_p]
         L.oracle_expf.argtypes = [ctypes.c_float]
         L.oracle_f32_to_bf16.restype = ctypes.c_uint16
         L.oracle_f32_to_bf16.argtypes = [ctypes.c_float]
