@@ -16,6 +16,9 @@ Workloads:
                  metric tokens/s = 12288 / step time; at N GPUs each rank
                  denoises its own temporal chunk (config 5's chunk-parallel
                  axis: independent chunks, no collective), value = N*12288/t.
+                 With --parallel tp the N ranks instead split ONE sequence's
+                 model (heads and FFN units per rank, NCCL allreduce after
+                 each row-split projection): strong scaling, value = 12288/t.
   dequant_merge  config 1: FP8 e4m3 [4096,4096] (+scale) + rank-64 bf16 LoRA
                  -> bf16 [4096,4096], metric GB/s of algorithmic bytes; also
                  reported as the `dequant_merge` object of the step line.
@@ -265,11 +268,14 @@ def run_denoise_step(args, rank, ws, device):
     torch.cuda.set_device(device)
     ctx = ltx_b200.Context(device)
     t0 = time.time()
-    model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(CFG4), seed=7 + rank, lora_rank=64,
+    tp = args.parallel == "tp" and ws > 1
+    if tp:
+        ltx_b200.init_tensor_parallel(ctx)   # this rank's shard of one model
+    model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(CFG4), seed=7 if tp else 7 + rank, lora_rank=64,
                                                   lora_strength=1.0)
     ctx.synchronize()
     load_s = time.time() - t0
-    inp = make_step_inputs(LAT_F, LAT_H, LAT_W, S_CTX, D, seed=100 + rank)
+    inp = make_step_inputs(LAT_F, LAT_H, LAT_W, S_CTX, D, seed=100 if tp else 100 + rank)
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
     lat0 = inp["latent"]
     lat, clean, mask = dev(lat0), dev(inp["clean"]), dev(inp["mask"])
@@ -335,17 +341,18 @@ def run_denoise_step(args, rank, ws, device):
     gemm_tf = 2.0 * M * N * K / (gemm_ms * 1e-3) / 1e12
     res = {
         "metric": "DiT denoise-step tokens/s (config 4: 48 blocks, T=12288, CFG batch 2 + Euler)",
-        "value": ws * T_TOTAL / (ms * 1e-3),
+        "value": (1 if tp else ws) * T_TOTAL / (ms * 1e-3),
         "unit": "tokens/s",
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if tp else "weak",
         "dtype": "bf16 (tensor-core GEMM/attention inputs; f32 accumulate, residual and sampler)",
         "config": {"workload": "denoise_step_config4", "layers": 48, "hidden": D, "heads": 32, "head_dim": 128,
                    "ffn": FF, "tokens": T_TOTAL, "latent": [1, 128, LAT_F, LAT_H, LAT_W], "ic_reference": True,
                    "context_tokens": S_CTX, "cfg_batch": 2, "guidance": 3.0, "rescale": 0.7,
                    "weights": "random-init fp8 e4m3 per-tensor scale + rank-64 LoRA merged on device",
-                   "parallelism": f"chunk-parallel x{ws} (one independent chunk per GPU)",
+                   "parallelism": (f"tp{ws} (one sequence; heads and FFN split, NCCL allreduce)" if tp else
+                                   f"chunk-parallel x{ws} (one independent chunk per GPU)"),
                    "l2": "inputs and weights exceed L2 (25.8 GB bf16 weights streamed per step)",
                    "step_tflop": total / 1e12, "model_load_s": load_s},
         "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMM, FFN-in + GELU (M=24576, N=16384, K=4096)",
@@ -355,9 +362,9 @@ def run_denoise_step(args, rank, ws, device):
                      "step_tflops_achieved": total / (ms * 1e-3) / 1e12,
                      "step_frac_of_sustained": total / (ms * 1e-3) / 1e12 / peaks.get("bf16_tflops_sustained",
                                                                                       peaks["bf16_tflops"])},
-        "e2e": {"value": ws * T_TOTAL / (e2e_ms * 1e-3), "unit": "tokens/s",
+        "e2e": {"value": (1 if tp else ws) * T_TOTAL / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": lat_h.numel() * 4, "d2h_bytes_per_step": out_h.numel() * 4},
-        "gpu_launches": args.steps * launches_per_step(48),
+        "gpu_launches": args.steps * launches_per_step(48, tp),
         "clocks": clk.summary(),
         "finite_output": ok,
     }
@@ -366,12 +373,16 @@ def run_denoise_step(args, rank, ws, device):
     return res
 
 
-def launches_per_step(L):
-    """Kernels one ltx_denoise_step enqueues (counted from model.cpp's forward):
-    head 9 (convert, patchify GEMM, sinusoid, 3 small linears, tables, RoPE, ctx
-    convert), per block 16 (3 norms, 6 GEMMs, 3 QK-norm, 2 attention + 2 spare
-    for the cross K/V norm and q norm counted above), output 2, sampler 2."""
-    return 9 + L * 15 + 2 + 2
+def launches_per_step(L, tp=False):
+    """Kernels one ltx_denoise_step enqueues, counted from model.cpp's forward.
+    Head 8: latent convert, patchify GEMM, sinusoid, 3 small linears, adaLN
+    tables, context convert (+1 RoPE table when split over ranks).  Per block
+    15: 3 norm+modulate, QKV / out / cross-q / cross-kv / out / FFN-in /
+    FFN-out GEMMs, fused Q/K norm+RoPE, cross q and k norms, 2 attentions.
+    Split over ranks, per block 22: the Q/K norms become 3 sum-of-squares and
+    4 apply launches, and each of the 3 row-split projections adds a residual
+    add (NCCL's own kernels are not counted).  Output head 2, sampler 2."""
+    return (9 + L * 22 if tp else 8 + L * 15) + 2 + 2
 
 
 def cpu_baseline_step(blocks=1, threads=None):
@@ -463,6 +474,8 @@ def main():
     ap.add_argument("--workload", default="denoise_step", choices=["denoise_step", "dequant_merge"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=5.0)
+    ap.add_argument("--parallel", default="chunk", choices=["chunk", "tp"],
+                    help="N>1: independent chunk per GPU (default) or one sequence split over the GPUs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_env()

@@ -50,7 +50,8 @@ typedef enum {
     LTX_ERR_UNSUPPORTED = 17,     /* a configuration this build does not implement          */
     LTX_ERR_MISSING_CONFIG = 18,  /* WeightError::MissingConfig                             */
     LTX_ERR_NEGATIVE_CONTEXT = 19, /* SamplerError::MissingNegativeContext                  */
-    LTX_ERR_CHUNK_PLAN = 20       /* ChunkError (crates/ltx-chunk/src/error.rs)             */
+    LTX_ERR_CHUNK_PLAN = 20,      /* ChunkError (crates/ltx-chunk/src/error.rs)             */
+    LTX_ERR_TARGET_TOKENS = 21    /* SamplerError::TargetTokensTooLarge (loop_.rs:162-185)  */
 } ltx_status;
 
 /* Element types, named after the safetensors dtype strings. */
@@ -82,6 +83,45 @@ void *ltx_ctx_stream(const ltx_ctx *ctx);
 /* Blocks until the context's stream is idle, then reports any device-side
  * timeout flag a kernel raised (LTX_ERR_TIMEOUT) and clears it. */
 int ltx_ctx_synchronize(ltx_ctx *ctx);
+
+/* ── tensor parallelism ───────────────────────────────────────────────────── */
+
+/* One model split over several GPUs (one process or thread per GPU): the
+ * heads of every attention and the FFN's hidden units are divided among the
+ * ranks, and each block's three output projections end in a sum-allreduce.
+ * No reference counterpart (the reference runs one device).  Flow:
+ *   rank 0: ltx_comm_unique_id(id); send id to the other ranks (any channel)
+ *   every rank: ltx_ctx_init_comm(ctx, id, nranks, rank)     (collective)
+ *   every rank: ltx_model_load / ltx_model_init_random on that context: the
+ *               model keeps only this rank's shard
+ *   every rank: the same ltx_model_forward / ltx_denoise_step / ltx_denoise_loop
+ *               calls with the same inputs; outputs are replicated.
+ * The communicator is NCCL, loaded at run time (the copy the process already
+ * has, else libnccl.so.2); LTX_ERR_NCCL when it is unavailable or fails. */
+#define LTX_COMM_ID_BYTES 128
+/* Host-only: a fresh communicator id into id_out (len >= LTX_COMM_ID_BYTES). */
+int ltx_comm_unique_id(uint8_t *id_out, size_t len);
+/* Collective over the nranks contexts: binds this context to rank `rank`. */
+int ltx_ctx_init_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t nranks, int32_t rank);
+/* LTX_ERR_NCCL if the communicator has recorded an asynchronous error. */
+int ltx_ctx_comm_check(ltx_ctx *ctx);
+/* Aborts the communicator (after a peer failed); the context falls back to
+ * one rank and models built on it can no longer run. */
+void ltx_ctx_abort_comm(ltx_ctx *ctx);
+
+/* ── device-side signalling ───────────────────────────────────────────────── */
+
+/* Enqueues on the context's stream a wait until *flag_dev == expect (a
+ * 32-bit flag in device memory, possibly a peer GPU's): the stream's later
+ * work runs only after another stream or GPU set the flag (ltx_set_flag).
+ * The wait is bounded: after timeout_ms (0 or more than 2000 means 2000) it
+ * records a code in the context's timeout flag and returns, so a peer that
+ * never signals is reported by ltx_ctx_synchronize as LTX_ERR_TIMEOUT and the
+ * context stays usable.  No reference counterpart (the reference is one
+ * device, ordered by the host). */
+int ltx_wait_flag(ltx_ctx *ctx, const int32_t *flag_dev, int32_t expect, uint32_t timeout_ms);
+/* Enqueues a release store of `value` to *flag_dev on the context's stream. */
+int ltx_set_flag(ltx_ctx *ctx, int32_t *flag_dev, int32_t value);
 
 /* ── ltx-weights: dequant + LoRA merge ────────────────────────────────────── */
 
@@ -271,6 +311,31 @@ int ltx_denoise_step(ltx_model *model, ltx_ctx *ctx, float *latent_dev, const fl
                      const float *ctx_cond_dev, const float *ctx_uncond_dev, int32_t tokens,
                      int32_t context_tokens, float sigma, float sigma_next, float cfg_scale,
                      float rescale_scale);
+
+/* euler_denoising_loop (crates/ltx-sampler/src/loop_.rs:93-149) followed by
+ * clear_conditioning (loop_.rs:162-185), all on the device: for each pair
+ * (sigmas_host[i], sigmas_host[i+1]) one ltx_denoise_step on latent_dev (in
+ * place, [tokens, C]), with no host round trip between steps.  Then the first
+ * target_tokens tokens of the final latent are copied to out_dev
+ * ([target_tokens, C]; may be NULL to keep only latent_dev).  Errors, checked
+ * before anything is enqueued: LTX_ERR_SCHEDULE (fewer than 2 sigmas),
+ * LTX_ERR_SIGMA (a step sigma not finite or <= 0, a next sigma not finite or
+ * < 0), LTX_ERR_TARGET_TOKENS, LTX_ERR_NEGATIVE_CONTEXT.  The reference
+ * checks each sigma pair when it reaches it; since it then returns no state,
+ * checking them all first is observably the same. */
+int ltx_denoise_loop(ltx_model *model, ltx_ctx *ctx, float *latent_dev, const float *clean_dev,
+                     const float *mask_host, const float *mask_dev, const float *positions_dev,
+                     const float *ctx_cond_dev, const float *ctx_uncond_dev, int32_t tokens,
+                     int32_t context_tokens, const float *sigmas_host, int32_t n_sigmas, float cfg_scale,
+                     float rescale_scale, int32_t target_tokens, float *out_dev);
+/* GaussianNoiser::apply_with_noise (crates/ltx-sampler/src/noiser.rs:91-106)
+ * on the device, in place on latent_dev [tokens, C], bit-exact:
+ *   noised = latent * (1 - s) + noise * s
+ *   latent = clean * (1 - mask) + noised * mask        (mask per token)
+ * The caller supplies the N(0,1) noise (the reference's StdRng stream is
+ * host-side and seed-specific; parity fixtures use apply_with_noise too). */
+int ltx_apply_noise(ltx_ctx *ctx, float *latent_dev, const float *noise_dev, const float *clean_dev,
+                    const float *mask_dev, int32_t tokens, int32_t channels, float noise_scale);
 
 /* LTX2Scheduler::execute (crates/ltx-sampler/src/scheduler.rs:67-125): writes
  * steps + 1 sigmas with the reference's f32 operations (bit-exact).  Defaults

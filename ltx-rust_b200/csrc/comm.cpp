@@ -1,0 +1,131 @@
+// Tensor-parallel communicator of a context: NCCL, loaded at run time.
+//
+// The library does not link NCCL: a process that never splits a model across
+// GPUs needs no NCCL at all, and a process that already has one (PyTorch
+// loads its own libnccl.so.2) must use that same copy rather than a second
+// one.  So the first call that needs NCCL dlopens "libnccl.so.2", preferring
+// the copy already mapped into the process (RTLD_NOLOAD), and resolves the
+// handful of entry points below.  nccl.h supplies only the types.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "internal.hpp"
+
+namespace ltx {
+
+namespace {
+
+struct NcclApi {
+    bool ok = false;
+    std::string why;
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t *) = nullptr;
+    const char *(*get_error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi &nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+        if (!h) {
+            api.why = std::string("cannot load libnccl.so.2: ") + (dlerror() ? dlerror() : "not found");
+            return;
+        }
+        auto sym = [&](const char *name) { return dlsym(h, name); };
+        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
+        api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
+        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+        api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
+        api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
+        api.comm_get_async_error = reinterpret_cast<decltype(api.comm_get_async_error)>(sym("ncclCommGetAsyncError"));
+        api.get_error_string = reinterpret_cast<decltype(api.get_error_string)>(sym("ncclGetErrorString"));
+        api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.comm_abort && api.all_reduce &&
+                 api.comm_get_async_error && api.get_error_string;
+        if (!api.ok) api.why = "libnccl.so.2 lacks an expected entry point";
+    });
+    return api;
+}
+
+const char *nccl_str(ncclResult_t r) { return nccl().get_error_string ? nccl().get_error_string(r) : "?"; }
+
+}  // namespace
+
+int allreduce_sum(ltx_ctx *ctx, float *buf, size_t count) {
+    if (ctx->tp_size <= 1 || count == 0) return LTX_OK;
+    const NcclApi &api = nccl();
+    ncclResult_t r = api.all_reduce(buf, buf, count, ncclFloat32, ncclSum, static_cast<ncclComm_t>(ctx->comm),
+                                    ctx->stream);
+    if (r != ncclSuccess) return fail(ctx, LTX_ERR_NCCL, "allreduce of %zu floats: %s", count, nccl_str(r));
+    return LTX_OK;
+}
+
+void comm_release(ltx_ctx *ctx, bool abort) {
+    if (!ctx->comm) return;
+    const NcclApi &api = nccl();
+    if (abort)
+        api.comm_abort(static_cast<ncclComm_t>(ctx->comm));
+    else
+        api.comm_destroy(static_cast<ncclComm_t>(ctx->comm));
+    ctx->comm = nullptr;
+    ctx->tp_size = 1;
+    ctx->tp_rank = 0;
+}
+
+}  // namespace ltx
+
+extern "C" int ltx_comm_unique_id(uint8_t *id_out, size_t len) {
+    if (!id_out || len < LTX_COMM_ID_BYTES) return ltx::host_fail(LTX_ERR_INVALID_ARG, "id buffer shorter than 128 bytes");
+    const auto &api = ltx::nccl();
+    if (!api.ok) return ltx::host_fail(LTX_ERR_NCCL, "%s", api.why.c_str());
+    ncclUniqueId id;
+    ncclResult_t r = api.get_unique_id(&id);
+    if (r != ncclSuccess) return ltx::host_fail(LTX_ERR_NCCL, "ncclGetUniqueId: %s", ltx::nccl_str(r));
+    static_assert(sizeof(id.internal) == LTX_COMM_ID_BYTES, "NCCL unique id size");
+    memcpy(id_out, id.internal, LTX_COMM_ID_BYTES);
+    return LTX_OK;
+}
+
+extern "C" int ltx_ctx_init_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t nranks, int32_t rank) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    if (!id || len < LTX_COMM_ID_BYTES || nranks < 1 || rank < 0 || rank >= nranks)
+        return ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_ctx_init_comm: bad id, rank %d or size %d", rank, nranks);
+    if (ctx->comm) return ltx::fail(ctx, LTX_ERR_INVALID_ARG, "context already has a communicator");
+    if (nranks == 1) return LTX_OK;
+    const auto &api = ltx::nccl();
+    if (!api.ok) return ltx::fail(ctx, LTX_ERR_NCCL, "%s", api.why.c_str());
+    cudaSetDevice(ctx->device);
+    ncclUniqueId uid;
+    memcpy(uid.internal, id, LTX_COMM_ID_BYTES);
+    ncclComm_t comm = nullptr;
+    ncclResult_t r = api.comm_init_rank(&comm, nranks, uid, rank);
+    if (r != ncclSuccess) return ltx::fail(ctx, LTX_ERR_NCCL, "ncclCommInitRank: %s", ltx::nccl_str(r));
+    ctx->comm = comm;
+    ctx->tp_size = nranks;
+    ctx->tp_rank = rank;
+    return LTX_OK;
+}
+
+extern "C" int ltx_ctx_comm_check(ltx_ctx *ctx) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    if (!ctx->comm) return LTX_OK;
+    ncclResult_t async = ncclSuccess;
+    ncclResult_t r = ltx::nccl().comm_get_async_error(static_cast<ncclComm_t>(ctx->comm), &async);
+    if (r != ncclSuccess || async != ncclSuccess)
+        return ltx::fail(ctx, LTX_ERR_NCCL, "communicator error: %s", ltx::nccl_str(r != ncclSuccess ? r : async));
+    return LTX_OK;
+}
+
+extern "C" void ltx_ctx_abort_comm(ltx_ctx *ctx) {
+    if (ctx) ltx::comm_release(ctx, true);
+}

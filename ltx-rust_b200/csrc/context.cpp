@@ -73,6 +73,7 @@ extern "C" void ltx_ctx_destroy(ltx_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
+    ltx::comm_release(ctx, false);
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->work) cudaFree(ctx->work);
     if (ctx->pinned) cudaFreeHost(ctx->pinned);

@@ -709,3 +709,31 @@ extern "C" int ltx_unpatchify(ltx_ctx *ctx, const float *tokens_dev, int32_t bat
                                     (int64_t)frames * height * width, false);
     return e == cudaSuccess ? LTX_OK : ltx::cuda_fail(ctx, e, "ltx_unpatchify");
 }
+
+// GaussianNoiser::apply_with_noise (crates/ltx-sampler/src/noiser.rs:91-106):
+// lerp(latent, noise, s) then lerp(clean, noised, mask), each Burn op one f32
+// rounding (mul_scalar, add, ones - mask, mul, add), bit-exact.
+namespace {
+__global__ void apply_noise_kernel(float *latent, const float *noise, const float *clean, const float *mask,
+                                   int64_t n, int C, float s, float one_minus_s) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float m = mask[i / C];
+        const float noised = __fadd_rn(__fmul_rn(latent[i], one_minus_s), __fmul_rn(noise[i], s));
+        latent[i] = __fadd_rn(__fmul_rn(clean[i], __fsub_rn(1.0f, m)), __fmul_rn(noised, m));
+    }
+}
+}  // namespace
+
+extern "C" int ltx_apply_noise(ltx_ctx *ctx, float *latent_dev, const float *noise_dev, const float *clean_dev,
+                               const float *mask_dev, int32_t tokens, int32_t channels, float noise_scale) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    if (!latent_dev || !noise_dev || !clean_dev || !mask_dev || tokens < 0 || channels <= 0)
+        return ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_apply_noise: bad arguments");
+    const int64_t n = (int64_t)tokens * channels;
+    if (n == 0) return LTX_OK;
+    apply_noise_kernel<<<ltx::grid_for(n, ctx->sm_count), 256, 0, ctx->stream>>>(latent_dev, noise_dev, clean_dev, mask_dev,
+                                                                            n, channels, noise_scale,
+                                                                            1.0f - noise_scale);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? LTX_OK : ltx::cuda_fail(ctx, e, "ltx_apply_noise");
+}

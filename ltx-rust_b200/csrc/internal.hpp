@@ -31,6 +31,9 @@ struct ltx_ctx {
     void *pinned = nullptr;
     size_t pinned_bytes = 0;
     cudaEvent_t upload_done = nullptr;
+    // Tensor-parallel communicator (an ncclComm_t), or null: one GPU.
+    void *comm = nullptr;
+    int tp_size = 1, tp_rank = 0;
 };
 
 namespace ltx {
@@ -56,6 +59,12 @@ int ensure_scratch(ltx_ctx *ctx, size_t bytes);
 // Copies host bytes to the device through the context's pinned staging
 // buffer (waits for the previous upload from that buffer to finish first).
 int upload(ltx_ctx *ctx, void *dst_dev, const void *src_host, size_t bytes);
+
+// Sum-allreduce of `count` floats in place over the context's communicator,
+// on its stream (a no-op without one).
+int allreduce_sum(ltx_ctx *ctx, float *buf, size_t count);
+// Destroys (or aborts) the context's communicator.
+void comm_release(ltx_ctx *ctx, bool abort);
 
 // Message of the last failed host-only call (no context) on this thread.
 inline std::string &host_error() {

@@ -52,4 +52,15 @@ cudaError_t cfg_euler(cudaStream_t st, int sms, float *x, const float *vc, const
                       const float *mask, const float *clean, int T, int C, float g, float rescale, bool use_cfg,
                       double *partial, float sigma, float sigma_next);
 
+// Tensor-parallel pieces (tp_kernels.cu): per-row sums of squares of nseg
+// segments, the Q/K RMSNorm(gamma)+RoPE applied with all-rank sums, and the
+// residual add of summed partial projections.
+cudaError_t tp_sumsq_rows(cudaStream_t st, const __nv_bfloat16 *x, int64_t ld, int rows, int cols, int nseg,
+                          int64_t seg_stride, float *out);
+cudaError_t tp_norm_apply_rope(cudaStream_t st, __nv_bfloat16 *x, int64_t ld, int rows, int cols, int D, int d,
+                               int head0, float eps, const float *gamma, const float *ss, const float *cos_t,
+                               const float *sin_t, bool interleaved);
+cudaError_t tp_resid_add(cudaStream_t st, int sms, float *x, const float *p, int rows, int D, const float *bias,
+                         const float *gate, const int *gidx, int64_t ld_gate);
+
 }  // namespace ltx

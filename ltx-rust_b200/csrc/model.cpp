@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstring>
 #include <map>
+#include <set>
 #include <new>
 #include <string>
 #include <vector>
@@ -100,6 +101,9 @@ struct BlockW {
 struct ltx_model {
     int device = 0;
     ltx::DitConfig cfg;
+    // tensor-parallel shard: this model holds rank tr of tp (heads and FFN
+    // hidden units split; everything else replicated)
+    int tp = 1, tr = 0;
     void *arena = nullptr;
     size_t arena_bytes = 0;
     __nv_bfloat16 *patch_w = nullptr, *out_w = nullptr;
@@ -131,7 +135,9 @@ struct Arena {
 // Assigns every weight a slice of one allocation (sizing pass when a.base == null).
 static void layout(ltx_model *m, Arena &a) {
     const DitConfig &c = m->cfg;
-    const int64_t D = c.inner(), Dc = c.cross_dim, F = 4 * D, H = c.heads, K = c.coeff();
+    const int64_t D = c.inner(), Dc = c.cross_dim, K = c.coeff();
+    // this rank's share of the split dimensions
+    const int64_t Dl = D / m->tp, Fl = 4 * D / m->tp, Hl = c.heads / m->tp;
     m->patch_w = a.take<__nv_bfloat16>(D * c.in_ch);
     m->patch_b = a.take<float>(D);
     m->t1_w = a.take<float>(D * 256);
@@ -149,30 +155,30 @@ static void layout(ltx_model *m, Arena &a) {
     m->sst_list = a.take<float *>(c.layers);
     m->blocks.resize(c.layers);
     for (auto &b : m->blocks) {
-        b.qkv = a.take<__nv_bfloat16>(3 * D * D);
-        b.qkv_b = a.take<float>(3 * D);
-        b.qn = a.take<float>(D);
-        b.kn = a.take<float>(D);
-        b.o = a.take<__nv_bfloat16>(D * D);
+        b.qkv = a.take<__nv_bfloat16>(3 * Dl * D);
+        b.qkv_b = a.take<float>(3 * Dl);
+        b.qn = a.take<float>(Dl);
+        b.kn = a.take<float>(Dl);
+        b.o = a.take<__nv_bfloat16>(D * Dl);
         b.o_b = a.take<float>(D);
-        b.q2 = a.take<__nv_bfloat16>(D * D);
-        b.q2_b = a.take<float>(D);
-        b.kv2 = a.take<__nv_bfloat16>(2 * D * Dc);
-        b.kv2_b = a.take<float>(2 * D);
-        b.qn2 = a.take<float>(D);
-        b.kn2 = a.take<float>(D);
-        b.o2 = a.take<__nv_bfloat16>(D * D);
+        b.q2 = a.take<__nv_bfloat16>(Dl * D);
+        b.q2_b = a.take<float>(Dl);
+        b.kv2 = a.take<__nv_bfloat16>(2 * Dl * Dc);
+        b.kv2_b = a.take<float>(2 * Dl);
+        b.qn2 = a.take<float>(Dl);
+        b.kn2 = a.take<float>(Dl);
+        b.o2 = a.take<__nv_bfloat16>(D * Dl);
         b.o2_b = a.take<float>(D);
-        b.ff1 = a.take<__nv_bfloat16>(F * D);
-        b.ff1_b = c.ff_bias ? a.take<float>(F) : nullptr;
-        b.ff2 = a.take<__nv_bfloat16>(D * F);
+        b.ff1 = a.take<__nv_bfloat16>(Fl * D);
+        b.ff1_b = c.ff_bias ? a.take<float>(Fl) : nullptr;
+        b.ff2 = a.take<__nv_bfloat16>(D * Fl);
         b.ff2_b = c.ff_bias ? a.take<float>(D) : nullptr;
         b.sst = a.take<float>(K * D);
         b.pst = c.cross_adaln ? a.take<float>(2 * D) : nullptr;
-        b.g1 = c.gated ? a.take<__nv_bfloat16>(H * D) : nullptr;
-        b.g1_b = c.gated ? a.take<float>(H) : nullptr;
-        b.g2 = c.gated ? a.take<__nv_bfloat16>(H * D) : nullptr;
-        b.g2_b = c.gated ? a.take<float>(H) : nullptr;
+        b.g1 = c.gated ? a.take<__nv_bfloat16>(Hl * D) : nullptr;
+        b.g1_b = c.gated ? a.take<float>(Hl) : nullptr;
+        b.g2 = c.gated ? a.take<__nv_bfloat16>(Hl * D) : nullptr;
+        b.g2_b = c.gated ? a.take<float>(Hl) : nullptr;
     }
 }
 
@@ -181,6 +187,15 @@ static int alloc_model(ltx_ctx *ctx, const DitConfig &cfg, ltx_model *&m) {
     if (!m) return LTX_ERR_OOM;
     m->device = ctx->device;
     m->cfg = cfg;
+    m->tp = ctx->tp_size;
+    m->tr = ctx->tp_rank;
+    if (m->tp > 1 && (cfg.heads % m->tp || (cfg.inner() / m->tp) % 8)) {
+        const int tp = m->tp;
+        delete m;
+        m = nullptr;
+        return fail(ctx, LTX_ERR_UNSUPPORTED, "%d heads of width %d do not split over %d ranks", cfg.heads,
+                    cfg.head_dim, tp);
+    }
     Arena sizing;
     layout(m, sizing);
     m->arena_bytes = sizing.off + 256;
@@ -215,11 +230,44 @@ static int alloc_model(ltx_ctx *ctx, const DitConfig &cfg, ltx_model *&m) {
     return LTX_OK;
 }
 
+// ── tensor-parallel slices ───────────────────────────────────────────────────
+
+// Which part of a full row-major [R, C] tensor a rank keeps.  ROWS: the rows
+// form `nseg` equal blocks (the fused Q|K|V or K|V projections) and the rank
+// keeps its 1/n of every block; COLS: it keeps its 1/n of the columns.
+struct Split {
+    enum Kind { ALL, ROWS, COLS } kind = ALL;
+    int nseg = 1;
+};
+static const Split kAll{Split::ALL, 1}, kRows{Split::ROWS, 1}, kCols{Split::COLS, 1};
+
+static cudaError_t slice_to(cudaStream_t st, void *dst, const void *full, int64_t R, int64_t C, size_t es, Split sp,
+                            int n, int r) {
+    const char *src = static_cast<const char *>(full);
+    char *d = static_cast<char *>(dst);
+    if (sp.kind == Split::ALL || n == 1)
+        return cudaMemcpyAsync(dst, full, (size_t)(R * C) * es, cudaMemcpyDeviceToDevice, st);
+    if (sp.kind == Split::ROWS) {
+        const int64_t blk = R / sp.nseg, part = blk / n;
+        for (int s = 0; s < sp.nseg; ++s) {
+            cudaError_t e = cudaMemcpyAsync(d + (size_t)(s * part * C) * es, src + (size_t)((s * blk + r * part) * C) * es,
+                                            (size_t)(part * C) * es, cudaMemcpyDeviceToDevice, st);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    }
+    const int64_t part = C / n;
+    return cudaMemcpy2DAsync(d, (size_t)part * es, src + (size_t)(r * part) * es, (size_t)C * es, (size_t)part * es,
+                             (size_t)R, cudaMemcpyDeviceToDevice, st);
+}
+
 // ── loading from a weight store (load.rs:47-396) ─────────────────────────────
 
 struct Loader {
     ltx_store *st;
     ltx_ctx *ctx;
+    int n = 1, r = 0;
+    void *tmp = nullptr;      // full-tensor staging for sharded reads (n > 1)
     int shape_check(const std::string &key, std::vector<int64_t> want) {
         auto it = st->entries.find(key);
         if (it == st->entries.end()) return fail(ctx, LTX_ERR_MISSING_KEY, "missing key: \"%s\"", key.c_str());
@@ -232,19 +280,27 @@ struct Loader {
         }
         return LTX_OK;
     }
-    int req(const std::string &key, std::vector<int64_t> shape, void *dst, int dt) {
+    // reads the full tensor `key` (checked against `shape`) and keeps this
+    // rank's `sp` part of it in dst
+    int req(const std::string &key, std::vector<int64_t> shape, void *dst, int dt, Split sp = kAll) {
         int rc = shape_check(key, shape);
         if (rc) return rc;
-        return store_read_device(st, key, dt, dst, numel(shape));
+        if (n == 1 || sp.kind == Split::ALL) return store_read_device(st, key, dt, dst, numel(shape));
+        rc = store_read_device(st, key, dt, tmp, numel(shape));
+        if (rc) return rc;
+        const int64_t R = shape[0], C = shape.size() > 1 ? shape[1] : 1;
+        LTX_CUDA_TRY(ctx, slice_to(ctx->stream, dst, tmp, R, C, dtype_size(dt), sp, n, r));
+        return LTX_OK;
     }
     // optional tensor (bias): absent -> left zero, returns whether present
-    int opt(const std::string &key, std::vector<int64_t> shape, void *dst, int dt, bool *present = nullptr) {
+    int opt(const std::string &key, std::vector<int64_t> shape, void *dst, int dt, Split sp = kAll,
+            bool *present = nullptr) {
         if (!st->entries.count(key)) {
             if (present) *present = false;
             return LTX_OK;
         }
         if (present) *present = true;
-        return req(key, shape, dst, dt);
+        return req(key, shape, dst, dt, sp);
     }
 };
 
@@ -254,10 +310,10 @@ struct Loader {
         if (_rc) return _rc;     \
     } while (0)
 
-static int load_weights(ltx_model *m, ltx_store *st, ltx_ctx *ctx) {
+static int load_weights_into(ltx_model *m, Loader &L) {
     const DitConfig &c = m->cfg;
     const int64_t D = c.inner(), Dc = c.cross_dim, F = 4 * D, H = c.heads, K = c.coeff();
-    Loader L{st, ctx};
+    const int64_t Dl = D / m->tp;
     TRY(L.req("patchify_proj.weight", {D, c.in_ch}, m->patch_w, LTX_BF16));
     TRY(L.opt("patchify_proj.bias", {D}, m->patch_b, LTX_F32));
     TRY(L.req("adaln_single.emb.timestep_embedder.linear_1.weight", {D, 256}, m->t1_w, LTX_F32));
@@ -273,42 +329,58 @@ static int load_weights(ltx_model *m, ltx_store *st, ltx_ctx *ctx) {
         BlockW &b = m->blocks[i];
         const std::string p = "transformer_blocks." + std::to_string(i) + ".";
         const std::string a1 = p + "attn1.", a2 = p + "attn2.";
-        TRY(L.req(a1 + "to_q.weight", {D, D}, b.qkv, LTX_BF16));
-        TRY(L.req(a1 + "to_k.weight", {D, D}, b.qkv + D * D, LTX_BF16));
-        TRY(L.req(a1 + "to_v.weight", {D, D}, b.qkv + 2 * D * D, LTX_BF16));
-        TRY(L.opt(a1 + "to_q.bias", {D}, b.qkv_b, LTX_F32));
-        TRY(L.opt(a1 + "to_k.bias", {D}, b.qkv_b + D, LTX_F32));
-        TRY(L.opt(a1 + "to_v.bias", {D}, b.qkv_b + 2 * D, LTX_F32));
-        TRY(L.req(a1 + "q_norm.weight", {D}, b.qn, LTX_F32));
-        TRY(L.req(a1 + "k_norm.weight", {D}, b.kn, LTX_F32));
-        TRY(L.req(a1 + "to_out.0.weight", {D, D}, b.o, LTX_BF16));
+        TRY(L.req(a1 + "to_q.weight", {D, D}, b.qkv, LTX_BF16, kRows));
+        TRY(L.req(a1 + "to_k.weight", {D, D}, b.qkv + Dl * D, LTX_BF16, kRows));
+        TRY(L.req(a1 + "to_v.weight", {D, D}, b.qkv + 2 * Dl * D, LTX_BF16, kRows));
+        TRY(L.opt(a1 + "to_q.bias", {D}, b.qkv_b, LTX_F32, kRows));
+        TRY(L.opt(a1 + "to_k.bias", {D}, b.qkv_b + Dl, LTX_F32, kRows));
+        TRY(L.opt(a1 + "to_v.bias", {D}, b.qkv_b + 2 * Dl, LTX_F32, kRows));
+        TRY(L.req(a1 + "q_norm.weight", {D}, b.qn, LTX_F32, kRows));
+        TRY(L.req(a1 + "k_norm.weight", {D}, b.kn, LTX_F32, kRows));
+        TRY(L.req(a1 + "to_out.0.weight", {D, D}, b.o, LTX_BF16, kCols));
         TRY(L.opt(a1 + "to_out.0.bias", {D}, b.o_b, LTX_F32));
-        TRY(L.req(a2 + "to_q.weight", {D, D}, b.q2, LTX_BF16));
-        TRY(L.opt(a2 + "to_q.bias", {D}, b.q2_b, LTX_F32));
-        TRY(L.req(a2 + "to_k.weight", {D, Dc}, b.kv2, LTX_BF16));
-        TRY(L.req(a2 + "to_v.weight", {D, Dc}, b.kv2 + D * Dc, LTX_BF16));
-        TRY(L.opt(a2 + "to_k.bias", {D}, b.kv2_b, LTX_F32));
-        TRY(L.opt(a2 + "to_v.bias", {D}, b.kv2_b + D, LTX_F32));
-        TRY(L.req(a2 + "q_norm.weight", {D}, b.qn2, LTX_F32));
-        TRY(L.req(a2 + "k_norm.weight", {D}, b.kn2, LTX_F32));
-        TRY(L.req(a2 + "to_out.0.weight", {D, D}, b.o2, LTX_BF16));
+        TRY(L.req(a2 + "to_q.weight", {D, D}, b.q2, LTX_BF16, kRows));
+        TRY(L.opt(a2 + "to_q.bias", {D}, b.q2_b, LTX_F32, kRows));
+        TRY(L.req(a2 + "to_k.weight", {D, Dc}, b.kv2, LTX_BF16, kRows));
+        TRY(L.req(a2 + "to_v.weight", {D, Dc}, b.kv2 + Dl * Dc, LTX_BF16, kRows));
+        TRY(L.opt(a2 + "to_k.bias", {D}, b.kv2_b, LTX_F32, kRows));
+        TRY(L.opt(a2 + "to_v.bias", {D}, b.kv2_b + Dl, LTX_F32, kRows));
+        TRY(L.req(a2 + "q_norm.weight", {D}, b.qn2, LTX_F32, kRows));
+        TRY(L.req(a2 + "k_norm.weight", {D}, b.kn2, LTX_F32, kRows));
+        TRY(L.req(a2 + "to_out.0.weight", {D, D}, b.o2, LTX_BF16, kCols));
         TRY(L.opt(a2 + "to_out.0.bias", {D}, b.o2_b, LTX_F32));
         if (c.gated) {
-            TRY(L.req(a1 + "to_gate_logits.weight", {H, D}, b.g1, LTX_BF16));
-            TRY(L.opt(a1 + "to_gate_logits.bias", {H}, b.g1_b, LTX_F32));
-            TRY(L.req(a2 + "to_gate_logits.weight", {H, D}, b.g2, LTX_BF16));
-            TRY(L.opt(a2 + "to_gate_logits.bias", {H}, b.g2_b, LTX_F32));
+            TRY(L.req(a1 + "to_gate_logits.weight", {H, D}, b.g1, LTX_BF16, kRows));
+            TRY(L.opt(a1 + "to_gate_logits.bias", {H}, b.g1_b, LTX_F32, kRows));
+            TRY(L.req(a2 + "to_gate_logits.weight", {H, D}, b.g2, LTX_BF16, kRows));
+            TRY(L.opt(a2 + "to_gate_logits.bias", {H}, b.g2_b, LTX_F32, kRows));
         }
-        TRY(L.req(p + "ff.net.0.proj.weight", {F, D}, b.ff1, LTX_BF16));
-        TRY(L.req(p + "ff.net.2.weight", {D, F}, b.ff2, LTX_BF16));
+        TRY(L.req(p + "ff.net.0.proj.weight", {F, D}, b.ff1, LTX_BF16, kRows));
+        TRY(L.req(p + "ff.net.2.weight", {D, F}, b.ff2, LTX_BF16, kCols));
         if (c.ff_bias) {
-            TRY(L.opt(p + "ff.net.0.proj.bias", {F}, b.ff1_b, LTX_F32));
+            TRY(L.opt(p + "ff.net.0.proj.bias", {F}, b.ff1_b, LTX_F32, kRows));
             TRY(L.opt(p + "ff.net.2.bias", {D}, b.ff2_b, LTX_F32));
         }
         TRY(L.req(p + "scale_shift_table", {K, D}, b.sst, LTX_F32));
         if (c.cross_adaln) TRY(L.req(p + "prompt_scale_shift_table", {2, D}, b.pst, LTX_F32));
     }
+    return LTX_OK;
+}
+
+static int load_weights(ltx_model *m, ltx_store *st, ltx_ctx *ctx) {
+    const DitConfig &c = m->cfg;
+    const int64_t D = c.inner();
+    Loader L{st, ctx, m->tp, m->tr};
+    if (m->tp > 1) {
+        // the largest split tensor, as f32: [4D, D] or [D, cross_dim]
+        const size_t big = (size_t)std::max<int64_t>(4 * D * D, D * c.cross_dim) * 4;
+        cudaError_t e = cudaMalloc(&L.tmp, big);
+        if (e != cudaSuccess) return fail(ctx, LTX_ERR_OOM, "shard staging of %zu bytes: %s", big, cudaGetErrorString(e));
+    }
+    int rc = load_weights_into(m, L);
     cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (L.tmp) cudaFree(L.tmp);
+    if (rc) return rc;
     if (e != cudaSuccess) return cuda_fail(ctx, e, "model load");
     return LTX_OK;
 }
@@ -320,19 +392,23 @@ struct Synth {
     uint64_t seed;
     int rank;
     float strength;
+    int n = 1, r = 0;            // tensor-parallel shard kept
     uint64_t sid = 1;
     float *f32 = nullptr;        // [max numel]
     uint8_t *q8 = nullptr;       // [max numel]
     __nv_bfloat16 *la = nullptr, *lb = nullptr;
     float *scale_dev = nullptr;
     unsigned int *work = nullptr;
+    void *full = nullptr;        // full merged tensor before slicing (n > 1)
     // W ~ N(0, 0.02) -> e4m3 with scale amax/448; LoRA A [r, in], B [out, r]
-    // bf16 ~ N(0, 0.01), alpha = rank; merged through ltx_dequant_merge.
-    int linear(void *dst, int64_t out, int64_t in, int dst_dt) {
-        const int64_t n = out * in;
+    // bf16 ~ N(0, 0.01), alpha = rank; merged through ltx_dequant_merge.  The
+    // whole tensor is always generated (same random stream and FP8 scale on
+    // every shard count), then this rank's part is kept.
+    int linear(void *dst, int64_t out, int64_t in, int dst_dt, Split sp = kAll) {
+        const int64_t n_el = out * in;
         cudaStream_t st = ctx->stream;
-        LTX_CUDA_TRY(ctx, synth_normal_f32(st, ctx->sm_count, f32, n, seed, sid++, 0.f, 0.02f));
-        LTX_CUDA_TRY(ctx, synth_quantize_fp8(st, ctx->sm_count, f32, n, q8, scale_dev, work));
+        LTX_CUDA_TRY(ctx, synth_normal_f32(st, ctx->sm_count, f32, n_el, seed, sid++, 0.f, 0.02f));
+        LTX_CUDA_TRY(ctx, synth_quantize_fp8(st, ctx->sm_count, f32, n_el, q8, scale_dev, work));
         float scale = 0.f;
         LTX_CUDA_TRY(ctx, cudaMemcpyAsync(&scale, scale_dev, 4, cudaMemcpyDeviceToHost, st));
         LTX_CUDA_TRY(ctx, cudaStreamSynchronize(st));
@@ -344,10 +420,17 @@ struct Synth {
             d = ltx_lora_delta{la, lb, rank, LTX_BF16, LTX_BF16, ltx_lora_coeff(strength, (float)rank, rank)};
             nd = 1;
         }
-        return dequant_merge(ctx, st, q8, LTX_F8_E4M3, 1, scale, out, in, &d, nd, dst, dst_dt);
+        const bool sliced = n > 1 && sp.kind != Split::ALL;
+        const int rc = dequant_merge(ctx, st, q8, LTX_F8_E4M3, 1, scale, out, in, &d, nd, sliced ? full : dst, dst_dt);
+        if (rc || !sliced) return rc;
+        LTX_CUDA_TRY(ctx, slice_to(st, dst, full, out, in, dtype_size(dst_dt), sp, n, r));
+        return LTX_OK;
     }
-    int vec(float *dst, int64_t n, float mean, float std) {
-        LTX_CUDA_TRY(ctx, synth_normal_f32(ctx->stream, ctx->sm_count, dst, n, seed, sid++, mean, std));
+    int vec(float *dst, int64_t n_el, float mean, float std, Split sp = kAll) {
+        const bool sliced = n > 1 && sp.kind != Split::ALL;
+        LTX_CUDA_TRY(ctx, synth_normal_f32(ctx->stream, ctx->sm_count, sliced ? static_cast<float *>(full) : dst, n_el,
+                                           seed, sid++, mean, std));
+        if (sliced) LTX_CUDA_TRY(ctx, slice_to(ctx->stream, dst, full, n_el, 1, 4, sp, n, r));
         return LTX_OK;
     }
 };
@@ -356,8 +439,9 @@ static int init_random(ltx_model *m, ltx_ctx *ctx, uint64_t seed, int rank, floa
     const DitConfig &c = m->cfg;
     const int64_t D = c.inner(), Dc = c.cross_dim, F = 4 * D, H = c.heads, K = c.coeff();
     const int64_t maxn = std::max<int64_t>({F * D, K * D * D, 2 * D * Dc, 3 * D * D});
-    Synth s{ctx, seed, rank, strength};
+    Synth s{ctx, seed, rank, strength, m->tp, m->tr};
     // scratch: f32 weight [maxn] | fp8 [maxn] | LoRA A [rank*max_in] | LoRA B [max_out*rank] | scale | amax
+    //          | full merged tensor [maxn] (sharded models only)
     const int64_t max_in = std::max<int64_t>({F, Dc, D, 256, (int64_t)c.in_ch});
     const int64_t max_out = std::max<int64_t>({K * D, F, 3 * D, 2 * D, (int64_t)c.out_ch});
     Arena sz;
@@ -367,6 +451,7 @@ static int init_random(ltx_model *m, ltx_ctx *ctx, uint64_t seed, int rank, floa
     sz.take<__nv_bfloat16>(max_out * rank);
     sz.take<float>(1);
     sz.take<unsigned int>(1);
+    if (m->tp > 1) sz.take<float>(maxn);
     void *buf = nullptr;
     if (cudaMalloc(&buf, sz.off + 256) != cudaSuccess) return fail(ctx, LTX_ERR_OOM, "synthetic init scratch");
     Arena ar;
@@ -377,6 +462,8 @@ static int init_random(ltx_model *m, ltx_ctx *ctx, uint64_t seed, int rank, floa
     s.lb = ar.take<__nv_bfloat16>(max_out * rank);
     s.scale_dev = ar.take<float>(1);
     s.work = ar.take<unsigned int>(1);
+    if (m->tp > 1) s.full = ar.take<float>(maxn);
+    const Split qkv3{Split::ROWS, 3}, kv2{Split::ROWS, 2};
     int rc = [&]() -> int {
         TRY(s.linear(m->patch_w, D, c.in_ch, LTX_BF16));
         TRY(s.linear(m->t1_w, D, 256, LTX_F32));
@@ -385,22 +472,22 @@ static int init_random(ltx_model *m, ltx_ctx *ctx, uint64_t seed, int rank, floa
         TRY(s.vec(m->sst_out, 2 * D, 0.f, 0.02f));
         TRY(s.linear(m->out_w, c.out_ch, D, LTX_BF16));
         for (auto &b : m->blocks) {
-            TRY(s.linear(b.qkv, 3 * D, D, LTX_BF16));
-            TRY(s.linear(b.o, D, D, LTX_BF16));
-            TRY(s.linear(b.q2, D, D, LTX_BF16));
-            TRY(s.linear(b.kv2, 2 * D, Dc, LTX_BF16));
-            TRY(s.linear(b.o2, D, D, LTX_BF16));
-            TRY(s.linear(b.ff1, F, D, LTX_BF16));
-            TRY(s.linear(b.ff2, D, F, LTX_BF16));
-            TRY(s.vec(b.qn, D, 1.f, 0.02f));
-            TRY(s.vec(b.kn, D, 1.f, 0.02f));
-            TRY(s.vec(b.qn2, D, 1.f, 0.02f));
-            TRY(s.vec(b.kn2, D, 1.f, 0.02f));
+            TRY(s.linear(b.qkv, 3 * D, D, LTX_BF16, qkv3));
+            TRY(s.linear(b.o, D, D, LTX_BF16, kCols));
+            TRY(s.linear(b.q2, D, D, LTX_BF16, kRows));
+            TRY(s.linear(b.kv2, 2 * D, Dc, LTX_BF16, kv2));
+            TRY(s.linear(b.o2, D, D, LTX_BF16, kCols));
+            TRY(s.linear(b.ff1, F, D, LTX_BF16, kRows));
+            TRY(s.linear(b.ff2, D, F, LTX_BF16, kCols));
+            TRY(s.vec(b.qn, D, 1.f, 0.02f, kRows));
+            TRY(s.vec(b.kn, D, 1.f, 0.02f, kRows));
+            TRY(s.vec(b.qn2, D, 1.f, 0.02f, kRows));
+            TRY(s.vec(b.kn2, D, 1.f, 0.02f, kRows));
             TRY(s.vec(b.sst, K * D, 0.f, 0.02f));
             if (b.pst) TRY(s.vec(b.pst, 2 * D, 0.f, 0.02f));
             if (b.g1) {
-                TRY(s.linear(b.g1, H, D, LTX_BF16));
-                TRY(s.linear(b.g2, H, D, LTX_BF16));
+                TRY(s.linear(b.g1, H, D, LTX_BF16, kRows));
+                TRY(s.linear(b.g2, H, D, LTX_BF16, kRows));
             }
         }
         return LTX_OK;
@@ -418,13 +505,17 @@ struct Work {
     int *idx;
     float *ts_u;
     double *partial;
+    float *part, *ss;   // tensor-parallel: summed partial projections, Q/K sums of squares
     size_t bytes;
 };
 
-static Work carve_work(char *base, const DitConfig &c, int64_t rows, int64_t crow, int U, int L) {
+// Forward workspace for `rows` latent rows and `crow` context rows on a model
+// split over `tp` ranks (tp = 1: whole model).
+static Work carve_work(char *base, const DitConfig &c, int64_t rows, int64_t crow, int U, int L, int tp) {
     Arena a;
     a.base = base;
     const int64_t D = c.inner(), Dc = c.cross_dim, K = c.coeff();
+    const int64_t Dl = D / tp, Fl = 4 * D / tp, Hl = c.heads / tp;
     Work w{};
     w.x = a.take<float>(rows * D);
     w.out32 = a.take<float>(rows * std::max(c.out_ch, 1));
@@ -440,16 +531,18 @@ static Work carve_work(char *base, const DitConfig &c, int64_t rows, int64_t cro
     const int width = c.interleaved ? (int)D : (int)(D / 2);
     w.cos = a.take<float>(rows * width);
     w.sin = a.take<float>(rows * width);
-    w.glog = a.take<float>(rows * c.heads);
+    w.glog = a.take<float>(rows * Hl);
     w.xn = a.take<__nv_bfloat16>(rows * D);
-    w.qkv = a.take<__nv_bfloat16>(rows * 3 * D);
-    w.att = a.take<__nv_bfloat16>(rows * D);
+    w.qkv = a.take<__nv_bfloat16>(rows * 3 * Dl);
+    w.att = a.take<__nv_bfloat16>(rows * Dl);
     w.q2 = w.qkv;   // cross-attention reuses the self-attention projection buffer
-    w.kv2 = a.take<__nv_bfloat16>(crow * 2 * D);
+    w.kv2 = a.take<__nv_bfloat16>(crow * 2 * Dl);
     w.ctxb = a.take<__nv_bfloat16>(crow * Dc);
-    w.ffh = a.take<__nv_bfloat16>(rows * 4 * D);
+    w.ffh = a.take<__nv_bfloat16>(rows * Fl);
     w.latb = a.take<__nv_bfloat16>(rows * std::max(c.in_ch, 8));
     w.partial = a.take<double>((int64_t)cfg_scratch_bytes() / 8);
+    w.part = tp > 1 ? a.take<float>(rows * D) : nullptr;
+    w.ss = tp > 1 ? a.take<float>(2 * rows + crow) : nullptr;
     w.bytes = a.off + 256;
     return w;
 }
@@ -496,6 +589,9 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
                         const float *positions, const float *context, int B, int T, int S, float *out,
                         const Work *given = nullptr, Work *work_out = nullptr) {
     const DitConfig &c = m->cfg;
+    if (ctx->tp_size != m->tp || ctx->tp_rank != m->tr)
+        return fail(ctx, LTX_ERR_INVALID_ARG, "model shard %d of %d run on a context of rank %d of %d", m->tr, m->tp,
+                    ctx->tp_rank, ctx->tp_size);
     const int64_t D = c.inner(), Dc = c.cross_dim, H = c.heads, d = c.head_dim, K = c.coeff();
     const int64_t rows = (int64_t)B * T, crow = (int64_t)B * S;
     cudaStream_t st = ctx->stream;
@@ -507,9 +603,9 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
     if (given) {
         w = *given;
     } else {
-        Work sizing = carve_work(nullptr, c, rows, crow, U, c.layers);
+        Work sizing = carve_work(nullptr, c, rows, crow, U, c.layers, m->tp);
         TRY(ensure_work(ctx, sizing.bytes));
-        w = carve_work(static_cast<char *>(ctx->work), c, rows, crow, U, c.layers);
+        w = carve_work(static_cast<char *>(ctx->work), c, rows, crow, U, c.layers, m->tp);
     }
     if (work_out) *work_out = w;
     {
@@ -539,17 +635,43 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
     const int width = c.interleaved ? (int)D : (int)(D / 2);
     // The fused Q/K kernel computes RoPE angles in registers for the production
     // shape (D 4096, head dim 128, split RoPE); other shapes use the tables.
-    const bool fused_qk = D == 4096 && d == 128 && !c.interleaved;
+    const bool fused_qk = m->tp == 1 && D == 4096 && d == 128 && !c.interleaved;
     if (!fused_qk)
         CU(rope_table(st, sms, positions, B, T, m->rope_freq, m->rope_grid, mp, c.use_mid, c.interleaved, width, w.cos,
                       w.sin));
     if (!c.cross_adaln) CU(f32_to_bf16(st, sms, context, crow * Dc, w.ctxb));
 
+    // Tensor-parallel split: this rank runs heads [tr*Hl, (tr+1)*Hl) and FFN
+    // units [tr*Fl, (tr+1)*Fl); everything else is replicated.  tp = 1 is the
+    // whole model.
+    const int tp = m->tp;
+    const int64_t Dl = D / tp, Hl = H / tp, Fl = 4 * D / tp, head0 = (int64_t)m->tr * Hl;
     const float scale = 1.0f / sqrtf((float)d);
     auto attend = [&](const __nv_bfloat16 *q, int64_t ldq, const __nv_bfloat16 *k, int64_t ldk, const __nv_bfloat16 *v,
                       int64_t ldv, int Tk) -> int {
-        if (d == 128) return attention_fwd(ctx, st, q, ldq, k, ldk, v, ldv, B, (int)H, T, Tk, scale, w.att, D, true);
-        CU(attention_generic(st, q, ldq, k, ldk, v, ldv, B, (int)H, T, Tk, (int)d, scale, w.att, D));
+        if (d == 128) return attention_fwd(ctx, st, q, ldq, k, ldk, v, ldv, B, (int)Hl, T, Tk, scale, w.att, Dl, true);
+        CU(attention_generic(st, q, ldq, k, ldk, v, ldv, B, (int)Hl, T, Tk, (int)d, scale, w.att, Dl));
+        return LTX_OK;
+    };
+    // x += (A . W^T + bias) * gate: fused into the GEMM epilogue on one GPU;
+    // split over ranks, the partial products are summed first.
+    auto project_residual = [&](const __nv_bfloat16 *a, int64_t lda, const __nv_bfloat16 *wt, int64_t kdim,
+                                const float *bias, const float *gate) -> int {
+        const int *gidx = gate ? w.idx : nullptr;
+        if (tp == 1)
+            return gemm_bf16(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, LTX_EPI_RESID, bias, w.x, D, gate,
+                             gidx, K * D);
+        TRY(gemm_bf16(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, LTX_EPI_F32, nullptr, w.part, D, nullptr,
+                      nullptr, 0));
+        TRY(allreduce_sum(ctx, w.part, (size_t)rows * D));
+        CU(tp_resid_add(st, sms, w.x, w.part, (int)rows, (int)D, bias, gate, gidx, K * D));
+        return LTX_OK;
+    };
+    // RMSNorm(gamma) over the full inner dimension of `nseg` projections that
+    // each hold Dl columns per row here (+ RoPE with the tables when given)
+    auto norm_split = [&](__nv_bfloat16 *buf, int64_t ld, int nrows, const float *gamma, float *ss, bool rope) -> int {
+        CU(tp_norm_apply_rope(st, buf, ld, nrows, (int)Dl, (int)D, (int)d, (int)head0, c.eps, gamma, ss,
+                              rope ? w.cos : nullptr, rope ? w.sin : nullptr, c.interleaved));
         return LTX_OK;
     };
     for (int l = 0; l < c.layers; ++l) {
@@ -558,10 +680,15 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         // self-attention: x += attn(mod(rms(x))) * gate_msa
         CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 0, w.xn, D));
         // V columns come out as f16: the attention keeps P in f16 for the P.V MMA
-        const int vcol = d == 128 ? (int)(2 * D) : (int)(3 * D);
-        TRY(gemm_bf16(ctx, st, w.xn, D, b.qkv, D, (int)rows, (int)(3 * D), (int)D, LTX_EPI_BF16, b.qkv_b, w.qkv,
-                      3 * D, nullptr, nullptr, 0, vcol));
-        if (fused_qk) {
+        const int vcol = d == 128 ? (int)(2 * Dl) : (int)(3 * Dl);
+        TRY(gemm_bf16(ctx, st, w.xn, D, b.qkv, D, (int)rows, (int)(3 * Dl), (int)D, LTX_EPI_BF16, b.qkv_b, w.qkv,
+                      3 * Dl, nullptr, nullptr, 0, vcol));
+        if (tp > 1) {
+            CU(tp_sumsq_rows(st, w.qkv, 3 * Dl, (int)rows, (int)Dl, 2, Dl, w.ss));
+            TRY(allreduce_sum(ctx, w.ss, (size_t)2 * rows));
+            TRY(norm_split(w.qkv, 3 * Dl, (int)rows, b.qn, w.ss, true));
+            TRY(norm_split(w.qkv + Dl, 3 * Dl, (int)rows, b.kn, w.ss + rows, true));
+        } else if (fused_qk) {
             cudaError_t qe = cudaSuccess;
             qk_norm_rope_fused(st, w.qkv, w.qkv + D, 3 * D, (int)rows, T, (int)D, c.eps, b.qn, b.kn, positions,
                                m->rope_freq, m->rope_grid, mp, c.use_mid, &qe);
@@ -570,40 +697,45 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
             CU(qk_norm_rope(st, w.qkv, 3 * D, (int)rows, (int)D, (int)H, c.eps, b.qn, w.cos, w.sin, c.interleaved));
             CU(qk_norm_rope(st, w.qkv + D, 3 * D, (int)rows, (int)D, (int)H, c.eps, b.kn, w.cos, w.sin, c.interleaved));
         }
-        TRY(attend(w.qkv, 3 * D, w.qkv + D, 3 * D, w.qkv + 2 * D, 3 * D, T));
+        TRY(attend(w.qkv, 3 * Dl, w.qkv + Dl, 3 * Dl, w.qkv + 2 * Dl, 3 * Dl, T));
         if (c.gated) {
-            TRY(gemm_bf16(ctx, st, w.xn, D, b.g1, D, (int)rows, (int)H, (int)D, LTX_EPI_F32, b.g1_b, w.glog, H, nullptr,
-                          nullptr, 0));
-            CU(head_gate(st, sms, w.att, D, w.glog, H, (int)rows, (int)H, (int)d));
+            TRY(gemm_bf16(ctx, st, w.xn, D, b.g1, D, (int)rows, (int)Hl, (int)D, LTX_EPI_F32, b.g1_b, w.glog, Hl,
+                          nullptr, nullptr, 0));
+            CU(head_gate(st, sms, w.att, Dl, w.glog, Hl, (int)rows, (int)Hl, (int)d));
         }
-        TRY(gemm_bf16(ctx, st, w.att, D, b.o, D, (int)rows, (int)D, (int)D, LTX_EPI_RESID, b.o_b, w.x, D, tab + 2 * D,
-                      w.idx, K * D));
+        TRY(project_residual(w.att, Dl, b.o, Dl, b.o_b, tab + 2 * D));
         // cross-attention: x += attn(rms(x), ctx)   [flag path: modulated q, gated, modulated ctx]
         if (c.cross_adaln)
             CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 6, w.xn, D));
         else
             CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 0, nullptr, 0, nullptr, 0, w.xn, D));
-        TRY(gemm_bf16(ctx, st, w.xn, D, b.q2, D, (int)rows, (int)D, (int)D, LTX_EPI_BF16, b.q2_b, w.q2, D, nullptr,
+        TRY(gemm_bf16(ctx, st, w.xn, D, b.q2, D, (int)rows, (int)Dl, (int)D, LTX_EPI_BF16, b.q2_b, w.q2, Dl, nullptr,
                       nullptr, 0));
-        CU(qk_norm_rope(st, w.q2, D, (int)rows, (int)D, (int)H, c.eps, b.qn2, nullptr, nullptr, false));
         if (c.cross_adaln) CU(ctx_mod(st, sms, context, crow * Dc, (int)Dc, b.pst, w.ctxb));
-        TRY(gemm_bf16(ctx, st, w.ctxb, Dc, b.kv2, Dc, (int)crow, (int)(2 * D), (int)Dc, LTX_EPI_BF16, b.kv2_b, w.kv2,
-                      2 * D, nullptr, nullptr, 0, d == 128 ? (int)D : (int)(2 * D)));
-        CU(qk_norm_rope(st, w.kv2, 2 * D, (int)crow, (int)D, (int)H, c.eps, b.kn2, nullptr, nullptr, false));
-        TRY(attend(w.q2, D, w.kv2, 2 * D, w.kv2 + D, 2 * D, S));
-        if (c.gated) {
-            TRY(gemm_bf16(ctx, st, w.xn, D, b.g2, D, (int)rows, (int)H, (int)D, LTX_EPI_F32, b.g2_b, w.glog, H, nullptr,
-                          nullptr, 0));
-            CU(head_gate(st, sms, w.att, D, w.glog, H, (int)rows, (int)H, (int)d));
+        TRY(gemm_bf16(ctx, st, w.ctxb, Dc, b.kv2, Dc, (int)crow, (int)(2 * Dl), (int)Dc, LTX_EPI_BF16, b.kv2_b, w.kv2,
+                      2 * Dl, nullptr, nullptr, 0, d == 128 ? (int)Dl : (int)(2 * Dl)));
+        if (tp > 1) {
+            CU(tp_sumsq_rows(st, w.q2, Dl, (int)rows, (int)Dl, 1, 0, w.ss));
+            CU(tp_sumsq_rows(st, w.kv2, 2 * Dl, (int)crow, (int)Dl, 1, 0, w.ss + rows));
+            TRY(allreduce_sum(ctx, w.ss, (size_t)(rows + crow)));
+            TRY(norm_split(w.q2, Dl, (int)rows, b.qn2, w.ss, false));
+            TRY(norm_split(w.kv2, 2 * Dl, (int)crow, b.kn2, w.ss + rows, false));
+        } else {
+            CU(qk_norm_rope(st, w.q2, D, (int)rows, (int)D, (int)H, c.eps, b.qn2, nullptr, nullptr, false));
+            CU(qk_norm_rope(st, w.kv2, 2 * D, (int)crow, (int)D, (int)H, c.eps, b.kn2, nullptr, nullptr, false));
         }
-        TRY(gemm_bf16(ctx, st, w.att, D, b.o2, D, (int)rows, (int)D, (int)D, LTX_EPI_RESID, b.o2_b, w.x, D,
-                      c.cross_adaln ? tab + 8 * D : nullptr, c.cross_adaln ? w.idx : nullptr, K * D));
+        TRY(attend(w.q2, Dl, w.kv2, 2 * Dl, w.kv2 + Dl, 2 * Dl, S));
+        if (c.gated) {
+            TRY(gemm_bf16(ctx, st, w.xn, D, b.g2, D, (int)rows, (int)Hl, (int)D, LTX_EPI_F32, b.g2_b, w.glog, Hl,
+                          nullptr, nullptr, 0));
+            CU(head_gate(st, sms, w.att, Dl, w.glog, Hl, (int)rows, (int)Hl, (int)d));
+        }
+        TRY(project_residual(w.att, Dl, b.o2, Dl, b.o2_b, c.cross_adaln ? tab + 8 * D : nullptr));
         // feed-forward: x += ff(mod(rms(x))) * gate_mlp
         CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 3, w.xn, D));
-        TRY(gemm_bf16(ctx, st, w.xn, D, b.ff1, D, (int)rows, (int)(4 * D), (int)D, LTX_EPI_GELU_BF16, b.ff1_b, w.ffh,
-                      4 * D, nullptr, nullptr, 0));
-        TRY(gemm_bf16(ctx, st, w.ffh, 4 * D, b.ff2, 4 * D, (int)rows, (int)D, (int)(4 * D), LTX_EPI_RESID, b.ff2_b, w.x,
-                      D, tab + 5 * D, w.idx, K * D));
+        TRY(gemm_bf16(ctx, st, w.xn, D, b.ff1, D, (int)rows, (int)Fl, (int)D, LTX_EPI_GELU_BF16, b.ff1_b, w.ffh, Fl,
+                      nullptr, nullptr, 0));
+        TRY(project_residual(w.ffh, Fl, b.ff2, Fl, b.ff2_b, tab + 5 * D));
     }
     // output head: LN(x) * (1 + scale) + shift -> proj_out (model.rs:237-254)
     CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 2, w.otab, 2, w.idx, 0, w.xn, D));
@@ -683,61 +815,170 @@ extern "C" int ltx_model_forward(ltx_model *m, ltx_ctx *ctx, const float *latent
     return forward_impl(m, ctx, latent_dev, ts, positions_dev, context_dev, batch, tokens, context_tokens, out_dev);
 }
 
+namespace ltx {
+
+// Step buffers ahead of the forward's workspace in ctx->work, so that their
+// offsets do not depend on the forward's sizing: the batch-2 latent copy, the
+// velocity output, and the batch-2 positions and contexts.
+struct StepBufs {
+    float *lat2, *vel, *pos2, *ctx2;
+    size_t bytes;
+};
+
+static StepBufs carve_step(char *base, const DitConfig &c, int B, int T, int S) {
+    Arena a;
+    a.base = base;
+    StepBufs b{};
+    b.lat2 = a.take<float>((int64_t)B * T * c.in_ch);
+    b.vel = a.take<float>((int64_t)B * T * c.out_ch);
+    b.pos2 = a.take<float>((int64_t)B * 3 * T * 2);
+    b.ctx2 = a.take<float>((int64_t)B * S * c.cross_dim);
+    b.bytes = (a.off + 255) & ~size_t(255);
+    return b;
+}
+
+// Bytes of ctx->work one step needs with U distinct timesteps.
+static size_t step_work_bytes(const ltx_model *m, int B, int T, int S, int U) {
+    const DitConfig &c = m->cfg;
+    return carve_step(nullptr, c, B, T, S).bytes +
+           carve_work(nullptr, c, (int64_t)B * T, (int64_t)B * S, U, c.layers, m->tp).bytes;
+}
+
+// Copies positions and the cond/uncond contexts into the batch-2 layout.
+static int stage_static(ltx_ctx *ctx, const StepBufs &sb, const float *positions_dev, const float *cc,
+                        const float *cu, int B, int T, int S, int64_t Dc) {
+    cudaStream_t st = ctx->stream;
+    for (int b = 0; b < B; ++b) {
+        CU(cudaMemcpyAsync(sb.pos2 + (int64_t)b * 3 * T * 2, positions_dev, (size_t)3 * T * 2 * 4,
+                           cudaMemcpyDeviceToDevice, st));
+        CU(cudaMemcpyAsync(sb.ctx2 + (int64_t)b * S * Dc, b == 0 ? cc : cu, (size_t)S * Dc * 4,
+                           cudaMemcpyDeviceToDevice, st));
+    }
+    return LTX_OK;
+}
+
 // One Euler step of euler_denoising_loop (loop_.rs:93-149) with GuidedDenoiser::apply
-// (guidance.rs:102-166): the cond and uncond passes run as ONE batch-2 forward.
+// (guidance.rs:102-166): the cond and uncond passes run as ONE batch-2 forward,
+// then the CFG/rescale combine, post_process and the Euler update in one kernel.
+// Arguments are validated by the callers.  static_ready: positions/contexts are
+// already in the step buffers (the loop stages them once).
+static int denoise_step_core(ltx_model *m, ltx_ctx *ctx, float *latent_dev, const float *clean_dev,
+                             const float *mask_host, const float *mask_dev, const float *positions_dev,
+                             const float *cc, const float *cu, int T, int S, float sigma, float sigma_next,
+                             float cfg_scale, float rescale_scale, bool static_ready) {
+    const DitConfig &c = m->cfg;
+    const bool use_cfg = std::fabs(cfg_scale - 1.0f) > 1e-5f;   // needs_uncond (guidance.rs:58-60)
+    const int B = use_cfg ? 2 : 1, C = c.in_ch;
+    cudaStream_t st = ctx->stream;
+    // per-token timesteps = mask * sigma (guidance.rs:114), both CFG halves
+    std::vector<float> ts((size_t)B * T);
+    for (int b = 0; b < B; ++b)
+        for (int t = 0; t < T; ++t) ts[(size_t)b * T + t] = mask_host[t] * sigma;
+    std::vector<float> uq;
+    std::vector<int> ix;
+    const int U = unique_timesteps(ts, uq, ix);
+    TRY(ensure_work(ctx, step_work_bytes(m, B, T, S, U)));   // grow-only: a no-op inside a loop
+    char *base = static_cast<char *>(ctx->work);
+    const StepBufs sb = carve_step(base, c, B, T, S);
+    Work w = carve_work(base + sb.bytes, c, (int64_t)B * T, (int64_t)B * S, U, c.layers, m->tp);
+    if (!static_ready) TRY(stage_static(ctx, sb, positions_dev, cc, cu, B, T, S, c.cross_dim));
+    for (int b = 0; b < B; ++b)
+        CU(cudaMemcpyAsync(sb.lat2 + (int64_t)b * T * C, latent_dev, (size_t)T * C * 4, cudaMemcpyDeviceToDevice, st));
+    TRY(forward_impl(m, ctx, sb.lat2, ts, sb.pos2, sb.ctx2, B, T, S, sb.vel, &w));
+    // per-token t for the velocity -> x0 adapter: x0 = x - t * v
+    TRY(upload(ctx, w.tok_t, ts.data(), (size_t)T * 4));
+    CU(cfg_euler(st, ctx->sm_count, latent_dev, sb.vel, use_cfg ? sb.vel + (int64_t)T * C : sb.vel, w.tok_t, mask_dev,
+                 clean_dev, T, C, cfg_scale, rescale_scale, use_cfg, w.partial, sigma, sigma_next));
+    return LTX_OK;
+}
+
+// Validation shared by the step and the loop entry points.
+static int check_step_args(ltx_model *m, ltx_ctx *ctx, const void *latent_dev, const void *clean_dev,
+                           const void *mask_dev, const void *positions_dev, const void *cc, const void *cu,
+                           int32_t tokens, int32_t context_tokens, float cfg_scale, const char *who) {
+    if (!m || !latent_dev || !clean_dev || !mask_dev || !positions_dev || !cc)
+        return fail(ctx, LTX_ERR_INVALID_ARG, "%s: null argument", who);
+    if (tokens <= 0 || context_tokens <= 0) return fail(ctx, LTX_ERR_SHAPE, "%s: empty tokens/context", who);
+    if (std::fabs(cfg_scale - 1.0f) > 1e-5f && !cu)
+        return fail(ctx, LTX_ERR_NEGATIVE_CONTEXT, "cfg_scale != 1 needs a negative context");
+    if (m->cfg.in_ch != m->cfg.out_ch) return fail(ctx, LTX_ERR_CONFIG, "denoising needs in_channels == out_channels");
+    return LTX_OK;
+}
+
+}  // namespace ltx
+
 extern "C" int ltx_denoise_step(ltx_model *m, ltx_ctx *ctx, float *latent_dev, const float *clean_dev,
                                 const float *mask_host, const float *mask_dev, const float *positions_dev,
                                 const float *ctx_cond_dev, const float *ctx_uncond_dev, int32_t tokens,
                                 int32_t context_tokens, float sigma, float sigma_next, float cfg_scale,
                                 float rescale_scale) {
-    if (!m || !ctx || !latent_dev || !clean_dev || !mask_dev || !positions_dev || !ctx_cond_dev)
-        return ctx ? fail(ctx, LTX_ERR_INVALID_ARG, "ltx_denoise_step: null argument") : LTX_ERR_INVALID_ARG;
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    TRY(check_step_args(m, ctx, latent_dev, clean_dev, mask_dev, positions_dev, ctx_cond_dev, ctx_uncond_dev, tokens,
+                        context_tokens, cfg_scale, "ltx_denoise_step"));
     if (!std::isfinite(sigma) || sigma <= 0.f) return fail(ctx, LTX_ERR_SIGMA, "invalid sigma %g", (double)sigma);
     if (!std::isfinite(sigma_next) || sigma_next < 0.f)
         return fail(ctx, LTX_ERR_SIGMA, "invalid next sigma %g", (double)sigma_next);
-    const bool use_cfg = std::fabs(cfg_scale - 1.0f) > 1e-5f;   // needs_uncond (guidance.rs:58-60)
-    if (use_cfg && !ctx_uncond_dev) return fail(ctx, LTX_ERR_NEGATIVE_CONTEXT, "cfg_scale != 1 needs a negative context");
+    std::vector<float> mask_copy;
+    if (!mask_host) {
+        mask_copy.resize(tokens);
+        CU(cudaMemcpyAsync(mask_copy.data(), mask_dev, (size_t)tokens * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        CU(cudaStreamSynchronize(ctx->stream));
+        mask_host = mask_copy.data();
+    }
+    return denoise_step_core(m, ctx, latent_dev, clean_dev, mask_host, mask_dev, positions_dev, ctx_cond_dev,
+                             ctx_uncond_dev, tokens, context_tokens, sigma, sigma_next, cfg_scale, rescale_scale, false);
+}
+
+// euler_denoising_loop (loop_.rs:93-149) + clear_conditioning (loop_.rs:162-185)
+// on the device: every step is enqueued without a host round trip; the
+// positions and contexts are staged once, the workspace is sized once for the
+// whole schedule.
+extern "C" int ltx_denoise_loop(ltx_model *m, ltx_ctx *ctx, float *latent_dev, const float *clean_dev,
+                                const float *mask_host, const float *mask_dev, const float *positions_dev,
+                                const float *ctx_cond_dev, const float *ctx_uncond_dev, int32_t tokens,
+                                int32_t context_tokens, const float *sigmas_host, int32_t n_sigmas, float cfg_scale,
+                                float rescale_scale, int32_t target_tokens, float *out_dev) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    TRY(check_step_args(m, ctx, latent_dev, clean_dev, mask_dev, positions_dev, ctx_cond_dev, ctx_uncond_dev, tokens,
+                        context_tokens, cfg_scale, "ltx_denoise_loop"));
+    if (!sigmas_host || n_sigmas < 2)
+        return fail(ctx, LTX_ERR_SCHEDULE, "schedule has %d sigmas; need at least 2", sigmas_host ? n_sigmas : 0);
+    // the reference checks each pair as it reaches it and returns no state on
+    // error, so checking every pair first gives the same result
+    for (int i = 0; i + 1 < n_sigmas; ++i) {
+        const float s = sigmas_host[i], sn = sigmas_host[i + 1];
+        if (!std::isfinite(s) || s <= 0.f) return fail(ctx, LTX_ERR_SIGMA, "step %d: invalid sigma %g", i, (double)s);
+        if (!std::isfinite(sn) || sn < 0.f)
+            return fail(ctx, LTX_ERR_SIGMA, "step %d: invalid sigma %g", i + 1, (double)sn);
+    }
+    if (target_tokens < 0 || target_tokens > tokens)
+        return fail(ctx, LTX_ERR_TARGET_TOKENS, "target token count %d exceeds the state's %d tokens", target_tokens,
+                    tokens);
     const DitConfig &c = m->cfg;
-    const int B = use_cfg ? 2 : 1, T = tokens, S = context_tokens, C = c.in_ch;
-    if (c.in_ch != c.out_ch) return fail(ctx, LTX_ERR_CONFIG, "denoise step needs in_channels == out_channels");
-    const int64_t D = c.inner(), Dc = c.cross_dim;
-    cudaStream_t st = ctx->stream;
-    // per-token timesteps = mask * sigma (guidance.rs:114), both CFG halves
+    const bool use_cfg = std::fabs(cfg_scale - 1.0f) > 1e-5f;
+    const int B = use_cfg ? 2 : 1, T = tokens, S = context_tokens;
     std::vector<float> mask_copy;
     if (!mask_host) {
         mask_copy.resize(T);
-        CU(cudaMemcpyAsync(mask_copy.data(), mask_dev, (size_t)T * 4, cudaMemcpyDeviceToHost, st));
-        CU(cudaStreamSynchronize(st));
+        CU(cudaMemcpyAsync(mask_copy.data(), mask_dev, (size_t)T * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        CU(cudaStreamSynchronize(ctx->stream));
         mask_host = mask_copy.data();
     }
-    std::vector<float> ts((size_t)B * T);
-    for (int b = 0; b < B; ++b)
-        for (int t = 0; t < T; ++t) ts[(size_t)b * T + t] = mask_host[t] * sigma;
-    // batch-2 inputs live in the step workspace after the forward's own
-    const int64_t rows = (int64_t)B * T;
-    std::vector<float> uq;
-    std::vector<int> ix;
-    const int U = unique_timesteps(ts, uq, ix);
-    Work sizing = carve_work(nullptr, c, rows, (int64_t)B * S, U, c.layers);
-    const size_t extra = (size_t)rows * C * 4 * 2 + (size_t)B * 3 * T * 2 * 4 + (size_t)B * S * Dc * 4 + 4096;
-    TRY(ensure_work(ctx, sizing.bytes + extra));
-    Work w = carve_work(static_cast<char *>(ctx->work), c, rows, (int64_t)B * S, U, c.layers);
-    char *ex = static_cast<char *>(ctx->work) + ((sizing.bytes + 255) & ~size_t(255));
-    float *lat2 = reinterpret_cast<float *>(ex);
-    float *vel = lat2 + rows * C;
-    float *pos2 = vel + rows * C;
-    float *ctx2 = pos2 + (int64_t)B * 3 * T * 2;
-    for (int b = 0; b < B; ++b) {
-        CU(cudaMemcpyAsync(lat2 + (int64_t)b * T * C, latent_dev, (size_t)T * C * 4, cudaMemcpyDeviceToDevice, st));
-        CU(cudaMemcpyAsync(pos2 + (int64_t)b * 3 * T * 2, positions_dev, (size_t)3 * T * 2 * 4, cudaMemcpyDeviceToDevice, st));
-        CU(cudaMemcpyAsync(ctx2 + (int64_t)b * S * Dc, b == 0 ? ctx_cond_dev : ctx_uncond_dev, (size_t)S * Dc * 4,
-                           cudaMemcpyDeviceToDevice, st));
+    // distinct mask values bound the distinct timesteps of every step
+    std::set<uint32_t> mvals;
+    for (int t = 0; t < T; ++t) {
+        uint32_t bits;
+        memcpy(&bits, &mask_host[t], 4);
+        mvals.insert(bits);
     }
-    TRY(forward_impl(m, ctx, lat2, ts, pos2, ctx2, B, T, S, vel, &w));
-    // per-token t for the velocity -> x0 adapter: x0 = x - t * v
-    TRY(upload(ctx, w.tok_t, ts.data(), (size_t)T * 4));
-    CU(cfg_euler(st, ctx->sm_count, latent_dev, vel, use_cfg ? vel + (int64_t)T * C : vel, w.tok_t, mask_dev, clean_dev,
-                 T, C, cfg_scale, rescale_scale, use_cfg, w.partial, sigma, sigma_next));
-    (void)D;
+    TRY(ensure_work(ctx, step_work_bytes(m, B, T, S, (int)mvals.size())));
+    const StepBufs sb = carve_step(static_cast<char *>(ctx->work), c, B, T, S);
+    TRY(stage_static(ctx, sb, positions_dev, ctx_cond_dev, ctx_uncond_dev, B, T, S, c.cross_dim));
+    for (int i = 0; i + 1 < n_sigmas; ++i)
+        TRY(denoise_step_core(m, ctx, latent_dev, clean_dev, mask_host, mask_dev, positions_dev, ctx_cond_dev,
+                              ctx_uncond_dev, T, S, sigmas_host[i], sigmas_host[i + 1], cfg_scale, rescale_scale, true));
+    if (out_dev && target_tokens > 0)
+        CU(cudaMemcpyAsync(out_dev, latent_dev, (size_t)target_tokens * c.in_ch * 4, cudaMemcpyDeviceToDevice,
+                           ctx->stream));
     return LTX_OK;
 }

@@ -15,12 +15,14 @@ LIB_PATH = os.path.join(_HERE, "libltx_b200.so")
 
 LTX_F32, LTX_F16, LTX_BF16, LTX_F8_E4M3, LTX_F8_E5M2 = 0, 1, 2, 3, 4
 MAX_DELTAS = 8
+COMM_ID_BYTES = 128
 
 STATUS = {
     0: "OK", 1: "INVALID_ARG", 2: "SHAPE", 3: "DTYPE", 4: "MISSING_KEY", 5: "DUPLICATE_KEY",
     6: "LORA_RANK", 7: "NO_LORA_MATCHES", 8: "IO", 9: "FORMAT", 10: "CONFIG", 11: "SIGMA",
     12: "SCHEDULE", 13: "CUDA", 14: "NCCL", 15: "TIMEOUT", 16: "OOM", 17: "UNSUPPORTED",
     18: "MISSING_CONFIG", 19: "NEGATIVE_CONTEXT", 20: "CHUNK_PLAN",
+    21: "TARGET_TOKENS",
 }
 
 
@@ -87,12 +89,21 @@ def lib() -> ctypes.CDLL:
         "ltx_model_weight_bytes": (I64, [V]),
         "ltx_model_forward": (I, [V, V, P, P, P, P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, P]),
         "ltx_denoise_step": (I, [V, V, P, P, P, P, P, P, P, ctypes.c_int32, ctypes.c_int32, F, F, F, F]),
+        "ltx_denoise_loop": (I, [V, V, P, P, P, P, P, P, P, ctypes.c_int32, ctypes.c_int32, P, ctypes.c_int32, F, F,
+                                 ctypes.c_int32, P]),
+        "ltx_apply_noise": (I, [V, P, P, P, P, ctypes.c_int32, ctypes.c_int32, F]),
         "ltx_scheduler_execute": (I, [ctypes.c_int32, ctypes.c_uint64, F, F, ctypes.c_int32, F, P]),
         "ltx_target_positions": (I, [ctypes.c_uint32] * 7 + [F, P]),
         "ltx_reference_positions": (I, [ctypes.c_uint32] * 8 + [F, ctypes.c_uint32, ctypes.c_uint32, P]),
         "ltx_patchify": (I, [V, P] + [ctypes.c_int32] * 5 + [P]),
         "ltx_unpatchify": (I, [V, P] + [ctypes.c_int32] * 5 + [P]),
         "ltx_host_last_error": (ctypes.c_char_p, []),
+        "ltx_comm_unique_id": (I, [P, ctypes.c_size_t]),
+        "ltx_ctx_init_comm": (I, [V, P, ctypes.c_size_t, ctypes.c_int32, ctypes.c_int32]),
+        "ltx_ctx_comm_check": (I, [V]),
+        "ltx_ctx_abort_comm": (None, [V]),
+        "ltx_wait_flag": (I, [V, P, ctypes.c_int32, ctypes.c_uint32]),
+        "ltx_set_flag": (I, [V, P, ctypes.c_int32]),
         "ltx_chunk_plan": (I, [ctypes.c_uint32] * 3 + [ctypes.POINTER(Chunk), ctypes.c_int32,
                                                         ctypes.POINTER(ctypes.c_int32)]),
         "ltx_crossfade_weight": (F, [ctypes.c_uint32, ctypes.c_uint32]),
@@ -126,6 +137,24 @@ class Context:
         if rc != 0:
             msg = lib().ltx_last_error(self.h)
             raise LtxError(rc, f"{what}: {msg.decode() if msg else ''}")
+
+    def init_comm(self, comm_id: bytes, nranks: int, rank: int):
+        """Binds this context to rank `rank` of a tensor-parallel group (collective)."""
+        buf = ctypes.create_string_buffer(bytes(comm_id), COMM_ID_BYTES)
+        self.check(lib().ltx_ctx_init_comm(self.h, buf, COMM_ID_BYTES, nranks, rank), "ltx_ctx_init_comm")
+
+    def comm_check(self):
+        self.check(lib().ltx_ctx_comm_check(self.h), "ltx_ctx_comm_check")
+
+    def abort_comm(self):
+        lib().ltx_ctx_abort_comm(self.h)
+
+    def wait_flag(self, flag, expect: int, timeout_ms: int = 2000):
+        """Enqueues a bounded device-side wait until flag (int32 device tensor/pointer) == expect."""
+        self.check(lib().ltx_wait_flag(self.h, _ptr(flag), expect, timeout_ms), "ltx_wait_flag")
+
+    def set_flag(self, flag, value: int):
+        self.check(lib().ltx_set_flag(self.h, _ptr(flag), value), "ltx_set_flag")
 
     def synchronize(self):
         self.check(lib().ltx_ctx_synchronize(self.h), "synchronize")
@@ -280,6 +309,21 @@ class VideoTransformer:
                                               _ptr(positions), _ptr(ctx_cond), _ptr(ctx_uncond), T, S, sigma,
                                               sigma_next, cfg_scale, rescale_scale), "ltx_denoise_step")
 
+    def denoise_loop(self, latent, clean, mask, positions, ctx_cond, ctx_uncond, sigmas, cfg_scale=1.0,
+                     rescale_scale=0.7, target_tokens=None, out=None, mask_host=None):
+        """euler_denoising_loop + clear_conditioning on the device (ltx_denoise_loop): every
+        step in place on latent [T, C]; the first target_tokens tokens are copied to out."""
+        import numpy as np
+        T = latent.shape[0]
+        S = ctx_cond.shape[0]
+        sig = np.ascontiguousarray(np.asarray(sigmas, np.float32))
+        mh = None if mask_host is None else mask_host.ctypes.data_as(ctypes.c_void_p)
+        tt = T if target_tokens is None else target_tokens
+        self.ctx.check(lib().ltx_denoise_loop(self.h, self.ctx.h, _ptr(latent), _ptr(clean), mh, _ptr(mask),
+                                              _ptr(positions), _ptr(ctx_cond), _ptr(ctx_uncond), T, S,
+                                              sig.ctypes.data_as(ctypes.c_void_p), len(sig), cfg_scale,
+                                              rescale_scale, tt, _ptr(out)), "ltx_denoise_loop")
+
     def close(self):
         if self.h:
             lib().ltx_model_destroy(self.h)
@@ -290,6 +334,13 @@ class VideoTransformer:
             self.close()
         except Exception:
             pass
+
+
+def apply_noise(ctx: "Context", latent, noise, clean, mask, noise_scale):
+    """GaussianNoiser::apply_with_noise in place on latent [T, C] (ltx_apply_noise)."""
+    T, C = latent.shape
+    ctx.check(lib().ltx_apply_noise(ctx.h, _ptr(latent), _ptr(noise), _ptr(clean), _ptr(mask), T, C, noise_scale),
+              "ltx_apply_noise")
 
 
 def scheduler_execute(steps, num_tokens, max_shift=2.05, base_shift=0.95, stretch=True, terminal=0.1):
@@ -389,3 +440,30 @@ def chunk_assemble(ctx: "Context", chunk_tensors, chunks, dst):
     arr = (Chunk * n)(*[Chunk(*c) for c in chunks])
     fv = dst.numel() // max(dst.shape[0], 1)
     ctx.check(lib().ltx_chunk_assemble(ctx.h, ptrs, arr, n, fv, _ptr(dst)), "ltx_chunk_assemble")
+
+
+# ── tensor parallelism ─────────────────────────────────────────────────────────
+
+def comm_unique_id() -> bytes:
+    """A fresh communicator id (host only; rank 0 makes it and shares it)."""
+    buf = ctypes.create_string_buffer(COMM_ID_BYTES)
+    rc = lib().ltx_comm_unique_id(buf, COMM_ID_BYTES)
+    if rc:
+        raise LtxError(rc, lib().ltx_host_last_error().decode())
+    return buf.raw
+
+
+def share_comm_id(group=None) -> bytes:
+    """Rank 0's fresh communicator id, broadcast to every rank of a torch.distributed group."""
+    import torch.distributed as dist
+    obj = [comm_unique_id() if dist.get_rank(group) == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    return obj[0]
+
+
+def init_tensor_parallel(ctx: "Context", group=None):
+    """Binds ctx to this process's rank of a torch.distributed group (collective)."""
+    import torch.distributed as dist
+    rank, ws = dist.get_rank(group), dist.get_world_size(group)
+    if ws > 1:
+        ctx.init_comm(share_comm_id(group), ws, rank)

@@ -283,3 +283,95 @@ def test_wide_model_forward(ctx, tmp_path):
     err = rel_l2(out.cpu().numpy(), exp)
     print(f"\nwide model forward rel-L2 {err:.2e}")
     assert err < 1e-2
+
+
+def _loop_state(cfg, F=4, Hh=8, W=8, S=64, seed=5):
+    rng = np.random.default_rng(seed)
+    C, Tt = cfg["in_channels"], F * Hh * W
+    init = sampler.LatentState(rng.standard_normal((1, Tt, C)).astype(np.float32), np.ones((1, Tt, 1), np.float32),
+                               sampler.target_positions(F, Hh, W), np.zeros((1, Tt, C), np.float32))
+    ref = rng.standard_normal((1, C, F, Hh, W)).astype(np.float32)
+    state = sampler.apply_reference(init, ref, strength=1.0)
+    cc = rng.standard_normal((1, S, cfg["cross_attention_dim"])).astype(np.float32)
+    cu = rng.standard_normal((1, S, cfg["cross_attention_dim"])).astype(np.float32)
+    return state, cc, cu, Tt
+
+
+def test_denoise_loop_equals_steps_and_matches_oracle(ctx, mid_ckpt):
+    """ltx_denoise_loop over 3 sigma pairs == 3 ltx_denoise_step calls (bit-exact: same
+    kernels in the same order), and matches the oracle's euler_denoising_loop."""
+    import ltx_b200
+    cfg, ck, lo, params = mid_ckpt
+    st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+    st.merge_lora(lo, 0.9)
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    state, cc, cu, Tt = _loop_state(cfg)
+    sig = [float(x) for x in sampler.scheduler_execute(8, Tt)[:4]]
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+    clean, mask, pos = dev(state.clean_latent[0]), dev(state.denoise_mask[0, :, 0]), dev(state.positions)
+    lat_a = dev(state.latent[0])
+    for i in range(3):
+        model.denoise_step(lat_a, clean, mask, pos, dev(cc[0]), dev(cu[0]), sig[i], sig[i + 1], 3.0, 0.7)
+    lat_b = dev(state.latent[0])
+    out = torch.full((Tt, cfg["in_channels"]), float("nan"), device="cuda")
+    model.denoise_loop(lat_b, clean, mask, pos, dev(cc[0]), dev(cu[0]), sig, 3.0, 0.7, target_tokens=Tt, out=out)
+    ctx.synchronize()
+    a, b = lat_a.cpu().numpy(), lat_b.cpu().numpy()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), b[:Tt].view(np.uint32))
+    c = dit.DiTConfig.from_json(cfg)
+
+    def model_x0(latent, ts, pos_, ctx_):
+        with torch.no_grad():
+            v = dit.model_forward(params, c, torch.from_numpy(latent), torch.from_numpy(ts), torch.from_numpy(pos_),
+                                  torch.from_numpy(ctx_)).numpy()
+        return sampler.velocity_to_x0(latent, ts, v)
+
+    exp = sampler.euler_loop(sig, state, Tt, model_x0, cc, cu, cfg_scale=3.0, rescale_scale=0.7).latent[0]
+    err = rel_l2(out.cpu().numpy(), exp)
+    d_err = rel_l2(out.cpu().numpy() - state.latent[0, :Tt], exp - state.latent[0, :Tt])
+    print(f"\ndenoise loop (3 steps): target latent rel-L2 {err:.2e}, update rel-L2 {d_err:.2e}")
+    assert err < 1e-2 and d_err < 2e-2
+
+
+def test_denoise_loop_errors(ctx, mid_ckpt):
+    import ltx_b200
+    cfg, ck, lo, _ = mid_ckpt
+    st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    T, C = 64, cfg["in_channels"]
+    z = torch.zeros(T, C, device="cuda")
+    m = torch.ones(T, device="cuda")
+    pos = torch.from_numpy(sampler.target_positions(1, 8, 8)).cuda()
+    cc = torch.zeros(8, cfg["cross_attention_dim"], device="cuda")
+    for sig, kind in (([0.5], "SCHEDULE"), ([], "SCHEDULE"), ([0.9, 0.5, 0.0, 0.0], "SIGMA"),
+                      ([0.9, float("nan")], "SIGMA"), ([0.9, -0.1], "SIGMA")):
+        with pytest.raises(ltx_b200.LtxError) as e:
+            model.denoise_loop(z, z, m, pos, cc, None, sig, 1.0)
+        assert e.value.kind == kind, (sig, e.value)
+    with pytest.raises(ltx_b200.LtxError) as e:
+        model.denoise_loop(z, z, m, pos, cc, None, [0.9, 0.0], 1.0, target_tokens=T + 1)
+    assert e.value.kind == "TARGET_TOKENS"
+    with pytest.raises(ltx_b200.LtxError) as e:
+        model.denoise_loop(z, z, m, pos, cc, None, [0.9, 0.0], 3.0)
+    assert e.value.kind == "NEGATIVE_CONTEXT"
+    # nothing ran: the latent is untouched
+    assert float(z.abs().sum()) == 0.0
+
+
+def test_apply_noise_bit_exact(ctx):
+    import ltx_b200
+    rng = np.random.default_rng(2)
+    T, C = 1000, 128
+    lat = rng.standard_normal((1, T, C)).astype(np.float32)
+    noise = rng.standard_normal((1, T, C)).astype(np.float32)
+    clean = rng.standard_normal((1, T, C)).astype(np.float32)
+    mask = rng.choice(np.array([0.0, 0.25, 1.0], np.float32), size=(1, T, 1))
+    st = sampler.LatentState(lat, mask, None, clean)
+    for s in (1.0, 0.731, 0.0):
+        exp = sampler.apply_noise(st, noise, s).latent[0]
+        d = torch.from_numpy(lat[0].copy()).cuda()
+        ltx_b200.apply_noise(ctx, d, torch.from_numpy(noise[0]).cuda(), torch.from_numpy(clean[0]).cuda(),
+                             torch.from_numpy(mask[0, :, 0].copy()).cuda(), s)
+        ctx.synchronize()
+        assert np.array_equal(d.cpu().numpy().view(np.uint32), exp.view(np.uint32)), s

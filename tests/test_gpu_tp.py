@@ -1,0 +1,105 @@
+"""Tensor-parallel model (heads and FFN units split over two GPUs, allreduce
+after each row-split projection) against the same model on one GPU.
+
+Needs two GPUs; each rank is a spawned process.  The whole model on one GPU
+is the reference: same seed, same synthetic FP8 + LoRA weights (every shard
+count generates the full tensors, then keeps its part), same inputs.  The
+ranks' sums come in a different order than the single GPU's fused epilogue,
+so the comparison is by relative L2, not bits.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")]
+
+
+def _rel_l2(a, b):
+    return float(np.linalg.norm((a - b).ravel()) / max(np.linalg.norm(b.ravel()), 1e-30))
+
+
+def _cfg(heads, head_dim, layers):
+    from dit_checkpoint import small_config
+    return small_config(heads=heads, head_dim=head_dim, layers=layers)
+
+
+def _worker(rank, ws, port, cfg, T_frames, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+    import ltx_b200
+    from oracle import sampler
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=timedelta(seconds=90))
+    try:
+        ctx = ltx_b200.Context(rank)
+        ltx_b200.init_tensor_parallel(ctx)
+        cj = json.dumps(cfg)
+        model = ltx_b200.VideoTransformer.init_random(ctx, cj, seed=21, lora_rank=8, lora_strength=0.8)
+        F, Hh, W, S = T_frames, 8, 8, 40
+        rng = np.random.default_rng(4)
+        Tt = F * Hh * W
+        T = 2 * Tt
+        C, Dc = cfg["in_channels"], cfg["cross_attention_dim"]
+        lat = rng.standard_normal((1, T, C)).astype(np.float32)
+        ts = np.concatenate([np.full(Tt, 0.6, np.float32), np.zeros(Tt, np.float32)])[None]
+        pos = np.concatenate([sampler.target_positions(F, Hh, W), sampler.reference_positions(F, Hh, W)], axis=2)
+        ctxt = rng.standard_normal((1, S, Dc)).astype(np.float32)
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+        out = torch.empty(lat.shape, device="cuda")
+        model.forward(dev(lat), dev(ts), dev(pos), dev(ctxt), out)
+        # one guided Euler step on the replicated latent
+        clean = np.concatenate([np.zeros((Tt, C), np.float32), rng.standard_normal((Tt, C)).astype(np.float32)])
+        mask = np.concatenate([np.ones(Tt, np.float32), np.zeros(Tt, np.float32)])
+        unc = rng.standard_normal((S, Dc)).astype(np.float32)
+        lat_s = dev(lat[0])
+        model.denoise_step(lat_s, dev(clean), dev(mask), dev(pos), dev(ctxt[0]), dev(unc), 0.8, 0.6, 3.0, 0.7)
+        ctx.synchronize()
+        ctx.comm_check()
+        got_f, got_s = out.cpu().numpy(), lat_s.cpu().numpy()
+        outs = [None] * ws
+        dist.all_gather_object(outs, (got_f, got_s))
+        if rank == 0:
+            # the whole model on this GPU, no communicator
+            ctx1 = ltx_b200.Context(0)
+            m1 = ltx_b200.VideoTransformer.init_random(ctx1, cj, seed=21, lora_rank=8, lora_strength=0.8)
+            ref = torch.empty(lat.shape, device="cuda")
+            m1.forward(dev(lat), dev(ts), dev(pos), dev(ctxt), ref)
+            lat1 = dev(lat[0])
+            m1.denoise_step(lat1, dev(clean), dev(mask), dev(pos), dev(ctxt[0]), dev(unc), 0.8, 0.6, 3.0, 0.7)
+            ctx1.synchronize()
+            ref_f, ref_s = ref.cpu().numpy(), lat1.cpu().numpy()
+            same_ranks = all(np.array_equal(o[0], outs[0][0]) and np.array_equal(o[1], outs[0][1]) for o in outs)
+            q.put((same_ranks, _rel_l2(got_f, ref_f), _rel_l2(got_s - lat[0], ref_s - lat[0])))
+            m1.close()
+            ctx1.close()
+        model.close()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("heads,head_dim,layers,frames", [(4, 128, 2, 2), (32, 128, 1, 1)])
+def test_tensor_parallel_two_gpus_matches_one(heads, head_dim, layers, frames):
+    import socket
+    import torch.multiprocessing as mp
+    cfg = _cfg(heads, head_dim, layers)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mctx = mp.get_context("spawn")
+    q = mctx.Queue()
+    procs = [mctx.Process(target=_worker, args=(r, 2, port, cfg, frames, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    same, err_f, err_s = q.get(timeout=5)
+    print(f"\nTP x2 ({heads} heads, {layers} layers): forward rel-L2 {err_f:.2e}, step update rel-L2 {err_s:.2e}")
+    assert same, "ranks disagree on the replicated output"
+    assert err_f < 1e-2 and err_s < 1e-2
