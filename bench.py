@@ -113,6 +113,14 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+_T0 = time.time()
+
+
+def _log(msg):
+    """Progress on stderr (the JSON result line is the only stdout)."""
+    print(f"[bench {time.time() - _T0:7.1f}s] {msg}", file=sys.stderr, flush=True)
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -275,6 +283,7 @@ def run_denoise_step(args, rank, ws, device):
                                                   lora_strength=1.0)
     ctx.synchronize()
     load_s = time.time() - t0
+    _log(f"model initialised in {load_s:.1f}s")
     inp = make_step_inputs(LAT_F, LAT_H, LAT_W, S_CTX, D, seed=100 if tp else 100 + rank)
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
     lat0 = inp["latent"]
@@ -292,6 +301,7 @@ def run_denoise_step(args, rank, ws, device):
     for i in range(args.warmup):
         step(i)
     ctx.synchronize()
+    _log(f"{args.warmup} warm-up steps done")
     stream = torch.cuda.current_stream()
     barrier(ws)
     torch.cuda.synchronize()
@@ -305,6 +315,7 @@ def run_denoise_step(args, rank, ws, device):
     ctx.synchronize()
     barrier(ws)
     ms = max_over_ranks(start.elapsed_time(end) / args.steps, ws)
+    _log(f"{args.steps} timed steps: {ms:.1f} ms/step")
     # e2e through the C ABI from host buffers: pinned latent in, new latent out, each step
     lat_h = torch.from_numpy(np.ascontiguousarray(lat0, np.float32)).pin_memory()
     out_h = torch.empty_like(lat_h).pin_memory()
@@ -320,6 +331,7 @@ def run_denoise_step(args, rank, ws, device):
     e2.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / n_e2e, ws)
+    _log(f"e2e: {e2e_ms:.1f} ms/step")
     ok = bool(torch.isfinite(out_h).all())
     # dominant kernel timed alone: FFN-in GEMM (GELU epilogue) at the step's shape
     M, N, K = 2 * T_TOTAL, FF, D
@@ -335,6 +347,7 @@ def run_denoise_step(args, rank, ws, device):
     ge.record(stream)
     torch.cuda.synchronize()
     gemm_ms = gs.elapsed_time(ge) / 10
+    _log(f"FFN-in GEMM alone: {gemm_ms:.3f} ms")
     del a, w, o
     peaks, src = measured_peaks()
     total, gemm_f, attn_f = step_flops()
@@ -527,13 +540,16 @@ def main():
         res = run_denoise_step(args, rank, ws, local)
         dq_args = argparse.Namespace(steps=20, warmup=5)
         dq = run_dequant_merge(dq_args, rank, ws, local)
+        _log(f"dequant+merge: {dq['value']:.0f} GB/s")
         if rank == 0:
             res.update({"n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
                         "data": "synthetic (random-init FP8+LoRA weights, N(0,1) latent/reference/contexts)"})
             res["dequant_merge"] = {k: dq[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "e2e")}
             if ws == 1 and args.cpu_seconds > 0:
                 res["cpu_baseline"] = cpu_baseline_step(blocks=1)
+                _log(f"CPU baseline (one block): {res['cpu_baseline']['sample']}")
                 res["dequant_merge"]["cpu_baseline"] = cpu_baseline_dequant(seconds=min(args.cpu_seconds, 3.0))
+                _log("CPU dequant baseline done")
             print(json.dumps(res))
     if ws > 1:
         import torch.distributed as dist

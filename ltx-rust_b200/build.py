@@ -47,6 +47,8 @@ def compile_one(src, force, extra):
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         return obj, f"{' '.join(cmd)}\n{r.stdout}\n{r.stderr}"
+    if extra and r.stderr:
+        print(r.stderr, end="")   # -Xptxas -v: registers, spills, shared memory
     return obj, None
 
 

@@ -238,7 +238,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m_ref = -INFINITY;   // the max P is taken against
         float l = 0.f;
         for (int j = 0; j < n_kv && !aborted; ++j) {
-            if (!mbar_wait(&s_full[t], j & 1, p.timeout_flag, 211, &aborted)) break;
+            // warp-uniform outcome: the tcgen05.ld/st below are warp-collective
+            if (!warp_wait(&s_full[t], j & 1, p.timeout_flag, 211, &aborted)) break;
             tc_fence_after();
             const int kv0 = j * BKV;
             const bool ragged = kv0 + BKV > p.Tk;   // only the last tile can be
@@ -256,10 +257,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             mx *= p.scale_log2;   // scale > 0: max(s * scale) = scale * max(s)
-            if (mx > m_ref + kRescaleLog2) {
+            // The rows of one warp decide together: tcgen05.ld/st are
+            // warp-collective (.sync.aligned), so the O rescale runs for the
+            // whole warp when any of its rows needs it; a row that does not
+            // keeps its reference (alpha = 1).
+            const bool grow = mx > m_ref + kRescaleLog2;
+            if (__any_sync(0xffffffffu, grow)) {
                 // O_t and l are relative to m_ref; move them to mx.  P.V of the
                 // previous tile has completed (its commit preceded this S).
-                const float alpha = ex2(m_ref - mx);   // 0 when m_ref = -inf
+                const float alpha = grow ? ex2(m_ref - mx) : 1.0f;   // 0 when m_ref = -inf
                 if (j > 0) {
                     const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
@@ -278,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st_wait();
                 }
                 l *= alpha;
-                m_ref = mx;
+                if (grow) m_ref = mx;
             }
             // pass 2: P = exp2(s * scale - m_ref) (<= 2^kRescaleLog2), two per MUFU op; row sum in f32.
             const float2 nm2 = make_float2(-m_ref, -m_ref);
@@ -324,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(&p_full[t]);
         }
         // O_t is final once the last P.V has completed.
-        if (!aborted && mbar_wait(&pv_done[t], (n_kv - 1) & 1, p.timeout_flag, 212, &aborted)) {
+        if (!aborted && warp_wait(&pv_done[t], (n_kv - 1) & 1, p.timeout_flag, 212, &aborted)) {
             tc_fence_after();
             const int q_row = qt * 2 * BQ + t * BQ + row_in_tile;
             const float inv = 1.f / l;

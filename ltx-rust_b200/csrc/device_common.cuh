@@ -112,6 +112,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *f
     return true;
 }
 
+// mbar_wait by every lane of a warp with one outcome for the whole warp: it
+// fails (and aborts every lane) if any lane's wait failed.  Use it before
+// warp-collective instructions (tcgen05.ld/st .sync.aligned), which must not
+// be reached by part of a warp.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *flag, int code, bool *aborted) {
+    const bool ok = mbar_wait(bar, parity, flag, code, aborted);
+    if (__all_sync(0xffffffffu, ok)) return true;
+    *aborted = true;
+    return false;
+}
+
 // ── TMA ─────────────────────────────────────────────────────────────────────
 
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, uint64_t *bar, int x, int y) {

@@ -173,7 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int mb, nb;
             tile_coords(t, m_blocks, n_blocks, mb, nb);
             const uint32_t acc = tile_i & 1, aph = (tile_i >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], aph, p.timeout_flag, 104, &aborted)) break;
+            // warp-uniform outcome: the tcgen05.ld below are warp-collective
+            if (!warp_wait(&tfull[acc], aph, p.timeout_flag, 104, &aborted)) break;
             tc_fence_after();
             const int row = mb * BM + quad * 32 + lane;
             const bool row_ok = row < p.M;

@@ -64,6 +64,28 @@ def test_attention_strided_qkv(ctx):
     assert rel_l2(out.float(), ref) < 1e-2
 
 
+@pytest.mark.parametrize("Tq,Tk", [(512, 1024), (300, 777)])
+def test_attention_row_max_grows_unevenly(ctx, Tq, Tk):
+    """Logits whose row maxima grow along the keys at different rates per query
+    row: the lazy O rescale then triggers for some rows of a warp and not for
+    others, which a warp-collective TMEM access must handle (deep DiT layers
+    produce such logits; N(0,1) inputs almost never do)."""
+    import ltx_b200
+    B, H = 1, 2
+    g = torch.Generator(device="cuda").manual_seed(Tq + Tk)
+    row_gain = 1.0 + 10.0 * (torch.rand(B * Tq, 1, device="cuda", generator=g) > 0.5).float()
+    key_gain = 0.2 + 3.0 * torch.arange(B * Tk, device="cuda").float().view(-1, 1) / (B * Tk)
+    q = (torch.randn(B * Tq, H * 128, device="cuda", generator=g) * row_gain).to(torch.bfloat16)
+    k = (torch.randn(B * Tk, H * 128, device="cuda", generator=g) * key_gain).to(torch.bfloat16)
+    v = torch.randn(B * Tk, H * 128, device="cuda", generator=g).to(torch.float16)
+    out = torch.zeros(B * Tq, H * 128, device="cuda", dtype=torch.bfloat16)
+    scale = 1.0 / math.sqrt(128)
+    ltx_b200.attention(ctx, q, k, v, out, B, H, Tq, Tk, scale)
+    ctx.synchronize()
+    ref = ref_attention(q, k, v, B, H, Tq, Tk, scale).reshape(B * Tq, H * 128)
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
 def test_attention_full_size(ctx):
     """The config-3/4 self-attention shape: B=2 (CFG), H=32, T=12288; checked on sampled rows."""
     import ltx_b200
