@@ -13,7 +13,7 @@
 //   Two TMEM accumulators (2 x BN columns) let the epilogue of tile i run
 //   under the mainloop of tile i+1.  Tiles are walked in groups of 16
 //   M-blocks so the A panel and the W panel of concurrent tiles stay in L2.
-// No TMA multicast anywhere: each CTA loads its own tiles from local HBM.
+// Each CTA loads its own tiles from local HBM; no load is shared across a cluster.
 #include <cuda.h>
 
 #include "device_common.cuh"
