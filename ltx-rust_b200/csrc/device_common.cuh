@@ -172,6 +172,17 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
         "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f8f6f4 (both operands e4m3,
+// K = 32 per instruction: one 128-byte swizzle row holds 128 of them).
+__device__ __forceinline__ void umma_f8_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
 // Arrives once on `bar` when all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -185,6 +196,15 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool b
            | ((bf16 ? 1u : 0u) << 7)                  // A format
            | ((bf16 ? 1u : 0u) << 10)                 // B format
            | ((b_mn_major ? 1u : 0u) << 16)           // B major
+           | ((uint32_t)(N >> 3) << 17)               // N / 8
+           | ((uint32_t)(M >> 4) << 24);              // M / 16
+}
+
+// Instruction descriptor for kind::f8f6f4 with f32 accumulation: A and B both
+// e4m3 (format code 0), K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
+    return (1u << 4)                                   // D format f32
+           | (0u << 7) | (0u << 10)                   // A, B format e4m3
            | ((uint32_t)(N >> 3) << 17)               // N / 8
            | ((uint32_t)(M >> 4) << 24);              // M / 16
 }

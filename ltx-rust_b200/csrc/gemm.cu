@@ -31,6 +31,8 @@ enum GemmEpilogue : int {
 
 struct GemmParams {
     int M, N, K;
+    const float *a_scale;   // FP8 operands: per-row scale of A [M] (null = 1)
+    float w_scale;          // FP8 operands: per-tensor scale of W
     const float *bias;      // [N] or null
     void *out;              // bf16 / f32 [M, ldo]
     int64_t ldo;
@@ -47,11 +49,16 @@ constexpr int BM = 128, BK = 64;
 constexpr int kGroupM = 16;
 constexpr int kThreads = 192;
 
-template <int BN>
+// F8: e4m3 operands (kind::f8f6f4), 128 elements of K per stage; otherwise
+// bf16 (kind::f16), 64 per stage.  Either way a stage row is one 128-byte
+// swizzle row, so the tile bytes, the descriptors and the 4 MMAs per stage
+// (K = 32 e4m3 or 16 bf16 each, +32 bytes apart) are the same.
+template <int BN, bool F8 = false>
 struct GemmCfg {
     static constexpr int STAGES = BN == 256 ? 4 : 6;
-    static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int BKE = F8 ? 128 : 64;   // K elements per stage
+    static constexpr int A_BYTES = BM * 128;
+    static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;  // power of two >= 32
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
@@ -73,10 +80,10 @@ __device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, i
     nb = r / gm;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool F8>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
-    using C = GemmCfg<BN>;
+    using C = GemmCfg<BN, F8>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *sA = smem;
@@ -90,7 +97,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_blocks = (p.M + BM - 1) / BM, n_blocks = (p.N + BN - 1) / BN;
     const int num_tiles = m_blocks * n_blocks;
-    const int k_blocks = (p.K + BK - 1) / BK;
+    const int k_blocks = (p.K + C::BKE - 1) / C::BKE;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -126,8 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t ph = (it / C::STAGES) & 1;
                     if (!mbar_wait(&empty[s], ph ^ 1, p.timeout_flag, 101, &aborted)) break;
                     mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-                    tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * BK, mb * BM);
-                    tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * BK, nb * BN);
+                    tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * C::BKE, mb * BM);
+                    tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * C::BKE, nb * BN);
                 }
             }
             if (aborted) {
@@ -139,7 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         if (elect_one()) {
-            constexpr uint32_t idesc = idesc_f16(BM, BN, true);
+            constexpr uint32_t idesc = F8 ? idesc_e4m3(BM, BN) : idesc_f16(BM, BN, true);
             uint32_t it = 0, tile_i = 0;
             for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tile_i) {
                 const uint32_t acc = tile_i & 1, aph = (tile_i >> 1) & 1;
@@ -154,10 +161,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
+                    for (int kk = 0; kk < 4; ++kk) {
                         const uint64_t ad = sdesc_sw128(a_addr + kk * 32, 16, 1024);
                         const uint64_t bd = sdesc_sw128(b_addr + kk * 32, 16, 1024);
-                        umma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+                        if constexpr (F8)
+                            umma_f8_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+                        else
+                            umma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
                     }
                     umma_commit(&empty[s]);
                 }
@@ -190,6 +200,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                if constexpr (F8) {
+                    // acc is in units of (row scale x weight scale)
+                    const float sc = (p.a_scale ? __ldg(p.a_scale + row) : 1.0f) * p.w_scale;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] *= sc;
+                }
                 const bool full_cols = col0 + 32 <= p.N;
                 if (p.bias) {
 #pragma unroll
@@ -295,23 +311,28 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D bf16 row-major [rows, cols] with leading dimension ld (elements), box {64, box_rows}.
-bool make_tmap_bf16(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// 2-D row-major [rows, cols] of 1- or 2-byte elements with leading dimension
+// ld (elements); the box is one 128-byte swizzle row wide: {128 / es, box_rows}.
+bool make_tmap_2d(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows, int es) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return fn(m, es == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr),
+              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int EPI>
+bool make_tmap_bf16(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+    return make_tmap_2d(m, ptr, rows, cols, ld, box_rows, 2);
+}
+
+template <int BN, int EPI, bool F8>
 cudaError_t launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int sms, cudaStream_t st) {
-    using C = GemmCfg<BN>;
-    auto k = gemm_kernel<BN, EPI>;
+    using C = GemmCfg<BN, F8>;
+    auto k = gemm_kernel<BN, EPI, F8>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return e;
     const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
@@ -320,15 +341,45 @@ cudaError_t launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const Gemm
     return cudaGetLastError();
 }
 
-template <int BN>
+template <int BN, bool F8>
 cudaError_t dispatch_epi(int epi, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int sms,
                          cudaStream_t st) {
     switch (epi) {
-    case EPI_BF16: return launch_gemm<BN, EPI_BF16>(ta, tb, p, sms, st);
-    case EPI_GELU_BF16: return launch_gemm<BN, EPI_GELU_BF16>(ta, tb, p, sms, st);
-    case EPI_F32: return launch_gemm<BN, EPI_F32>(ta, tb, p, sms, st);
-    default: return launch_gemm<BN, EPI_RESID>(ta, tb, p, sms, st);
+    case EPI_BF16: return launch_gemm<BN, EPI_BF16, F8>(ta, tb, p, sms, st);
+    case EPI_GELU_BF16: return launch_gemm<BN, EPI_GELU_BF16, F8>(ta, tb, p, sms, st);
+    case EPI_F32: return launch_gemm<BN, EPI_F32, F8>(ta, tb, p, sms, st);
+    default: return launch_gemm<BN, EPI_RESID, F8>(ta, tb, p, sms, st);
     }
+}
+
+// Shared by the bf16 and e4m3 entry points: es = element bytes (2 or 1).
+int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, const float *a_scale, const void *W,
+             int64_t ldw, float w_scale, int M, int N, int K, int epi, const float *bias, void *out, int64_t ldo,
+             const float *gate, const int *gate_idx, int64_t ld_gate, int f16_from_col) {
+    if (!A || !W || !out) return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: null pointer");
+    if (M <= 0 || N <= 0 || K <= 0) return fail(ctx, LTX_ERR_SHAPE, "gemm: empty shape %d x %d x %d", M, N, K);
+    const int align = 16 / es;   // elements per 16 bytes (TMA strides and the innermost coordinate)
+    if (lda % align || ldw % align || lda < K || ldw < K || ((uintptr_t)A & 15) || ((uintptr_t)W & 15))
+        return fail(ctx, LTX_ERR_SHAPE, "gemm: operands need 16-byte aligned rows (lda %lld ldw %lld)", (long long)lda,
+                    (long long)ldw);
+    if (epi < EPI_BF16 || epi > EPI_RESID) return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: bad epilogue %d", epi);
+    const int BN = N <= 128 ? 128 : 256;
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, A, M, K, lda, BM, es) || !make_tmap_2d(&tb, W, N, K, ldw, BN, es))
+        return fail(ctx, LTX_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed");
+    if (f16_from_col < 0 || f16_from_col > N) f16_from_col = N;
+    if (f16_from_col < N && (epi != EPI_BF16 || f16_from_col % 32))
+        return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: f16 columns need the bf16 epilogue and a multiple of 32");
+    GemmParams p{M, N, K, a_scale, w_scale, bias, out, ldo, gate, gate_idx, ld_gate, ctx->timeout_flag, f16_from_col};
+    cudaError_t e;
+    if (es == 1)
+        e = BN == 128 ? dispatch_epi<128, true>(epi, ta, tb, p, ctx->sm_count, st)
+                      : dispatch_epi<256, true>(epi, ta, tb, p, ctx->sm_count, st);
+    else
+        e = BN == 128 ? dispatch_epi<128, false>(epi, ta, tb, p, ctx->sm_count, st)
+                      : dispatch_epi<256, false>(epi, ta, tb, p, ctx->sm_count, st);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm launch");
+    return LTX_OK;
 }
 
 }  // namespace
@@ -338,24 +389,17 @@ cudaError_t dispatch_epi(int epi, const CUtensorMap &ta, const CUtensorMap &tb, 
 int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
               int K, int epi, const float *bias, void *out, int64_t ldo, const float *gate, const int *gate_idx,
               int64_t ld_gate, int f16_from_col) {
-    if (!A || !W || !out) return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: null pointer");
-    if (M <= 0 || N <= 0 || K <= 0) return fail(ctx, LTX_ERR_SHAPE, "gemm: empty shape %d x %d x %d", M, N, K);
-    if (lda % 8 || ldw % 8 || lda < K || ldw < K || ((uintptr_t)A & 15) || ((uintptr_t)W & 15))
-        return fail(ctx, LTX_ERR_SHAPE, "gemm: operands need 16-byte aligned rows (lda %lld ldw %lld)", (long long)lda,
-                    (long long)ldw);
-    if (epi < EPI_BF16 || epi > EPI_RESID) return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: bad epilogue %d", epi);
-    const int BN = N <= 128 ? 128 : 256;
-    CUtensorMap ta, tb;
-    if (!make_tmap_bf16(&ta, A, M, K, lda, BM) || !make_tmap_bf16(&tb, W, N, K, ldw, BN))
-        return fail(ctx, LTX_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed");
-    if (f16_from_col < 0 || f16_from_col > N) f16_from_col = N;
-    if (f16_from_col < N && (epi != EPI_BF16 || f16_from_col % 32))
-        return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: f16 columns need the bf16 epilogue and a multiple of 32");
-    GemmParams p{M, N, K, bias, out, ldo, gate, gate_idx, ld_gate, ctx->timeout_flag, f16_from_col};
-    cudaError_t e = BN == 128 ? dispatch_epi<128>(epi, ta, tb, p, ctx->sm_count, st)
-                              : dispatch_epi<256>(epi, ta, tb, p, ctx->sm_count, st);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm launch");
-    return LTX_OK;
+    return gemm_any(ctx, st, 2, A, lda, nullptr, W, ldw, 1.0f, M, N, K, epi, bias, out, ldo, gate, gate_idx, ld_gate,
+                    f16_from_col);
+}
+
+// The same with e4m3 A and W (leading dimensions multiples of 16): the
+// accumulator is multiplied by a_scale[row] * w_scale before the epilogue.
+int gemm_e4m3(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const float *a_scale, const void *W,
+              int64_t ldw, float w_scale, int M, int N, int K, int epi, const float *bias, void *out, int64_t ldo,
+              const float *gate, const int *gate_idx, int64_t ld_gate, int f16_from_col) {
+    return gemm_any(ctx, st, 1, A, lda, a_scale, W, ldw, w_scale, M, N, K, epi, bias, out, ldo, gate, gate_idx, ld_gate,
+                    f16_from_col);
 }
 
 }  // namespace ltx
@@ -366,4 +410,13 @@ extern "C" int ltx_gemm_bf16(ltx_ctx *ctx, const void *a_dev, int64_t lda, const
     if (!ctx) return LTX_ERR_INVALID_ARG;
     return ltx::gemm_bf16(ctx, ctx->stream, a_dev, lda, w_dev, ldw, m, n, k, epilogue, bias_dev, out_dev, ldo, gate_dev,
                           gate_idx_dev, ld_gate, n);
+}
+
+extern "C" int ltx_gemm_e4m3(ltx_ctx *ctx, const void *a_dev, int64_t lda, const float *a_scale_dev, const void *w_dev,
+                             int64_t ldw, float w_scale, int32_t m, int32_t n, int32_t k, int32_t epilogue,
+                             const float *bias_dev, void *out_dev, int64_t ldo, const float *gate_dev,
+                             const int32_t *gate_idx_dev, int64_t ld_gate) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    return ltx::gemm_e4m3(ctx, ctx->stream, a_dev, lda, a_scale_dev, w_dev, ldw, w_scale, m, n, k, epilogue, bias_dev,
+                          out_dev, ldo, gate_dev, gate_idx_dev, ld_gate, n);
 }

@@ -16,6 +16,10 @@ int dequant_merge(ltx_ctx *ctx, cudaStream_t stream, const void *w, int w_dt, in
 int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
               int K, int epi, const float *bias, void *out, int64_t ldo, const float *gate, const int *gate_idx,
               int64_t ld_gate, int f16_from_col = 1 << 30);
+// e4m3 operands (lda/ldw multiples of 16); acc * a_scale[row] * w_scale before the epilogue
+int gemm_e4m3(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const float *a_scale, const void *W,
+              int64_t ldw, float w_scale, int M, int N, int K, int epi, const float *bias, void *out, int64_t ldo,
+              const float *gate, const int *gate_idx, int64_t ld_gate, int f16_from_col = 1 << 30);
 
 // attention.cu (head_dim 128)
 int attention_fwd(ltx_ctx *ctx, cudaStream_t st, const void *q, int64_t ldq, const void *k, int64_t ldk, const void *v,

@@ -69,6 +69,8 @@ def lib() -> ctypes.CDLL:
                                   ctypes.POINTER(LoraDelta), ctypes.c_int32, P, ctypes.c_int32]),
         "ltx_gemm_bf16": (I, [V, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                               P, P, I64, P, P, I64]),
+        "ltx_gemm_e4m3": (I, [V, P, I64, P, P, I64, F, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                              P, P, I64, P, P, I64]),
         "ltx_attention_fwd": (I, [V, P, I64, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                   ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, F, P, I64]),
         "ltx_store_open": (I, [V, ctypes.POINTER(ctypes.c_char_p), ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(V)]),
@@ -195,6 +197,16 @@ def gemm(ctx: "Context", a, w, out, epilogue=EPI_BF16, bias=None, gate=None, gat
     ctx.check(lib().ltx_gemm_bf16(ctx.h, _ptr(a), a.stride(0), _ptr(w), w.stride(0), M, N, K, epilogue,
                                   _ptr(bias), _ptr(out), out.stride(0), _ptr(gate), _ptr(gate_idx),
                                   gate.stride(0) if gate is not None else 0), "ltx_gemm_bf16")
+
+
+def gemm_e4m3(ctx: "Context", a, a_scale, w, w_scale, out, epilogue=EPI_BF16, bias=None, gate=None, gate_idx=None):
+    """out = epilogue((a * a_scale[:, None]) @ (w * w_scale).T) with e4m3 operands held as
+    uint8 (or float8_e4m3fn) CUDA tensors a [M,K], w [N,K]; a_scale f32 [M] or None."""
+    M, K = a.shape
+    N = w.shape[0]
+    ctx.check(lib().ltx_gemm_e4m3(ctx.h, _ptr(a), a.stride(0), _ptr(a_scale), _ptr(w), w.stride(0), float(w_scale),
+                                  M, N, K, epilogue, _ptr(bias), _ptr(out), out.stride(0), _ptr(gate), _ptr(gate_idx),
+                                  gate.stride(0) if gate is not None else 0), "ltx_gemm_e4m3")
 
 
 def attention(ctx: "Context", q, k, v, out, batch, heads, tq, tk, scale, head_dim=128):

@@ -1,7 +1,7 @@
 """Times one library kernel at a chosen shape (CUDA events, after warm-up).
 
     python ltx-rust_b200/ltx_b200/kernel_bench.py attention --B 1 --H 8 --T 4096 [--Tk N] [--iters 3]
-    python ltx-rust_b200/ltx_b200/kernel_bench.py gemm --M 4096 --N 4096 --K 4096 [--epi 0..3]
+    python ltx-rust_b200/ltx_b200/kernel_bench.py gemm --M 4096 --N 4096 --K 4096 [--epi 0..3] [--fp8]
     python ltx-rust_b200/ltx_b200/kernel_bench.py merge --rows 4096 --cols 4096 --rank 64
 
 Used for small, self-contained profiler captures of a single kernel and for
@@ -39,6 +39,7 @@ def main():
     ap.add_argument("--N", type=int, default=4096)
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--epi", type=int, default=0)
+    ap.add_argument("--fp8", action="store_true", help="gemm: e4m3 operands (native FP8)")
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--cols", type=int, default=4096)
     ap.add_argument("--rank", type=int, default=64)
@@ -57,13 +58,19 @@ def main():
         flops = 4.0 * a.B * a.H * a.T * Tk * 128
         unit = "TFLOP/s"
     elif a.kernel == "gemm":
-        x = torch.randn(a.M, a.K, device="cuda", generator=g).to(torch.bfloat16)
-        w = (torch.randn(a.N, a.K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
         if a.epi in (2, 3):
             o = torch.zeros(a.M, a.N, device="cuda")
         else:
             o = torch.empty(a.M, a.N, device="cuda", dtype=torch.bfloat16)
-        fn = lambda: ltx_b200.gemm(ctx, x, w, o, a.epi)
+        if a.fp8:
+            x = torch.randn(a.M, a.K, device="cuda", generator=g).to(torch.float8_e4m3fn).view(torch.uint8)
+            w = torch.randn(a.N, a.K, device="cuda", generator=g).to(torch.float8_e4m3fn).view(torch.uint8)
+            sa = torch.full((a.M,), 0.05, device="cuda")
+            fn = lambda: ltx_b200.gemm_e4m3(ctx, x, sa, w, 0.02, o, a.epi)
+        else:
+            x = torch.randn(a.M, a.K, device="cuda", generator=g).to(torch.bfloat16)
+            w = (torch.randn(a.N, a.K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+            fn = lambda: ltx_b200.gemm(ctx, x, w, o, a.epi)
         flops = 2.0 * a.M * a.N * a.K
         unit = "TFLOP/s"
     else:

@@ -109,3 +109,60 @@ def test_gemm_throughput_report(ctx):
     ref_ms = s.elapsed_time(e) / 10
     print(f"\nGEMM {M}x{N}x{K}: {ms:.3f} ms = {2 * M * N * K / ms / 1e9:.1f} TFLOP/s; "
           f"torch/cuBLAS {ref_ms:.3f} ms = {2 * M * N * K / ref_ms / 1e9:.1f} TFLOP/s")
+
+
+def _e4m3(x, per_row):
+    """Quantise to e4m3 with scale amax/448 (per row or per tensor): (uint8 bits, scale, dequantised f32)."""
+    amax = x.abs().amax(dim=1, keepdim=True) if per_row else x.abs().max()
+    s = (amax / 448.0).clamp_min(1e-30)
+    q = (x / s).to(torch.float8_e4m3fn)
+    return q.view(torch.uint8), s.reshape(-1).float(), q.float() * s
+
+
+@pytest.mark.parametrize("M,N,K,epi", [(128, 256, 128, 0), (300, 1000, 272, 0), (256, 512, 4096, 1),
+                                       (1000, 128, 4096, 2), (2048, 4096, 16384, 3), (77, 8, 48, 2)])
+def test_gemm_e4m3_against_dequantised_fp32(ctx, M, N, K, epi):
+    """Native FP8: e4m3 A (per-row scale) and W (per-tensor scale).  The reference is the
+    fp32 product of the dequantised operands, so the only differences are the f32
+    accumulation order and the output rounding."""
+    import ltx_b200
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + epi)
+    a32 = torch.randn(M, K, device="cuda", generator=g) * (1 + torch.rand(M, 1, device="cuda", generator=g) * 4)
+    w32 = torch.randn(N, K, device="cuda", generator=g) * 0.02
+    aq, a_s, a_deq = _e4m3(a32, True)
+    wq, w_s, w_deq = _e4m3(w32, False)
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    ref = a_deq @ w_deq.t() + bias
+    if epi == ltx_b200.EPI_GELU_BF16:
+        ref = torch.nn.functional.gelu(ref, approximate="tanh")
+    if epi in (ltx_b200.EPI_BF16, ltx_b200.EPI_GELU_BF16):
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    else:
+        out = torch.zeros(M, N, device="cuda")
+    gate = torch.rand(2, N, device="cuda", generator=g) if epi == ltx_b200.EPI_RESID else None
+    gidx = (torch.arange(M, device="cuda", dtype=torch.int32) % 2) if gate is not None else None
+    ltx_b200.gemm_e4m3(ctx, aq, a_s, wq, float(w_s), out, epi, bias, gate, gidx)
+    ctx.synchronize()
+    if gate is not None:
+        ref = ref * gate[gidx.long()]
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
+def test_gemm_e4m3_throughput(ctx):
+    """FFN-in shape of the step (informational): e4m3 vs bf16 on the same shape."""
+    import ltx_b200
+    M, N, K = 24576, 16384, 4096
+    a = torch.randint(0, 120, (M, K), device="cuda", dtype=torch.uint8)
+    w = torch.randint(0, 120, (N, K), device="cuda", dtype=torch.uint8)
+    sa = torch.full((M,), 0.01, device="cuda")
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):
+        ltx_b200.gemm_e4m3(ctx, a, sa, w, 0.01, out, ltx_b200.EPI_GELU_BF16)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(5):
+        ltx_b200.gemm_e4m3(ctx, a, sa, w, 0.01, out, ltx_b200.EPI_GELU_BF16)
+    e.record()
+    ctx.synchronize()
+    ms = s.elapsed_time(e) / 5
+    print(f"\ne4m3 GEMM {M}x{N}x{K} + GELU: {ms:.3f} ms = {2 * M * N * K / ms / 1e9:.0f} TFLOP/s")
