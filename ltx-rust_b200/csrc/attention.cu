@@ -243,18 +243,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int kv0 = j * BKV;
             const bool ragged = kv0 + BKV > p.Tk;   // only the last tile can be
-            // pass 1: row max over the 128 scores (read from TMEM in 32-column chunks)
-            float mx = -INFINITY;
+            // pass 1: the row max over the 128 scores, all four 32-column TMEM
+            // loads in flight together (one wait), 8 independent partial maxima
+            float mx;
+            {
+                uint32_t r[4][32];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(s_tmem + c * 32, r);
+                for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(s_tmem + c * 32, r[c]);
                 tmem_ld_wait();
+                float m8[8];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const float v = (ragged && kv0 + c * 32 + e >= p.Tk) ? -INFINITY : __uint_as_float(r[e]);
-                    mx = fmaxf(mx, v);
+                for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
+#pragma unroll
+                for (int e = 0; e < 128; ++e) {
+                    const float v = (ragged && kv0 + e >= p.Tk) ? -INFINITY : __uint_as_float(r[e >> 5][e & 31]);
+                    m8[e & 7] = fmaxf(m8[e & 7], v);
                 }
+                mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             }
             mx *= p.scale_log2;   // scale > 0: max(s * scale) = scale * max(s)
             // The rows of one warp decide together: tcgen05.ld/st are
@@ -270,16 +275,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        uint32_t r[32];
-                        tmem_ld_32x32b_x32(o_tmem + c * 32, r);
+                        uint32_t o[32];
+                        tmem_ld_32x32b_x32(o_tmem + c * 32, o);
                         tmem_ld_wait();
 #pragma unroll
                         for (int e = 0; e < 16; ++e) {
-                            const float2 v = __fmul2_rn(make_float2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1])), a2);
-                            r[2 * e] = __float_as_uint(v.x);
-                            r[2 * e + 1] = __float_as_uint(v.y);
+                            const float2 v = __fmul2_rn(make_float2(__uint_as_float(o[2 * e]), __uint_as_float(o[2 * e + 1])), a2);
+                            o[2 * e] = __float_as_uint(v.x);
+                            o[2 * e + 1] = __float_as_uint(v.y);
                         }
-                        tmem_st_32x32b_x32(o_tmem + c * 32, r);
+                        tmem_st_32x32b_x32(o_tmem + c * 32, o);
                     }
                     tmem_st_wait();
                 }
@@ -287,26 +292,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (grow) m_ref = mx;
             }
             // pass 2: P = exp2(s * scale - m_ref) (<= 2^kRescaleLog2), two per MUFU op; row sum in f32.
+            // Scores re-read from TMEM 64 columns (one swizzle atom of P) at a time.
             const float2 nm2 = make_float2(-m_ref, -m_ref);
             float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {           // keys c*32 .. c*32+31: atom c>>1, chunks (c&1)*4 ..
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(s_tmem + c * 32, r);
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t r[2][32];
+                tmem_ld_32x32b_x32(s_tmem + hf * 64, r[0]);
+                tmem_ld_32x32b_x32(s_tmem + hf * 64 + 32, r[1]);
                 tmem_ld_wait();
                 if (ragged) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (kv0 + c * 32 + e >= p.Tk) r[e] = __float_as_uint(-INFINITY);
+                    for (int e = 0; e < 64; ++e)
+                        if (kv0 + hf * 64 + e >= p.Tk) r[e >> 5][e & 31] = __float_as_uint(-INFINITY);
                 }
-                unsigned char *atom = p_row + (c >> 1) * HALF_BYTES;
+                unsigned char *atom = p_row + hf * HALF_BYTES;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {      // 16-byte chunk: 8 keys
+                for (int q = 0; q < 8; ++q) {      // 16-byte chunk q of the atom row: keys 8q .. 8q+7
                     uint32_t pk[4];
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int e = q * 8 + 2 * u;
-                        const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sl2, nm2);
+                        const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e >> 5][e & 31]),
+                                                                __uint_as_float(r[e >> 5][(e & 31) + 1])), sl2, nm2);
                         uint32_t in, out;
                         asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(x.y), "f"(x.x));
                         asm("ex2.approx.f16x2 %0, %1;" : "=r"(out) : "r"(in));
@@ -319,8 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             pk[u] = *reinterpret_cast<uint32_t *>(&hv);
                         }
                     }
-                    const int chunk = (c & 1) * 4 + q;
-                    *reinterpret_cast<uint4 *>(atom + ((chunk ^ sw) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    *reinterpret_cast<uint4 *>(atom + ((q ^ sw) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
             }
             l += sum2.x + sum2.y;
