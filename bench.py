@@ -393,14 +393,14 @@ def run_denoise_step(args, rank, ws, device):
 
 def launches_per_step(L, tp=False):
     """Kernels one ltx_denoise_step enqueues, counted from model.cpp's forward.
-    Head 8: latent convert, patchify GEMM, sinusoid, 3 small linears, adaLN
-    tables, context convert (+1 RoPE table when split over ranks).  Per block
-    15: 3 norm+modulate, QKV / out / cross-q / cross-kv / out / FFN-in /
-    FFN-out GEMMs, fused Q/K norm+RoPE, cross q and k norms, 2 attentions.
-    Split over ranks, per block 22: the Q/K norms become 3 sum-of-squares and
-    4 apply launches, and each of the 3 row-split projections adds a residual
-    add (NCCL's own kernels are not counted).  Output head 2, sampler 2."""
-    return (9 + L * 22 if tp else 8 + L * 15) + 2 + 2
+    Head 9: latent convert, patchify GEMM, sinusoid, 3 small linears, adaLN
+    tables, RoPE table, context convert.  Per block 15: 3 norm+modulate, QKV /
+    out / cross-q / cross-kv / out / FFN-in / FFN-out GEMMs, fused Q/K
+    norm+RoPE, cross q and k norms, 2 attentions.  Split over ranks, per block
+    22: the Q/K norms become 3 sum-of-squares and 4 apply launches, and each of
+    the 3 row-split projections adds a residual add (NCCL's own kernels are
+    not counted).  Output head 2, sampler 2."""
+    return 9 + L * (22 if tp else 15) + 2 + 2
 
 
 def cpu_baseline_step(blocks=1, threads=None):

@@ -488,25 +488,23 @@ __global__ void __launch_bounds__(256) rmsnorm_gamma_warp_kernel(__nv_bfloat16 *
 }
 
 // Self-attention Q and K of one token, in place: RMSNorm(gamma) over the full
-// inner dim for each, then split RoPE with the angles computed here from the
-// token's positions (the same f32 operations as rope_table_kernel), so no
-// cos/sin table is read.  Head dim 128, H = D/128 heads, warp per token; lane l
-// owns pairs j = 2l, 2l+1 of every head (columns h*128 + {2l, 2l+1} and
-// h*128 + 64 + {2l, 2l+1}).
+// inner dim for each, then split RoPE with cos/sin read from the forward's
+// tables ([table rows][D/2], built once per forward by rope_table_kernel; row
+// `row % tab_rows`, so CFG rows that share their positions share one table
+// row).  Head dim 128, H = D/128 heads, warp per token; lane l owns pairs
+// j = 2l, 2l+1 of every head (columns h*128 + {2l, 2l+1} and
+// h*128 + 64 + {2l, 2l+1}), i.e. table entries h*64 + 2l, 2l+1.
 template <int H>
 __global__ void __launch_bounds__(256) qk_norm_rope_fused_kernel(__nv_bfloat16 *q, __nv_bfloat16 *k, int64_t ld,
-                                                                 int rows, int T, float eps, const float *gq,
-                                                                 const float *gk, const float *pos, const float *freq,
-                                                                 int grid, float mp0, float mp1, float mp2,
-                                                                 int use_mid) {
+                                                                 int rows, float eps, const float *gq, const float *gk,
+                                                                 const float *cos_t, const float *sin_t, int tab_rows) {
     constexpr int D = H * 128;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     uint32_t *qr = reinterpret_cast<uint32_t *>(q + (int64_t)row * ld);
     uint32_t *kr = reinterpret_cast<uint32_t *>(k + (int64_t)row * ld);
-    // word index of pair (2l, 2l+1) in head h: h*64 + l (first half), h*64 + 32 + l (second half).
     // Phase 1 streams the row for the two sums of squares; phase 2 re-reads it
-    // (L1-resident, 16 KB per warp) to normalise, rotate and store.
+    // (L1/L2-resident) to normalise, rotate and store.
     float sq = 0.f, sk = 0.f;
 #pragma unroll 8
     for (int w = lane; w < D / 2; w += 32) {
@@ -517,34 +515,17 @@ __global__ void __launch_bounds__(256) qk_norm_rope_fused_kernel(__nv_bfloat16 *
     }
     const float dq = sqrtf(warp_sum_all(sq) / (float)D + eps);
     const float dk = sqrtf(warp_sum_all(sk) / (float)D + eps);
-    // normalised position per axis for this token (rope.rs:90-98)
-    const int b = row / T, t = row % T;
-    float fm[3];
-#pragma unroll
-    for (int ax = 0; ax < 3; ++ax) {
-        const float *pp = pos + (((int64_t)b * 3 + ax) * T + t) * 2;
-        const float mp = ax == 0 ? mp0 : (ax == 1 ? mp1 : mp2);
-        const float frac = use_mid ? __fdiv_rn(__fdiv_rn(__fadd_rn(pp[0], pp[1]), 2.0f), mp) : __fdiv_rn(pp[0], mp);
-        fm[ax] = __fadd_rn(__fmul_rn(frac, 2.0f), -1.0f);
-    }
-    const int pad = D / 2 - 3 * grid;
+    const int64_t trow = (int64_t)(row % tab_rows) * (D / 2);
+    const float2 *ct = reinterpret_cast<const float2 *>(cos_t + trow);
+    const float2 *stb = reinterpret_cast<const float2 *>(sin_t + trow);
 #pragma unroll 4
     for (int h = 0; h < H; ++h) {
         const float2 qa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qr[h * 64 + lane]));
         const float2 qb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&qr[h * 64 + 32 + lane]));
         const float2 ka = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[h * 64 + lane]));
         const float2 kb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&kr[h * 64 + 32 + lane]));
-        float c[2], s[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            const int entry = h * 64 + 2 * lane + e;   // index into the [D/2] cos/sin row
-            c[e] = 1.f;
-            s[e] = 0.f;
-            if (entry >= pad) {
-                const int idx = entry - pad, g = idx / 3, ax = idx % 3;
-                sincosf(__fmul_rn(fm[ax], __ldg(freq + g)), &s[e], &c[e]);
-            }
-        }
+        const float2 c2 = __ldg(ct + h * 32 + lane), s2 = __ldg(stb + h * 32 + lane);
+        const float c[2] = {c2.x, c2.y}, s[2] = {s2.x, s2.y};
         const int col = h * 128 + 2 * lane;
         const float q1x = qa.x / dq * __ldg(gq + col), q1y = qa.y / dq * __ldg(gq + col + 1);
         const float q2x = qb.x / dq * __ldg(gq + col + 64), q2y = qb.y / dq * __ldg(gq + col + 65);
@@ -564,12 +545,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_fused_kernel(__nv_bfloat16 *
 
 }  // namespace
 
-bool qk_norm_rope_fused(cudaStream_t st, __nv_bfloat16 *q, __nv_bfloat16 *k, int64_t ld, int rows, int T, int D,
-                        float eps, const float *gq, const float *gk, const float *pos, const float *freq, int grid,
-                        const float max_pos[3], bool use_mid, cudaError_t *err) {
-    if (D != 4096 || (ld % 2) || ((uintptr_t)q & 3) || ((uintptr_t)k & 3)) return false;
-    qk_norm_rope_fused_kernel<32><<<(rows + 7) / 8, 256, 0, st>>>(q, k, ld, rows, T, eps, gq, gk, pos, freq, grid,
-                                                                   max_pos[0], max_pos[1], max_pos[2], use_mid);
+bool qk_norm_rope_fused(cudaStream_t st, __nv_bfloat16 *q, __nv_bfloat16 *k, int64_t ld, int rows, int D, float eps,
+                        const float *gq, const float *gk, const float *cos_t, const float *sin_t, int tab_rows,
+                        cudaError_t *err) {
+    if (D != 4096 || (ld % 2) || ((uintptr_t)q & 3) || ((uintptr_t)k & 3) || ((uintptr_t)cos_t & 7) ||
+        ((uintptr_t)sin_t & 7) || tab_rows <= 0)
+        return false;
+    qk_norm_rope_fused_kernel<32><<<(rows + 7) / 8, 256, 0, st>>>(q, k, ld, rows, eps, gq, gk, cos_t, sin_t, tab_rows);
     *err = cudaGetLastError();
     return true;
 }

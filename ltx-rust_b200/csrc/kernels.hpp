@@ -45,11 +45,12 @@ cudaError_t head_gate(cudaStream_t st, int sms, __nv_bfloat16 *o, int64_t ldo, c
 cudaError_t attention_generic(cudaStream_t st, const __nv_bfloat16 *q, int64_t ldq, const __nv_bfloat16 *k, int64_t ldk,
                               const __nv_bfloat16 *v, int64_t ldv, int B, int H, int Tq, int Tk, int d, float scale,
                               __nv_bfloat16 *out, int64_t ldo);
-// Fused self-attention Q/K RMSNorm(gamma) + split RoPE with in-register angles; returns
-// false (nothing launched) when the shape is not the specialised one (D 4096, head dim 128).
-bool qk_norm_rope_fused(cudaStream_t st, __nv_bfloat16 *q, __nv_bfloat16 *k, int64_t ld, int rows, int T, int D,
-                        float eps, const float *gq, const float *gk, const float *pos, const float *freq, int grid,
-                        const float max_pos[3], bool use_mid, cudaError_t *err);
+// Fused self-attention Q/K RMSNorm(gamma) + split RoPE from the forward's cos/sin
+// tables ([tab_rows][D/2], row = token row % tab_rows); returns false (nothing
+// launched) when the shape is not the specialised one (D 4096, head dim 128).
+bool qk_norm_rope_fused(cudaStream_t st, __nv_bfloat16 *q, __nv_bfloat16 *k, int64_t ld, int rows, int D, float eps,
+                        const float *gq, const float *gk, const float *cos_t, const float *sin_t, int tab_rows,
+                        cudaError_t *err);
 cudaError_t permute_ct(cudaStream_t st, int sms, const float *in, float *out, int B, int C, int64_t T, bool to_tokens);
 size_t cfg_scratch_bytes();
 cudaError_t cfg_euler(cudaStream_t st, int sms, float *x, const float *vc, const float *vu, const float *tok_t,

@@ -585,9 +585,11 @@ static int unique_timesteps(const std::vector<float> &ts, std::vector<float> &un
 
 // The full forward on device buffers.  `ts_host` are the per-token timesteps
 // (B*T, host copy) used to build the distinct-timestep index.
+// pos_shared: every batch row has the same positions (the CFG halves of a
+// denoise step), so the RoPE tables are built for T rows instead of B*T.
 static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const std::vector<float> &ts_host,
                         const float *positions, const float *context, int B, int T, int S, float *out,
-                        const Work *given = nullptr, Work *work_out = nullptr) {
+                        const Work *given = nullptr, Work *work_out = nullptr, bool pos_shared = false) {
     const DitConfig &c = m->cfg;
     if (ctx->tp_size != m->tp || ctx->tp_rank != m->tr)
         return fail(ctx, LTX_ERR_INVALID_ARG, "model shard %d of %d run on a context of rank %d of %d", m->tr, m->tp,
@@ -633,12 +635,13 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
     // RoPE tables (rope.rs:46-167)
     const float mp[3] = {(float)c.max_pos[0], (float)c.max_pos[1], (float)c.max_pos[2]};
     const int width = c.interleaved ? (int)D : (int)(D / 2);
-    // The fused Q/K kernel computes RoPE angles in registers for the production
-    // shape (D 4096, head dim 128, split RoPE); other shapes use the tables.
+    // Built once per forward, read by every block's Q/K norm.  The fused Q/K
+    // kernel (D 4096, head dim 128, split RoPE, one GPU) indexes the table by
+    // row % tab_rows, so rows that share positions share table rows.
     const bool fused_qk = m->tp == 1 && D == 4096 && d == 128 && !c.interleaved;
-    if (!fused_qk)
-        CU(rope_table(st, sms, positions, B, T, m->rope_freq, m->rope_grid, mp, c.use_mid, c.interleaved, width, w.cos,
-                      w.sin));
+    const int tab_b = fused_qk && pos_shared ? 1 : B;
+    CU(rope_table(st, sms, positions, tab_b, T, m->rope_freq, m->rope_grid, mp, c.use_mid, c.interleaved, width, w.cos,
+                  w.sin));
     if (!c.cross_adaln) CU(f32_to_bf16(st, sms, context, crow * Dc, w.ctxb));
 
     // Tensor-parallel split: this rank runs heads [tr*Hl, (tr+1)*Hl) and FFN
@@ -690,8 +693,9 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
             TRY(norm_split(w.qkv + Dl, 3 * Dl, (int)rows, b.kn, w.ss + rows, true));
         } else if (fused_qk) {
             cudaError_t qe = cudaSuccess;
-            qk_norm_rope_fused(st, w.qkv, w.qkv + D, 3 * D, (int)rows, T, (int)D, c.eps, b.qn, b.kn, positions,
-                               m->rope_freq, m->rope_grid, mp, c.use_mid, &qe);
+            if (!qk_norm_rope_fused(st, w.qkv, w.qkv + D, 3 * D, (int)rows, (int)D, c.eps, b.qn, b.kn, w.cos, w.sin,
+                                    tab_b * T, &qe))
+                return fail(ctx, LTX_ERR_UNSUPPORTED, "fused Q/K norm: unexpected layout");
             CU(qe);
         } else {
             CU(qk_norm_rope(st, w.qkv, 3 * D, (int)rows, (int)D, (int)H, c.eps, b.qn, w.cos, w.sin, c.interleaved));
@@ -884,7 +888,7 @@ static int denoise_step_core(ltx_model *m, ltx_ctx *ctx, float *latent_dev, cons
     if (!static_ready) TRY(stage_static(ctx, sb, positions_dev, cc, cu, B, T, S, c.cross_dim));
     for (int b = 0; b < B; ++b)
         CU(cudaMemcpyAsync(sb.lat2 + (int64_t)b * T * C, latent_dev, (size_t)T * C * 4, cudaMemcpyDeviceToDevice, st));
-    TRY(forward_impl(m, ctx, sb.lat2, ts, sb.pos2, sb.ctx2, B, T, S, sb.vel, &w));
+    TRY(forward_impl(m, ctx, sb.lat2, ts, sb.pos2, sb.ctx2, B, T, S, sb.vel, &w, nullptr, true));
     // per-token t for the velocity -> x0 adapter: x0 = x - t * v
     TRY(upload(ctx, w.tok_t, ts.data(), (size_t)T * 4));
     CU(cfg_euler(st, ctx->sm_count, latent_dev, sb.vel, use_cfg ? sb.vel + (int64_t)T * C : sb.vel, w.tok_t, mask_dev,
