@@ -398,25 +398,42 @@ __device__ __forceinline__ float warp_sum_all(float v) {
     return v;
 }
 
-// norm_mod with one warp per row and the row held in registers: lane l owns
-// float4 columns l*4 + 128*i, i < NV (NV = D/128).  Same modes as norm_mod_kernel.
-template <int NV>
-__global__ void __launch_bounds__(256) norm_mod_warp_kernel(const float *x, int64_t ldx, int rows, float eps, int mode,
-                                                            const float *tab, int tab_coeff, const int *idx,
-                                                            int k_shift, __nv_bfloat16 *out, int64_t ldo) {
-    constexpr int D = NV * 128;
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)row * ldx);
+// norm_mod for D = 4096 with each row split over SPLIT warps (lane l of part w
+// owns float4 columns w*D/SPLIT + l*4 + 128*i): the row stays in registers
+// with a per-thread state small enough for 2 blocks (16 warps) per SM.  The partial sums
+// meet in shared memory.  Same modes and results as norm_mod_kernel.
+template <int SPLIT>
+__global__ void __launch_bounds__(256) norm_mod_split_kernel(const float *x, int64_t ldx, int rows, float eps, int mode,
+                                                             const float *tab, int tab_coeff, const int *idx,
+                                                             int k_shift, __nv_bfloat16 *out, int64_t ldo) {
+    constexpr int D = 4096, NV = D / 128 / SPLIT, RPB = 8 / SPLIT;   // float4 per lane, rows per block
+    __shared__ float part[2][8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rib = warp / SPLIT, piece = warp % SPLIT;
+    const int row = blockIdx.x * RPB + rib;
+    const bool live = row < rows;
+    const int col0 = piece * (D / SPLIT);
     float4 v[NV];
+    if (live) {
+        const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)row * ldx + col0);
 #pragma unroll
-    for (int i = 0; i < NV; ++i) v[i] = __ldcs(xr + lane + 32 * i);
+        for (int i = 0; i < NV; ++i) v[i] = __ldcs(xr + lane + 32 * i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     float mean = 0.f;
     if (mode == 2) {
         float s = 0.f;
 #pragma unroll
         for (int i = 0; i < NV; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-        mean = warp_sum_all(s) / (float)D;
+        s = warp_sum_all(s);
+        if (lane == 0) part[0][warp] = s;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int q = 0; q < SPLIT; ++q) tot += part[0][rib * SPLIT + q];
+        mean = tot / (float)D;
     }
     float ss = 0.f;
 #pragma unroll
@@ -424,15 +441,22 @@ __global__ void __launch_bounds__(256) norm_mod_warp_kernel(const float *x, int6
         v[i].x -= mean; v[i].y -= mean; v[i].z -= mean; v[i].w -= mean;
         ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
     }
-    const float denom = sqrtf(warp_sum_all(ss) / (float)D + eps);
+    ss = warp_sum_all(ss);
+    if (lane == 0) part[1][warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int q = 0; q < SPLIT; ++q) tot += part[1][rib * SPLIT + q];
+    if (!live) return;
+    const float denom = sqrtf(tot / (float)D + eps);
     const float4 *sh = nullptr, *sc = nullptr;
     if (mode != 0) {
         const int u = idx ? idx[row] : 0;
-        const float *shift = tab + ((int64_t)u * tab_coeff + k_shift) * D;
+        const float *shift = tab + ((int64_t)u * tab_coeff + k_shift) * D + col0;
         sh = reinterpret_cast<const float4 *>(shift);
         sc = reinterpret_cast<const float4 *>(shift + D);
     }
-    uint2 *o = reinterpret_cast<uint2 *>(out + (int64_t)row * ldo);
+    uint2 *o = reinterpret_cast<uint2 *>(out + (int64_t)row * ldo + col0);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         float a = v[i].x / denom, b = v[i].y / denom, c = v[i].z / denom, d = v[i].w / denom;
@@ -578,7 +602,8 @@ cudaError_t norm_mod(cudaStream_t st, const float *x, int64_t ldx, int rows, int
     const bool vec = ldx % 4 == 0 && ldo % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 7) == 0 &&
                      (!tab || ((uintptr_t)tab & 15) == 0);
     if (vec && D == 4096) {
-        norm_mod_warp_kernel<32><<<(rows + 7) / 8, 256, 0, st>>>(x, ldx, rows, eps, mode, tab, tab_coeff, idx, k_shift,
+        // two warps per row, 4 rows per 256-thread block
+        norm_mod_split_kernel<2><<<(rows + 3) / 4, 256, 0, st>>>(x, ldx, rows, eps, mode, tab, tab_coeff, idx, k_shift,
                                                                   out, ldo);
         return cudaGetLastError();
     }

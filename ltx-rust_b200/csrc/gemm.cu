@@ -11,8 +11,8 @@
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (one row per
 //               thread), fused bias / GELU(tanh) / gated residual, store.
 //   Two TMEM accumulators (2 x BN columns) let the epilogue of tile i run
-//   under the mainloop of tile i+1.  Tiles are walked in groups of 16
-//   M-blocks so the A panel and the W panel of concurrent tiles stay in L2.
+//   under the mainloop of tile i+1.  Tiles are walked in groups of M-blocks
+//   whose A panel fits ~48 MB of L2, so W is streamed once per group.
 // Each CTA loads its own tiles from local HBM; no load is shared across a cluster.
 #include <cuda.h>
 
@@ -41,12 +41,13 @@ struct GemmParams {
     int64_t ld_gate;
     int *timeout_flag;
     int f16_from_col;       // EPI_BF16: columns >= this are written as f16 (N = none)
+    int group_m;            // M-blocks walked together (their A panel stays in L2)
 };
 
 namespace {
 
 constexpr int BM = 128, BK = 64;
-constexpr int kGroupM = 16;
+constexpr size_t kGroupPanelBytes = 48u << 20;   // A panel kept in L2 while W streams past it
 constexpr int kThreads = 192;
 
 // F8: e4m3 operands (kind::f8f6f4), 128 elements of K per stage; otherwise
@@ -70,11 +71,14 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return 0.5f * x * (1.0f + tanhf(u));
 }
 
-__device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, int &mb, int &nb) {
-    const int per_group = kGroupM * n_blocks;
+// Tile t -> (M-block, N-block): groups of group_m M-blocks, M fastest inside a
+// group, so the ~148 tiles in flight share a few W panels and one A panel, and
+// W is streamed from DRAM once per group.
+__device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, int group_m, int &mb, int &nb) {
+    const int per_group = group_m * n_blocks;
     const int g = t / per_group;
-    const int first_m = g * kGroupM;
-    const int gm = min(kGroupM, m_blocks - first_m);
+    const int first_m = g * group_m;
+    const int gm = min(group_m, m_blocks - first_m);
     const int r = t - g * per_group;
     mb = first_m + r % gm;
     nb = r / gm;
@@ -127,7 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t it = 0;
             for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
                 int mb, nb;
-                tile_coords(t, m_blocks, n_blocks, mb, nb);
+                tile_coords(t, m_blocks, n_blocks, p.group_m, mb, nb);
                 for (int kb = 0; kb < k_blocks; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     const uint32_t ph = (it / C::STAGES) & 1;
@@ -181,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t tile_i = 0;
         for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tile_i) {
             int mb, nb;
-            tile_coords(t, m_blocks, n_blocks, mb, nb);
+            tile_coords(t, m_blocks, n_blocks, p.group_m, mb, nb);
             const uint32_t acc = tile_i & 1, aph = (tile_i >> 1) & 1;
             // warp-uniform outcome: the tcgen05.ld below are warp-collective
             if (!warp_wait(&tfull[acc], aph, p.timeout_flag, 104, &aborted)) break;
@@ -370,7 +374,12 @@ int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, 
     if (f16_from_col < 0 || f16_from_col > N) f16_from_col = N;
     if (f16_from_col < N && (epi != EPI_BF16 || f16_from_col % 32))
         return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: f16 columns need the bf16 epilogue and a multiple of 32");
-    GemmParams p{M, N, K, a_scale, w_scale, bias, out, ldo, gate, gate_idx, ld_gate, ctx->timeout_flag, f16_from_col};
+    // as many M-blocks per group as keep their A panel within ~48 MB of L2
+    const int m_blocks = (M + BM - 1) / BM;
+    const size_t panel = (size_t)BM * K * es;
+    const int group_m = (int)std::max<size_t>(1, std::min<size_t>((size_t)m_blocks, kGroupPanelBytes / panel));
+    GemmParams p{M,   N,       K,        a_scale,           w_scale,      bias,   out,
+                 ldo, gate,    gate_idx, ld_gate,           ctx->timeout_flag, f16_from_col, group_m};
     cudaError_t e;
     if (es == 1)
         e = BN == 128 ? dispatch_epi<128, true>(epi, ta, tb, p, ctx->sm_count, st)
