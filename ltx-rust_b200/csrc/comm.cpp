@@ -70,6 +70,15 @@ int allreduce_sum(ltx_ctx *ctx, float *buf, size_t count) {
     return LTX_OK;
 }
 
+int allreduce_sum_bf16(ltx_ctx *ctx, void *buf, size_t count) {
+    if (ctx->tp_size <= 1 || count == 0) return LTX_OK;
+    const NcclApi &api = nccl();
+    ncclResult_t r = api.all_reduce(buf, buf, count, ncclBfloat16, ncclSum, static_cast<ncclComm_t>(ctx->comm),
+                                    ctx->stream);
+    if (r != ncclSuccess) return fail(ctx, LTX_ERR_NCCL, "allreduce of %zu bf16: %s", count, nccl_str(r));
+    return LTX_OK;
+}
+
 void comm_release(ltx_ctx *ctx, bool abort) {
     if (!ctx->comm) return;
     const NcclApi &api = nccl();

@@ -63,6 +63,7 @@ int upload(ltx_ctx *ctx, void *dst_dev, const void *src_host, size_t bytes);
 // Sum-allreduce of `count` floats in place over the context's communicator,
 // on its stream (a no-op without one).
 int allreduce_sum(ltx_ctx *ctx, float *buf, size_t count);
+int allreduce_sum_bf16(ltx_ctx *ctx, void *buf, size_t count);
 // Destroys (or aborts) the context's communicator.
 void comm_release(ltx_ctx *ctx, bool abort);
 

@@ -65,7 +65,7 @@ cudaError_t tp_sumsq_rows(cudaStream_t st, const __nv_bfloat16 *x, int64_t ld, i
 cudaError_t tp_norm_apply_rope(cudaStream_t st, __nv_bfloat16 *x, int64_t ld, int rows, int cols, int D, int d,
                                int head0, float eps, const float *gamma, const float *ss, const float *cos_t,
                                const float *sin_t, bool interleaved);
-cudaError_t tp_resid_add(cudaStream_t st, int sms, float *x, const float *p, int rows, int D, const float *bias,
-                         const float *gate, const int *gidx, int64_t ld_gate);
+cudaError_t tp_resid_add(cudaStream_t st, int sms, float *x, const __nv_bfloat16 *p, int rows, int D,
+                         const float *bias, const float *gate, const int *gidx, int64_t ld_gate);
 
 }  // namespace ltx

@@ -505,7 +505,8 @@ struct Work {
     int *idx;
     float *ts_u;
     double *partial;
-    float *part, *ss;   // tensor-parallel: summed partial projections, Q/K sums of squares
+    __nv_bfloat16 *part;   // tensor-parallel: summed partial projections (bf16)
+    float *ss;             // tensor-parallel: Q/K sums of squares
     size_t bytes;
 };
 
@@ -541,7 +542,7 @@ static Work carve_work(char *base, const DitConfig &c, int64_t rows, int64_t cro
     w.ffh = a.take<__nv_bfloat16>(rows * Fl);
     w.latb = a.take<__nv_bfloat16>(rows * std::max(c.in_ch, 8));
     w.partial = a.take<double>((int64_t)cfg_scratch_bytes() / 8);
-    w.part = tp > 1 ? a.take<float>(rows * D) : nullptr;
+    w.part = tp > 1 ? a.take<__nv_bfloat16>(rows * D) : nullptr;
     w.ss = tp > 1 ? a.take<float>(2 * rows + crow) : nullptr;
     w.bytes = a.off + 256;
     return w;
@@ -664,9 +665,10 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         if (tp == 1)
             return gemm_bf16(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, LTX_EPI_RESID, bias, w.x, D, gate,
                              gidx, K * D);
-        TRY(gemm_bf16(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, LTX_EPI_F32, nullptr, w.part, D, nullptr,
-                      nullptr, 0));
-        TRY(allreduce_sum(ctx, w.part, (size_t)rows * D));
+        // the partial products travel as bf16: half the bytes of the allreduce
+        TRY(gemm_bf16(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, LTX_EPI_BF16, nullptr, w.part, D,
+                      nullptr, nullptr, 0));
+        TRY(allreduce_sum_bf16(ctx, w.part, (size_t)rows * D));
         CU(tp_resid_add(st, sms, w.x, w.part, (int)rows, (int)D, bias, gate, gidx, K * D));
         return LTX_OK;
     };

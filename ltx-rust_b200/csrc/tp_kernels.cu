@@ -3,8 +3,8 @@
 // so the Q/K RMSNorm over the full inner dimension (Attention::forward,
 // crates/ltx-dit/src/attention.rs:137-195; RmsNorm_gamma over all D) runs in
 // two halves around a sum-allreduce of per-row sums of squares; and each
-// row-split output projection's partial product is summed across ranks
-// before the bias, gate and residual add that the single-GPU GEMM epilogue
+// row-split output projection's partial product (bf16) is summed across
+// ranks before the bias, gate and residual add that the single-GPU GEMM epilogue
 // fuses.  All three are HBM-bound streaming kernels.
 #include "device_common.cuh"
 #include "internal.hpp"
@@ -86,15 +86,19 @@ __global__ void __launch_bounds__(256) norm_apply_rope_kernel(__nv_bfloat16 *x, 
 }
 
 // x[row][c] += (p[row][c] + bias[c]) * gate[idx[row]][c]: the single-GPU
-// EPI_RESID epilogue, applied after the partial products were summed.
-__global__ void __launch_bounds__(256) resid_add_kernel(float *x, const float *p, int rows, int D, const float *bias,
-                                                        const float *gate, const int *gidx, int64_t ld_gate) {
+// EPI_RESID epilogue, applied after the partial products (bf16) were summed.
+__global__ void __launch_bounds__(256) resid_add_kernel(float *x, const __nv_bfloat16 *p, int rows, int D,
+                                                        const float *bias, const float *gate, const int *gidx,
+                                                        int64_t ld_gate) {
     const int64_t n4 = (int64_t)rows * D / 4;
     for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < n4; v += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = v * 4;
         const int row = (int)(i / D), col = (int)(i % D);
         float4 xv = reinterpret_cast<float4 *>(x)[v];
-        const float4 pv = reinterpret_cast<const float4 *>(p)[v];
+        const uint2 pu = reinterpret_cast<const uint2 *>(p)[v];
+        const float2 p01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&pu.x));
+        const float2 p23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&pu.y));
+        const float4 pv = make_float4(p01.x, p01.y, p23.x, p23.y);
         float b[4] = {0.f, 0.f, 0.f, 0.f}, g[4] = {1.f, 1.f, 1.f, 1.f};
         if (bias) {
             const float4 b4 = *reinterpret_cast<const float4 *>(bias + col);
@@ -142,8 +146,8 @@ cudaError_t tp_norm_apply_rope(cudaStream_t st, __nv_bfloat16 *x, int64_t ld, in
     return cudaGetLastError();
 }
 
-cudaError_t tp_resid_add(cudaStream_t st, int sms, float *x, const float *p, int rows, int D, const float *bias,
-                         const float *gate, const int *gidx, int64_t ld_gate) {
+cudaError_t tp_resid_add(cudaStream_t st, int sms, float *x, const __nv_bfloat16 *p, int rows, int D,
+                         const float *bias, const float *gate, const int *gidx, int64_t ld_gate) {
     if (rows == 0) return cudaSuccess;
     if (D % 4) return cudaErrorInvalidValue;
     resid_add_kernel<<<grid_cap((int64_t)rows * D / 4, 256, sms), 256, 0, st>>>(x, p, rows, D, bias, gate, gidx,
