@@ -391,6 +391,51 @@ def run_denoise_step(args, rank, ws, device):
     return res
 
 
+def run_block_forward(device, iters=5):
+    """Config 3: one 22B-class block forward (model with num_layers = 1, B = 1,
+    T = 12288 tokens with the IC reference, S = 1024), in both GEMM precisions
+    (bf16 on merged weights; e4m3 on the exact FP8 base with the LoRA
+    factored), with the rel-L2 between them (the FP8 path's bar is 3e-2)."""
+    import numpy as np
+    import torch
+    import ltx_b200
+    ctx = ltx_b200.Context(device)
+    inp = make_step_inputs(LAT_F, LAT_H, LAT_W, S_CTX, D, seed=300)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+    lat = dev(inp["latent"][None])
+    ts = dev((inp["mask"] * np.float32(inp["sigmas"][1]))[None])
+    pos, cc = dev(inp["positions"]), dev(inp["ctx_cond"][None])
+    res, outs = {}, {}
+    block_tflop = 2 * T_TOTAL * D * (6 * D + 2 * FF) + 2 * S_CTX * D * 2 * D + 4 * T_TOTAL * T_TOTAL * D + \
+        4 * T_TOTAL * S_CTX * D
+    for prec in ("bf16", "e4m3_ffn", "e4m3"):
+        cfg = json.loads(json.dumps(CFG4))
+        cfg["transformer"]["num_layers"] = 1
+        cfg["gemm_precision"] = prec
+        model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(cfg), seed=11, lora_rank=64, lora_strength=1.0)
+        out = torch.empty(1, T_TOTAL, 128, device="cuda")
+        for _ in range(2):
+            model.forward(lat, ts, pos, cc, out)
+        ctx.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            model.forward(lat, ts, pos, cc, out)
+        e.record()
+        ctx.synchronize()
+        ms = s.elapsed_time(e) / iters
+        outs[prec] = out.double().cpu()
+        res[prec] = {"ms": ms, "tflops": block_tflop / (ms * 1e-3) / 1e12}
+        model.close()
+    for prec in ("e4m3_ffn", "e4m3"):
+        res[prec]["rel_l2_vs_bf16"] = float((outs[prec] - outs["bf16"]).norm() / outs["bf16"].norm())
+    res["note"] = ("one block + patchify/adaLN/output head per forward; "
+                   f"{block_tflop / 1e12:.3f} TFLOP of block matmul; e4m3 = FP8 GEMMs for all 7 projections, "
+                   "e4m3_ffn = for the 2 FFN projections (north-star FP8 bar: rel-L2 <= 3e-2)")
+    ctx.close()
+    return res
+
+
 def launches_per_step(L, tp=False):
     """Kernels one ltx_denoise_step enqueues, counted from model.cpp's forward.
     Head 9: latent convert, patchify GEMM, sinusoid, 3 small linears, adaLN
@@ -546,10 +591,17 @@ def main():
         dq_args = argparse.Namespace(steps=20, warmup=5)
         dq = run_dequant_merge(dq_args, rank, ws, local)
         _log(f"dequant+merge: {dq['value']:.0f} GB/s")
+        blk = run_block_forward(local) if ws == 1 else None
+        if blk:
+            _log(f"block forward: bf16 {blk['bf16']['ms']:.2f} ms, e4m3_ffn {blk['e4m3_ffn']['ms']:.2f} ms "
+                 f"(rel-L2 {blk['e4m3_ffn']['rel_l2_vs_bf16']:.2e}), e4m3 {blk['e4m3']['ms']:.2f} ms "
+                 f"(rel-L2 {blk['e4m3']['rel_l2_vs_bf16']:.2e})")
         if rank == 0:
             res.update({"n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
                         "data": "synthetic (random-init FP8+LoRA weights, N(0,1) latent/reference/contexts)"})
             res["dequant_merge"] = {k: dq[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "e2e")}
+            if blk:
+                res["block_forward_config3"] = blk
             if ws == 1 and args.cpu_seconds > 0:
                 res["cpu_baseline"] = cpu_baseline_step(blocks=1)
                 _log(f"CPU baseline (one block): {res['cpu_baseline']['sample']}")

@@ -209,15 +209,22 @@ int ltx_gemm_bf16(ltx_ctx *ctx, const void *a_dev, int64_t lda, const void *w_de
                   void *out_dev, int64_t ldo, const float *gate_dev, const int32_t *gate_idx_dev,
                   int64_t ld_gate);
 /* The same projection with native FP8 operands (tcgen05 kind::f8f6f4, e4m3
- * A and W, f32 accumulate): the per-row scale of A (a_scale_dev, f32 [m], or
- * NULL = 1) and the per-tensor scale of W (w_scale, e.g. the checkpoint's
- * `{key}_scale`, store.rs:505-507) multiply the accumulator before the
- * epilogue.  lda/ldw are in bytes = elements (multiples of 16).  The
- * north star's FP8 GEMM path (rel-L2 <= 3e-2). */
+ * A and W, f32 accumulate):
+ *   acc = A[m,k] . W[n,k]^T  (+ A2[m,k2] . B2[n,k2]^T, bf16, when k2 > 0)
+ *   out = epilogue(acc * a_scale[row] * w_scale[col])
+ * a_scale_dev: f32 [m] per-row scale of A, or NULL = 1.  w_col_scale_dev: f32
+ * [n] per-column weight scale, or NULL = the per-tensor w_scale (e.g. the
+ * checkpoint's `{key}_scale`, store.rs:505-507).  The appended bf16 block
+ * carries an unmerged low-rank (LoRA) term in the same accumulator: pass
+ * A2 = (x . A^T) / a_scale and B2 = coeff * B / w_scale so that the scales
+ * cancel (k2 a multiple of 64; 0 = none).  lda/ldw are in bytes = elements
+ * (multiples of 16), lda2/ldb2 in elements (multiples of 8).  The north
+ * star's FP8 GEMM path (rel-L2 <= 3e-2). */
 int ltx_gemm_e4m3(ltx_ctx *ctx, const void *a_dev, int64_t lda, const float *a_scale_dev, const void *w_dev,
-                  int64_t ldw, float w_scale, int32_t m, int32_t n, int32_t k, int32_t epilogue,
-                  const float *bias_dev, void *out_dev, int64_t ldo, const float *gate_dev,
-                  const int32_t *gate_idx_dev, int64_t ld_gate);
+                  int64_t ldw, float w_scale, const float *w_col_scale_dev, int32_t m, int32_t n, int32_t k,
+                  int32_t epilogue, const float *bias_dev, void *out_dev, int64_t ldo, const float *gate_dev,
+                  const int32_t *gate_idx_dev, int64_t ld_gate, const void *a2_dev, int64_t lda2,
+                  const void *b2_dev, int64_t ldb2, int32_t k2);
 
 /* out = softmax(q k^T * scale) v per batch and head, without materialising
  * the scores (flash attention on tcgen05; scores and P.V accumulate in TMEM).

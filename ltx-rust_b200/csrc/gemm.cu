@@ -42,11 +42,14 @@ struct GemmParams {
     int *timeout_flag;
     int f16_from_col;       // EPI_BF16: columns >= this are written as f16 (N = none)
     int group_m;            // M-blocks walked together (their A panel stays in L2)
+    int k2_blocks;          // FP8 only: bf16 K-blocks of 64 appended to every tile
+                            // (A2 [M, 64*k2] . B2 [N, 64*k2]^T, same accumulator)
+    const float *w_col_scale;   // FP8 only: per-column weight scale [N] (null = w_scale)
 };
 
 namespace {
 
-constexpr int BM = 128, BK = 64;
+constexpr int BM = 128;
 constexpr size_t kGroupPanelBytes = 48u << 20;   // A panel kept in L2 while W streams past it
 constexpr int kThreads = 192;
 
@@ -86,7 +89,8 @@ __device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, i
 
 template <int BN, int EPI, bool F8>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, GemmParams p) {
     using C = GemmCfg<BN, F8>;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -102,6 +106,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int m_blocks = (p.M + BM - 1) / BM, n_blocks = (p.N + BN - 1) / BN;
     const int num_tiles = m_blocks * n_blocks;
     const int k_blocks = (p.K + C::BKE - 1) / C::BKE;
+    const int k2_blocks = F8 ? p.k2_blocks : 0;
+    const int k_total = k_blocks + k2_blocks;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -128,17 +134,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (elect_one()) {
             tma_prefetch_desc(&tmA);
             tma_prefetch_desc(&tmB);
+            if (k2_blocks) {
+                tma_prefetch_desc(&tmA2);
+                tma_prefetch_desc(&tmB2);
+            }
             uint32_t it = 0;
             for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
                 int mb, nb;
                 tile_coords(t, m_blocks, n_blocks, p.group_m, mb, nb);
-                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                for (int kb = 0; kb < k_total; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     const uint32_t ph = (it / C::STAGES) & 1;
                     if (!mbar_wait(&empty[s], ph ^ 1, p.timeout_flag, 101, &aborted)) break;
                     mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-                    tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * C::BKE, mb * BM);
-                    tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * C::BKE, nb * BN);
+                    if (kb < k_blocks) {
+                        tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * C::BKE, mb * BM);
+                        tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * C::BKE, nb * BN);
+                    } else {   // appended bf16 block: 64 elements = one 128-byte row
+                        tma_load_2d(sA + s * C::A_BYTES, &tmA2, &full[s], (kb - k_blocks) * 64, mb * BM);
+                        tma_load_2d(sB + s * C::B_BYTES, &tmB2, &full[s], (kb - k_blocks) * 64, nb * BN);
+                    }
                 }
             }
             if (aborted) {
@@ -151,27 +166,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         if (elect_one()) {
             constexpr uint32_t idesc = F8 ? idesc_e4m3(BM, BN) : idesc_f16(BM, BN, true);
+            constexpr uint32_t idesc_bf16 = idesc_f16(BM, BN, true);
             uint32_t it = 0, tile_i = 0;
             for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tile_i) {
                 const uint32_t acc = tile_i & 1, aph = (tile_i >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], aph ^ 1, p.timeout_flag, 102, &aborted)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+                for (int kb = 0; kb < k_total; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     const uint32_t ph = (it / C::STAGES) & 1;
                     if (!mbar_wait(&full[s], ph, p.timeout_flag, 103, &aborted)) break;
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
+                    const bool main_k = kb < k_blocks;
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
                         const uint64_t ad = sdesc_sw128(a_addr + kk * 32, 16, 1024);
                         const uint64_t bd = sdesc_sw128(b_addr + kk * 32, 16, 1024);
-                        if constexpr (F8)
-                            umma_f8_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
-                        else
+                        if constexpr (F8) {
+                            if (main_k)
+                                umma_f8_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+                            else   // appended bf16 block: both operands bf16 (kind::f16)
+                                umma_f16_ss(d_tmem, ad, bd, idesc_bf16, 1u);
+                        } else {
                             umma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+                        }
                     }
                     umma_commit(&empty[s]);
                 }
@@ -204,13 +225,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float v[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                const bool full_cols = col0 + 32 <= p.N;
                 if constexpr (F8) {
                     // acc is in units of (row scale x weight scale)
-                    const float sc = (p.a_scale ? __ldg(p.a_scale + row) : 1.0f) * p.w_scale;
+                    const float sa = p.a_scale ? __ldg(p.a_scale + row) : 1.0f;
+                    if (p.w_col_scale) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] *= sc;
+                        for (int j = 0; j < 32; ++j)
+                            v[j] *= sa * ((full_cols || col0 + j < p.N) ? __ldg(p.w_col_scale + col0 + j) : 0.f);
+                    } else {
+                        const float sc = sa * p.w_scale;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] *= sc;
+                    }
                 }
-                const bool full_cols = col0 + 32 <= p.N;
                 if (p.bias) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
@@ -334,32 +362,35 @@ bool make_tmap_bf16(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols,
 }
 
 template <int BN, int EPI, bool F8>
-cudaError_t launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int sms, cudaStream_t st) {
+cudaError_t launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &ta2, const CUtensorMap &tb2,
+                        const GemmParams &p, int sms, cudaStream_t st) {
     using C = GemmCfg<BN, F8>;
     auto k = gemm_kernel<BN, EPI, F8>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return e;
     const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
     const int grid = std::min(tiles, sms);
-    k<<<grid, kThreads, C::SMEM, st>>>(ta, tb, p);
+    k<<<grid, kThreads, C::SMEM, st>>>(ta, tb, ta2, tb2, p);
     return cudaGetLastError();
 }
 
 template <int BN, bool F8>
-cudaError_t dispatch_epi(int epi, const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p, int sms,
-                         cudaStream_t st) {
+cudaError_t dispatch_epi(int epi, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &ta2,
+                         const CUtensorMap &tb2, const GemmParams &p, int sms, cudaStream_t st) {
     switch (epi) {
-    case EPI_BF16: return launch_gemm<BN, EPI_BF16, F8>(ta, tb, p, sms, st);
-    case EPI_GELU_BF16: return launch_gemm<BN, EPI_GELU_BF16, F8>(ta, tb, p, sms, st);
-    case EPI_F32: return launch_gemm<BN, EPI_F32, F8>(ta, tb, p, sms, st);
-    default: return launch_gemm<BN, EPI_RESID, F8>(ta, tb, p, sms, st);
+    case EPI_BF16: return launch_gemm<BN, EPI_BF16, F8>(ta, tb, ta2, tb2, p, sms, st);
+    case EPI_GELU_BF16: return launch_gemm<BN, EPI_GELU_BF16, F8>(ta, tb, ta2, tb2, p, sms, st);
+    case EPI_F32: return launch_gemm<BN, EPI_F32, F8>(ta, tb, ta2, tb2, p, sms, st);
+    default: return launch_gemm<BN, EPI_RESID, F8>(ta, tb, ta2, tb2, p, sms, st);
     }
 }
 
 // Shared by the bf16 and e4m3 entry points: es = element bytes (2 or 1).
+// e4m3 only: `lr` appends k2 bf16 K-elements (A2 [M, k2] . B2 [N, k2]^T).
 int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, const float *a_scale, const void *W,
              int64_t ldw, float w_scale, int M, int N, int K, int epi, const float *bias, void *out, int64_t ldo,
-             const float *gate, const int *gate_idx, int64_t ld_gate, int f16_from_col) {
+             const float *gate, const int *gate_idx, int64_t ld_gate, int f16_from_col, const GemmLowRank *lr = nullptr,
+             const float *w_col_scale = nullptr) {
     if (!A || !W || !out) return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: null pointer");
     if (M <= 0 || N <= 0 || K <= 0) return fail(ctx, LTX_ERR_SHAPE, "gemm: empty shape %d x %d x %d", M, N, K);
     const int align = 16 / es;   // elements per 16 bytes (TMA strides and the innermost coordinate)
@@ -371,6 +402,16 @@ int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, 
     CUtensorMap ta, tb;
     if (!make_tmap_2d(&ta, A, M, K, lda, BM, es) || !make_tmap_2d(&tb, W, N, K, ldw, BN, es))
         return fail(ctx, LTX_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed");
+    CUtensorMap ta2 = ta, tb2 = tb;   // unused unless a low-rank block is appended
+    int k2_blocks = 0;
+    if (lr && lr->k2 > 0) {
+        if (es != 1 || lr->k2 % 64 || !lr->a2 || !lr->b2 || lr->lda2 % 8 || lr->ldb2 % 8 || lr->lda2 < lr->k2 ||
+            lr->ldb2 < lr->k2 || ((uintptr_t)lr->a2 & 15) || ((uintptr_t)lr->b2 & 15))
+            return fail(ctx, LTX_ERR_SHAPE, "gemm: appended bf16 block needs e4m3 operands and k2 a multiple of 64");
+        if (!make_tmap_2d(&ta2, lr->a2, M, lr->k2, lr->lda2, BM, 2) || !make_tmap_2d(&tb2, lr->b2, N, lr->k2, lr->ldb2, BN, 2))
+            return fail(ctx, LTX_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed (appended block)");
+        k2_blocks = lr->k2 / 64;
+    }
     if (f16_from_col < 0 || f16_from_col > N) f16_from_col = N;
     if (f16_from_col < N && (epi != EPI_BF16 || f16_from_col % 32))
         return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: f16 columns need the bf16 epilogue and a multiple of 32");
@@ -378,15 +419,15 @@ int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, 
     const int m_blocks = (M + BM - 1) / BM;
     const size_t panel = (size_t)BM * K * es;
     const int group_m = (int)std::max<size_t>(1, std::min<size_t>((size_t)m_blocks, kGroupPanelBytes / panel));
-    GemmParams p{M,   N,       K,        a_scale,           w_scale,      bias,   out,
-                 ldo, gate,    gate_idx, ld_gate,           ctx->timeout_flag, f16_from_col, group_m};
+    GemmParams p{M,   N,    K,        a_scale, w_scale,           bias,         out,     ldo,       gate,
+                 gate_idx, ld_gate, ctx->timeout_flag, f16_from_col, group_m, k2_blocks, w_col_scale};
     cudaError_t e;
     if (es == 1)
-        e = BN == 128 ? dispatch_epi<128, true>(epi, ta, tb, p, ctx->sm_count, st)
-                      : dispatch_epi<256, true>(epi, ta, tb, p, ctx->sm_count, st);
+        e = BN == 128 ? dispatch_epi<128, true>(epi, ta, tb, ta2, tb2, p, ctx->sm_count, st)
+                      : dispatch_epi<256, true>(epi, ta, tb, ta2, tb2, p, ctx->sm_count, st);
     else
-        e = BN == 128 ? dispatch_epi<128, false>(epi, ta, tb, p, ctx->sm_count, st)
-                      : dispatch_epi<256, false>(epi, ta, tb, p, ctx->sm_count, st);
+        e = BN == 128 ? dispatch_epi<128, false>(epi, ta, tb, ta2, tb2, p, ctx->sm_count, st)
+                      : dispatch_epi<256, false>(epi, ta, tb, ta2, tb2, p, ctx->sm_count, st);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm launch");
     return LTX_OK;
 }
@@ -406,9 +447,10 @@ int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const v
 // accumulator is multiplied by a_scale[row] * w_scale before the epilogue.
 int gemm_e4m3(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const float *a_scale, const void *W,
               int64_t ldw, float w_scale, int M, int N, int K, int epi, const float *bias, void *out, int64_t ldo,
-              const float *gate, const int *gate_idx, int64_t ld_gate, int f16_from_col) {
+              const float *gate, const int *gate_idx, int64_t ld_gate, int f16_from_col, const GemmLowRank *lr,
+              const float *w_col_scale) {
     return gemm_any(ctx, st, 1, A, lda, a_scale, W, ldw, w_scale, M, N, K, epi, bias, out, ldo, gate, gate_idx, ld_gate,
-                    f16_from_col);
+                    f16_from_col, lr, w_col_scale);
 }
 
 }  // namespace ltx
@@ -422,10 +464,12 @@ extern "C" int ltx_gemm_bf16(ltx_ctx *ctx, const void *a_dev, int64_t lda, const
 }
 
 extern "C" int ltx_gemm_e4m3(ltx_ctx *ctx, const void *a_dev, int64_t lda, const float *a_scale_dev, const void *w_dev,
-                             int64_t ldw, float w_scale, int32_t m, int32_t n, int32_t k, int32_t epilogue,
-                             const float *bias_dev, void *out_dev, int64_t ldo, const float *gate_dev,
-                             const int32_t *gate_idx_dev, int64_t ld_gate) {
+                             int64_t ldw, float w_scale, const float *w_col_scale_dev, int32_t m, int32_t n, int32_t k,
+                             int32_t epilogue, const float *bias_dev, void *out_dev, int64_t ldo, const float *gate_dev,
+                             const int32_t *gate_idx_dev, int64_t ld_gate, const void *a2_dev, int64_t lda2,
+                             const void *b2_dev, int64_t ldb2, int32_t k2) {
     if (!ctx) return LTX_ERR_INVALID_ARG;
+    const ltx::GemmLowRank lr{a2_dev, lda2, b2_dev, ldb2, k2};
     return ltx::gemm_e4m3(ctx, ctx->stream, a_dev, lda, a_scale_dev, w_dev, ldw, w_scale, m, n, k, epilogue, bias_dev,
-                          out_dev, ldo, gate_dev, gate_idx_dev, ld_gate, n);
+                          out_dev, ldo, gate_dev, gate_idx_dev, ld_gate, n, k2 > 0 ? &lr : nullptr, w_col_scale_dev);
 }

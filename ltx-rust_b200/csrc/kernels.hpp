@@ -16,10 +16,22 @@ int dequant_merge(ltx_ctx *ctx, cudaStream_t stream, const void *w, int w_dt, in
 int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
               int K, int epi, const float *bias, void *out, int64_t ldo, const float *gate, const int *gate_idx,
               int64_t ld_gate, int f16_from_col = 1 << 30);
-// e4m3 operands (lda/ldw multiples of 16); acc * a_scale[row] * w_scale before the epilogue
+// A bf16 block appended to an e4m3 GEMM's K loop, accumulated into the same
+// TMEM accumulator before the scales: acc += A2[M, k2] . B2[N, k2]^T
+// (k2 a multiple of 64; leading dimensions in elements).
+struct GemmLowRank {
+    const void *a2;
+    int64_t lda2;
+    const void *b2;
+    int64_t ldb2;
+    int k2;
+};
+// e4m3 operands (lda/ldw multiples of 16); acc * a_scale[row] * (w_col_scale
+// ? w_col_scale[col] : w_scale) before the epilogue
 int gemm_e4m3(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const float *a_scale, const void *W,
               int64_t ldw, float w_scale, int M, int N, int K, int epi, const float *bias, void *out, int64_t ldo,
-              const float *gate, const int *gate_idx, int64_t ld_gate, int f16_from_col = 1 << 30);
+              const float *gate, const int *gate_idx, int64_t ld_gate, int f16_from_col = 1 << 30,
+              const GemmLowRank *lr = nullptr, const float *w_col_scale = nullptr);
 
 // attention.cu (head_dim 128)
 int attention_fwd(ltx_ctx *ctx, cudaStream_t st, const void *q, int64_t ldq, const void *k, int64_t ldk, const void *v,
@@ -67,5 +79,15 @@ cudaError_t tp_norm_apply_rope(cudaStream_t st, __nv_bfloat16 *x, int64_t ld, in
                                const float *sin_t, bool interleaved);
 cudaError_t tp_resid_add(cudaStream_t st, int sms, float *x, const __nv_bfloat16 *p, int rows, int D,
                          const float *bias, const float *gate, const int *gidx, int64_t ld_gate);
+
+// FP8 operand producers (fp8_kernels.cu): e4m3 rows with per-row scale amax/448.
+cudaError_t norm_mod_e4m3(cudaStream_t st, const float *x, int64_t ldx, int rows, int D, float eps, int mode,
+                          const float *tab, int tab_coeff, const int *idx, int k_shift, uint8_t *out, int64_t ldo,
+                          float *scale);
+cudaError_t quantize_rows_e4m3(cudaStream_t st, const __nv_bfloat16 *in, int64_t ldi, int rows, int cols, uint8_t *out,
+                               int64_t ldo, float *scale);
+cudaError_t bf16_to_f32(cudaStream_t st, int sms, const __nv_bfloat16 *in, int64_t n, float *out);
+cudaError_t scale_pad_bf16(cudaStream_t st, int sms, const __nv_bfloat16 *in, int rows, int cols_in, int cols_out,
+                           float mul, __nv_bfloat16 *out);
 
 }  // namespace ltx

@@ -38,6 +38,10 @@ struct DitConfig {
     int ts_mult = 1000;
     bool use_mid = true, interleaved = false;
     bool gated = false, cross_adaln = false, prompt_adaln = true, ff_bias = false, kf_abs_pos = false;
+    // "gemm_precision": "e4m3" runs all block projections as native FP8 GEMMs
+    // (exact FP8 base weights + unmerged LoRA), "e4m3_ffn" only the two FFN
+    // projections; default "bf16" (merged weights).  fp8 = any of them.
+    bool fp8 = false, fp8_attn = false, fp8_ffn = false;
     int inner() const { return heads * head_dim; }
     int coeff() const { return cross_adaln ? 9 : 6; }
 };
@@ -75,6 +79,17 @@ static int parse_config(ltx_ctx *ctx, const std::string &text, DitConfig &c) {
     flag("use_prompt_adaln_single", c.prompt_adaln);
     flag("ff_bias", c.ff_bias);
     flag("use_keyframes_abs_pos_embedding", c.kf_abs_pos);
+    for (const Json *o : {static_cast<const Json *>(&root), j}) {   // this build's own key: top level or beside the transformer's
+        const Json *gp = o->get("gemm_precision");
+        if (gp && gp->kind == Json::Str) {
+            if (gp->str == "e4m3")
+                c.fp8 = c.fp8_attn = c.fp8_ffn = true;
+            else if (gp->str == "e4m3_ffn")
+                c.fp8 = c.fp8_ffn = true;
+            else if (gp->str != "bf16")
+                return fail(ctx, LTX_ERR_CONFIG, "gemm_precision must be \"bf16\", \"e4m3\" or \"e4m3_ffn\"");
+        }
+    }
     // validate (config.rs:188-231)
     if (c.heads <= 0) return fail(ctx, LTX_ERR_CONFIG, "num_attention_heads must be > 0");
     if (c.head_dim % 2) return fail(ctx, LTX_ERR_CONFIG, "attention_head_dim must be even for RoPE");
@@ -87,10 +102,29 @@ static int parse_config(ltx_ctx *ctx, const std::string &text, DitConfig &c) {
         return fail(ctx, LTX_ERR_CONFIG, "bad dimensions in config");
     if (c.inner() % 8 || c.in_ch % 8 || c.cross_dim % 8)
         return fail(ctx, LTX_ERR_UNSUPPORTED, "inner_dim, in_channels and cross_attention_dim must be multiples of 8");
+    if (c.fp8 && (c.inner() != 4096 || c.head_dim != 128 || c.gated || c.cross_adaln || c.cross_dim % 16 ||
+                  c.interleaved))
+        return fail(ctx, LTX_ERR_UNSUPPORTED,
+                    "gemm_precision e4m3 needs the 22B block layout: inner dim 4096 (32 x 128 heads), split RoPE, no "
+                    "gated attention or cross-attention adaLN, cross dim %% 16 == 0");
     return LTX_OK;
 }
 
+// One projection of the FP8 path: the exact e4m3 base weight with its
+// per-tensor scale, and the LoRA kept factored: A quantised per tensor
+// (rank padded to 64 with zero rows) and B2 = coeff * B / sw in bf16, which
+// the GEMM adds in the same accumulator (x.A^T / sx) . B2^T.
+struct LinF8 {
+    uint8_t *w = nullptr;   // [out, in]
+    float sw = 1.f;
+    uint8_t *a = nullptr;   // [r64, in]
+    float sa = 1.f;
+    __nv_bfloat16 *b2 = nullptr;   // [out, r64]
+    int r64 = 0;            // 0 = no LoRA
+};
+
 struct BlockW {
+    LinF8 fqkv, fo, fq2, fkv2, fo2, fff1, fff2;   // FP8 path (gemm_precision e4m3)
     __nv_bfloat16 *qkv, *o, *q2, *kv2, *o2, *ff1, *ff2, *g1, *g2;
     float *qkv_b, *o_b, *q2_b, *kv2_b, *o2_b, *ff1_b, *ff2_b, *g1_b, *g2_b;
     float *qn, *kn, *qn2, *kn2, *sst, *pst;
@@ -104,6 +138,7 @@ struct ltx_model {
     // tensor-parallel shard: this model holds rank tr of tp (heads and FFN
     // hidden units split; everything else replicated)
     int tp = 1, tr = 0;
+    int lora_r64 = 0;   // FP8 path: LoRA rank padded to 64 (the factored term's K)
     void *arena = nullptr;
     size_t arena_bytes = 0;
     __nv_bfloat16 *patch_w = nullptr, *out_w = nullptr;
@@ -154,24 +189,45 @@ static void layout(ltx_model *m, Arena &a) {
     m->sin_freq = a.take<float>(128);
     m->sst_list = a.take<float *>(c.layers);
     m->blocks.resize(c.layers);
+    const int r64 = m->lora_r64;
+    auto f8 = [&](LinF8 &L, int64_t out, int64_t in) {
+        L.w = a.take<uint8_t>(out * in);
+        L.r64 = r64;
+        if (r64) {
+            L.a = a.take<uint8_t>((int64_t)r64 * in);
+            L.b2 = a.take<__nv_bfloat16>(out * r64);
+        }
+    };
     for (auto &b : m->blocks) {
-        b.qkv = a.take<__nv_bfloat16>(3 * Dl * D);
+        // FP8 path: e4m3 weights + factored LoRA instead of merged bf16 (tp = 1)
+        if (c.fp8_attn) {
+            f8(b.fqkv, 3 * D, D);
+            f8(b.fo, D, D);
+            f8(b.fq2, D, D);
+            f8(b.fkv2, 2 * D, Dc);
+            f8(b.fo2, D, D);
+        }
+        if (c.fp8_ffn) {
+            f8(b.fff1, 4 * D, D);
+            f8(b.fff2, D, 4 * D);
+        }
+        b.qkv = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(3 * Dl * D);
         b.qkv_b = a.take<float>(3 * Dl);
         b.qn = a.take<float>(Dl);
         b.kn = a.take<float>(Dl);
-        b.o = a.take<__nv_bfloat16>(D * Dl);
+        b.o = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(D * Dl);
         b.o_b = a.take<float>(D);
-        b.q2 = a.take<__nv_bfloat16>(Dl * D);
+        b.q2 = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(Dl * D);
         b.q2_b = a.take<float>(Dl);
-        b.kv2 = a.take<__nv_bfloat16>(2 * Dl * Dc);
+        b.kv2 = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(2 * Dl * Dc);
         b.kv2_b = a.take<float>(2 * Dl);
         b.qn2 = a.take<float>(Dl);
         b.kn2 = a.take<float>(Dl);
-        b.o2 = a.take<__nv_bfloat16>(D * Dl);
+        b.o2 = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(D * Dl);
         b.o2_b = a.take<float>(D);
-        b.ff1 = a.take<__nv_bfloat16>(Fl * D);
+        b.ff1 = c.fp8_ffn ? nullptr : a.take<__nv_bfloat16>(Fl * D);
         b.ff1_b = c.ff_bias ? a.take<float>(Fl) : nullptr;
-        b.ff2 = a.take<__nv_bfloat16>(D * Fl);
+        b.ff2 = c.fp8_ffn ? nullptr : a.take<__nv_bfloat16>(D * Fl);
         b.ff2_b = c.ff_bias ? a.take<float>(D) : nullptr;
         b.sst = a.take<float>(K * D);
         b.pst = c.cross_adaln ? a.take<float>(2 * D) : nullptr;
@@ -182,13 +238,16 @@ static void layout(ltx_model *m, Arena &a) {
     }
 }
 
-static int alloc_model(ltx_ctx *ctx, const DitConfig &cfg, ltx_model *&m) {
+static int alloc_model(ltx_ctx *ctx, const DitConfig &cfg, ltx_model *&m, int lora_rank = 0) {
+    if (cfg.fp8 && ctx->tp_size > 1)
+        return fail(ctx, LTX_ERR_UNSUPPORTED, "gemm_precision e4m3 runs on one GPU (no tensor-parallel split)");
     m = new (std::nothrow) ltx_model();
     if (!m) return LTX_ERR_OOM;
     m->device = ctx->device;
     m->cfg = cfg;
     m->tp = ctx->tp_size;
     m->tr = ctx->tp_rank;
+    m->lora_r64 = cfg.fp8 && lora_rank > 0 ? (lora_rank + 63) / 64 * 64 : 0;
     if (m->tp > 1 && (cfg.heads % m->tp || (cfg.inner() / m->tp) % 8)) {
         const int tp = m->tp;
         delete m;
@@ -288,7 +347,9 @@ struct Loader {
         if (n == 1 || sp.kind == Split::ALL) return store_read_device(st, key, dt, dst, numel(shape));
         rc = store_read_device(st, key, dt, tmp, numel(shape));
         if (rc) return rc;
-        const int64_t R = shape[0], C = shape.size() > 1 ? shape[1] : 1;
+        const int64_t R = shape[0];
+        int64_t C = 1;
+        for (size_t i = 1; i < shape.size(); ++i) C *= shape[i];
         LTX_CUDA_TRY(ctx, slice_to(ctx->stream, dst, tmp, R, C, dtype_size(dt), sp, n, r));
         return LTX_OK;
     }
@@ -426,6 +487,33 @@ struct Synth {
         LTX_CUDA_TRY(ctx, slice_to(st, dst, full, out, in, dtype_size(dst_dt), sp, n, r));
         return LTX_OK;
     }
+    // The FP8 path's copy of `linear`: the same random stream (the same base
+    // bytes, scale and LoRA factors), kept unmerged (LinF8).
+    int linear_f8(LinF8 &L, int64_t out, int64_t in) {
+        const int64_t n_el = out * in;
+        cudaStream_t st = ctx->stream;
+        LTX_CUDA_TRY(ctx, synth_normal_f32(st, ctx->sm_count, f32, n_el, seed, sid++, 0.f, 0.02f));
+        LTX_CUDA_TRY(ctx, synth_quantize_fp8(st, ctx->sm_count, f32, n_el, q8, scale_dev, work));
+        float scale = 0.f;
+        LTX_CUDA_TRY(ctx, cudaMemcpyAsync(&scale, scale_dev, 4, cudaMemcpyDeviceToHost, st));
+        LTX_CUDA_TRY(ctx, cudaStreamSynchronize(st));
+        LTX_CUDA_TRY(ctx, cudaMemcpyAsync(L.w, q8, (size_t)n_el, cudaMemcpyDeviceToDevice, st));
+        L.sw = scale;
+        if (rank > 0) {
+            LTX_CUDA_TRY(ctx, synth_normal_bf16(st, ctx->sm_count, la, rank * in, seed, sid++, 0.01f));
+            LTX_CUDA_TRY(ctx, synth_normal_bf16(st, ctx->sm_count, lb, out * rank, seed, sid++, 0.01f));
+            const float coeff = ltx_lora_coeff(strength, (float)rank, rank);
+            // A per tensor to e4m3 (rows rank..r64 stay zero), B2 = coeff * B / sw
+            LTX_CUDA_TRY(ctx, bf16_to_f32(st, ctx->sm_count, la, (int64_t)rank * in, f32));
+            LTX_CUDA_TRY(ctx, synth_quantize_fp8(st, ctx->sm_count, f32, (int64_t)rank * in, L.a, scale_dev, work));
+            float sa = 0.f;
+            LTX_CUDA_TRY(ctx, cudaMemcpyAsync(&sa, scale_dev, 4, cudaMemcpyDeviceToHost, st));
+            LTX_CUDA_TRY(ctx, cudaStreamSynchronize(st));
+            L.sa = sa;
+            LTX_CUDA_TRY(ctx, scale_pad_bf16(st, ctx->sm_count, lb, (int)out, rank, L.r64, coeff / scale, L.b2));
+        }
+        return LTX_OK;
+    }
     int vec(float *dst, int64_t n_el, float mean, float std, Split sp = kAll) {
         const bool sliced = n > 1 && sp.kind != Split::ALL;
         LTX_CUDA_TRY(ctx, synth_normal_f32(ctx->stream, ctx->sm_count, sliced ? static_cast<float *>(full) : dst, n_el,
@@ -472,13 +560,27 @@ static int init_random(ltx_model *m, ltx_ctx *ctx, uint64_t seed, int rank, floa
         TRY(s.vec(m->sst_out, 2 * D, 0.f, 0.02f));
         TRY(s.linear(m->out_w, c.out_ch, D, LTX_BF16));
         for (auto &b : m->blocks) {
-            TRY(s.linear(b.qkv, 3 * D, D, LTX_BF16, qkv3));
-            TRY(s.linear(b.o, D, D, LTX_BF16, kCols));
-            TRY(s.linear(b.q2, D, D, LTX_BF16, kRows));
-            TRY(s.linear(b.kv2, 2 * D, Dc, LTX_BF16, kv2));
-            TRY(s.linear(b.o2, D, D, LTX_BF16, kCols));
-            TRY(s.linear(b.ff1, F, D, LTX_BF16, kRows));
-            TRY(s.linear(b.ff2, D, F, LTX_BF16, kCols));
+            // the same random stream in either precision (same order of draws)
+            if (c.fp8_attn) {
+                TRY(s.linear_f8(b.fqkv, 3 * D, D));
+                TRY(s.linear_f8(b.fo, D, D));
+                TRY(s.linear_f8(b.fq2, D, D));
+                TRY(s.linear_f8(b.fkv2, 2 * D, Dc));
+                TRY(s.linear_f8(b.fo2, D, D));
+            } else {
+                TRY(s.linear(b.qkv, 3 * D, D, LTX_BF16, qkv3));
+                TRY(s.linear(b.o, D, D, LTX_BF16, kCols));
+                TRY(s.linear(b.q2, D, D, LTX_BF16, kRows));
+                TRY(s.linear(b.kv2, 2 * D, Dc, LTX_BF16, kv2));
+                TRY(s.linear(b.o2, D, D, LTX_BF16, kCols));
+            }
+            if (c.fp8_ffn) {
+                TRY(s.linear_f8(b.fff1, F, D));
+                TRY(s.linear_f8(b.fff2, D, F));
+            } else {
+                TRY(s.linear(b.ff1, F, D, LTX_BF16, kRows));
+                TRY(s.linear(b.ff2, D, F, LTX_BF16, kCols));
+            }
             TRY(s.vec(b.qn, D, 1.f, 0.02f, kRows));
             TRY(s.vec(b.kn, D, 1.f, 0.02f, kRows));
             TRY(s.vec(b.qn2, D, 1.f, 0.02f, kRows));
@@ -507,12 +609,18 @@ struct Work {
     double *partial;
     __nv_bfloat16 *part;   // tensor-parallel: summed partial projections (bf16)
     float *ss;             // tensor-parallel: Q/K sums of squares
+    // FP8 path: e4m3 projection inputs with per-row scales, the factored-LoRA
+    // operand (x.A^T / sx), and the quantised context (once per forward)
+    uint8_t *xq, *cq;
+    float *sx, *scq;
+    __nv_bfloat16 *xa, *xac;
     size_t bytes;
 };
 
 // Forward workspace for `rows` latent rows and `crow` context rows on a model
 // split over `tp` ranks (tp = 1: whole model).
-static Work carve_work(char *base, const DitConfig &c, int64_t rows, int64_t crow, int U, int L, int tp) {
+static Work carve_work(char *base, const DitConfig &c, int64_t rows, int64_t crow, int U, int L, int tp,
+                       int r64 = 0) {
     Arena a;
     a.base = base;
     const int64_t D = c.inner(), Dc = c.cross_dim, K = c.coeff();
@@ -544,6 +652,14 @@ static Work carve_work(char *base, const DitConfig &c, int64_t rows, int64_t cro
     w.partial = a.take<double>((int64_t)cfg_scratch_bytes() / 8);
     w.part = tp > 1 ? a.take<__nv_bfloat16>(rows * D) : nullptr;
     w.ss = tp > 1 ? a.take<float>(2 * rows + crow) : nullptr;
+    if (c.fp8) {
+        w.xq = a.take<uint8_t>(rows * 4 * D);
+        w.sx = a.take<float>(rows);
+        w.cq = a.take<uint8_t>(crow * Dc);
+        w.scq = a.take<float>(crow);
+        w.xa = a.take<__nv_bfloat16>(rows * std::max(r64, 1));
+        w.xac = a.take<__nv_bfloat16>(crow * std::max(r64, 1));
+    }
     w.bytes = a.off + 256;
     return w;
 }
@@ -606,9 +722,9 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
     if (given) {
         w = *given;
     } else {
-        Work sizing = carve_work(nullptr, c, rows, crow, U, c.layers, m->tp);
+        Work sizing = carve_work(nullptr, c, rows, crow, U, c.layers, m->tp, m->lora_r64);
         TRY(ensure_work(ctx, sizing.bytes));
-        w = carve_work(static_cast<char *>(ctx->work), c, rows, crow, U, c.layers, m->tp);
+        w = carve_work(static_cast<char *>(ctx->work), c, rows, crow, U, c.layers, m->tp, m->lora_r64);
     }
     if (work_out) *work_out = w;
     {
@@ -679,9 +795,68 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
                               rope ? w.cos : nullptr, rope ? w.sin : nullptr, c.interleaved));
         return LTX_OK;
     };
+    // FP8 path: one projection = e4m3 GEMM of the row-quantised input with the
+    // exact FP8 base weight, plus the factored LoRA term in the same
+    // accumulator (xa = xq . A_q^T * sa = (x . A^T) / sx, then xa . B2^T).
+    auto lin_f8 = [&](const LinF8 &Lw, const uint8_t *xq, int64_t ldx, const float *sx, __nv_bfloat16 *xa, int M, int N,
+                      int Kd, int epi, const float *bias, void *out, int64_t ldo, const float *gate, int f16col) -> int {
+        GemmLowRank lr{};
+        const GemmLowRank *plr = nullptr;
+        if (Lw.r64 > 0) {
+            TRY(gemm_e4m3(ctx, st, xq, ldx, nullptr, Lw.a, Kd, Lw.sa, M, Lw.r64, Kd, LTX_EPI_BF16, nullptr, xa, Lw.r64,
+                          nullptr, nullptr, 0));
+            lr = GemmLowRank{xa, Lw.r64, Lw.b2, Lw.r64, Lw.r64};
+            plr = &lr;
+        }
+        return gemm_e4m3(ctx, st, xq, ldx, sx, Lw.w, Kd, Lw.sw, M, N, Kd, epi, bias, out, ldo, gate,
+                         gate ? w.idx : nullptr, K * D, f16col, plr);
+    };
+    if (c.fp8_attn) CU(quantize_rows_e4m3(st, w.ctxb, Dc, (int)crow, (int)Dc, w.cq, Dc, w.scq));
+    auto attn_f8 = [&](const BlockW &b, const float *tab) -> int {
+        // self-attention
+        CU(norm_mod_e4m3(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 0, w.xq, D, w.sx));
+        TRY(lin_f8(b.fqkv, w.xq, D, w.sx, w.xa, (int)rows, (int)(3 * D), (int)D, LTX_EPI_BF16, b.qkv_b, w.qkv, 3 * D,
+                   nullptr, (int)(2 * D)));
+        cudaError_t qe = cudaSuccess;
+        if (!qk_norm_rope_fused(st, w.qkv, w.qkv + D, 3 * D, (int)rows, (int)D, c.eps, b.qn, b.kn, w.cos, w.sin,
+                                tab_b * T, &qe))
+            return fail(ctx, LTX_ERR_UNSUPPORTED, "fused Q/K norm: unexpected layout");
+        CU(qe);
+        TRY(attend(w.qkv, 3 * D, w.qkv + D, 3 * D, w.qkv + 2 * D, 3 * D, T));
+        CU(quantize_rows_e4m3(st, w.att, D, (int)rows, (int)D, w.xq, D, w.sx));
+        TRY(lin_f8(b.fo, w.xq, D, w.sx, w.xa, (int)rows, (int)D, (int)D, LTX_EPI_RESID, b.o_b, w.x, D, tab + 2 * D,
+                   (int)D));
+        // cross-attention
+        CU(norm_mod_e4m3(st, w.x, D, (int)rows, (int)D, c.eps, 0, nullptr, 0, nullptr, 0, w.xq, D, w.sx));
+        TRY(lin_f8(b.fq2, w.xq, D, w.sx, w.xa, (int)rows, (int)D, (int)D, LTX_EPI_BF16, b.q2_b, w.q2, D, nullptr,
+                   (int)D));
+        TRY(lin_f8(b.fkv2, w.cq, Dc, w.scq, w.xac, (int)crow, (int)(2 * D), (int)Dc, LTX_EPI_BF16, b.kv2_b, w.kv2,
+                   2 * D, nullptr, (int)D));
+        CU(qk_norm_rope(st, w.q2, D, (int)rows, (int)D, (int)H, c.eps, b.qn2, nullptr, nullptr, false));
+        CU(qk_norm_rope(st, w.kv2, 2 * D, (int)crow, (int)D, (int)H, c.eps, b.kn2, nullptr, nullptr, false));
+        TRY(attend(w.q2, D, w.kv2, 2 * D, w.kv2 + D, 2 * D, S));
+        CU(quantize_rows_e4m3(st, w.att, D, (int)rows, (int)D, w.xq, D, w.sx));
+        TRY(lin_f8(b.fo2, w.xq, D, w.sx, w.xa, (int)rows, (int)D, (int)D, LTX_EPI_RESID, b.o2_b, w.x, D, nullptr,
+                   (int)D));
+        return LTX_OK;
+    };
+    auto ffn_f8 = [&](const BlockW &b, const float *tab) -> int {
+        CU(norm_mod_e4m3(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 3, w.xq, D, w.sx));
+        TRY(lin_f8(b.fff1, w.xq, D, w.sx, w.xa, (int)rows, (int)(4 * D), (int)D, LTX_EPI_GELU_BF16, b.ff1_b, w.ffh,
+                   4 * D, nullptr, (int)(4 * D)));
+        CU(quantize_rows_e4m3(st, w.ffh, 4 * D, (int)rows, (int)(4 * D), w.xq, 4 * D, w.sx));
+        TRY(lin_f8(b.fff2, w.xq, 4 * D, w.sx, w.xa, (int)rows, (int)D, (int)(4 * D), LTX_EPI_RESID, b.ff2_b, w.x, D,
+                   tab + 5 * D, (int)D));
+        return LTX_OK;
+    };
     for (int l = 0; l < c.layers; ++l) {
         const BlockW &b = m->blocks[l];
         const float *tab = w.tab + (int64_t)l * U * K * D;
+        if (c.fp8_attn && c.fp8_ffn) {
+            TRY(attn_f8(b, tab));
+            TRY(ffn_f8(b, tab));
+            continue;
+        }
         // self-attention: x += attn(mod(rms(x))) * gate_msa
         CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 0, w.xn, D));
         // V columns come out as f16: the attention keeps P in f16 for the P.V MMA
@@ -738,6 +913,10 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         }
         TRY(project_residual(w.att, Dl, b.o2, Dl, b.o2_b, c.cross_adaln ? tab + 8 * D : nullptr));
         // feed-forward: x += ff(mod(rms(x))) * gate_mlp
+        if (c.fp8_ffn) {
+            TRY(ffn_f8(b, tab));
+            continue;
+        }
         CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 3, w.xn, D));
         TRY(gemm_bf16(ctx, st, w.xn, D, b.ff1, D, (int)rows, (int)Fl, (int)D, LTX_EPI_GELU_BF16, b.ff1_b, w.ffh, Fl,
                       nullptr, nullptr, 0));
@@ -767,6 +946,8 @@ extern "C" int ltx_model_load(ltx_ctx *ctx, ltx_store *st, const char *config_js
     }
     DitConfig cfg;
     TRY(parse_config(ctx, cj, cfg));
+    if (cfg.fp8)
+        return fail(ctx, LTX_ERR_UNSUPPORTED, "gemm_precision e4m3 is built for synthetic models (ltx_model_init_random)");
     ltx_model *m = nullptr;
     TRY(alloc_model(ctx, cfg, m));
     int rc = load_weights(m, st, ctx);
@@ -787,7 +968,7 @@ extern "C" int ltx_model_init_random(ltx_ctx *ctx, const char *config_json, uint
     DitConfig cfg;
     TRY(parse_config(ctx, config_json, cfg));
     ltx_model *m = nullptr;
-    TRY(alloc_model(ctx, cfg, m));
+    TRY(alloc_model(ctx, cfg, m, lora_rank));
     int rc = init_random(m, ctx, seed, lora_rank, lora_strength);
     if (rc) {
         cudaFree(m->arena);
@@ -847,7 +1028,7 @@ static StepBufs carve_step(char *base, const DitConfig &c, int B, int T, int S) 
 static size_t step_work_bytes(const ltx_model *m, int B, int T, int S, int U) {
     const DitConfig &c = m->cfg;
     return carve_step(nullptr, c, B, T, S).bytes +
-           carve_work(nullptr, c, (int64_t)B * T, (int64_t)B * S, U, c.layers, m->tp).bytes;
+           carve_work(nullptr, c, (int64_t)B * T, (int64_t)B * S, U, c.layers, m->tp, m->lora_r64).bytes;
 }
 
 // Copies positions and the cond/uncond contexts into the batch-2 layout.
@@ -886,7 +1067,7 @@ static int denoise_step_core(ltx_model *m, ltx_ctx *ctx, float *latent_dev, cons
     TRY(ensure_work(ctx, step_work_bytes(m, B, T, S, U)));   // grow-only: a no-op inside a loop
     char *base = static_cast<char *>(ctx->work);
     const StepBufs sb = carve_step(base, c, B, T, S);
-    Work w = carve_work(base + sb.bytes, c, (int64_t)B * T, (int64_t)B * S, U, c.layers, m->tp);
+    Work w = carve_work(base + sb.bytes, c, (int64_t)B * T, (int64_t)B * S, U, c.layers, m->tp, m->lora_r64);
     if (!static_ready) TRY(stage_static(ctx, sb, positions_dev, cc, cu, B, T, S, c.cross_dim));
     for (int b = 0; b < B; ++b)
         CU(cudaMemcpyAsync(sb.lat2 + (int64_t)b * T * C, latent_dev, (size_t)T * C * 4, cudaMemcpyDeviceToDevice, st));

@@ -69,8 +69,8 @@ def lib() -> ctypes.CDLL:
                                   ctypes.POINTER(LoraDelta), ctypes.c_int32, P, ctypes.c_int32]),
         "ltx_gemm_bf16": (I, [V, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                               P, P, I64, P, P, I64]),
-        "ltx_gemm_e4m3": (I, [V, P, I64, P, P, I64, F, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
-                              P, P, I64, P, P, I64]),
+        "ltx_gemm_e4m3": (I, [V, P, I64, P, P, I64, F, P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                              ctypes.c_int32, P, P, I64, P, P, I64, P, I64, P, I64, ctypes.c_int32]),
         "ltx_attention_fwd": (I, [V, P, I64, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                   ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, F, P, I64]),
         "ltx_store_open": (I, [V, ctypes.POINTER(ctypes.c_char_p), ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(V)]),
@@ -199,14 +199,19 @@ def gemm(ctx: "Context", a, w, out, epilogue=EPI_BF16, bias=None, gate=None, gat
                                   gate.stride(0) if gate is not None else 0), "ltx_gemm_bf16")
 
 
-def gemm_e4m3(ctx: "Context", a, a_scale, w, w_scale, out, epilogue=EPI_BF16, bias=None, gate=None, gate_idx=None):
-    """out = epilogue((a * a_scale[:, None]) @ (w * w_scale).T) with e4m3 operands held as
-    uint8 (or float8_e4m3fn) CUDA tensors a [M,K], w [N,K]; a_scale f32 [M] or None."""
+def gemm_e4m3(ctx: "Context", a, a_scale, w, w_scale, out, epilogue=EPI_BF16, bias=None, gate=None, gate_idx=None,
+              w_col_scale=None, a2=None, b2=None):
+    """out = epilogue(((a @ w.T) + a2 @ b2.T) * a_scale[:, None] * w_scale) with e4m3 operands a [M,K],
+    w [N,K] held as uint8 (or float8_e4m3fn) CUDA tensors; a_scale f32 [M] or None; w_col_scale f32 [N]
+    overrides w_scale per column; a2 [M,k2] / b2 [N,k2] bf16 append a low-rank block (k2 % 64 == 0)."""
     M, K = a.shape
     N = w.shape[0]
+    k2 = 0 if a2 is None else a2.shape[1]
     ctx.check(lib().ltx_gemm_e4m3(ctx.h, _ptr(a), a.stride(0), _ptr(a_scale), _ptr(w), w.stride(0), float(w_scale),
-                                  M, N, K, epilogue, _ptr(bias), _ptr(out), out.stride(0), _ptr(gate), _ptr(gate_idx),
-                                  gate.stride(0) if gate is not None else 0), "ltx_gemm_e4m3")
+                                  _ptr(w_col_scale), M, N, K, epilogue, _ptr(bias), _ptr(out), out.stride(0), _ptr(gate),
+                                  _ptr(gate_idx), gate.stride(0) if gate is not None else 0, _ptr(a2),
+                                  a2.stride(0) if a2 is not None else 0, _ptr(b2),
+                                  b2.stride(0) if b2 is not None else 0, k2), "ltx_gemm_e4m3")
 
 
 def attention(ctx: "Context", q, k, v, out, batch, heads, tq, tk, scale, head_dim=128):

@@ -375,3 +375,44 @@ def test_apply_noise_bit_exact(ctx):
                              torch.from_numpy(mask[0, :, 0].copy()).cuda(), s)
         ctx.synchronize()
         assert np.array_equal(d.cpu().numpy().view(np.uint32), exp.view(np.uint32)), s
+
+
+@pytest.mark.parametrize("prec,bar", [("e4m3_ffn", 3e-2), ("e4m3", 6e-2)])
+@pytest.mark.parametrize("layers", [1, 2])
+def test_fp8_model_matches_bf16_model(ctx, layers, prec, bar):
+    """Native FP8 block projections (exact e4m3 base weights, per-row e4m3 activations, LoRA
+    factored in the same accumulator) against the bf16 model built from the same synthetic
+    weights (itself checked against the oracle above).
+
+    e4m3_ffn (the two FFN projections, 56% of the block's GEMM FLOPs) meets the north star's
+    FP8 bar of rel-L2 <= 3e-2.  e4m3 on all seven projections does not: e4m3 keeps 3 mantissa
+    bits, so each quantised activation carries ~3.6% rounding error, and in this synthetic
+    model the block update dominates the residual stream; its bound here is 6e-2."""
+    import json
+    import ltx_b200
+    from dit_checkpoint import small_config
+    cfg = small_config(heads=32, head_dim=128, layers=layers)
+    outs = {}
+    lat, ts, pos, ctxt = make_inputs(cfg, F=2, Hh=8, W=8, S=64, seed=3)
+    for p in ("bf16", prec):
+        c = dict(cfg, gemm_precision=p)
+        model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(c), seed=5, lora_rank=64, lora_strength=1.0)
+        out = torch.empty(lat.shape, dtype=torch.float32, device="cuda")
+        model.forward(*(torch.from_numpy(a).cuda() for a in (lat, ts, pos, ctxt)), out)
+        ctx.synchronize()
+        outs[p] = out.cpu().numpy()
+        model.close()
+    err = rel_l2(outs[prec], outs["bf16"])
+    print(f"\n{prec} vs bf16 model ({layers} block(s)): rel-L2 {err:.2e}")
+    assert err < bar
+
+
+def test_fp8_config_rejections(ctx):
+    import json
+    import ltx_b200
+    from dit_checkpoint import small_config
+    for bad in (dict(small_config(heads=2, head_dim=128, layers=1), gemm_precision="e4m3"),       # not the 22B width
+                dict(small_config(heads=32, head_dim=128, layers=1), gemm_precision="fp4")):
+        with pytest.raises(ltx_b200.LtxError) as e:
+            ltx_b200.VideoTransformer.init_random(ctx, json.dumps(bad), seed=1, lora_rank=8)
+        assert e.value.kind in ("UNSUPPORTED", "CONFIG")
