@@ -121,13 +121,13 @@ constexpr int kWarps = 8;
 constexpr int kRowsPerWarp = 16;
 constexpr int kTileRows = kWarps * kRowsPerWarp;  // 128
 constexpr int kTileCols = 128;                     // per lane: 4 columns at lane*4
-constexpr int kRChunk = 16;                        // chain steps per stage
+constexpr int kRChunk = 32;                        // chain steps per stage
 
 struct MergeSmem {
-    float a[2][kRChunk][kTileCols];    // A chain rows                       16 KB
-    float2 c[2][kRChunk][kTileRows];   // {c, c} = coeff*B, paired for FFMA2  32 KB
+    float a[2][kRChunk][kTileCols];    // A chain rows                       32 KB
+    float2 c[2][kRChunk][kTileRows];   // {c, c} = coeff*B, paired for FFMA2  64 KB
     uint8_t w8[kTileRows][kTileCols];  // FP8 base tile                       16 KB
-};
+};   // 112 KB: two CTAs per SM
 
 struct ChainMap {
     int n;                      // deltas
@@ -211,9 +211,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
     const int64_t mycol = col0 + lane * 4;
     if (base_vec) {
         // FP8 only: decode the staged base tile.
-        if (nchunks > 1) issue(1, 1);
-        cp_async_commit();
-        cp_async_wait<1>();
+        cp_async_wait<0>();
         __syncthreads();
 #pragma unroll
         for (int i = 0; i < kRowsPerWarp; ++i) {
@@ -245,7 +243,6 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 
     for (int ch = 0; ch < nchunks; ++ch) {
         const int buf = ch & 1;
-        // With base_vec, chunk ch+1 was issued one step earlier (chunk 1 in the prologue).
         if (!base_vec) {
             if (ch + 1 < nchunks) {
                 issue(ch + 1, buf ^ 1);
@@ -255,10 +252,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
                 cp_async_wait<0>();
             }
         } else {
-            // chunk ch is in the oldest outstanding group; chunk ch+1 (if any) in the newer one.
-            if (ch + 1 < nchunks) cp_async_wait<1>(); else cp_async_wait<0>();
+            cp_async_wait<0>();   // chunk ch (the only group in flight) has landed
         }
+        // One barrier per chunk: past it every thread's copies of chunk ch have
+        // landed and every thread has finished chunk ch-1, so the other buffer
+        // can be refilled with chunk ch+1 under this chunk's FMAs.
         __syncthreads();
+        if (base_vec && ch + 1 < nchunks) {
+            issue(ch + 1, buf ^ 1);
+            cp_async_commit();
+        }
         const int nr = min(kRChunk, ktot - ch * kRChunk);
         auto step = [&](int r) {
             const float4 a4 = *reinterpret_cast<const float4 *>(&s.a[buf][r][lane * 4]);
@@ -279,11 +282,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
         } else {
             for (int r = 0; r < nr; ++r) step(r);
         }
-        __syncthreads();   // buffer `buf` is refilled below
-        if (base_vec && ch + 2 < nchunks) {
-            issue(ch + 2, buf);
-            cp_async_commit();
-        }
+        if (!base_vec) __syncthreads();   // buffer `buf` is refilled at the top of the next chunk
     }
 
 #pragma unroll
