@@ -404,6 +404,85 @@ def run_denoise_step(args, rank, ws, device):
     return res
 
 
+def run_chunk_pipeline(args, rank, ws, device):
+    """Config 5: 8 overlapping temporal chunks (pixel chunk_len 121 -> 16 latent
+    frames, overlap 16 pixel frames -> 2 latent frames), each a config-4 state
+    denoised through the full 8-step schedule with ltx_denoise_loop, chunks
+    spread over the ranks (one per GPU at 8 GPUs), then the seam frames are
+    exchanged point to point, smoothstep-blended on the device
+    (ltx_seam_blend) and the clip gathered on rank 0.  Total work is fixed
+    (strong scaling); value = chunks x steps x 12288 tokens / time."""
+    import numpy as np
+    import torch
+    import ltx_b200
+    from ltx_b200 import chunks as cp
+    torch.cuda.set_device(device)
+    ctx = ltx_b200.Context(device)
+    n_chunks, lat_len, lat_ov = 8, LAT_F, 2
+    pix_plan = ltx_b200.chunk_plan(105 * (n_chunks - 1) + 121, 121, 16)
+    assert len(pix_plan) == n_chunks and all(c[2] in (0, 16) for c in pix_plan)
+    plan = [(n * (lat_len - lat_ov), n * (lat_len - lat_ov) + lat_len, lat_ov if n else 0) for n in range(n_chunks)]
+    total_lat = plan[-1][1]
+    asg = cp.assign(n_chunks, ws)
+    model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(CFG4), seed=7, lora_rank=64, lora_strength=1.0)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+    states = {}
+    for n in asg[rank]:
+        inp = make_step_inputs(LAT_F, LAT_H, LAT_W, S_CTX, D, seed=1000 + n)   # seed = base + chunk index
+        states[n] = {k: dev(inp[k]) for k in ("latent", "clean", "mask", "positions", "ctx_cond", "ctx_uncond")}
+        states[n]["mask_h"] = np.ascontiguousarray(inp["mask"], np.float32)
+        states[n]["sigmas"] = inp["sigmas"]
+    outs = {n: torch.empty(T_TARGET, 128, device="cuda") for n in asg[rank]}
+
+    def pipeline(steps_limit=None):
+        for n in asg[rank]:
+            st = states[n]
+            lat = st["latent"].clone()
+            sig = st["sigmas"] if steps_limit is None else st["sigmas"][:steps_limit + 1]
+            model.denoise_loop(lat, st["clean"], st["mask"], st["positions"], st["ctx_cond"], st["ctx_uncond"],
+                               sig, 3.0, 0.7, target_tokens=T_TARGET, out=outs[n], mask_host=st["mask_h"])
+        data = {n: outs[n].view(lat_len, -1) for n in asg[rank]}
+        recv = cp.exchange_seams(plan, asg, rank, data)
+        cp.blend_seams(ctx, plan, recv, data)
+        return cp.gather_clip(plan, asg, rank, data, (total_lat, LAT_H * LAT_W * 128))
+
+    pipeline(steps_limit=1)   # warm-up: one Euler step per chunk, the exchange and the gather
+    ctx.synchronize()
+    barrier(ws)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device) as clk:
+        start.record(stream)
+        clip = pipeline()
+        end.record(stream)
+        torch.cuda.synchronize()
+    ctx.synchronize()
+    barrier(ws)
+    ms = max_over_ranks(start.elapsed_time(end), ws)
+    steps = len(states[asg[rank][0]]["sigmas"]) - 1 if asg[rank] else 8
+    res = {
+        "metric": "chunk-parallel pipeline tokens/s (config 5: 8 chunks x 8 Euler steps of config 4, latent seam blend)",
+        "value": n_chunks * 8 * T_TOTAL / (ms * 1e-3),
+        "unit": "tokens/s",
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "dtype": "bf16 (tensor-core GEMM/attention inputs; f32 accumulate, residual and sampler)",
+        "config": {"workload": "chunk_pipeline_config5", "chunks": n_chunks, "euler_steps": steps,
+                   "pixel_plan": pix_plan, "latent_plan": plan, "clip_latent_frames": total_lat,
+                   "parallelism": f"{len(asg[0])} chunk(s) per GPU over {ws} GPU(s)",
+                   "seam": "2 latent frames per seam, sent point to point (NCCL), blended with ltx_seam_blend"},
+        "clip_finite": bool(torch.isfinite(clip).all()) if clip is not None else None,
+        # per chunk: 8 Euler steps (each as ltx_denoise_step) + 1 seam blend per received seam
+        "gpu_launches": len(asg[rank]) * steps * launches_per_step(48) + sum(1 for n in asg[rank] if n > 0),
+        "clocks": clk.summary(),
+    }
+    model.close()
+    ctx.close()
+    return res
+
+
 def run_block_forward(device, iters=5):
     """Config 3: one 22B-class block forward (model with num_layers = 1, B = 1,
     T = 12288 tokens with the IC reference, S = 1024), in both GEMM precisions
@@ -547,7 +626,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="denoise_step", choices=["denoise_step", "dequant_merge"])
+    ap.add_argument("--workload", default="denoise_step", choices=["denoise_step", "dequant_merge", "chunk_pipeline"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=5.0)
     ap.add_argument("--parallel", default="chunk", choices=["chunk", "tp"],
@@ -592,7 +671,13 @@ def main():
         from datetime import timedelta
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    if args.workload == "dequant_merge":
+    if args.workload == "chunk_pipeline":
+        res = run_chunk_pipeline(args, rank, ws, local)
+        if rank == 0:
+            res.update({"n_gpus": ws, "steps": 1, "warmup": 1, "vs_baseline": None,
+                        "data": "synthetic (random-init FP8+LoRA weights, N(0,1) latents/contexts per chunk)"})
+            print(json.dumps(res))
+    elif args.workload == "dequant_merge":
         res = run_dequant_merge(args, rank, ws, local)
         if rank == 0:
             res.update({"n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
