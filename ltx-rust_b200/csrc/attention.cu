@@ -12,9 +12,12 @@
 //              3-slot ring of 32 KB tiles (3-D tensor maps {H*128, T, B}, so
 //              a tile never reads the next batch).
 //   warp 1     one thread issues tcgen05.mma in the order
-//                QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) ...
+//                QK_A(0) QK_B(0) | QK_A(j+1) PV_A(j) QK_B(j+1) PV_B(j) ...
 //              S_X = Q_X K_j^T -> TMEM S_X; O_X += P_X V_j -> TMEM O_X
-//              (P from smem, V as an MN-major B operand), so tile A's
+//              (P from smem, V as an MN-major B operand).  QK_t(j+1) goes
+//              out as soon as tile t's softmax has read S_t(j) into registers
+//              (s_free), PV_t(j) once P_t(j) is in smem (p_full): the next
+//              scores are computed under the current exp/P work, and tile A's
 //              softmax runs under tile B's MMAs and vice versa.
 //   warps 2-5  softmax of tile A, warps 6-9 of tile B: one query row per
 //              thread; the row's 128 scores are read from TMEM into
@@ -22,8 +25,8 @@
 //              P (f16 or bf16) written to smem in the 128B-swizzled K-major
 //              layout.  O stays in TMEM; it is rescaled in place (tcgen05.ld/
 //              st) only when a row max grows by more than kRescaleLog2 over
-//              the max P is taken against — safe because the scores of tile
-//              j are ready only after the P.V of tile j-1 has completed.
+//              the max P is taken against.  Before P_t(j) is written or O_t
+//              rescaled, the softmax waits for PV_t(j-1) (pv_done).
 // All waits are bounded (2 s) and report LTX_ERR_TIMEOUT through the flag.
 #include <cuda.h>
 
@@ -56,7 +59,7 @@ struct AttnSmemLayout {
     static constexpr int P = Q + 2 * TILE_BYTES;        // P_A, P_B
     static constexpr int RING = P + 2 * TILE_BYTES;     // kRing K/V slots
     static constexpr int BAR = RING + kRing * TILE_BYTES;
-    static constexpr int BYTES = BAR + 128;
+    static constexpr int BYTES = BAR + 256;
 };
 constexpr size_t kAttnSmem = AttnSmemLayout::BYTES + 1024;
 static_assert(kAttnSmem <= 232448, "attention smem exceeds the per-CTA limit");
@@ -108,7 +111,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *s_full = bars + 7;            // [2]  tile A, B
     uint64_t *p_full = bars + 9;            // [2]
     uint64_t *pv_done = bars + 11;          // [2]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 13);
+    uint64_t *s_free = bars + 13;           // [2]  S_t read into registers by all 4 softmax warps
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 15);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q_tiles = (p.Tq + 2 * BQ - 1) / (2 * BQ);
@@ -127,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], 4);
             mbar_init(&pv_done[i], 1);
+            mbar_init(&s_free[i], 4);
         }
         fence_barrier_init();
     }
@@ -206,18 +211,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                 umma_commit(&slot_empty[slot_of(0)]);   // K_0 read by both
             }
             for (int j = 0; ok && j < n_kv; ++j) {
-                // V_j, then per tile: PV_t(j) once P_t(j) is ready, then QK_t(j+1)
+                // Per tile: QK_t(j+1) as soon as the softmax has read S_t(j) into
+                // registers (s_free), then PV_t(j) once P_t(j) is in smem (p_full):
+                // the next scores are computed under the current tile's exp/P work.
                 if (!wait_slot(2 * j + 1, 207)) break;
                 const bool next = j + 1 < n_kv;
                 if (next && !wait_slot(2 * j + 2, 208)) break;
                 for (int t = 0; t < 2; ++t) {
+                    if (next) {
+                        if (!mbar_wait(&s_free[t], j & 1, p.timeout_flag, 213 + t, &aborted)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        issue_qk(t, j + 1);
+                    }
                     if (!mbar_wait(&p_full[t], j & 1, p.timeout_flag, 209 + t, &aborted)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     issue_pv(t, j);
-                    if (next) issue_qk(t, j + 1);
                 }
                 if (!ok) break;
                 umma_commit(&slot_empty[slot_of(2 * j + 1)]);        // V_j read by both PVs
@@ -267,9 +281,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             // whole warp when any of its rows needs it; a row that does not
             // keeps its reference (alpha = 1).
             const bool grow = mx > m_ref + kRescaleLog2;
+            // P_t and O_t belong to PV_t(j-1) until it completes (it is issued
+            // after QK_t(j), so S_t(j) being ready does not imply it).
+            if (j > 0 && !warp_wait(&pv_done[t], (j - 1) & 1, p.timeout_flag, 215, &aborted)) break;
             if (__any_sync(0xffffffffu, grow)) {
-                // O_t and l are relative to m_ref; move them to mx.  P.V of the
-                // previous tile has completed (its commit preceded this S).
+                // O_t and l are relative to m_ref; move them to mx (P.V of the
+                // previous tile has completed: waited for above).
                 const float alpha = grow ? ex2(m_ref - mx) : 1.0f;   // 0 when m_ref = -inf
                 if (j > 0) {
                     const float2 a2 = make_float2(alpha, alpha);
@@ -301,6 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld_32x32b_x32(s_tmem + hf * 64, r[0]);
                 tmem_ld_32x32b_x32(s_tmem + hf * 64 + 32, r[1]);
                 tmem_ld_wait();
+                if (hf == 1) {
+                    // S_t is in registers: the MMA warp may overwrite it with QK_t(j+1)
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s_free[t]);
+                }
                 if (ragged) {
 #pragma unroll
                     for (int e = 0; e < 64; ++e)
