@@ -94,6 +94,20 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// tcgen05.wait::ld that also names the 32 destination registers of an earlier
+// tcgen05.ld as read-write operands, so no use of them can be scheduled before
+// the wait (the loads land asynchronously).
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;"
+        : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]),
+          "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]),
+          "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]),
+          "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+        :
+        : "memory");
+}
+
 // VF16: V (and so P) are f16; otherwise bf16.  Q and K are always bf16.
 template <bool VF16>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -258,20 +272,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int kv0 = j * BKV;
             const bool ragged = kv0 + BKV > p.Tk;   // only the last tile can be
             // pass 1: the row max over the 128 scores, all four 32-column TMEM
-            // loads in flight together (one wait), 8 independent partial maxima
+            // loads in flight together (one wait), 8 independent partial maxima.
+            // Keys 64..127 stay in registers (rh) for pass 2.
+            uint32_t rh[2][32];
             float mx;
             {
-                uint32_t r[4][32];
+                uint32_t r01[2][32];
+                tmem_ld_32x32b_x32(s_tmem + 0, r01[0]);
+                tmem_ld_32x32b_x32(s_tmem + 32, r01[1]);
+                tmem_ld_32x32b_x32(s_tmem + 64, rh[0]);
+                tmem_ld_32x32b_x32(s_tmem + 96, rh[1]);
+                tmem_ld_wait_regs(r01[0]);
+                tmem_ld_wait_regs(r01[1]);
+                tmem_ld_wait_regs(rh[0]);
+                tmem_ld_wait_regs(rh[1]);
+                if (ragged) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(s_tmem + c * 32, r[c]);
-                tmem_ld_wait();
+                    for (int e = 0; e < 64; ++e) {
+                        if (kv0 + e >= p.Tk) r01[e >> 5][e & 31] = __float_as_uint(-INFINITY);
+                        if (kv0 + 64 + e >= p.Tk) rh[e >> 5][e & 31] = __float_as_uint(-INFINITY);
+                    }
+                }
                 float m8[8];
 #pragma unroll
                 for (int u = 0; u < 8; ++u) m8[u] = -INFINITY;
 #pragma unroll
-                for (int e = 0; e < 128; ++e) {
-                    const float v = (ragged && kv0 + e >= p.Tk) ? -INFINITY : __uint_as_float(r[e >> 5][e & 31]);
-                    m8[e & 7] = fmaxf(m8[e & 7], v);
+                for (int e = 0; e < 64; ++e) {
+                    m8[e & 7] = fmaxf(m8[e & 7], __uint_as_float(r01[e >> 5][e & 31]));
+                    m8[(e + 4) & 7] = fmaxf(m8[(e + 4) & 7], __uint_as_float(rh[e >> 5][e & 31]));
                 }
                 mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             }
@@ -309,29 +337,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (grow) m_ref = mx;
             }
             // pass 2: P = exp2(s * scale - m_ref) (<= 2^kRescaleLog2), two per MUFU op; row sum in f32.
-            // Scores re-read from TMEM 64 columns (one swizzle atom of P) at a time.
+            // Keys 0..63 are re-read from TMEM while keys 64..127 (kept in
+            // registers) are turned into P; once the re-read lands S_t is free.
             const float2 nm2 = make_float2(-m_ref, -m_ref);
             float2 sum2 = make_float2(0.f, 0.f);
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                uint32_t r[2][32];
-                tmem_ld_32x32b_x32(s_tmem + hf * 64, r[0]);
-                tmem_ld_32x32b_x32(s_tmem + hf * 64 + 32, r[1]);
-                tmem_ld_wait();
-                if (hf == 1) {
-                    // S_t is in registers: the MMA warp may overwrite it with QK_t(j+1)
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&s_free[t]);
-                }
-                if (ragged) {
-#pragma unroll
-                    for (int e = 0; e < 64; ++e)
-                        if (kv0 + hf * 64 + e >= p.Tk) r[e >> 5][e & 31] = __float_as_uint(-INFINITY);
-                }
+            auto p_half = [&](uint32_t (&r)[2][32], int hf) {
                 unsigned char *atom = p_row + hf * HALF_BYTES;
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {      // 16-byte chunk q of the atom row: keys 8q .. 8q+7
+                for (int q = 0; q < 8; ++q) {      // 16-byte chunk q of the atom row: keys hf*64 + 8q ..
                     uint32_t pk[4];
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
@@ -352,6 +365,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     *reinterpret_cast<uint4 *>(atom + ((q ^ sw) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
+            };
+            {
+                uint32_t r0[2][32];
+                tmem_ld_32x32b_x32(s_tmem + 0, r0[0]);
+                tmem_ld_32x32b_x32(s_tmem + 32, r0[1]);
+                p_half(rh, 1);
+                tmem_ld_wait_regs(r0[0]);
+                tmem_ld_wait_regs(r0[1]);
+                // S_t is in registers: the MMA warp may overwrite it with QK_t(j+1)
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[t]);
+                if (ragged) {
+#pragma unroll
+                    for (int e = 0; e < 64; ++e)
+                        if (kv0 + e >= p.Tk) r0[e >> 5][e & 31] = __float_as_uint(-INFINITY);
+                }
+                p_half(r0, 0);
             }
             l += sum2.x + sum2.y;
             tc_fence_before();
