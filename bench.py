@@ -483,6 +483,85 @@ def run_chunk_pipeline(args, rank, ws, device):
     return res
 
 
+def run_ffn_config2(device, iters=5):
+    """Config 2: x bf16 [12288, 4096] N(0,1) -> linear 4096->4096 -> FFN
+    4096->16384 (tanh-GELU) -> 4096, weights FP8 e4m3 (per-tensor scale) with
+    a rank-64 LoRA.  bf16: the merged weights (ltx_dequant_merge) on the bf16
+    tcgen05 GEMM.  e4m3: per-row e4m3 activations (ltx_quantize_rows_e4m3)
+    against the exact FP8 base weights on the FP8 GEMM, the LoRA factored in
+    the same accumulator.  Both against an f32 reference on the merged f32
+    weights; bias zeros (no bias)."""
+    import torch
+    import ltx_b200
+    ctx = ltx_b200.Context(device)
+    g = torch.Generator(device="cuda").manual_seed(42)
+    M, R = 12288, 64
+    x = torch.randn(M, D, device="cuda", generator=g).to(torch.bfloat16)
+    layers = []
+    for (n_out, n_in) in ((D, D), (FF, D), (D, FF)):
+        w32 = torch.randn(n_out, n_in, device="cuda", generator=g) * 0.02
+        sw = float(w32.abs().max() / 448.0)
+        wq = (w32 / sw).to(torch.float8_e4m3fn).view(torch.uint8)
+        A = (torch.randn(R, n_in, device="cuda", generator=g) * 0.01).to(torch.bfloat16)
+        B = (torch.randn(n_out, R, device="cuda", generator=g) * 0.01).to(torch.bfloat16)
+        coeff = ltx_b200.lora_coeff(1.0, float(R), R)
+        d = [(A.data_ptr(), B.data_ptr(), R, ltx_b200.LTX_BF16, ltx_b200.LTX_BF16, coeff)]
+        w_bf16 = torch.empty(n_out, n_in, device="cuda", dtype=torch.bfloat16)
+        w_f32 = torch.empty(n_out, n_in, device="cuda")
+        ctx.dequant_merge(wq.data_ptr(), ltx_b200.LTX_F8_E4M3, True, sw, n_out, n_in, d, w_bf16.data_ptr(),
+                          ltx_b200.LTX_BF16)
+        ctx.dequant_merge(wq.data_ptr(), ltx_b200.LTX_F8_E4M3, True, sw, n_out, n_in, d, w_f32.data_ptr(),
+                          ltx_b200.LTX_F32)
+        sa = float(A.float().abs().max() / 448.0)
+        aq = (A.float() / sa).to(torch.float8_e4m3fn).view(torch.uint8)
+        b2 = (coeff * B.float() / sw).to(torch.bfloat16)
+        layers.append(dict(n_out=n_out, n_in=n_in, wq=wq, sw=sw, w_bf16=w_bf16, w_f32=w_f32, aq=aq, sa=sa, b2=b2))
+    ctx.synchronize()
+    y = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    h = torch.empty(M, FF, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    xq = torch.empty(M, FF, device="cuda", dtype=torch.uint8)
+    sx = torch.empty(M, device="cuda")
+    xa = torch.empty(M, R, device="cuda", dtype=torch.bfloat16)
+    epis = (ltx_b200.EPI_BF16, ltx_b200.EPI_GELU_BF16, ltx_b200.EPI_BF16)
+
+    def bf16_chain():
+        ltx_b200.gemm(ctx, x, layers[0]["w_bf16"], y, epis[0])
+        ltx_b200.gemm(ctx, y, layers[1]["w_bf16"], h, epis[1])
+        ltx_b200.gemm(ctx, h, layers[2]["w_bf16"], out, epis[2])
+
+    def e4m3_chain():
+        for L, inp, dst, epi in zip(layers, (x, y, h), (y, h, out), epis):
+            q = xq[:, :L["n_in"]]
+            ltx_b200.quantize_rows_e4m3(ctx, inp, q, sx)
+            ltx_b200.gemm_e4m3(ctx, q, None, L["aq"], L["sa"], xa)                     # (x A^T) / sx
+            ltx_b200.gemm_e4m3(ctx, q, sx, L["wq"], L["sw"], dst, epi, a2=xa, b2=L["b2"])
+
+    res = {}
+    with torch.no_grad():
+        ref = x.float() @ layers[0]["w_f32"].t()
+        ref = torch.nn.functional.gelu(ref @ layers[1]["w_f32"].t(), approximate="tanh")
+        ref = ref @ layers[2]["w_f32"].t()
+    tflop = 2.0 * M * D * D + 2 * 2.0 * M * D * FF
+    for name, chain in (("bf16", bf16_chain), ("e4m3", e4m3_chain)):
+        for _ in range(2):
+            chain()
+        ctx.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            chain()
+        e.record()
+        ctx.synchronize()
+        ms = s.elapsed_time(e) / iters
+        err = float((out.float() - ref).norm() / ref.norm())
+        res[name] = {"ms": ms, "tflops": tflop / (ms * 1e-3) / 1e12, "rel_l2_vs_f32": err}
+    res["note"] = (f"{tflop / 1e12:.3f} TFLOP per chain (linear + FFN at 12288 tokens); e4m3 includes the row "
+                   "quantisation passes and the skinny x.A^T GEMMs of the factored LoRA")
+    ctx.close()
+    return res
+
+
 def run_block_forward(device, iters=5):
     """Config 3: one 22B-class block forward (model with num_layers = 1, B = 1,
     T = 12288 tokens with the IC reference, S = 1024), in both GEMM precisions
@@ -689,6 +768,11 @@ def main():
         dq_args = argparse.Namespace(steps=20, warmup=5)
         dq = run_dequant_merge(dq_args, rank, ws, local)
         _log(f"dequant+merge: {dq['value']:.0f} GB/s")
+        ffn = run_ffn_config2(local) if ws == 1 else None
+        if ffn:
+            _log(f"config 2 (linear+FFN): bf16 {ffn['bf16']['ms']:.2f} ms {ffn['bf16']['tflops']:.0f} TFLOP/s "
+                 f"rel-L2 {ffn['bf16']['rel_l2_vs_f32']:.2e}; e4m3 {ffn['e4m3']['ms']:.2f} ms "
+                 f"{ffn['e4m3']['tflops']:.0f} TFLOP/s rel-L2 {ffn['e4m3']['rel_l2_vs_f32']:.2e}")
         blk = run_block_forward(local) if ws == 1 else None
         if blk:
             _log(f"block forward: bf16 {blk['bf16']['ms']:.2f} ms, e4m3_ffn {blk['e4m3_ffn']['ms']:.2f} ms "
@@ -698,6 +782,8 @@ def main():
             res.update({"n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
                         "data": "synthetic (random-init FP8+LoRA weights, N(0,1) latent/reference/contexts)"})
             res["dequant_merge"] = {k: dq[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "e2e")}
+            if ffn:
+                res["linear_ffn_config2"] = ffn
             if blk:
                 res["block_forward_config3"] = blk
             if ws == 1 and args.cpu_seconds > 0:

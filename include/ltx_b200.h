@@ -226,6 +226,13 @@ int ltx_gemm_e4m3(ltx_ctx *ctx, const void *a_dev, int64_t lda, const float *a_s
                   const int32_t *gate_idx_dev, int64_t ld_gate, const void *a2_dev, int64_t lda2,
                   const void *b2_dev, int64_t ldb2, int32_t k2);
 
+/* Per-row e4m3 quantisation of bf16 rows (the activations of the FP8 GEMM
+ * path): scale[row] = amax(row) / 448 (1 for an all-zero row), out = the e4m3
+ * bytes of in / scale, round to nearest even, saturating.  cols, ldi and ldo
+ * multiples of 8.  No reference counterpart (the reference computes in f32). */
+int ltx_quantize_rows_e4m3(ltx_ctx *ctx, const void *in_dev, int64_t ldi, int32_t rows, int32_t cols,
+                           void *out_dev, int64_t ldo, float *scale_dev);
+
 /* out = softmax(q k^T * scale) v per batch and head, without materialising
  * the scores (flash attention on tcgen05; scores and P.V accumulate in TMEM).
  * Replaces sdp_attention / chunked_sdp_attention (attention.rs:228-285,

@@ -5,7 +5,7 @@
 //   norm_mod_e4m3          RMSNorm / adaLN modulate (norm.rs:23-53,
 //                          block.rs:131-132, :150-151) straight to e4m3
 //   quantize_rows_e4m3     bf16 rows (attention output, GELU output, context)
-//   bf16_to_f32, scale_cols_bf16   load-time helpers for the LoRA factors
+//   bf16_to_f32, scale_pad_bf16    load-time helpers for the LoRA factors
 #include <cuda_fp8.h>
 
 #include "device_common.cuh"
@@ -206,3 +206,16 @@ cudaError_t scale_pad_bf16(cudaStream_t st, int sms, const __nv_bfloat16 *in, in
 }
 
 }  // namespace ltx
+
+extern "C" int ltx_quantize_rows_e4m3(ltx_ctx *ctx, const void *in_dev, int64_t ldi, int32_t rows, int32_t cols,
+                                      void *out_dev, int64_t ldo, float *scale_dev) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    if (!in_dev || !out_dev || !scale_dev || rows < 0 || cols < 0)
+        return ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_quantize_rows_e4m3: bad arguments");
+    cudaError_t e = ltx::quantize_rows_e4m3(ctx->stream, static_cast<const __nv_bfloat16 *>(in_dev), ldi, rows, cols,
+                                            static_cast<uint8_t *>(out_dev), ldo, scale_dev);
+    if (e == cudaErrorInvalidValue)
+        return ltx::fail(ctx, LTX_ERR_SHAPE, "ltx_quantize_rows_e4m3: cols and leading dimensions must be multiples of 8, "
+                         "16-byte aligned input");
+    return e == cudaSuccess ? LTX_OK : ltx::cuda_fail(ctx, e, "ltx_quantize_rows_e4m3");
+}

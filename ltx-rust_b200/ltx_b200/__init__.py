@@ -71,6 +71,7 @@ def lib() -> ctypes.CDLL:
                               P, P, I64, P, P, I64]),
         "ltx_gemm_e4m3": (I, [V, P, I64, P, P, I64, F, P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                               ctypes.c_int32, P, P, I64, P, P, I64, P, I64, P, I64, ctypes.c_int32]),
+        "ltx_quantize_rows_e4m3": (I, [V, P, I64, ctypes.c_int32, ctypes.c_int32, P, I64, P]),
         "ltx_attention_fwd": (I, [V, P, I64, P, I64, P, I64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                   ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, F, P, I64]),
         "ltx_store_open": (I, [V, ctypes.POINTER(ctypes.c_char_p), ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(V)]),
@@ -212,6 +213,13 @@ def gemm_e4m3(ctx: "Context", a, a_scale, w, w_scale, out, epilogue=EPI_BF16, bi
                                   _ptr(gate_idx), gate.stride(0) if gate is not None else 0, _ptr(a2),
                                   a2.stride(0) if a2 is not None else 0, _ptr(b2),
                                   b2.stride(0) if b2 is not None else 0, k2), "ltx_gemm_e4m3")
+
+
+def quantize_rows_e4m3(ctx: "Context", x, out, scale):
+    """Per-row e4m3 of a bf16 [rows, cols] CUDA tensor into uint8 out [rows, cols] and f32 scale [rows]."""
+    rows, cols = x.shape
+    ctx.check(lib().ltx_quantize_rows_e4m3(ctx.h, _ptr(x), x.stride(0), rows, cols, _ptr(out), out.stride(0),
+                                           _ptr(scale)), "ltx_quantize_rows_e4m3")
 
 
 def attention(ctx: "Context", q, k, v, out, batch, heads, tq, tk, scale, head_dim=128):
