@@ -72,6 +72,7 @@ typedef struct ltx_ctx ltx_ctx;
  * reference counterpart: the reference picks its device through Burn's
  * `B::Device`. */
 int ltx_ctx_create(int device, void *stream, ltx_ctx **out);
+/* Stores and models made on a context are destroyed before it. */
 void ltx_ctx_destroy(ltx_ctx *ctx);
 /* Message of the last failed call on this context ("" if none). */
 const char *ltx_last_error(const ltx_ctx *ctx);

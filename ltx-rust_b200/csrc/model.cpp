@@ -42,6 +42,9 @@ struct DitConfig {
     // (exact FP8 base weights + unmerged LoRA), "e4m3_ffn" only the two FFN
     // projections; default "bf16" (merged weights).  fp8 = any of them.
     bool fp8 = false, fp8_attn = false, fp8_ffn = false;
+    // "offload_blocks": n > 0 keeps the blocks in host memory with n on the
+    // device at a time (OffloadMode::Stream { n_blocks: n }); 0 = Resident
+    int offload_blocks = 0;
     int inner() const { return heads * head_dim; }
     int coeff() const { return cross_adaln ? 9 : 6; }
 };
@@ -90,6 +93,11 @@ static int parse_config(ltx_ctx *ctx, const std::string &text, DitConfig &c) {
                 return fail(ctx, LTX_ERR_CONFIG, "gemm_precision must be \"bf16\", \"e4m3\" or \"e4m3_ffn\"");
         }
     }
+    for (const Json *o : {static_cast<const Json *>(&root), j}) {
+        const Json *ob = o->get("offload_blocks");
+        if (ob && ob->kind == Json::Num) c.offload_blocks = (int)ob->num;
+    }
+    if (c.offload_blocks < 0) return fail(ctx, LTX_ERR_CONFIG, "offload_blocks must be >= 0");
     // validate (config.rs:188-231)
     if (c.heads <= 0) return fail(ctx, LTX_ERR_CONFIG, "num_attention_heads must be > 0");
     if (c.head_dim % 2) return fail(ctx, LTX_ERR_CONFIG, "attention_head_dim must be even for RoPE");
@@ -139,6 +147,17 @@ struct ltx_model {
     // hidden units split; everything else replicated)
     int tp = 1, tr = 0;
     int lora_r64 = 0;   // FP8 path: LoRA rank padded to 64 (the factored term's K)
+    // OffloadMode::Stream (crates/ltx-dit/src/offload.rs:43-56): the blocks'
+    // weights live in pinned host memory (blocks[l] views into it) and at most
+    // offload_n of them are on the device, in slots[], uploaded on copy_stream
+    // just before use.  offload_n = 0: every block resident in the arena.
+    int offload_n = 0;
+    size_t block_bytes = 0;
+    void *host_blocks = nullptr;
+    std::vector<ltx::BlockW> slots;
+    std::vector<char *> slot_base;
+    cudaStream_t copy_stream = nullptr;
+    std::vector<cudaEvent_t> copied, freed;   // per slot: upload done / block computed
     void *arena = nullptr;
     size_t arena_bytes = 0;
     __nv_bfloat16 *patch_w = nullptr, *out_w = nullptr;
@@ -168,11 +187,74 @@ struct Arena {
 };
 
 // Assigns every weight a slice of one allocation (sizing pass when a.base == null).
-static void layout(ltx_model *m, Arena &a) {
+// One block's projection weights, biases and norms (everything of a block
+// except its modulation tables), laid out from the arena's current offset.
+// With offload the same layout is used for the host image of every block and
+// for each device slot.
+static void layout_block(const ltx_model *m, BlockW &b, Arena &a) {
     const DitConfig &c = m->cfg;
-    const int64_t D = c.inner(), Dc = c.cross_dim, K = c.coeff();
+    const int64_t D = c.inner(), Dc = c.cross_dim;
     // this rank's share of the split dimensions
     const int64_t Dl = D / m->tp, Fl = 4 * D / m->tp, Hl = c.heads / m->tp;
+    const int r64 = m->lora_r64;
+    auto f8 = [&](LinF8 &L, int64_t out, int64_t in) {
+        L.w = a.take<uint8_t>(out * in);
+        L.r64 = r64;
+        if (r64) {
+            L.a = a.take<uint8_t>((int64_t)r64 * in);
+            L.b2 = a.take<__nv_bfloat16>(out * r64);
+        }
+    };
+    // FP8 path: e4m3 weights + factored LoRA instead of merged bf16 (tp = 1)
+    if (c.fp8_attn) {
+        f8(b.fqkv, 3 * D, D);
+        f8(b.fo, D, D);
+        f8(b.fq2, D, D);
+        f8(b.fkv2, 2 * D, Dc);
+        f8(b.fo2, D, D);
+    }
+    if (c.fp8_ffn) {
+        f8(b.fff1, 4 * D, D);
+        f8(b.fff2, D, 4 * D);
+    }
+    b.qkv = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(3 * Dl * D);
+    b.qkv_b = a.take<float>(3 * Dl);
+    b.qn = a.take<float>(Dl);
+    b.kn = a.take<float>(Dl);
+    b.o = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(D * Dl);
+    b.o_b = a.take<float>(D);
+    b.q2 = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(Dl * D);
+    b.q2_b = a.take<float>(Dl);
+    b.kv2 = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(2 * Dl * Dc);
+    b.kv2_b = a.take<float>(2 * Dl);
+    b.qn2 = a.take<float>(Dl);
+    b.kn2 = a.take<float>(Dl);
+    b.o2 = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(D * Dl);
+    b.o2_b = a.take<float>(D);
+    b.ff1 = c.fp8_ffn ? nullptr : a.take<__nv_bfloat16>(Fl * D);
+    b.ff1_b = c.ff_bias ? a.take<float>(Fl) : nullptr;
+    b.ff2 = c.fp8_ffn ? nullptr : a.take<__nv_bfloat16>(D * Fl);
+    b.ff2_b = c.ff_bias ? a.take<float>(D) : nullptr;
+    b.g1 = c.gated ? a.take<__nv_bfloat16>(Hl * D) : nullptr;
+    b.g1_b = c.gated ? a.take<float>(Hl) : nullptr;
+    b.g2 = c.gated ? a.take<__nv_bfloat16>(Hl * D) : nullptr;
+    b.g2_b = c.gated ? a.take<float>(Hl) : nullptr;
+}
+
+// Bytes of one block's image (layout_block from offset 0, 256-aligned).
+static size_t block_bytes(const ltx_model *m) {
+    Arena a;
+    BlockW b{};
+    layout_block(m, b, a);
+    return (a.off + 255) & ~size_t(255);
+}
+
+// Assigns every resident weight a slice of the device arena (sizing pass when
+// a.base == null): the head, the adaLN tables, every block's modulation
+// tables, and either all blocks (resident) or the offload slots.
+static void layout(ltx_model *m, Arena &a) {
+    const DitConfig &c = m->cfg;
+    const int64_t D = c.inner(), K = c.coeff();
     m->patch_w = a.take<__nv_bfloat16>(D * c.in_ch);
     m->patch_b = a.take<float>(D);
     m->t1_w = a.take<float>(D * 256);
@@ -189,53 +271,37 @@ static void layout(ltx_model *m, Arena &a) {
     m->sin_freq = a.take<float>(128);
     m->sst_list = a.take<float *>(c.layers);
     m->blocks.resize(c.layers);
-    const int r64 = m->lora_r64;
-    auto f8 = [&](LinF8 &L, int64_t out, int64_t in) {
-        L.w = a.take<uint8_t>(out * in);
-        L.r64 = r64;
-        if (r64) {
-            L.a = a.take<uint8_t>((int64_t)r64 * in);
-            L.b2 = a.take<__nv_bfloat16>(out * r64);
-        }
-    };
-    for (auto &b : m->blocks) {
-        // FP8 path: e4m3 weights + factored LoRA instead of merged bf16 (tp = 1)
-        if (c.fp8_attn) {
-            f8(b.fqkv, 3 * D, D);
-            f8(b.fo, D, D);
-            f8(b.fq2, D, D);
-            f8(b.fkv2, 2 * D, Dc);
-            f8(b.fo2, D, D);
-        }
-        if (c.fp8_ffn) {
-            f8(b.fff1, 4 * D, D);
-            f8(b.fff2, D, 4 * D);
-        }
-        b.qkv = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(3 * Dl * D);
-        b.qkv_b = a.take<float>(3 * Dl);
-        b.qn = a.take<float>(Dl);
-        b.kn = a.take<float>(Dl);
-        b.o = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(D * Dl);
-        b.o_b = a.take<float>(D);
-        b.q2 = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(Dl * D);
-        b.q2_b = a.take<float>(Dl);
-        b.kv2 = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(2 * Dl * Dc);
-        b.kv2_b = a.take<float>(2 * Dl);
-        b.qn2 = a.take<float>(Dl);
-        b.kn2 = a.take<float>(Dl);
-        b.o2 = c.fp8_attn ? nullptr : a.take<__nv_bfloat16>(D * Dl);
-        b.o2_b = a.take<float>(D);
-        b.ff1 = c.fp8_ffn ? nullptr : a.take<__nv_bfloat16>(Fl * D);
-        b.ff1_b = c.ff_bias ? a.take<float>(Fl) : nullptr;
-        b.ff2 = c.fp8_ffn ? nullptr : a.take<__nv_bfloat16>(D * Fl);
-        b.ff2_b = c.ff_bias ? a.take<float>(D) : nullptr;
+    for (auto &b : m->blocks) {   // modulation tables stay resident (adaLN reads all layers at once)
         b.sst = a.take<float>(K * D);
         b.pst = c.cross_adaln ? a.take<float>(2 * D) : nullptr;
-        b.g1 = c.gated ? a.take<__nv_bfloat16>(Hl * D) : nullptr;
-        b.g1_b = c.gated ? a.take<float>(Hl) : nullptr;
-        b.g2 = c.gated ? a.take<__nv_bfloat16>(Hl * D) : nullptr;
-        b.g2_b = c.gated ? a.take<float>(Hl) : nullptr;
     }
+    if (m->offload_n > 0) {
+        m->slots.resize(m->offload_n);
+        m->slot_base.clear();
+        for (auto &sv : m->slots) {
+            const size_t start = (a.off + 255) & ~size_t(255);
+            Arena one;
+            one.base = a.base ? a.base + start : nullptr;
+            layout_block(m, sv, one);
+            if (a.base) m->slot_base.push_back(a.base + start);
+            a.off = start + m->block_bytes;
+        }
+    } else {
+        for (auto &b : m->blocks) layout_block(m, b, a);
+    }
+}
+
+// Frees everything a model owns (device arena, offload image, stream, events).
+static void free_model(ltx_model *m) {
+    if (!m) return;
+    if (m->arena) cudaFree(m->arena);
+    if (m->host_blocks) cudaFreeHost(m->host_blocks);
+    for (auto ev : m->copied)
+        if (ev) cudaEventDestroy(ev);
+    for (auto ev : m->freed)
+        if (ev) cudaEventDestroy(ev);
+    if (m->copy_stream) cudaStreamDestroy(m->copy_stream);
+    delete m;
 }
 
 static int alloc_model(ltx_ctx *ctx, const DitConfig &cfg, ltx_model *&m, int lora_rank = 0) {
@@ -248,6 +314,8 @@ static int alloc_model(ltx_ctx *ctx, const DitConfig &cfg, ltx_model *&m, int lo
     m->tp = ctx->tp_size;
     m->tr = ctx->tp_rank;
     m->lora_r64 = cfg.fp8 && lora_rank > 0 ? (lora_rank + 63) / 64 * 64 : 0;
+    m->offload_n = cfg.offload_blocks > 0 && cfg.offload_blocks < cfg.layers ? cfg.offload_blocks : 0;
+    if (m->offload_n) m->block_bytes = block_bytes(m);
     if (m->tp > 1 && (cfg.heads % m->tp || (cfg.inner() / m->tp) % 8)) {
         const int tp = m->tp;
         delete m;
@@ -268,6 +336,36 @@ static int alloc_model(ltx_ctx *ctx, const DitConfig &cfg, ltx_model *&m, int lo
     Arena real;
     real.base = static_cast<char *>(m->arena);
     layout(m, real);
+    if (m->offload_n) {
+        // pinned host image of every block (zeroed: absent biases stay 0), slots, copy stream, events
+        const size_t host_bytes = m->block_bytes * (size_t)cfg.layers;
+        e = cudaHostAlloc(&m->host_blocks, host_bytes, cudaHostAllocDefault);
+        if (e != cudaSuccess) {
+            m->host_blocks = nullptr;
+            const int rc = fail(ctx, LTX_ERR_OOM, "offloaded blocks: %zu bytes of pinned host memory: %s", host_bytes,
+                                cudaGetErrorString(e));
+            free_model(m);
+            m = nullptr;
+            return rc;
+        }
+        memset(m->host_blocks, 0, host_bytes);
+        for (int l = 0; l < cfg.layers; ++l) {
+            Arena one;
+            one.base = static_cast<char *>(m->host_blocks) + (size_t)l * m->block_bytes;
+            layout_block(m, m->blocks[l], one);
+        }
+        m->copied.resize(m->offload_n);
+        m->freed.resize(m->offload_n);
+        bool ok = cudaStreamCreateWithFlags(&m->copy_stream, cudaStreamNonBlocking) == cudaSuccess;
+        for (int i = 0; ok && i < m->offload_n; ++i)
+            ok = cudaEventCreateWithFlags(&m->copied[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&m->freed[i], cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
+            free_model(m);
+            m = nullptr;
+            return fail(ctx, LTX_ERR_CUDA, "offload stream/events");
+        }
+    }
     // host-computed tables: RoPE frequency grid (rope.rs:311-322, f64 -> f32) and
     // the sinusoid frequencies exp(-ln(1e4) * i / 128) in f32 (adaln.rs:43-59).
     std::vector<float> grid(m->rope_grid), sf(128);
@@ -371,6 +469,39 @@ struct Loader {
         if (_rc) return _rc;     \
     } while (0)
 
+// With offload, a block is written into device slot 0 (plus its resident
+// modulation tables) and then copied to its host image.  The slot is zeroed
+// first, so a weight the store lacks (an optional bias) reads 0 as it does in
+// the zeroed resident arena, not the previous block's value.
+static BlockW staging_view(ltx_model *m, ltx_ctx *ctx, int l) {
+    cudaMemsetAsync(m->slot_base[0], 0, m->block_bytes, ctx->stream);
+    BlockW b = m->slots[0];
+    b.sst = m->blocks[l].sst;
+    b.pst = m->blocks[l].pst;
+    return b;
+}
+
+// The per-tensor FP8 scales are host values of the block's LinF8 records,
+// not part of its device image: copied from the staging view to block l's
+// record at load, and from there into the slot's view at each use.
+static void copy_scales(BlockW &dst, const BlockW &src) {
+    LinF8 BlockW::*const f8[] = {&BlockW::fqkv, &BlockW::fo, &BlockW::fq2, &BlockW::fkv2,
+                                 &BlockW::fo2,  &BlockW::fff1, &BlockW::fff2};
+    for (auto f : f8) {
+        (dst.*f).sw = (src.*f).sw;
+        (dst.*f).sa = (src.*f).sa;
+    }
+}
+
+// Copies staged block l (slot 0) to its host image and keeps its FP8 scales.
+static int stash_block(ltx_model *m, ltx_ctx *ctx, int l, const BlockW &stage) {
+    LTX_CUDA_TRY(ctx, cudaMemcpyAsync(static_cast<char *>(m->host_blocks) + (size_t)l * m->block_bytes,
+                                      m->slot_base[0], m->block_bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    LTX_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));   // slot 0 is reused by the next block
+    copy_scales(m->blocks[l], stage);
+    return LTX_OK;
+}
+
 static int load_weights_into(ltx_model *m, Loader &L) {
     const DitConfig &c = m->cfg;
     const int64_t D = c.inner(), Dc = c.cross_dim, F = 4 * D, H = c.heads, K = c.coeff();
@@ -387,7 +518,8 @@ static int load_weights_into(ltx_model *m, Loader &L) {
     TRY(L.req("proj_out.weight", {c.out_ch, D}, m->out_w, LTX_BF16));
     TRY(L.opt("proj_out.bias", {c.out_ch}, m->out_b, LTX_F32));
     for (int i = 0; i < c.layers; ++i) {
-        BlockW &b = m->blocks[i];
+        BlockW stage = m->offload_n ? staging_view(m, L.ctx, i) : BlockW{};
+        BlockW &b = m->offload_n ? stage : m->blocks[i];
         const std::string p = "transformer_blocks." + std::to_string(i) + ".";
         const std::string a1 = p + "attn1.", a2 = p + "attn2.";
         TRY(L.req(a1 + "to_q.weight", {D, D}, b.qkv, LTX_BF16, kRows));
@@ -424,6 +556,7 @@ static int load_weights_into(ltx_model *m, Loader &L) {
         }
         TRY(L.req(p + "scale_shift_table", {K, D}, b.sst, LTX_F32));
         if (c.cross_adaln) TRY(L.req(p + "prompt_scale_shift_table", {2, D}, b.pst, LTX_F32));
+        if (m->offload_n) TRY(stash_block(m, L.ctx, i, b));
     }
     return LTX_OK;
 }
@@ -559,7 +692,9 @@ static int init_random(ltx_model *m, ltx_ctx *ctx, uint64_t seed, int rank, floa
         TRY(s.linear(m->lin_w, K * D, D, LTX_F32));
         TRY(s.vec(m->sst_out, 2 * D, 0.f, 0.02f));
         TRY(s.linear(m->out_w, c.out_ch, D, LTX_BF16));
-        for (auto &b : m->blocks) {
+        for (int li = 0; li < c.layers; ++li) {
+            BlockW stage = m->offload_n ? staging_view(m, ctx, li) : BlockW{};
+            BlockW &b = m->offload_n ? stage : m->blocks[li];
             // the same random stream in either precision (same order of draws)
             if (c.fp8_attn) {
                 TRY(s.linear_f8(b.fqkv, 3 * D, D));
@@ -591,6 +726,7 @@ static int init_random(ltx_model *m, ltx_ctx *ctx, uint64_t seed, int rank, floa
                 TRY(s.linear(b.g1, H, D, LTX_BF16, kRows));
                 TRY(s.linear(b.g2, H, D, LTX_BF16, kRows));
             }
+            if (m->offload_n) TRY(stash_block(m, ctx, li, b));
         }
         return LTX_OK;
     }();
@@ -849,13 +985,25 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
                    tab + 5 * D, (int)D));
         return LTX_OK;
     };
-    for (int l = 0; l < c.layers; ++l) {
-        const BlockW &b = m->blocks[l];
-        const float *tab = w.tab + (int64_t)l * U * K * D;
+    // OffloadMode::Stream: block l's weights are uploaded into slot l % n on
+    // the copy stream once the block that used that slot before (l - n) has
+    // been computed; the compute stream waits for the upload.
+    const int n_off = m->offload_n;
+    auto prefetch = [&](int l) -> int {
+        const int slot = l % n_off;
+        CU(cudaStreamWaitEvent(m->copy_stream, m->freed[slot], 0));
+        CU(cudaMemcpyAsync(m->slot_base[slot], static_cast<char *>(m->host_blocks) + (size_t)l * m->block_bytes,
+                           m->block_bytes, cudaMemcpyHostToDevice, m->copy_stream));
+        CU(cudaEventRecord(m->copied[slot], m->copy_stream));
+        return LTX_OK;
+    };
+    for (int l = 0; n_off && l < std::min(n_off, c.layers); ++l) TRY(prefetch(l));
+    // one block: x updated in place on the compute stream
+    auto block_body = [&](const BlockW &b, const float *tab) -> int {
         if (c.fp8_attn && c.fp8_ffn) {
             TRY(attn_f8(b, tab));
             TRY(ffn_f8(b, tab));
-            continue;
+            return LTX_OK;
         }
         // self-attention: x += attn(mod(rms(x))) * gate_msa
         CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 0, w.xn, D));
@@ -915,12 +1063,29 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         // feed-forward: x += ff(mod(rms(x))) * gate_mlp
         if (c.fp8_ffn) {
             TRY(ffn_f8(b, tab));
-            continue;
+            return LTX_OK;
         }
         CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 3, w.xn, D));
         TRY(gemm_bf16(ctx, st, w.xn, D, b.ff1, D, (int)rows, (int)Fl, (int)D, LTX_EPI_GELU_BF16, b.ff1_b, w.ffh, Fl,
                       nullptr, nullptr, 0));
         TRY(project_residual(w.ffh, Fl, b.ff2, Fl, b.ff2_b, tab + 5 * D));
+        return LTX_OK;
+    };
+    for (int l = 0; l < c.layers; ++l) {
+        BlockW bv = m->blocks[l];
+        if (n_off) {
+            const int slot = l % n_off;
+            CU(cudaStreamWaitEvent(st, m->copied[slot], 0));
+            bv = m->slots[slot];
+            bv.sst = m->blocks[l].sst;
+            bv.pst = m->blocks[l].pst;
+            copy_scales(bv, m->blocks[l]);
+        }
+        TRY(block_body(bv, w.tab + (int64_t)l * U * K * D));
+        if (n_off) {   // the slot is free once this block's kernels ran; refill it with block l + n
+            CU(cudaEventRecord(m->freed[l % n_off], st));
+            if (l + n_off < c.layers) TRY(prefetch(l + n_off));
+        }
     }
     // output head: LN(x) * (1 + scale) + shift -> proj_out (model.rs:237-254)
     CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 2, w.otab, 2, w.idx, 0, w.xn, D));
@@ -952,8 +1117,7 @@ extern "C" int ltx_model_load(ltx_ctx *ctx, ltx_store *st, const char *config_js
     TRY(alloc_model(ctx, cfg, m));
     int rc = load_weights(m, st, ctx);
     if (rc) {
-        cudaFree(m->arena);
-        delete m;
+        free_model(m);
         return rc;
     }
     *out = m;
@@ -971,8 +1135,7 @@ extern "C" int ltx_model_init_random(ltx_ctx *ctx, const char *config_json, uint
     TRY(alloc_model(ctx, cfg, m, lora_rank));
     int rc = init_random(m, ctx, seed, lora_rank, lora_strength);
     if (rc) {
-        cudaFree(m->arena);
-        delete m;
+        free_model(m);
         return rc;
     }
     *out = m;
@@ -981,9 +1144,9 @@ extern "C" int ltx_model_init_random(ltx_ctx *ctx, const char *config_json, uint
 
 extern "C" void ltx_model_destroy(ltx_model *m) {
     if (!m) return;
+    cudaSetDevice(m->device);
     cudaDeviceSynchronize();
-    cudaFree(m->arena);
-    delete m;
+    free_model(m);
 }
 
 extern "C" int64_t ltx_model_weight_bytes(const ltx_model *m) { return m ? (int64_t)m->arena_bytes : 0; }

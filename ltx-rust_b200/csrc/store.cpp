@@ -19,6 +19,7 @@ MappedFile::~MappedFile() {
 }
 
 ltx_store::~ltx_store() {
+    cudaSetDevice(device);   // cudaFree synchronises the device before it frees
     for (auto &kv : deltas)
         for (auto &d : kv.second) {
             cudaFree(d.a);
@@ -234,6 +235,7 @@ extern "C" int ltx_store_open(ltx_ctx *ctx, const char *const *paths, int32_t n_
     ltx_store *st = new (std::nothrow) ltx_store();
     if (!st) return LTX_ERR_OOM;
     st->ctx = ctx;
+    st->device = ctx->device;
     for (int i = 0; i < n_paths; ++i) {
         MappedFile *mf = nullptr;
         std::map<std::string, std::string> meta;
@@ -271,7 +273,6 @@ extern "C" int ltx_store_open(ltx_ctx *ctx, const char *const *paths, int32_t n_
 
 extern "C" void ltx_store_destroy(ltx_store *st) {
     if (!st) return;
-    if (st->ctx) cudaStreamSynchronize(st->ctx->stream);
     delete st;
 }
 

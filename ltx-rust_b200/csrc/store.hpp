@@ -33,6 +33,7 @@ struct DeviceDelta {
 
 struct ltx_store {
     ltx_ctx *ctx = nullptr;
+    int device = 0;            // the context's device; destruction does not touch ctx
     std::vector<MappedFile *> files;
     std::map<std::string, StoreEntry> entries;
     std::set<std::string> scale_keys;

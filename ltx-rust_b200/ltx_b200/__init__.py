@@ -8,6 +8,7 @@ raises (there is no CPU fallback).
 from __future__ import annotations
 
 import ctypes
+import weakref
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -132,6 +133,9 @@ class Context:
             import torch
             stream = torch.cuda.current_stream(device).cuda_stream
         self.h = ctypes.c_void_p()
+        # stores and models made on this context: closed before it (their
+        # destructors synchronise on the context's stream)
+        self._owned = weakref.WeakSet()
         rc = lib().ltx_ctx_create(device, ctypes.c_void_p(stream), ctypes.byref(self.h))
         if rc != 0:
             raise LtxError(rc, f"ltx_ctx_create(device={device})")
@@ -164,6 +168,8 @@ class Context:
 
     def close(self):
         if self.h:
+            for obj in list(self._owned):
+                obj.close()
             lib().ltx_ctx_destroy(self.h)
             self.h = ctypes.c_void_p()
 
@@ -242,6 +248,7 @@ class WeightStore:
         self.h = ctypes.c_void_p()
         arr = (ctypes.c_char_p * len(paths))(*[p.encode() for p in paths])
         ctx.check(lib().ltx_store_open(ctx.h, arr, len(paths), keymap, ctypes.byref(self.h)), "ltx_store_open")
+        ctx._owned.add(self)
 
     def merge_lora(self, path: str, strength: float):
         m, u = ctypes.c_int32(), ctypes.c_int32()
@@ -297,6 +304,7 @@ class VideoTransformer:
 
     def __init__(self, ctx: Context, handle):
         self.ctx, self.h = ctx, handle
+        ctx._owned.add(self)
 
     @staticmethod
     def load(ctx: Context, store: WeightStore, config_json: str | None = None):

@@ -416,3 +416,57 @@ def test_fp8_config_rejections(ctx):
         with pytest.raises(ltx_b200.LtxError) as e:
             ltx_b200.VideoTransformer.init_random(ctx, json.dumps(bad), seed=1, lora_rank=8)
         assert e.value.kind in ("UNSUPPORTED", "CONFIG")
+
+
+@pytest.mark.parametrize("prec,n_blocks", [("bf16", 1), ("bf16", 2), ("e4m3_ffn", 1), ("e4m3", 3)])
+def test_offload_stream_matches_resident(ctx, prec, n_blocks):
+    """OffloadMode::Stream (crates/ltx-dit/src/offload.rs:43-56): with "offload_blocks": n the
+    blocks' weights live in pinned host memory and at most n are on the device, uploaded on a
+    copy stream just before use.  The same kernels run on the same weights, so the output is
+    bit-identical to the resident model's; so is a second forward (slots reused).  The FP8
+    layouts put other weights first in a block, so they are covered too."""
+    import json
+    import ltx_b200
+    from dit_checkpoint import small_config
+    heads = 2 if prec == "bf16" else 32   # the FP8 path runs at the 22B width only
+    cfg = dict(small_config(heads=heads, head_dim=128, layers=4), gemm_precision=prec)
+    lat, ts, pos, ctxt = make_inputs(cfg, F=2, Hh=8, W=8, S=40, seed=7)
+    outs = {}
+    for mode in (0, n_blocks):
+        c = dict(cfg, offload_blocks=mode)
+        model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(c), seed=9, lora_rank=16, lora_strength=0.7)
+        res = []
+        for _ in range(2):
+            out = torch.empty(lat.shape, dtype=torch.float32, device="cuda")
+            model.forward(*(torch.from_numpy(a).cuda() for a in (lat, ts, pos, ctxt)), out)
+            ctx.synchronize()
+            res.append(out.cpu().numpy())
+        outs[mode] = res
+        if mode:
+            assert model.weight_bytes() < resident_bytes   # only the slots and the resident parts on the device
+        else:
+            resident_bytes = model.weight_bytes()
+        model.close()
+    for k in range(2):
+        assert np.array_equal(outs[n_blocks][k].view(np.uint32), outs[0][k].view(np.uint32)), k
+
+
+def test_offload_stream_load_matches_resident(ctx, mid_ckpt):
+    """A checkpoint (with a LoRA merged) loaded into an offloaded model gives the same forward
+    as the resident load: each block is staged through a device slot into its host image."""
+    import json
+    import ltx_b200
+    cfg_m, ck, lo, _ = mid_ckpt
+    got = {}
+    for mode in (0, 1):
+        st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+        st.merge_lora(lo, 0.9)
+        model = ltx_b200.VideoTransformer.load(ctx, st, json.dumps(dict(cfg_m, offload_blocks=mode)))
+        l2, t2, p2, c2 = make_inputs(cfg_m, seed=2)
+        out = torch.empty(l2.shape, dtype=torch.float32, device="cuda")
+        model.forward(*(torch.from_numpy(a).cuda() for a in (l2, t2, p2, c2)), out)
+        ctx.synchronize()
+        got[mode] = out.cpu().numpy()
+        model.close()
+        st.close()
+    assert np.array_equal(got[1].view(np.uint32), got[0].view(np.uint32))
