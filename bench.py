@@ -295,7 +295,8 @@ def run_denoise_step(args, rank, ws, device):
     tp = args.parallel == "tp" and ws > 1
     if tp:
         ltx_b200.init_tensor_parallel(ctx)   # this rank's shard of one model
-    model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(CFG4), seed=7 if tp else 7 + rank, lora_rank=64,
+    cfg = dict(CFG4, offload_blocks=args.offload_blocks) if args.offload_blocks else CFG4
+    model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(cfg), seed=7 if tp else 7 + rank, lora_rank=64,
                                                   lora_strength=1.0)
     ctx.synchronize()
     load_s = time.time() - t0
@@ -385,7 +386,9 @@ def run_denoise_step(args, rank, ws, device):
                    "parallelism": (f"tp{ws} (one sequence; heads and FFN split, NCCL allreduce)" if tp else
                                    f"chunk-parallel x{ws} (one independent chunk per GPU)"),
                    "l2": "inputs and weights exceed L2 (25.8 GB bf16 weights streamed per step)",
-                   "step_tflop": total / 1e12, "model_load_s": load_s},
+                   "step_tflop": total / 1e12, "model_load_s": load_s,
+                   **({"offload_blocks": args.offload_blocks,
+                       "device_weight_bytes": model.weight_bytes()} if args.offload_blocks else {})},
         "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMM, FFN-in + GELU (M=24576, N=16384, K=4096)",
                      "achieved": gemm_tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": gemm_tf / peaks["bf16_tflops"], "traffic": FFN_IN_NCU_TRAFFIC, "peak_source": src,
@@ -710,6 +713,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=5.0)
     ap.add_argument("--parallel", default="chunk", choices=["chunk", "tp"],
                     help="N>1: independent chunk per GPU (default) or one sequence split over the GPUs")
+    ap.add_argument("--offload-blocks", type=int, default=0,
+                    help="denoise_step: keep the blocks in pinned host memory with this many on the device")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = dist_env()
