@@ -7,26 +7,32 @@
 //
 // One CTA per (batch, head, 256 queries) = two 128-row query tiles A and B
 // that share every K/V tile (half the L2->SM traffic of one tile per CTA).
+// TMEM (512 columns): S_A, S_B (128 f32 columns each) and O_A, O_B.  P_t is
+// written back into the upper half of S_t's columns as packed 16-bit pairs,
+// and the P.V MMA reads its A operand from there: P never touches shared
+// memory (no P stores or proxy fence in the softmax, and the 64 KB a shared
+// P buffer would take go to a deeper K/V ring).
 // 10 warps:
 //   warp 0     TMA: Q_A and Q_B once, then K_0, V_0, K_1, V_1, ... through a
-//              3-slot ring of 32 KB tiles (3-D tensor maps {H*128, T, B}, so
+//              5-slot ring of 32 KB tiles (3-D tensor maps {H*128, T, B}, so
 //              a tile never reads the next batch).
 //   warp 1     one thread issues tcgen05.mma in the order
-//                QK_A(0) QK_B(0) | QK_A(j+1) PV_A(j) QK_B(j+1) PV_B(j) ...
-//              S_X = Q_X K_j^T -> TMEM S_X; O_X += P_X V_j -> TMEM O_X
-//              (P from smem, V as an MN-major B operand).  QK_t(j+1) goes
-//              out as soon as tile t's softmax has read S_t(j) into registers
-//              (s_free), PV_t(j) once P_t(j) is in smem (p_full): the next
-//              scores are computed under the current exp/P work, and tile A's
-//              softmax runs under tile B's MMAs and vice versa.
+//                QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) ...
+//              S_t = Q_t K_j^T -> TMEM S_t; O_t += P_t V_j -> TMEM O_t (P_t
+//              from TMEM, V as an MN-major B operand from shared memory).
+//              PV_t(j) goes out once the softmax has stored P_t(j) (p_full);
+//              QK_t(j+1), which overwrites S_t/P_t, follows it in the same
+//              in-order MMA stream.  Tile A's softmax runs under tile B's
+//              MMAs and vice versa.
 //   warps 2-5  softmax of tile A, warps 6-9 of tile B: one query row per
 //              thread; the row's 128 scores are read from TMEM into
-//              registers, max and exp2 (two per MUFU op, ex2.approx.f16x2),
-//              P (f16 or bf16) written to smem in the 128B-swizzled K-major
-//              layout.  O stays in TMEM; it is rescaled in place (tcgen05.ld/
-//              st) only when a row max grows by more than kRescaleLog2 over
-//              the max P is taken against.  Before P_t(j) is written or O_t
-//              rescaled, the softmax waits for PV_t(j-1) (pv_done).
+//              registers, max, then exp2 in f32 (three quarters on the
+//              MUFU, a quarter by a polynomial on the FMA pipe), P (f16 or
+//              bf16) stored to TMEM with tcgen05.st.  O stays in
+//              TMEM; it is rescaled in place (tcgen05.ld/st) only when a row
+//              max grows by more than kRescaleLog2 over the max P is taken
+//              against.  S_t(j) being ready (s_full, committed after
+//              QK_t(j)) implies PV_t(j-1) completed, so O_t is stable then.
 // All waits are bounded (2 s) and report LTX_ERR_TIMEOUT through the flag.
 #include <cuda.h>
 
@@ -48,19 +54,25 @@ namespace {
 
 constexpr int D = 128;
 constexpr int BQ = 128, BKV = 128;
-constexpr int kRing = 3;                  // K/V tile slots
+constexpr int kRing = 5;                  // K/V tile slots
 constexpr int kThreads = 320;
 constexpr int TILE_BYTES = 128 * D * 2;   // 32 KB: 128 rows x 128 16-bit values (two 64-col swizzle atoms)
 constexpr int HALF_BYTES = 128 * 64 * 2;  // 16 KB: one atom column block
 constexpr float kRescaleLog2 = 8.0f;      // O is rescaled when a row max grows by more than 2^8
+// P pairs (of the 16 per 32-key chunk) whose exp2 runs on the FMA pipe
+// (exp2_fma2) instead of the MUFU: bit u set = pair u.  One MUFU ex2 costs
+// 6 cycles per warp per SM sub-partition (measured), so 128 per row per K/V
+// tile make the MUFU as busy as the tensor core; a quarter of them on the
+// FMA pipe measured fastest (12.5% and 31% were slower).
+constexpr uint32_t kEmuPairs = 0x1111u;
 
 struct AttnSmemLayout {
     static constexpr int Q = 0;                         // Q_A, Q_B
-    static constexpr int P = Q + 2 * TILE_BYTES;        // P_A, P_B
-    static constexpr int RING = P + 2 * TILE_BYTES;     // kRing K/V slots
+    static constexpr int RING = Q + 2 * TILE_BYTES;     // kRing K/V slots
     static constexpr int BAR = RING + kRing * TILE_BYTES;
     static constexpr int BYTES = BAR + 256;
 };
+static_assert((8 + 2 * kRing) * 8 <= 256, "attention barriers exceed their smem block");
 constexpr size_t kAttnSmem = AttnSmemLayout::BYTES + 1024;
 static_assert(kAttnSmem <= 232448, "attention smem exceeds the per-CTA limit");
 
@@ -72,8 +84,26 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const void *tmap, ui
         : "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+// 2^x on the FMA pipe, two at a time: 2^x = 2^n * 2^f with n = rint(x)
+// (Cody-Waite range reduction through the 1.5 * 2^23 rounding constant, whose
+// sum with x carries n in its low mantissa bits) and f = x - n in [-0.5, 0.5];
+// 2^f by the cubic c0 + f (c1 + f (c2 + f c3)), coefficients fitted here as
+// the minimax (Lawson-weighted least squares) relative-error polynomial on
+// [-0.5, 0.5]: max relative error 7.7e-5, below f16's half ulp (2.4e-4).
+// 2^n is added into the exponent field.  x is clamped at -30 first: 2^-30
+// rounds to 0 in f16, and the exponent add stays in range.
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+    constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
+    constexpr float c0 = 0x1.fff682p-1f, c1 = 0x1.62f1e0p-1f, c2 = 0x1.f0e03ap-3f, c3 = 0x1.c46242p-5f;
+    x = make_float2(fmaxf(x.x, -30.f), fmaxf(x.y, -30.f));
+    const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+    const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+    const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+    float2 q = __ffma2_rn(make_float2(c3, c3), f, make_float2(c2, c2));
+    q = __ffma2_rn(q, f, make_float2(c1, c1));
+    q = __ffma2_rn(q, f, make_float2(c0, c0));
+    return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -91,6 +121,13 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
         "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
         "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
         "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -116,17 +153,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *sQ = smem + AttnSmemLayout::Q;
-    unsigned char *sP = smem + AttnSmemLayout::P;
     unsigned char *sRing = smem + AttnSmemLayout::RING;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + AttnSmemLayout::BAR);
     uint64_t *q_full = bars + 0;
-    uint64_t *slot_full = bars + 1;         // [kRing]
-    uint64_t *slot_empty = bars + 4;        // [kRing]
-    uint64_t *s_full = bars + 7;            // [2]  tile A, B
-    uint64_t *p_full = bars + 9;            // [2]
-    uint64_t *pv_done = bars + 11;          // [2]
-    uint64_t *s_free = bars + 13;           // [2]  S_t read into registers by all 4 softmax warps
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 15);
+    uint64_t *slot_full = bars + 1;                 // [kRing]
+    uint64_t *slot_empty = bars + 1 + kRing;        // [kRing]
+    uint64_t *s_full = bars + 1 + 2 * kRing;        // [2]  tile A, B: QK_t(j) (and every earlier MMA) done
+    uint64_t *p_full = bars + 3 + 2 * kRing;        // [2]  P_t(j) stored by all 4 softmax warps
+    uint64_t *pv_done = bars + 5 + 2 * kRing;       // [2]  the last PV_t: O_t final
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 7 + 2 * kRing);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q_tiles = (p.Tq + 2 * BQ - 1) / (2 * BQ);
@@ -145,7 +180,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], 4);
             mbar_init(&pv_done[i], 1);
-            mbar_init(&s_free[i], 4);
         }
         fence_barrier_init();
     }
@@ -190,8 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         if (elect_one()) {
             constexpr uint32_t idesc_qk = idesc_f16(BQ, BKV, true, false);
-            constexpr uint32_t idesc_pv = idesc_f16(BQ, D, !VF16, true);   // B = V, MN-major
-            const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+            constexpr uint32_t idesc_pv = idesc_f16(BQ, D, !VF16, true);   // A = P (TMEM), B = V, MN-major
+            const uint32_t q_addr = smem_u32(sQ);
             auto slot_of = [](int s) { return s % kRing; };
             auto wait_slot = [&](int s, int code) {
                 return mbar_wait(&slot_full[slot_of(s)], (s / kRing) & 1, p.timeout_flag, code, &aborted);
@@ -206,16 +240,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 umma_commit(&s_full[t]);
             };
-            auto issue_pv = [&](int t, int j) {   // O_t (+)= P_t V_j
+            auto issue_pv = [&](int t, int j) {   // O_t (+)= P_t V_j; P_t: TMEM columns 64..127 of S_t
                 const uint32_t v_addr = smem_u32(sRing + slot_of(2 * j + 1) * TILE_BYTES);
-                const uint32_t pa = p_addr + t * TILE_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < BKV / 16; ++kk) {
-                    const uint64_t ad = sdesc_sw128(pa + (kk >> 2) * HALF_BYTES + (kk & 3) * 32, 16, 1024);
+                for (int kk = 0; kk < BKV / 16; ++kk) {   // 16 keys = 8 packed columns per MMA
                     const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, HALF_BYTES, 1024);
-                    umma_f16_ss(tmem + 256 + t * 128, ad, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                    umma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + 64 + kk * 8, bd, idesc_pv,
+                                (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                umma_commit(&pv_done[t]);
             };
             bool ok = mbar_wait(q_full, 0, p.timeout_flag, 205, &aborted) && wait_slot(0, 206);
             if (ok) {
@@ -225,27 +257,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 umma_commit(&slot_empty[slot_of(0)]);   // K_0 read by both
             }
             for (int j = 0; ok && j < n_kv; ++j) {
-                // Per tile: QK_t(j+1) as soon as the softmax has read S_t(j) into
-                // registers (s_free), then PV_t(j) once P_t(j) is in smem (p_full):
-                // the next scores are computed under the current tile's exp/P work.
+                // Per tile: PV_t(j) once the softmax has stored P_t(j) (p_full),
+                // then QK_t(j+1) into the same columns: MMAs of one thread run
+                // in issue order, so P_t(j) is read before S_t(j+1) lands.
                 if (!wait_slot(2 * j + 1, 207)) break;
                 const bool next = j + 1 < n_kv;
                 if (next && !wait_slot(2 * j + 2, 208)) break;
                 for (int t = 0; t < 2; ++t) {
-                    if (next) {
-                        if (!mbar_wait(&s_free[t], j & 1, p.timeout_flag, 213 + t, &aborted)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        issue_qk(t, j + 1);
-                    }
                     if (!mbar_wait(&p_full[t], j & 1, p.timeout_flag, 209 + t, &aborted)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     issue_pv(t, j);
+                    if (next)
+                        issue_qk(t, j + 1);
+                    else
+                        umma_commit(&pv_done[t]);
                 }
                 if (!ok) break;
                 umma_commit(&slot_empty[slot_of(2 * j + 1)]);        // V_j read by both PVs
@@ -260,8 +288,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
         const uint32_t s_tmem = tmem + lane_base + t * 128;
         const uint32_t o_tmem = tmem + lane_base + 256 + t * 128;
-        unsigned char *p_row = sP + t * TILE_BYTES + row_in_tile * 128;
-        const int sw = row_in_tile & 7;
         const float2 sl2 = make_float2(p.scale_log2, p.scale_log2);
         float m_ref = -INFINITY;   // the max P is taken against
         float l = 0.f;
@@ -309,12 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // whole warp when any of its rows needs it; a row that does not
             // keeps its reference (alpha = 1).
             const bool grow = mx > m_ref + kRescaleLog2;
-            // P_t and O_t belong to PV_t(j-1) until it completes (it is issued
-            // after QK_t(j), so S_t(j) being ready does not imply it).
-            if (j > 0 && !warp_wait(&pv_done[t], (j - 1) & 1, p.timeout_flag, 215, &aborted)) break;
             if (__any_sync(0xffffffffu, grow)) {
-                // O_t and l are relative to m_ref; move them to mx (P.V of the
-                // previous tile has completed: waited for above).
+                // O_t and l are relative to m_ref; move them to mx (PV_t(j-1)
+                // was issued before QK_t(j), whose completion was waited for).
                 const float alpha = grow ? ex2(m_ref - mx) : 1.0f;   // 0 when m_ref = -inf
                 if (j > 0) {
                     const float2 a2 = make_float2(alpha, alpha);
@@ -336,62 +359,57 @@ __global__ void __launch_bounds__(kThreads, 1)
                 l *= alpha;
                 if (grow) m_ref = mx;
             }
-            // pass 2: P = exp2(s * scale - m_ref) (<= 2^kRescaleLog2), two per MUFU op; row sum in f32.
-            // Keys 0..63 are re-read from TMEM while keys 64..127 (kept in
-            // registers) are turned into P; once the re-read lands S_t is free.
+            // pass 2: P = exp2(s * scale - m_ref) (<= 2^kRescaleLog2) in f32; row sum of the f32 values.
+            // P is stored as packed 16-bit pairs (key 2c in the low half of
+            // column c) into columns 64..127 of S_t: keys 0..63 -> 64..95,
+            // keys 64..127 -> 96..127.  Keys 64..127 are already in registers
+            // (rh); keys 0..63 are re-read from columns 0..63, which no P
+            // store touches.
             const float2 nm2 = make_float2(-m_ref, -m_ref);
             float2 sum2 = make_float2(0.f, 0.f);
-            auto p_half = [&](uint32_t (&r)[2][32], int hf) {
-                unsigned char *atom = p_row + hf * HALF_BYTES;
+            auto p_store = [&](const uint32_t (&r)[32], uint32_t col) {   // 32 keys -> 16 columns
+                uint32_t pk[16];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {      // 16-byte chunk q of the atom row: keys hf*64 + 8q ..
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int e = q * 8 + 2 * u;
-                        const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[e >> 5][e & 31]),
-                                                                __uint_as_float(r[e >> 5][(e & 31) + 1])), sl2, nm2);
-                        uint32_t in, out;
-                        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(in) : "f"(x.y), "f"(x.x));
-                        asm("ex2.approx.f16x2 %0, %1;" : "=r"(out) : "r"(in));
-                        const float2 pf = __half22float2(*reinterpret_cast<__half2 *>(&out));
-                        sum2 = __fadd2_rn(sum2, pf);
-                        if constexpr (VF16) {
-                            pk[u] = out;
-                        } else {
-                            __nv_bfloat162 hv = __floats2bfloat162_rn(pf.x, pf.y);
-                            pk[u] = *reinterpret_cast<uint32_t *>(&hv);
-                        }
+                for (int u = 0; u < 16; ++u) {
+                    const float2 x = __ffma2_rn(make_float2(__uint_as_float(r[2 * u]), __uint_as_float(r[2 * u + 1])),
+                                                sl2, nm2);
+                    const float2 pf = ((kEmuPairs >> u) & 1u) ? exp2_fma2(x) : make_float2(ex2(x.x), ex2(x.y));
+                    sum2 = __fadd2_rn(sum2, pf);
+                    if constexpr (VF16) {
+                        uint32_t out;
+                        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(out) : "f"(pf.y), "f"(pf.x));
+                        pk[u] = out;
+                    } else {
+                        __nv_bfloat162 hv = __floats2bfloat162_rn(pf.x, pf.y);
+                        pk[u] = *reinterpret_cast<uint32_t *>(&hv);
                     }
-                    *reinterpret_cast<uint4 *>(atom + ((q ^ sw) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
+                tmem_st_32x32b_x16(s_tmem + col, pk);
             };
             {
                 uint32_t r0[2][32];
                 tmem_ld_32x32b_x32(s_tmem + 0, r0[0]);
                 tmem_ld_32x32b_x32(s_tmem + 32, r0[1]);
-                p_half(rh, 1);
+                p_store(rh[0], 96);
+                p_store(rh[1], 112);
                 tmem_ld_wait_regs(r0[0]);
                 tmem_ld_wait_regs(r0[1]);
-                // S_t is in registers: the MMA warp may overwrite it with QK_t(j+1)
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_free[t]);
                 if (ragged) {
 #pragma unroll
                     for (int e = 0; e < 64; ++e)
                         if (kv0 + e >= p.Tk) r0[e >> 5][e & 31] = __float_as_uint(-INFINITY);
                 }
-                p_half(r0, 0);
+                p_store(r0[0], 64);
+                p_store(r0[1], 80);
             }
             l += sum2.x + sum2.y;
-            tc_fence_before();
-            fence_proxy_async_smem();   // P (generic-proxy writes) -> visible to the tensor core
+            tmem_st_wait();             // P_t(j) in TMEM ...
+            tc_fence_before();          // ... and ordered before the arrive for the MMA thread
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[t]);
         }
         // O_t is final once the last P.V has completed.
-        if (!aborted && warp_wait(&pv_done[t], (n_kv - 1) & 1, p.timeout_flag, 212, &aborted)) {
+        if (!aborted && warp_wait(&pv_done[t], 0, p.timeout_flag, 212, &aborted)) {   // one commit per tile
             tc_fence_after();
             const int q_row = qt * 2 * BQ + t * BQ + row_in_tile;
             const float inv = 1.f / l;
