@@ -31,6 +31,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import numpy as np
 import os
 import statistics
@@ -52,6 +53,9 @@ CFG1_FMAS = 4096 * 4096 * 64
 # launch, so its write-back is not in the figure.
 CFG1_NCU_TRAFFIC = 20.02e6 + 0.2455e6
 FFN_IN_NCU_TRAFFIC = 1.812415e9 + 0.78335488e9
+# self-attention at B=2, H=32, T=12288: DRAM read+write of a B=1, T=8192 launch
+# (201.56 MB + 46.14 MB) scaled by the Q/K/V/O bytes (805.3 MB / 268.4 MB)
+ATTN_NCU_TRAFFIC = (201.555968e6 + 46.135808e6) * 3.0
 
 
 def measured_peaks():
@@ -368,6 +372,25 @@ def run_denoise_step(args, rank, ws, device):
     gemm_ms = gs.elapsed_time(ge) / 10
     _log(f"FFN-in GEMM alone: {gemm_ms:.3f} ms")
     del a, w, o
+    # the step's largest kernel by time share, timed alone: self-attention
+    # (bf16 Q/K, f16 V as the model feeds it) at B=2, H=32, T=12288
+    H, TA = D // 128, T_TOTAL
+    q = torch.randn(2 * TA, D, device="cuda").to(torch.bfloat16)
+    kk = torch.randn(2 * TA, D, device="cuda").to(torch.bfloat16)
+    v = torch.randn(2 * TA, D, device="cuda").to(torch.float16)
+    ao = torch.empty(2 * TA, D, device="cuda", dtype=torch.bfloat16)
+    for _ in range(3):
+        ltx_b200.attention(ctx, q, kk, v, ao, 2, H, TA, TA, 1.0 / math.sqrt(128))
+    as_, ae = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    as_.record(stream)
+    for _ in range(10):
+        ltx_b200.attention(ctx, q, kk, v, ao, 2, H, TA, TA, 1.0 / math.sqrt(128))
+    ae.record(stream)
+    torch.cuda.synchronize()
+    attn_ms = as_.elapsed_time(ae) / 10
+    attn_flop = 4.0 * 2 * H * TA * TA * 128
+    _log(f"self-attention alone: {attn_ms:.3f} ms")
+    del q, kk, v, ao
     peaks, src = measured_peaks()
     total, gemm_f, attn_f = step_flops()
     gemm_tf = 2.0 * M * N * K / (gemm_ms * 1e-3) / 1e12
@@ -389,13 +412,18 @@ def run_denoise_step(args, rank, ws, device):
                    "step_tflop": total / 1e12, "model_load_s": load_s,
                    **({"offload_blocks": args.offload_blocks,
                        "device_weight_bytes": model.weight_bytes()} if args.offload_blocks else {})},
-        "roofline": {"bound": "tensor", "kernel": "tcgen05 GEMM, FFN-in + GELU (M=24576, N=16384, K=4096)",
-                     "achieved": gemm_tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": gemm_tf / peaks["bf16_tflops"], "traffic": FFN_IN_NCU_TRAFFIC, "peak_source": src,
-                     "algorithmic_flops_per_launch": 2.0 * M * N * K,
+        "roofline": {"bound": "tensor", "kernel": "attn_fwd_kernel, self-attention (B=2, H=32, T=12288, d=128)",
+                     "achieved": attn_flop / (attn_ms * 1e-3) / 1e12, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": attn_flop / (attn_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                     "traffic": ATTN_NCU_TRAFFIC, "peak_source": src, "algorithmic_flops_per_launch": attn_flop,
+                     "traffic_note": "ncu DRAM bytes of a B=1, T=8192 launch scaled by Q/K/V/O bytes",
                      "step_tflops_achieved": total / (ms * 1e-3) / 1e12,
                      "step_frac_of_sustained": total / (ms * 1e-3) / 1e12 / peaks.get("bf16_tflops_sustained",
                                                                                       peaks["bf16_tflops"])},
+        "roofline_gemm": {"bound": "tensor", "kernel": "tcgen05 GEMM, FFN-in + GELU (M=24576, N=16384, K=4096)",
+                     "achieved": gemm_tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": gemm_tf / peaks["bf16_tflops"], "traffic": FFN_IN_NCU_TRAFFIC, "peak_source": src,
+                     "algorithmic_flops_per_launch": 2.0 * M * N * K},
         "e2e": {"value": (1 if tp else ws) * T_TOTAL / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": lat_h.numel() * 4, "d2h_bytes_per_step": out_h.numel() * 4},
         "gpu_launches": args.steps * launches_per_step(48, tp),
