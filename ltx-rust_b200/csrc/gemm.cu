@@ -357,10 +357,6 @@ bool make_tmap_2d(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, i
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool make_tmap_bf16(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
-    return make_tmap_2d(m, ptr, rows, cols, ld, box_rows, 2);
-}
-
 template <int BN, int EPI, bool F8>
 cudaError_t launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &ta2, const CUtensorMap &tb2,
                         const GemmParams &p, int sms, cudaStream_t st) {
