@@ -16,7 +16,9 @@
  *     synchronise that stream first.
  *   - One ltx_ctx per host thread/stream.  Distinct contexts may be used from
  *     different threads concurrently.  A loaded model is read-only and may be
- *     shared by contexts on the same device.
+ *     shared by contexts on the same device, except one loaded with
+ *     "offload_blocks" > 0: its device block slots are shared state, so it
+ *     runs on one context at a time.
  */
 #ifndef LTX_B200_H
 #define LTX_B200_H
@@ -294,7 +296,11 @@ typedef struct ltx_model ltx_model;
  * and validated like DiTConfig::from_json (config.rs:176-231).  Linear
  * weights are read through the dequant+merge kernel into bf16; Q|K|V and
  * K|V projections are fused at load.  LTX_ERR_MISSING_KEY / LTX_ERR_SHAPE
- * mirror DitError::Weight. */
+ * mirror DitError::Weight.  "offload_blocks": n (0 < n < layers) in the
+ * config keeps every block's weights in pinned host memory with n device
+ * slots, each block uploaded on a copy stream before use
+ * (OffloadMode::Stream, crates/ltx-dit/src/offload.rs:43-56; outputs equal
+ * the resident model's). */
 int ltx_model_load(ltx_ctx *ctx, ltx_store *store, const char *config_json, ltx_model **out);
 /* A random-init model of the given config, built the way an FP8 LTX
  * checkpoint is loaded: every linear weight drawn N(0, 0.02) on the device,
