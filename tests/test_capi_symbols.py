@@ -35,6 +35,16 @@ def test_library_exports_every_declared_symbol():
     assert not missing, f"declared but not exported: {missing}"
 
 
+def test_rust_binding_in_integration_doc_declares_every_entry_point():
+    """The `-sys` crate INTEGRATION.md gives a maintainer binds every function of the header."""
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    rust = doc[doc.index("```rust"):]
+    rust = rust[:rust.index("```", 7)]
+    bound = set(re.findall(r"pub fn (ltx_\w+)\(", rust))
+    missing = sorted(declared_functions() - bound)
+    assert not missing, f"header functions without a Rust declaration: {missing}"
+
+
 def test_lora_coeff_matches_reference_formula():
     import numpy as np
     from ltx_b200 import lora_coeff
