@@ -45,6 +45,7 @@ struct GemmParams {
     int k2_blocks;          // FP8 only: bf16 K-blocks of 64 appended to every tile
                             // (A2 [M, 64*k2] . B2 [N, 64*k2]^T, same accumulator)
     const float *w_col_scale;   // FP8 only: per-column weight scale [N] (null = w_scale)
+    int resid_tma;          // EPI_RESID: the residual moves by TMA through shared memory (tmX)
 };
 
 namespace {
@@ -52,6 +53,10 @@ namespace {
 constexpr int BM = 128;
 constexpr size_t kGroupPanelBytes = 48u << 20;   // A panel kept in L2 while W streams past it
 constexpr int kThreads = 192;
+// EPI_RESID staging: two 128-row x 32-column f32 chunks of the residual,
+// 128-byte swizzled, filled and drained by TMA.
+constexpr int kXChunkBytes = BM * 32 * 4;
+constexpr int kXStageBytes = 2 * kXChunkBytes;
 
 // F8: e4m3 operands (kind::f8f6f4), 128 elements of K per stage; otherwise
 // bf16 (kind::f16), 64 per stage.  Either way a stage row is one 128-byte
@@ -87,20 +92,35 @@ __device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, i
     nb = r / gm;
 }
 
+__device__ __forceinline__ void tma_store_2d(const void *tmap, const void *smem_src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+                 "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 template <int BN, int EPI, bool F8>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, GemmParams p) {
+                const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                const __grid_constant__ CUtensorMap tmX, GemmParams p) {
     using C = GemmCfg<BN, F8>;
+    constexpr int XS = EPI == EPI_RESID ? kXStageBytes : 0;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *sA = smem;
     unsigned char *sB = smem + C::STAGES * C::A_BYTES;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+    float *xs = reinterpret_cast<float *>(smem + C::STAGES * C::STAGE_BYTES);   // EPI_RESID staging (XS bytes)
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES + XS);
     uint64_t *empty = full + C::STAGES;
     uint64_t *tfull = empty + C::STAGES;
     uint64_t *tempty = tfull + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    uint64_t *xfull = tempty + 2;   // [2] residual chunk landed (EPI_RESID with resid_tma)
+    uint64_t *xdone = xfull + 2;    // [2] the 128 epilogue threads have written it back
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xdone + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_blocks = (p.M + BM - 1) / BM, n_blocks = (p.N + BN - 1) / BN;
@@ -117,6 +137,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 4);
+            mbar_init(&xfull[a], 1);
+            mbar_init(&xdone[a], 128);
         }
         fence_barrier_init();
     }
@@ -199,6 +221,108 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (aborted) break;
                 umma_commit(&tfull[acc]);
             }
+        }
+    } else if (EPI == EPI_RESID && p.resid_tma) {
+        // Residual epilogue through shared memory: per 32-column chunk, one
+        // elected thread TMA-loads x[128 rows][32 cols] into a staging buffer
+        // (the next chunk's load is in flight while this one is processed),
+        // every thread updates its row there, and the elected thread TMA-stores
+        // the chunk back.  Global traffic moves in whole lines instead of one
+        // 16-byte piece of 32 different rows per instruction.
+        const int quad = warp & 3;
+        const int erow = quad * 32 + lane;   // row within the tile (TMEM lane)
+        const bool elected = warp == 2 && lane == 0;
+        uint32_t u = 0;                       // staging uses so far: buffer u & 1, phase (u >> 1) & 1
+        uint32_t issued = 0;                  // uses whose load the elected thread has started
+        auto load_chunk = [&](uint32_t uu, int mb, int nb, int c) {   // elected thread only
+            bulk_wait_read0();                // earlier stores have finished reading their buffers
+            issued = uu + 1;
+            const int b = uu & 1;
+            mbar_arrive_expect_tx(&xfull[b], kXChunkBytes);
+            tma_load_2d(xs + b * (kXChunkBytes / 4), &tmX, &xfull[b], nb * BN + c * 32, mb * BM);
+        };
+        uint32_t tile_i = 0;
+        for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tile_i) {
+            int mb, nb;
+            tile_coords(t, m_blocks, n_blocks, p.group_m, mb, nb);
+            const uint32_t acc = tile_i & 1, aph = (tile_i >> 1) & 1;
+            if (elected) load_chunk(u, mb, nb, 0);   // under this tile's mainloop
+            __syncwarp();
+            if (!warp_wait(&tfull[acc], aph, p.timeout_flag, 104, &aborted)) break;
+            tc_fence_after();
+            const int row = mb * BM + erow;
+            const bool row_ok = row < p.M;
+            const float *gate_row = nullptr;
+            if (p.gate) gate_row = p.gate + (int64_t)(p.gate_idx && row_ok ? p.gate_idx[row] : 0) * p.ld_gate;
+            const float sa = F8 && p.a_scale && row_ok ? __ldg(p.a_scale + row) : 1.0f;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c, ++u) {
+                if (elected && c + 1 < BN / 32) load_chunk(u + 1, mb, nb, c + 1);
+                __syncwarp();
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
+                tmem_ld_wait();
+                const int b = u & 1;
+                const uint32_t ph = (u >> 1) & 1;
+                if (!warp_wait(&xfull[b], ph, p.timeout_flag, 106, &aborted)) break;
+                const int col0 = nb * BN + c * 32;
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                if constexpr (F8) {
+                    // acc is in units of (row scale x weight scale)
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        v[j] *= sa * (p.w_col_scale ? (col0 + j < p.N ? __ldg(p.w_col_scale + col0 + j) : 0.f)
+                                                    : p.w_scale);
+                }
+                if (p.bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
+                }
+                // row erow of the 128-byte swizzled chunk: 16-byte piece q sits at q ^ (erow % 8)
+                float4 *xr = reinterpret_cast<float4 *>(xs + b * (kXChunkBytes / 4) + erow * 32);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int pos = q ^ (erow & 7);
+                    float4 x = xr[pos];
+                    float g[4] = {1.f, 1.f, 1.f, 1.f};
+                    if (gate_row) {
+                        if (col0 + 4 * q + 4 <= p.N) {
+                            const float4 g4 = __ldg(reinterpret_cast<const float4 *>(gate_row + col0 + 4 * q));
+                            g[0] = g4.x; g[1] = g4.y; g[2] = g4.z; g[3] = g4.w;
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) g[e] = col0 + 4 * q + e < p.N ? gate_row[col0 + 4 * q + e] : 0.f;
+                        }
+                    }
+                    x.x += v[4 * q] * g[0];
+                    x.y += v[4 * q + 1] * g[1];
+                    x.z += v[4 * q + 2] * g[2];
+                    x.w += v[4 * q + 3] * g[3];
+                    xr[pos] = x;
+                }
+                fence_proxy_async_smem();   // the writes above, visible to the TMA store
+                mbar_arrive(&xdone[b]);
+                if (elected) {
+                    if (mbar_wait(&xdone[b], ph, p.timeout_flag, 107, &aborted)) {
+                        tma_store_2d(&tmX, xs + b * (kXChunkBytes / 4), col0, mb * BM);
+                        bulk_commit();
+                    }
+                }
+                __syncwarp();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        if (elected) {
+            // Before the CTA exits: loads an abort left unconsumed have landed
+            // (bounded waits), and every store has completed.
+            bool quiet = false;
+            for (uint32_t uu = u; uu < issued; ++uu) mbar_wait(&xfull[uu & 1], (uu >> 1) & 1, nullptr, 0, &quiet);
+            bulk_wait_all();
         }
     } else {
         // Epilogue warps 2..5 own TMEM lane quadrant (warp % 4).
@@ -357,27 +481,44 @@ bool make_tmap_2d(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, i
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D row-major f32 [rows, cols] with leading dimension ld (elements), box
+// {box_cols, box_rows}, 128-byte swizzle (box_cols * 4 must be 128).
+bool make_tmap_f32(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                   int box_cols) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || box_cols * 4 != 128) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr ? const_cast<void *>(ptr) : nullptr, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int BN, int EPI, bool F8>
 cudaError_t launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &ta2, const CUtensorMap &tb2,
-                        const GemmParams &p, int sms, cudaStream_t st) {
+                        const CUtensorMap &tx, const GemmParams &p, int sms, cudaStream_t st) {
     using C = GemmCfg<BN, F8>;
+    constexpr size_t smem = C::SMEM + (EPI == EPI_RESID ? kXStageBytes : 0);
+    static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
     auto k = gemm_kernel<BN, EPI, F8>;
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
     const int grid = std::min(tiles, sms);
-    k<<<grid, kThreads, C::SMEM, st>>>(ta, tb, ta2, tb2, p);
+    k<<<grid, kThreads, smem, st>>>(ta, tb, ta2, tb2, tx, p);
     return cudaGetLastError();
 }
 
 template <int BN, bool F8>
 cudaError_t dispatch_epi(int epi, const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &ta2,
-                         const CUtensorMap &tb2, const GemmParams &p, int sms, cudaStream_t st) {
+                         const CUtensorMap &tb2, const CUtensorMap &tx, const GemmParams &p, int sms, cudaStream_t st) {
     switch (epi) {
-    case EPI_BF16: return launch_gemm<BN, EPI_BF16, F8>(ta, tb, ta2, tb2, p, sms, st);
-    case EPI_GELU_BF16: return launch_gemm<BN, EPI_GELU_BF16, F8>(ta, tb, ta2, tb2, p, sms, st);
-    case EPI_F32: return launch_gemm<BN, EPI_F32, F8>(ta, tb, ta2, tb2, p, sms, st);
-    default: return launch_gemm<BN, EPI_RESID, F8>(ta, tb, ta2, tb2, p, sms, st);
+    case EPI_BF16: return launch_gemm<BN, EPI_BF16, F8>(ta, tb, ta2, tb2, tx, p, sms, st);
+    case EPI_GELU_BF16: return launch_gemm<BN, EPI_GELU_BF16, F8>(ta, tb, ta2, tb2, tx, p, sms, st);
+    case EPI_F32: return launch_gemm<BN, EPI_F32, F8>(ta, tb, ta2, tb2, tx, p, sms, st);
+    default: return launch_gemm<BN, EPI_RESID, F8>(ta, tb, ta2, tb2, tx, p, sms, st);
     }
 }
 
@@ -417,13 +558,21 @@ int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, 
     const int group_m = (int)std::max<size_t>(1, std::min<size_t>((size_t)m_blocks, kGroupPanelBytes / panel));
     GemmParams p{M,   N,    K,        a_scale, w_scale,           bias,         out,     ldo,       gate,
                  gate_idx, ld_gate, ctx->timeout_flag, f16_from_col, group_m, k2_blocks, w_col_scale};
+    // EPI_RESID: the residual x [M, ldo] f32 as a TMA map with 128 x 32 boxes
+    // (rows 16-byte aligned); otherwise the epilogue updates it with plain loads.
+    CUtensorMap tx = ta;
+    if (epi == EPI_RESID && ((uintptr_t)out & 15) == 0 && ldo % 4 == 0 && ldo >= N) {
+        if (!make_tmap_f32(&tx, out, M, N, ldo, BM, 32))
+            return fail(ctx, LTX_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed (residual)");
+        p.resid_tma = 1;
+    }
     cudaError_t e;
     if (es == 1)
-        e = BN == 128 ? dispatch_epi<128, true>(epi, ta, tb, ta2, tb2, p, ctx->sm_count, st)
-                      : dispatch_epi<256, true>(epi, ta, tb, ta2, tb2, p, ctx->sm_count, st);
+        e = BN == 128 ? dispatch_epi<128, true>(epi, ta, tb, ta2, tb2, tx, p, ctx->sm_count, st)
+                      : dispatch_epi<256, true>(epi, ta, tb, ta2, tb2, tx, p, ctx->sm_count, st);
     else
-        e = BN == 128 ? dispatch_epi<128, false>(epi, ta, tb, ta2, tb2, p, ctx->sm_count, st)
-                      : dispatch_epi<256, false>(epi, ta, tb, ta2, tb2, p, ctx->sm_count, st);
+        e = BN == 128 ? dispatch_epi<128, false>(epi, ta, tb, ta2, tb2, tx, p, ctx->sm_count, st)
+                      : dispatch_epi<256, false>(epi, ta, tb, ta2, tb2, tx, p, ctx->sm_count, st);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm launch");
     return LTX_OK;
 }
