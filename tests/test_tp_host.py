@@ -45,7 +45,7 @@ def test_comm_unique_ids_differ():
     assert ltx_b200.comm_unique_id() != ltx_b200.comm_unique_id()
 
 
-def _leaver(rank, ws, port, q):
+def _leaver(rank, ws, port, q, step1_done):
     """Rank 1 leaves between steps; rank 0's next collective must end with an
     error within the process group's short timeout instead of hanging."""
     import torch
@@ -56,7 +56,9 @@ def _leaver(rank, ws, port, q):
     t = torch.ones(4)
     dist.all_reduce(t)                       # step 1: both ranks
     if rank == 1:
-        os._exit(0)                          # leaves without a goodbye, no collective in flight
+        step1_done.wait(30)                  # rank 0 has finished step 1 too: nothing is in flight
+        os._exit(0)                          # leaves without a goodbye
+    step1_done.set()
     import time
     t0 = time.time()
     try:
@@ -75,7 +77,8 @@ def test_lost_rank_is_detected_by_the_next_collective():
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_leaver, args=(r, 2, port, q)) for r in range(2)]
+    step1_done = ctx.Event()
+    procs = [ctx.Process(target=_leaver, args=(r, 2, port, q, step1_done)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
