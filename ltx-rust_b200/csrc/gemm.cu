@@ -555,7 +555,13 @@ int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, 
     // as many M-blocks per group as keep their A panel within ~48 MB of L2
     const int m_blocks = (M + BM - 1) / BM;
     const size_t panel = (size_t)BM * K * es;
-    const int group_m = (int)std::max<size_t>(1, std::min<size_t>((size_t)m_blocks, kGroupPanelBytes / panel));
+    // A weight that fits in that budget itself stays in L2 whatever the order:
+    // then the N-blocks of one M-block run back to back (group_m = 1) and
+    // every A panel is read from DRAM once.
+    const size_t w_bytes = (size_t)N * K * es;
+    const int group_m = w_bytes <= kGroupPanelBytes
+                            ? 1
+                            : (int)std::max<size_t>(1, std::min<size_t>((size_t)m_blocks, kGroupPanelBytes / panel));
     GemmParams p{M,   N,    K,        a_scale, w_scale,           bias,         out,     ldo,       gate,
                  gate_idx, ld_gate, ctx->timeout_flag, f16_from_col, group_m, k2_blocks, w_col_scale};
     // EPI_RESID: the residual x [M, ldo] f32 as a TMA map with 128 x 32 boxes
