@@ -205,8 +205,9 @@ typedef enum {
  * model.rs:187, :254).  A and W are bf16 row-major with leading dimensions
  * lda/ldw in elements (multiples of 8; 16-byte aligned base pointers).
  * `bias_dev` is f32 [n] or NULL.  For LTX_EPI_RESID, `gate_dev` is f32
- * [U, ld_gate] and `gate_idx_dev` int32 [m] selects the gate row per output
- * row (NULL = row 0).  Enqueued on the context stream. */
+ * [U, ld_gate] (16-byte aligned rows: ld_gate a multiple of 4) and
+ * `gate_idx_dev` int32 [m] selects the gate row per output row (NULL = row
+ * 0).  Enqueued on the context stream. */
 int ltx_gemm_bf16(ltx_ctx *ctx, const void *a_dev, int64_t lda, const void *w_dev, int64_t ldw,
                   int32_t m, int32_t n, int32_t k, int32_t epilogue, const float *bias_dev,
                   void *out_dev, int64_t ldo, const float *gate_dev, const int32_t *gate_idx_dev,

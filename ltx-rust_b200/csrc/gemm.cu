@@ -535,6 +535,8 @@ int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, 
         return fail(ctx, LTX_ERR_SHAPE, "gemm: operands need 16-byte aligned rows (lda %lld ldw %lld)", (long long)lda,
                     (long long)ldw);
     if (epi < EPI_BF16 || epi > EPI_RESID) return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: bad epilogue %d", epi);
+    if (epi == EPI_RESID && gate && (((uintptr_t)gate & 15) || ld_gate % 4))
+        return fail(ctx, LTX_ERR_SHAPE, "gemm: gate rows must be 16-byte aligned (ld_gate %lld)", (long long)ld_gate);
     const int BN = N <= 128 ? 128 : 256;
     CUtensorMap ta, tb;
     if (!make_tmap_2d(&ta, A, M, K, lda, BM, es) || !make_tmap_2d(&tb, W, N, K, ldw, BN, es))
