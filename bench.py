@@ -22,6 +22,9 @@ Workloads:
   dequant_merge  config 1: FP8 e4m3 [4096,4096] (+scale) + rank-64 bf16 LoRA
                  -> bf16 [4096,4096], metric GB/s of algorithmic bytes; also
                  reported as the `dequant_merge` object of the step line.
+  chunk_pipeline config 5: 8 overlapping temporal chunks x 8 Euler steps,
+                 chunks spread over the ranks, seams exchanged and blended on
+                 the device, clip gathered on rank 0 (strong scaling).
 
 `--impl reference` times the reference algorithm's CPU restatement (the
 reference is a Rust workspace that cannot be built here) on the host cores,
