@@ -3,8 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
 Prints ONE JSON line (rank 0).  For N > 1 it is launched under torchrun, one
-rank per GPU; each rank processes its own independent units (weak scaling,
-no collective on the data path) and the step time is the max over ranks.
+rank per GPU; the step time is the max over ranks.
 
 Workloads:
   denoise_step   config 4 (default): one Euler/CFG denoising step of the
@@ -13,15 +12,19 @@ Workloads:
                  reference), 1024 context tokens, guidance 3.0 (CFG batch 2:
                  cond / uncond contexts), rescale 0.7.  Random-init FP8 e4m3
                  weights merged with a rank-64 LoRA on the device at load.
-                 metric tokens/s = 12288 / step time; at N GPUs each rank
-                 denoises its own temporal chunk (config 5's chunk-parallel
-                 axis: independent chunks, no collective), value = N*12288/t.
-                 With --parallel tp the N ranks instead split ONE sequence's
-                 model (heads and FFN units per rank, NCCL allreduce after
-                 each row-split projection): strong scaling, value = 12288/t.
+                 metric tokens/s = 12288 / step time.  At N > 1 the N ranks
+                 split ONE sequence's model (tensor parallel, as config 4
+                 states: heads and FFN units per rank, NCCL allreduce after
+                 each row-split projection; strong scaling, value = 12288/t).
+                 The N > 1 line also carries `replicas` (one independent
+                 sequence per GPU, no collective: weak scaling) and
+                 `chunk_pipeline` (config 5 on the N GPUs).  --parallel chunk
+                 makes the replica figure the headline instead.  The N = 1
+                 line carries `step_fp8` (the same step with FP8 FFN GEMMs).
   dequant_merge  config 1: FP8 e4m3 [4096,4096] (+scale) + rank-64 bf16 LoRA
                  -> bf16 [4096,4096], metric GB/s of algorithmic bytes; also
-                 reported as the `dequant_merge` object of the step line.
+                 reported as the `dequant_merge` object of the step line, with
+                 the dequant-only (no LoRA) rate beside it.
   chunk_pipeline config 5: 8 overlapping temporal chunks x 8 Euler steps,
                  chunks spread over the ranks, seams exchanged and blended on
                  the device, clip gathered on rank 0 (strong scaling).
@@ -37,6 +40,7 @@ import json
 import math
 import numpy as np
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -50,11 +54,14 @@ L2_BYTES = 126 * 1024 * 1024
 # Config 1 algorithmic bytes: fp8 W + scale + bf16 A and B + bf16 output.
 CFG1_BYTES = 4096 * 4096 + 4 + 2 * (64 * 4096 * 2) + 4096 * 4096 * 2
 CFG1_FMAS = 4096 * 4096 * 64
+# Config 1 without the LoRA (dequant only): fp8 W + scale + bf16 output.
+CFG1_DQ_BYTES = 4096 * 4096 + 4 + 4096 * 4096 * 2
 # DRAM bytes (read + write) per launch, from one ncu capture of each kernel
 # at the bench's shape (kernel_bench.py merge 4096x4096 rank 64; gemm
-# 24576x16384x4096 GELU).  The merge's bf16 output stays in L2 during the
-# launch, so its write-back is not in the figure.
-CFG1_NCU_TRAFFIC = 20.02e6 + 0.2455e6
+# 24576x16384x4096 GELU).  The merge's 33.5 MB bf16 output is still dirty in
+# L2 when a lone captured launch ends (ncu read 20.02 MB, wrote 0.25 MB), so
+# its write-back, which happens after the launch, is added as output bytes.
+CFG1_NCU_TRAFFIC = 20.02e6 + 4096 * 4096 * 2
 FFN_IN_NCU_TRAFFIC = 1.812415e9 + 0.78335488e9
 # self-attention at B=2, H=32, T=12288: DRAM read+write of a B=1, T=8192 launch
 # (201.56 MB + 46.14 MB) scaled by the Q/K/V/O bytes (805.3 MB / 268.4 MB)
@@ -198,6 +205,24 @@ def run_dequant_merge(args, rank, ws, device):
     ctx.synchronize()
     ms = max_over_ranks(start.elapsed_time(end) / (args.steps * ROUNDS * SETS), ws)
     times = [ms]
+    # the same weights without a LoRA: the HBM-bound dequant-only kernel
+    for _ in range(args.warmup):
+        for i in range(SETS):
+            ctx.dequant_merge(qs[i].data_ptr(), ltx_b200.LTX_F8_E4M3, True, scale, 4096, 4096, [],
+                              outs[i].data_ptr(), ltx_b200.LTX_BF16)
+    barrier(ws)
+    torch.cuda.synchronize()
+    DQ_ROUNDS = 4 * ROUNDS
+    ds, de = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ds.record(stream)
+    for _ in range(args.steps * DQ_ROUNDS):
+        for i in range(SETS):
+            ctx.dequant_merge(qs[i].data_ptr(), ltx_b200.LTX_F8_E4M3, True, scale, 4096, 4096, [],
+                              outs[i].data_ptr(), ltx_b200.LTX_BF16)
+    de.record(stream)
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    dq_ms = max_over_ranks(ds.elapsed_time(de) / (args.steps * DQ_ROUNDS * SETS), ws)
     # e2e through the C ABI with host buffers: pinned H2D of the step's inputs,
     # the kernel, D2H of the result; all inside the timed region.
     qh, ah, bh = q.pin_memory(), a.pin_memory(), b.pin_memory()
@@ -237,10 +262,16 @@ def run_dequant_merge(args, rank, ws, device):
                      "frac": achieved / peaks["hbm_gbs"], "traffic": CFG1_NCU_TRAFFIC, "peak_source": src,
                      "algorithmic_bytes_per_launch": CFG1_BYTES,
                      "fp32_fma_per_launch": CFG1_FMAS,
-                     "note": "the bit-exact rank-64 FMA chain makes this kernel FP32-pipe bound, not HBM bound"},
+                     "note": "the bit-exact rank-64 FMA chain makes this kernel FP32-pipe bound, not HBM bound",
+                     "traffic_note": "ncu DRAM reads of one launch + the bf16 output's write-back (the output "
+                                     "was still in L2 when the captured launch ended)"},
         "e2e": {"value": ws * CFG1_BYTES / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": q.numel() + 2 * a.numel() + 2 * b.numel(),
                 "d2h_bytes_per_step": out.numel() * 2},
+        "dequant_only": {"value": ws * CFG1_DQ_BYTES / (dq_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": dq_ms,
+                         "frac": CFG1_DQ_BYTES / (dq_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"],
+                         "peak_source": src, "algorithmic_bytes_per_launch": CFG1_DQ_BYTES,
+                         "note": "config 1 without the LoRA (fp8 in, bf16 out): 8 distinct weight sets back to back"},
         "gpu_launches": 2 * SETS * ROUNDS * args.steps,   # pre-pass + merge kernel per merge
         "merges_timed": SETS * ROUNDS * args.steps,
         "clocks": clk.summary(),
@@ -265,7 +296,12 @@ S_CTX, D, FF = 1024, 4096, 16384
 
 
 def step_flops(layers=48, T=T_TOTAL, S=S_CTX, B=2):
-    """Matmul FLOPs of one CFG step (8.521 TF/block/pass + head)."""
+    """Matmul FLOPs of one CFG step, per pass of the batch: per block the seven
+    projections 2*T*D*(3D + D + D + D + 2F) (self QKV, self out, cross q, cross
+    out, FFN in + out) plus cross k/v 2*S*D*2D, and the two attentions
+    4*T*T*D + 4*T*S*D (Q.K^T and P.V); at T 12288, S 1024, D 4096, F 16384 that
+    is 8.521 TFLOP per block per pass.  The head adds patchify_proj and
+    proj_out, 2*T*128*D each."""
     gemm = 2 * T * D * (3 * D + D + D + D + 2 * FF) + 2 * S * D * 2 * D
     attn = 4 * T * T * D + 4 * T * S * D
     head = 2 * T * 128 * D + 2 * T * D * 128
@@ -292,75 +328,133 @@ def make_step_inputs(F, H, W, S, Dc, seed):
             "sigmas": ltx_b200.scheduler_execute(8, Tt)}
 
 
+def step_config(ws, tp):
+    """The config-4 workload as both arms' lines name it (identical dicts)."""
+    return {"workload": "denoise_step_config4", "layers": 48, "hidden": D, "heads": 32, "head_dim": 128,
+            "ffn": FF, "tokens": T_TOTAL, "latent": [1, 128, LAT_F, LAT_H, LAT_W], "ic_reference": True,
+            "context_tokens": S_CTX, "cfg_batch": 2, "guidance": 3.0, "rescale": 0.7,
+            "weights": "random-init fp8 e4m3 per-tensor scale + rank-64 LoRA merged on device",
+            "parallelism": (f"tp{ws}: one sequence, heads and FFN units split over {ws} GPUs, NCCL allreduce"
+                            if tp else (f"replicas x{ws}: one independent sequence per GPU" if ws > 1 else
+                                        "one GPU, one sequence")),
+            "l2": "inputs and weights exceed L2 (25.8 GB bf16 weights streamed per step)",
+            "step_tflop": step_flops()[0] / 1e12}
+
+
+class StepRunner:
+    """One config-4 model and sampler state on this rank's GPU, stepped through
+    the C ABI (ltx_denoise_step) on the context's stream."""
+
+    def __init__(self, ctx, seed_model, seed_inputs, precision="bf16", offload_blocks=0):
+        import torch
+        import ltx_b200
+        cfg = json.loads(json.dumps(CFG4))
+        if precision != "bf16":
+            cfg["gemm_precision"] = precision
+        if offload_blocks:
+            cfg["offload_blocks"] = offload_blocks
+        t0 = time.time()
+        self.model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(cfg), seed=seed_model, lora_rank=64,
+                                                           lora_strength=1.0)
+        ctx.synchronize()
+        self.load_s = time.time() - t0
+        self.ctx = ctx
+        inp = make_step_inputs(LAT_F, LAT_H, LAT_W, S_CTX, D, seed=seed_inputs)
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+        self.lat0 = inp["latent"]
+        self.lat, self.clean, self.mask = dev(self.lat0), dev(inp["clean"]), dev(inp["mask"])
+        self.pos, self.cc, self.cu = dev(inp["positions"]), dev(inp["ctx_cond"]), dev(inp["ctx_uncond"])
+        self.mask_h = np.ascontiguousarray(inp["mask"], np.float32)
+        self.sig = inp["sigmas"]
+
+    def step(self, i):
+        n = len(self.sig) - 1
+        s0, s1 = float(self.sig[i % n]), float(self.sig[i % n + 1])
+        self.model.denoise_step(self.lat, self.clean, self.mask, self.pos, self.cc, self.cu, s0, max(s1, 0.0), 3.0,
+                                0.7, mask_host=self.mask_h)
+
+    def reference_step(self):
+        """One step (sigma pair 1 -> 2) from the initial latent: the new latent, on the host."""
+        import torch
+        self.lat.copy_(torch.from_numpy(np.ascontiguousarray(self.lat0, np.float32)))
+        self.step(1)
+        self.ctx.synchronize()
+        return self.lat.double().cpu()
+
+    def timed(self, steps, warmup, ws, device, clocks=True):
+        """ms per step over `steps` steps after `warmup` (CUDA events on the stream, max over ranks)."""
+        import torch
+        for i in range(warmup):
+            self.step(i)
+        self.ctx.synchronize()
+        stream = torch.cuda.current_stream()
+        barrier(ws)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk = ClockSampler(device) if clocks else None
+        if clk:
+            clk.__enter__()
+        torch.cuda.nvtx.range_push("denoise_timed")   # lets a profiler capture just these launches
+        start.record(stream)
+        for i in range(steps):
+            self.step(i)
+        end.record(stream)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        if clk:
+            clk.__exit__(None, None, None)
+        self.ctx.synchronize()
+        barrier(ws)
+        return max_over_ranks(start.elapsed_time(end) / steps, ws), (clk.summary() if clk else None)
+
+    def e2e(self, n, ws):
+        """ms per step through the C ABI from host buffers: pinned latent in, new latent out, each step."""
+        import torch
+        lat_h = torch.from_numpy(np.ascontiguousarray(self.lat0, np.float32)).pin_memory()
+        out_h = torch.empty_like(lat_h).pin_memory()
+        stream = torch.cuda.current_stream()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(ws)
+        torch.cuda.synchronize()
+        s2.record(stream)
+        for i in range(n):
+            self.lat.copy_(lat_h, non_blocking=True)
+            self.step(i)
+            out_h.copy_(self.lat, non_blocking=True)
+        e2.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(s2.elapsed_time(e2) / n, ws)
+        return ms, lat_h.numel() * 4, out_h.numel() * 4, bool(torch.isfinite(out_h).all())
+
+    def close(self):
+        self.model.close()
+
+
 def run_denoise_step(args, rank, ws, device):
-    import numpy as np
     import torch
     import ltx_b200
     torch.cuda.set_device(device)
     ctx = ltx_b200.Context(device)
-    t0 = time.time()
     tp = args.parallel == "tp" and ws > 1
     if tp:
         ltx_b200.init_tensor_parallel(ctx)   # this rank's shard of one model
-    cfg = dict(CFG4, offload_blocks=args.offload_blocks) if args.offload_blocks else CFG4
-    model = ltx_b200.VideoTransformer.init_random(ctx, json.dumps(cfg), seed=7 if tp else 7 + rank, lora_rank=64,
-                                                  lora_strength=1.0)
-    ctx.synchronize()
-    load_s = time.time() - t0
-    _log(f"model initialised in {load_s:.1f}s")
-    inp = make_step_inputs(LAT_F, LAT_H, LAT_W, S_CTX, D, seed=100 if tp else 100 + rank)
-    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
-    lat0 = inp["latent"]
-    lat, clean, mask = dev(lat0), dev(inp["clean"]), dev(inp["mask"])
-    pos, cc, cu = dev(inp["positions"]), dev(inp["ctx_cond"]), dev(inp["ctx_uncond"])
-    mask_h = np.ascontiguousarray(inp["mask"], np.float32)
-    sig = inp["sigmas"]
-
-    def step(i):
-        s0, s1 = float(sig[i % (len(sig) - 1)]), float(sig[i % (len(sig) - 1) + 1])
-        if s1 <= 0:
-            s1 = 0.0
-        model.denoise_step(lat, clean, mask, pos, cc, cu, s0, s1, 3.0, 0.7, mask_host=mask_h)
-
-    for i in range(args.warmup):
-        step(i)
-    ctx.synchronize()
-    _log(f"{args.warmup} warm-up steps done")
-    stream = torch.cuda.current_stream()
-    barrier(ws)
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device) as clk:
-        torch.cuda.nvtx.range_push("denoise_timed")   # lets a profiler capture just these launches
-        start.record(stream)
-        for i in range(args.steps):
-            step(i)
-        end.record(stream)
-        torch.cuda.nvtx.range_pop()
-        torch.cuda.synchronize()
-    ctx.synchronize()
-    barrier(ws)
-    ms = max_over_ranks(start.elapsed_time(end) / args.steps, ws)
+    # one sequence split over the ranks: every rank holds the same weights and inputs
+    run = StepRunner(ctx, 7 if tp else 7 + rank, 100 if tp else 100 + rank, offload_blocks=args.offload_blocks)
+    _log(f"model initialised in {run.load_s:.1f}s")
+    ms, clocks = run.timed(args.steps, args.warmup, ws, device)
     _log(f"{args.steps} timed steps: {ms:.1f} ms/step")
-    # e2e through the C ABI from host buffers: pinned latent in, new latent out, each step
-    lat_h = torch.from_numpy(np.ascontiguousarray(lat0, np.float32)).pin_memory()
-    out_h = torch.empty_like(lat_h).pin_memory()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n_e2e = max(1, min(args.steps, 3))
-    barrier(ws)
-    torch.cuda.synchronize()
-    s2.record(stream)
-    for i in range(n_e2e):
-        lat.copy_(lat_h, non_blocking=True)
-        step(i)
-        out_h.copy_(lat, non_blocking=True)
-    e2.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / n_e2e, ws)
+    e2e_ms, h2d, d2h, ok = run.e2e(max(1, min(args.steps, 3)), ws)
     _log(f"e2e: {e2e_ms:.1f} ms/step")
-    ok = bool(torch.isfinite(out_h).all())
-    # dominant kernel timed alone: FFN-in GEMM (GELU epilogue) at the step's shape
+    bf16_ref = run.reference_step() if ws == 1 else None
+    weight_bytes = run.model.weight_bytes()
+    load_s = run.load_s
+    run.close()
+    # dominant kernels timed alone at the step's shapes
+    gemm_ms = attn_ms = None
     M, N, K = 2 * T_TOTAL, FF, D
+    H, TA = D // 128, T_TOTAL
+    attn_flop = 4.0 * 2 * H * TA * TA * 128
+    stream = torch.cuda.current_stream()
     a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
     w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
     o = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
@@ -377,7 +471,6 @@ def run_denoise_step(args, rank, ws, device):
     del a, w, o
     # the step's largest kernel by time share, timed alone: self-attention
     # (bf16 Q/K, f16 V as the model feeds it) at B=2, H=32, T=12288
-    H, TA = D // 128, T_TOTAL
     q = torch.randn(2 * TA, D, device="cuda").to(torch.bfloat16)
     kk = torch.randn(2 * TA, D, device="cuda").to(torch.bfloat16)
     v = torch.randn(2 * TA, D, device="cuda").to(torch.float16)
@@ -391,7 +484,6 @@ def run_denoise_step(args, rank, ws, device):
     ae.record(stream)
     torch.cuda.synchronize()
     attn_ms = as_.elapsed_time(ae) / 10
-    attn_flop = 4.0 * 2 * H * TA * TA * 128
     _log(f"self-attention alone: {attn_ms:.3f} ms")
     del q, kk, v, ao
     peaks, src = measured_peaks()
@@ -405,37 +497,93 @@ def run_denoise_step(args, rank, ws, device):
         "higher_is_better": True,
         "scaling": "strong" if tp else "weak",
         "dtype": "bf16 (tensor-core GEMM/attention inputs; f32 accumulate, residual and sampler)",
-        "config": {"workload": "denoise_step_config4", "layers": 48, "hidden": D, "heads": 32, "head_dim": 128,
-                   "ffn": FF, "tokens": T_TOTAL, "latent": [1, 128, LAT_F, LAT_H, LAT_W], "ic_reference": True,
-                   "context_tokens": S_CTX, "cfg_batch": 2, "guidance": 3.0, "rescale": 0.7,
-                   "weights": "random-init fp8 e4m3 per-tensor scale + rank-64 LoRA merged on device",
-                   "parallelism": (f"tp{ws} (one sequence; heads and FFN split, NCCL allreduce)" if tp else
-                                   f"chunk-parallel x{ws} (one independent chunk per GPU)"),
-                   "l2": "inputs and weights exceed L2 (25.8 GB bf16 weights streamed per step)",
-                   "step_tflop": total / 1e12, "model_load_s": load_s,
-                   **({"offload_blocks": args.offload_blocks,
-                       "device_weight_bytes": model.weight_bytes()} if args.offload_blocks else {})},
+        "config": step_config(ws, tp),
+        "model_load_s": load_s,
+        **({"offload_blocks": args.offload_blocks, "device_weight_bytes": weight_bytes}
+           if args.offload_blocks else {}),
         "roofline": {"bound": "tensor", "kernel": "attn_fwd_kernel, self-attention (B=2, H=32, T=12288, d=128)",
                      "achieved": attn_flop / (attn_ms * 1e-3) / 1e12, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": attn_flop / (attn_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
                      "traffic": ATTN_NCU_TRAFFIC, "peak_source": src, "algorithmic_flops_per_launch": attn_flop,
                      "traffic_note": "ncu DRAM bytes of a B=1, T=8192 launch scaled by Q/K/V/O bytes",
-                     "step_tflops_achieved": total / (ms * 1e-3) / 1e12,
-                     "step_frac_of_sustained": total / (ms * 1e-3) / 1e12 / peaks.get("bf16_tflops_sustained",
-                                                                                      peaks["bf16_tflops"])},
+                     "step_tflops_per_gpu": (total / ws if tp else total) / (ms * 1e-3) / 1e12,
+                     "step_frac_of_sustained": (total / ws if tp else total) / (ms * 1e-3) / 1e12 /
+                     peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])},
         "roofline_gemm": {"bound": "tensor", "kernel": "tcgen05 GEMM, FFN-in + GELU (M=24576, N=16384, K=4096)",
-                     "achieved": gemm_tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": gemm_tf / peaks["bf16_tflops"], "traffic": FFN_IN_NCU_TRAFFIC, "peak_source": src,
-                     "algorithmic_flops_per_launch": 2.0 * M * N * K},
+                          "achieved": gemm_tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                          "frac": gemm_tf / peaks["bf16_tflops"], "traffic": FFN_IN_NCU_TRAFFIC, "peak_source": src,
+                          "algorithmic_flops_per_launch": 2.0 * M * N * K},
         "e2e": {"value": (1 if tp else ws) * T_TOTAL / (e2e_ms * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": lat_h.numel() * 4, "d2h_bytes_per_step": out_h.numel() * 4},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps * launches_per_step(48, tp),
-        "clocks": clk.summary(),
+        "clocks": clocks,
         "finite_output": ok,
     }
-    model.close()
+    if ws == 1:
+        res["step_fp8"] = run_fp8_step(args, ctx, device, bf16_ref, ms)
     ctx.close()
     return res
+
+
+def run_fp8_step(args, ctx, device, bf16_ref, bf16_ms):
+    """Config 4 with the two FFN projections of every block as native FP8 GEMMs
+    (gemm_precision e4m3_ffn: exact e4m3 base weights, per-row e4m3 activations,
+    the LoRA factored in the same accumulator), on the same synthetic weights
+    as the bf16 step: tokens/s, the FP8 FFN-in GEMM alone, and the rel-L2 of
+    one step's new latent and of its update against the bf16 step."""
+    import torch
+    import ltx_b200
+    run = StepRunner(ctx, 7, 100, precision="e4m3_ffn")
+    steps = max(3, min(args.steps, 10))
+    ms, clocks = run.timed(steps, 3, 1, device)
+    got = run.reference_step()
+    lat0 = torch.from_numpy(np.ascontiguousarray(run.lat0, np.float64))
+    run.close()
+    err = float((got - bf16_ref).norm() / bf16_ref.norm())
+    upd_err = float(((got - lat0) - (bf16_ref - lat0)).norm() / (bf16_ref - lat0).norm())
+    _log(f"FP8-FFN step: {ms:.1f} ms, latent rel-L2 vs bf16 {err:.2e}, update rel-L2 {upd_err:.2e}")
+    # the FP8 FFN-in GEMM alone (e4m3 A and W, per-row / per-tensor scales, GELU)
+    M, N, K = 2 * T_TOTAL, FF, D
+    a = torch.randint(0, 126, (M, K), device="cuda", dtype=torch.uint8)   # finite e4m3 bytes
+    sa = torch.ones(M, device="cuda")
+    w = torch.randint(0, 126, (N, K), device="cuda", dtype=torch.uint8)
+    o = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    for _ in range(3):
+        ltx_b200.gemm_e4m3(ctx, a, sa, w, 1.0, o, ltx_b200.EPI_GELU_BF16)
+    stream = torch.cuda.current_stream()
+    gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gs.record(stream)
+    for _ in range(10):
+        ltx_b200.gemm_e4m3(ctx, a, sa, w, 1.0, o, ltx_b200.EPI_GELU_BF16)
+    ge.record(stream)
+    torch.cuda.synchronize()
+    g_ms = gs.elapsed_time(ge) / 10
+    del a, w, o
+    g_tf = 2.0 * M * N * K / (g_ms * 1e-3) / 1e12
+    return {"gemm_precision": "e4m3_ffn", "value": T_TOTAL / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "steps": steps, "speedup_vs_bf16_step": bf16_ms / ms,
+            "rel_l2_latent_vs_bf16_step": err, "rel_l2_update_vs_bf16_step": upd_err, "bar": 3e-2,
+            "fp8_ffn_in_gemm": {"achieved": g_tf, "unit": "TFLOP/s", "peak": 4500.0,
+                                "frac": g_tf / 4500.0, "peak_source": "nominal dense FP8 (no measured FP8 peak)"},
+            "clocks": clocks,
+            "note": "same seeded weights as the bf16 step (exact FP8 base, LoRA factored); one step from the same "
+                    "latent over all 48 blocks compared against the bf16 model's step"}
+
+
+def run_replicas(args, rank, ws, device):
+    """N independent sequences, one per GPU, no collective on the data path
+    (weak scaling): value = N * 12288 / max-over-ranks step time."""
+    import torch
+    import ltx_b200
+    torch.cuda.set_device(device)
+    ctx = ltx_b200.Context(device)
+    run = StepRunner(ctx, 7 + rank, 100 + rank)
+    steps = max(3, min(args.steps, 5))
+    ms, clocks = run.timed(steps, 3, ws, device, clocks=False)
+    run.close()
+    ctx.close()
+    return {"value": ws * T_TOTAL / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "scaling": "weak", "parallelism": f"replicas x{ws}: one independent sequence per GPU"}
 
 
 def run_chunk_pipeline(args, rank, ws, device):
@@ -468,13 +616,20 @@ def run_chunk_pipeline(args, rank, ws, device):
         states[n]["sigmas"] = inp["sigmas"]
     outs = {n: torch.empty(T_TARGET, 128, device="cuda") for n in asg[rank]}
 
+    chunk_events = []   # per chunk on this rank: device time of its denoise loop
+
     def pipeline(steps_limit=None):
+        chunk_events.clear()
         for n in asg[rank]:
             st = states[n]
             lat = st["latent"].clone()
             sig = st["sigmas"] if steps_limit is None else st["sigmas"][:steps_limit + 1]
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
             model.denoise_loop(lat, st["clean"], st["mask"], st["positions"], st["ctx_cond"], st["ctx_uncond"],
                                sig, 3.0, 0.7, target_tokens=T_TARGET, out=outs[n], mask_host=st["mask_h"])
+            ev[1].record()
+            chunk_events.append(ev)
         data = {n: outs[n].view(lat_len, -1) for n in asg[rank]}
         recv = cp.exchange_seams(plan, asg, rank, data)
         cp.blend_seams(ctx, plan, recv, data)
@@ -495,6 +650,9 @@ def run_chunk_pipeline(args, rank, ws, device):
     ctx.synchronize()
     barrier(ws)
     ms = max_over_ranks(start.elapsed_time(end), ws)
+    # the chunks' denoise loops back to back on one GPU: the sum of every
+    # chunk's loop time over all ranks (each chunk's loop runs alone on its GPU)
+    serial_ms = sum_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in chunk_events), ws)
     steps = len(states[asg[rank][0]]["sigmas"]) - 1 if asg[rank] else 8
     res = {
         "metric": "chunk-parallel pipeline tokens/s (config 5: 8 chunks x 8 Euler steps of config 4, latent seam blend)",
@@ -508,6 +666,8 @@ def run_chunk_pipeline(args, rank, ws, device):
                    "pixel_plan": pix_plan, "latent_plan": plan, "clip_latent_frames": total_lat,
                    "parallelism": f"{len(asg[0])} chunk(s) per GPU over {ws} GPU(s)",
                    "seam": "2 latent frames per seam, sent point to point (NCCL), blended with ltx_seam_blend"},
+        "serial_chunks_ms": serial_ms,
+        "speedup_vs_serial_chunks": serial_ms / ms,
         "clip_finite": bool(torch.isfinite(clip).all()) if clip is not None else None,
         # per chunk: 8 Euler steps (each as ltx_denoise_step) + 1 seam blend per received seam
         "gpu_launches": len(asg[rank]) * steps * launches_per_step(48) + sum(1 for n in asg[rank] if n > 0),
@@ -654,12 +814,29 @@ def launches_per_step(L, tp=False):
     return 9 + L * (22 if tp else 15) + 2 + 2
 
 
+def cpu_model():
+    """The host CPU's model string (from /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
 def cpu_baseline_step(blocks=1, threads=None):
-    """The torch-f32 oracle (oracle/dit.py) on the host cores: one full-size
-    block for the CFG batch 2 (T=12288, S=1024, D=4096), extrapolated x48 +
-    the output head to the step.  Sample = `blocks` block forward(s)."""
+    """The torch-f32 oracle (oracle/dit.py, oracle/sampler.py) on the host
+    cores, on the config-4 shapes: `blocks` full-size block forward(s) for the
+    CFG batch 2 (T=12288, S=1024, D=4096), the model's per-token head
+    (patchify_proj, the adaLN-single MLP on every token as model.rs:196-206
+    runs it, the RoPE tables, the output LN + proj_out) for the batch, and the
+    CFG combine + global-std rescale + post_process + Euler update.  The step
+    is extrapolated as 48 x block + head + sampler."""
     import torch
     from oracle import dit
+    from oracle import sampler as osam
     dit.SDPA_Q_CHUNK = 256
     threads = threads or os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -669,20 +846,24 @@ def cpu_baseline_step(blocks=1, threads=None):
     pre = "transformer_blocks.0."
     shapes = {"attn1.to_q": (D, D), "attn1.to_k": (D, D), "attn1.to_v": (D, D), "attn1.to_out.0": (D, D),
               "attn2.to_q": (D, D), "attn2.to_k": (D, D), "attn2.to_v": (D, D), "attn2.to_out.0": (D, D),
-              "ff.net.0.proj": (FF, D), "ff.net.2": (D, FF)}
+              "ff.net.0.proj": (FF, D), "ff.net.2": (D, FF),
+              "patchify_proj": (D, 128), "proj_out": (128, D),
+              "adaln_single.emb.timestep_embedder.linear_1": (D, 256),
+              "adaln_single.emb.timestep_embedder.linear_2": (D, D), "adaln_single.linear": (6 * D, D)}
     for k, (o, i) in shapes.items():
-        p[pre + k + ".weight"] = torch.randn(o, i, generator=g) * 0.02
+        name = k if not k.startswith(("attn", "ff.")) else pre + k
+        p[name + ".weight"] = torch.randn(o, i, generator=g) * 0.02
         if "ff." not in k:
-            p[pre + k + ".bias"] = torch.zeros(o)
+            p[name + ".bias"] = torch.zeros(o)
     for a in ("attn1.", "attn2."):
         p[pre + a + "q_norm.weight"] = torch.ones(D)
         p[pre + a + "k_norm.weight"] = torch.ones(D)
     p[pre + "scale_shift_table"] = torch.randn(6, D, generator=g) * 0.02
+    p["scale_shift_table"] = torch.randn(2, D, generator=g) * 0.02
     B = 2
     x = torch.randn(B, T_TOTAL, D, generator=g)
     ctx = torch.randn(B, S_CTX, D, generator=g)
     mod = torch.randn(B, T_TOTAL, 6 * D, generator=g) * 0.02
-    from oracle import sampler as osam
     pos = torch.from_numpy(np.concatenate([osam.target_positions(LAT_F, LAT_H, LAT_W, B),
                                            osam.reference_positions(LAT_F, LAT_H, LAT_W, B)], axis=2))
     pe = dit.precompute_freqs_cis(pos, cfg)
@@ -691,10 +872,30 @@ def cpu_baseline_step(blocks=1, threads=None):
         for _ in range(blocks):
             dit.block_forward(p, 0, cfg, x, ctx, mod, pe)
     per_block = (time.time() - t0) / blocks
-    step_s = per_block * 48
-    return {"value": T_TOTAL / step_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+    del x, mod, pe
+    # the head: model_forward with no blocks (patchify, per-token adaLN, RoPE tables, output head)
+    lat = torch.randn(B, T_TOTAL, 128, generator=g)
+    ts = torch.cat([torch.full((B, T_TARGET), 0.9), torch.zeros(B, T_TARGET)], dim=1)
+    t0 = time.time()
+    with torch.no_grad():
+        vel = dit.model_forward(p, cfg, lat, ts, pos, ctx, n_blocks=0).numpy()
+    head_s = time.time() - t0
+    # the sampler: velocity -> x0, CFG + rescale, post_process, Euler (numpy f32)
+    lat_np, ts_np = lat.numpy()[:1], ts.numpy()[:1]
+    mask = np.concatenate([np.ones((1, T_TARGET, 1), np.float32), np.zeros((1, T_TARGET, 1), np.float32)], 1)
+    t0 = time.time()
+    x0c = osam.velocity_to_x0(lat_np, ts_np, vel[:1])
+    x0u = osam.velocity_to_x0(lat_np, ts_np, vel[1:])
+    x0 = osam.post_process(osam.cfg_combine(x0c, x0u, 3.0, 0.7), mask, lat_np)
+    osam.euler_step(lat_np, x0, 0.9, 0.8)
+    sampler_s = time.time() - t0
+    step_s = per_block * 48 + head_s + sampler_s
+    return {"value": T_TOTAL / step_s, "unit": "tokens/s", "cores": threads, "cpu_model": cpu_model(),
+            "kind": "port", "blocks_timed": blocks, "extrapolated": True,
+            "block_s": per_block, "head_s": head_s, "sampler_s": sampler_s, "step_s": step_s,
             "sample": f"{blocks} full-size block forward(s) (CFG batch 2, T=12288, S=1024) on the torch-f32 "
-                      f"oracle: {per_block:.1f} s/block, extrapolated x48 blocks (output head excluded)"}
+                      f"oracle: {per_block:.1f} s/block, extrapolated x48 blocks, plus the per-token head "
+                      f"({head_s:.1f} s) and the CFG/Euler update ({sampler_s:.2f} s), each timed once"}
 
 
 def cpu_baseline_dequant(seconds=5.0, threads=None):
@@ -725,6 +926,16 @@ def barrier(ws):
         dist.barrier()
 
 
+def sum_over_ranks(x, ws):
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def max_over_ranks(x, ws):
     if ws == 1:
         return x
@@ -743,8 +954,9 @@ def main():
     ap.add_argument("--workload", default="denoise_step", choices=["denoise_step", "dequant_merge", "chunk_pipeline"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=5.0)
-    ap.add_argument("--parallel", default="chunk", choices=["chunk", "tp"],
-                    help="N>1: independent chunk per GPU (default) or one sequence split over the GPUs")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "chunk"],
+                    help="denoise_step at N>1: one sequence split over the GPUs (default, config 4's tensor "
+                         "parallel) or one independent sequence per GPU")
     ap.add_argument("--offload-blocks", type=int, default=0,
                     help="denoise_step: keep the blocks in pinned host memory with this many on the device")
     args = ap.parse_args()
@@ -762,16 +974,21 @@ def main():
                "metric": ("chunk-parallel pipeline tokens/s (config 5: 8 chunks x 8 Euler steps of config 4, latent "
                           "seam blend)" if pipe else
                           "DiT denoise-step tokens/s (config 4: 48 blocks, T=12288, CFG batch 2 + Euler)"),
-               "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-               "warmup": args.warmup,
+               "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+               # what ran: one extrapolated step from one timed block, the head and the sampler
+               "steps": 1, "warmup": 0, "blocks_timed": base["blocks_timed"], "extrapolated": True,
                "ms_per_step": (64 if pipe else 1) * T_TOTAL / base["value"] * 1e3,
-               "higher_is_better": True, "scaling": "strong" if pipe else "weak", "vs_baseline": None,
+               "higher_is_better": True, "scaling": "strong" if pipe else ("strong" if args.gpus > 1 else "weak"),
+               "vs_baseline": None,
                "dtype": "f32", "data": "synthetic (random-init weights, N(0,1) activations)",
-               "config": {"workload": "chunk_pipeline_config5" if pipe else "denoise_step_config4"},
+               "config": ({"workload": "chunk_pipeline_config5"} if pipe else
+                          step_config(args.gpus, args.gpus > 1 and args.parallel == "tp")),
                "cpu_baseline": base,
                "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-               "note": "CPU restatement of the reference (oracle/dit.py, torch f32): the Rust reference cannot be "
-                       "built here; one block timed and extrapolated to the 48-block step"}
+               "note": "CPU restatement of the reference (oracle/dit.py + oracle/sampler.py, torch/numpy f32): the "
+                       "Rust reference cannot be built here.  One full-size block, the head and the sampler update "
+                       "are each timed once on the host cores and the 48-block step is extrapolated from them; the "
+                       "driver's --steps/--warmup are not repeated (the line's steps/warmup say what ran)."}
         print(json.dumps(res))
         return
     if args.impl == "reference":
@@ -823,10 +1040,23 @@ def main():
             _log(f"block forward: bf16 {blk['bf16']['ms']:.2f} ms, e4m3_ffn {blk['e4m3_ffn']['ms']:.2f} ms "
                  f"(rel-L2 {blk['e4m3_ffn']['rel_l2_vs_bf16']:.2e}), e4m3 {blk['e4m3']['ms']:.2f} ms "
                  f"(rel-L2 {blk['e4m3']['rel_l2_vs_bf16']:.2e})")
+        if ws > 1:
+            if args.parallel == "tp":
+                rep = run_replicas(args, rank, ws, local)
+                _log(f"replicas: {rep['ms_per_step']:.1f} ms/step, {rep['value']:.0f} tokens/s")
+                res["replicas"] = rep
+            pl_args = argparse.Namespace(warmup=3)
+            pl = run_chunk_pipeline(pl_args, rank, ws, local)
+            _log(f"config-5 pipeline: {pl['ms_per_step'] / 1e3:.2f} s, {pl['speedup_vs_serial_chunks']:.2f}x the "
+                 "serial chunks")
+            res["chunk_pipeline"] = {k: pl[k] for k in ("metric", "value", "unit", "ms_per_step", "serial_chunks_ms",
+                                                        "speedup_vs_serial_chunks", "clip_finite")}
+            res["chunk_pipeline"]["config"] = pl["config"]
         if rank == 0:
             res.update({"n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "vs_baseline": None,
                         "data": "synthetic (random-init FP8+LoRA weights, N(0,1) latent/reference/contexts)"})
-            res["dequant_merge"] = {k: dq[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "e2e")}
+            res["dequant_merge"] = {k: dq[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "e2e",
+                                                       "dequant_only")}
             if ffn:
                 res["linear_ffn_config2"] = ffn
             if blk:

@@ -182,7 +182,8 @@ int ltx_dequant_merge(ltx_ctx *ctx, const void *w_dev, int32_t w_dtype, int32_t 
  * that array, so calls whose GPU work overlaps (e.g. on two streams) race on
  * it.  The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress) and caches it; make that first call before any
- * stream capture. */
+ * stream capture.  The cached address lives as long as the device's primary
+ * context: do not call this entry point again after cudaDeviceReset. */
 int ltx_dequant_merge_noalloc(void *stream, const void *w_dev, int32_t w_dtype, int32_t has_scale,
                               float scale, int64_t out_features, int64_t in_features,
                               const ltx_lora_delta *deltas, int32_t n_deltas, void *dst_dev,

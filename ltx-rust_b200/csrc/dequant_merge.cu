@@ -374,11 +374,21 @@ cudaError_t launch_merge(const MergeParams &p, cudaStream_t st, int sms, void *s
 
 }  // namespace
 
+// rows * cols without int64 overflow, and small enough (2^48 elements) that
+// every byte count derived from it stays in range.
+static bool merge_shape_fits(int64_t rows, int64_t cols) {
+    constexpr int64_t kMaxElements = int64_t(1) << 48;
+    return rows == 0 || cols == 0 || rows <= kMaxElements / cols;
+}
+
 // Validates and enqueues one dequant(+merge) on `stream`.
 int dequant_merge(ltx_ctx *ctx, cudaStream_t stream, const void *w, int w_dt, int has_scale, float scale, int64_t rows,
                   int64_t cols, const ltx_lora_delta *deltas, int n_deltas, void *dst, int dst_dt) {
     if (!w || !dst) return fail(ctx, LTX_ERR_INVALID_ARG, "dequant_merge: null pointer");
     if (rows < 0 || cols < 0) return fail(ctx, LTX_ERR_SHAPE, "dequant_merge: negative shape");
+    if (!merge_shape_fits(rows, cols))
+        return fail(ctx, LTX_ERR_SHAPE, "dequant_merge: %lld x %lld elements exceed 2^48", (long long)rows,
+                    (long long)cols);
     if (w_dt < LTX_F32 || w_dt > LTX_F8_E5M2) return fail(ctx, LTX_ERR_DTYPE, "dequant_merge: bad weight dtype %d", w_dt);
     if (dst_dt != LTX_F32 && dst_dt != LTX_BF16)
         return fail(ctx, LTX_ERR_DTYPE, "dequant_merge: output dtype must be F32 or BF16");
@@ -459,7 +469,10 @@ extern "C" int ltx_dequant_merge(ltx_ctx *ctx, const void *w_dev, int32_t w_dtyp
 //     same array used from two host threads with no ordering) race on it.
 //   * Set-up: the first call on each device resolves the array's device
 //     address with cudaGetSymbolAddress (with that device current) and caches
-//     it.  Make that first call before any stream capture.
+//     it.  Make that first call before any stream capture.  The cached address
+//     belongs to the device's primary context: after cudaDeviceReset (which
+//     destroys that context and the array with it) this entry point must not
+//     be called again in the process.
 namespace ltx {
 namespace {
 
@@ -493,6 +506,11 @@ extern "C" int ltx_dequant_merge_noalloc(void *stream, const void *w_dev, int32_
     }
     if (out_features < 0 || in_features < 0) {
         set_err(errbuf, errbuf_len, "dequant_merge_noalloc: negative shape");
+        return LTX_ERR_SHAPE;
+    }
+    if (!merge_shape_fits(out_features, in_features)) {
+        set_err(errbuf, errbuf_len, "dequant_merge_noalloc: %lld x %lld elements exceed 2^48",
+                (long long)out_features, (long long)in_features);
         return LTX_ERR_SHAPE;
     }
     if (w_dtype < LTX_F32 || w_dtype > LTX_F8_E5M2) {

@@ -701,8 +701,10 @@ cudaError_t cfg_euler(cudaStream_t st, int sms, float *x, const float *vc, const
 
 extern "C" int ltx_patchify(ltx_ctx *ctx, const float *latent_dev, int32_t batch, int32_t channels, int32_t frames,
                             int32_t height, int32_t width, float *tokens_dev) {
-    if (!ctx || !latent_dev || !tokens_dev || batch < 0 || channels < 0 || frames < 0 || height < 0 || width < 0)
+    if (!ctx || batch < 0 || channels < 0 || frames < 0 || height < 0 || width < 0)
         return ctx ? ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_patchify: bad arguments") : LTX_ERR_INVALID_ARG;
+    if ((int64_t)batch * channels * frames * height * width == 0) return LTX_OK;   // nothing to move
+    if (!latent_dev || !tokens_dev) return ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_patchify: null pointer");
     cudaError_t e = ltx::permute_ct(ctx->stream, ctx->sm_count, latent_dev, tokens_dev, batch, channels,
                                     (int64_t)frames * height * width, true);
     return e == cudaSuccess ? LTX_OK : ltx::cuda_fail(ctx, e, "ltx_patchify");
@@ -710,8 +712,10 @@ extern "C" int ltx_patchify(ltx_ctx *ctx, const float *latent_dev, int32_t batch
 
 extern "C" int ltx_unpatchify(ltx_ctx *ctx, const float *tokens_dev, int32_t batch, int32_t channels, int32_t frames,
                               int32_t height, int32_t width, float *latent_dev) {
-    if (!ctx || !latent_dev || !tokens_dev || batch < 0 || channels < 0 || frames < 0 || height < 0 || width < 0)
+    if (!ctx || batch < 0 || channels < 0 || frames < 0 || height < 0 || width < 0)
         return ctx ? ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_unpatchify: bad arguments") : LTX_ERR_INVALID_ARG;
+    if ((int64_t)batch * channels * frames * height * width == 0) return LTX_OK;   // nothing to move
+    if (!latent_dev || !tokens_dev) return ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_unpatchify: null pointer");
     cudaError_t e = ltx::permute_ct(ctx->stream, ctx->sm_count, tokens_dev, latent_dev, batch, channels,
                                     (int64_t)frames * height * width, false);
     return e == cudaSuccess ? LTX_OK : ltx::cuda_fail(ctx, e, "ltx_unpatchify");

@@ -12,7 +12,7 @@ Sources (paths inside the reference project):
   crates/ltx-dit/tests/fixtures/dit_parity*.safetensors  (tiny DiT forward;
       generator tools/parity/ltx-dit.py, upstream LTX-2 commit 9ec55f9)
 
-Usage:  python tests/golden/make_golden.py [reference_root]
+Usage:  python tests/golden/make_golden.py <reference_root>
 """
 import os
 import sys
@@ -47,4 +47,6 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <reference_root>  (the ltx-rust checkout)")
+    main(sys.argv[1])

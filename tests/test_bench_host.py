@@ -38,3 +38,21 @@ def test_reference_arm_prints_one_contract_line():
     assert d["impl"] == "reference" and d["value"] > 0 and d["warmup"] >= 3
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_names_what_it_ran_with_the_same_config(monkeypatch, capsys):
+    """The denoise-step reference arm extrapolates one timed block (plus head and sampler) to the
+    step: its line says so (blocks_timed, extrapolated, steps 1) and carries the same config
+    dict as this build's line at the same GPU count."""
+    import bench
+    canned = {"value": 10.0, "unit": "tokens/s", "cores": 4, "cpu_model": "x", "kind": "port",
+              "blocks_timed": 1, "extrapolated": True, "sample": "canned"}
+    monkeypatch.setattr(bench, "cpu_baseline_step", lambda blocks=1: dict(canned))
+    for gpus, tp in ((1, False), (8, True)):
+        monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--gpus", str(gpus), "--steps", "20",
+                                          "--warmup", "5"])
+        bench.main()
+        d = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+        assert d["impl"] == "reference" and d["steps"] == 1 and d["blocks_timed"] == 1 and d["extrapolated"]
+        assert d["config"] == bench.step_config(gpus, tp)
+        assert d["cpu_baseline"]["cpu_model"] == "x"

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_rust_binding_in_integration_doc_declares_every_entry_point():
-    """The `-sys` crate INTEGRATION.md gives a maintainer binds every function of the header."""
+    """The Rust `-sys` declarations of the integration guide bind every function of the header."""
     doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
     rust = doc[doc.index("```rust"):]
     rust = rust[:rust.index("```", 7)]

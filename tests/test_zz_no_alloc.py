@@ -6,8 +6,12 @@ run the FP8 dequant + LoRA merge through ltx_dequant_merge_noalloc, which
 keeps its chain scratch in a fixed file-scope device array instead of
 allocating.  These tests call it through the C ABI and check that it gives
 exactly what ltx_dequant_merge gives (bit-exact: both run the same kernels),
-on two different calls in a row so that the shared scratch is reused, and
-that a merge too large for the array is refused with a clear error.
+on calls in a row so that the shared scratch is reused: a config-1 merge, a
+ragged f32 merge with two stacked deltas, a merge with no LoRA at all, and
+the largest 22B DiT weight (the 24576 x 4096 adaLN projection with a rank-64
+LoRA, 13.6 MB of its 16 MiB scratch).  They also check that the device's free
+memory does not change across a call once the library is loaded, and that a
+merge too large for the array is refused with a clear error.
 
 Named test_zz_* so it is collected after every other test file; it creates
 its own context and inputs, so it also passes alone in a fresh process.
@@ -51,18 +55,31 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls():
         (0, 4096, 4096, [(64, ltx_b200.LTX_BF16)], ltx_b200.LTX_F8_E4M3, ltx_b200.LTX_BF16),
         # a second, different call: ragged f32 weight, two stacked deltas, f32 out
         (1, 1000, 777, [(33, ltx_b200.LTX_F32), (7, ltx_b200.LTX_BF16)], ltx_b200.LTX_F32, ltx_b200.LTX_F32),
+        # no LoRA: the dequant-only kernel, no scratch
+        (2, 512, 4096, [], ltx_b200.LTX_F8_E4M3, ltx_b200.LTX_BF16),
+        # the largest 22B DiT weight with a rank-64 LoRA: close to the scratch limit
+        (3, 24576, 4096, [(64, ltx_b200.LTX_BF16)], ltx_b200.LTX_F8_E4M3, ltx_b200.LTX_BF16),
     ]
+    free_after = []
     for seed, rows, cols, specs, wdt, odt in cases:
         w, keep, deltas = _case(seed, rows, cols, specs, wdt)
         tdt = torch.bfloat16 if odt == ltx_b200.LTX_BF16 else torch.float32
         ref = torch.empty(rows * cols, dtype=tdt, device="cuda")
         got = torch.full((rows * cols,), float("nan"), dtype=tdt, device="cuda")
         ctx.dequant_merge(w.data_ptr(), wdt, True, 0.02 * 4.5 / 448, rows, cols, deltas, ref.data_ptr(), odt)
+        ctx.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
         ltx_b200.dequant_merge_noalloc(stream, w.data_ptr(), wdt, True, 0.02 * 4.5 / 448, rows, cols, deltas,
                                        got.data_ptr(), odt)
         ctx.synchronize()
+        free_after.append((free_before, torch.cuda.mem_get_info()[0]))
         assert np.array_equal(_bits(got), _bits(ref)), f"case {seed}: outputs differ"
+        del w, keep, ref, got
     ctx.close()
+    # The first call on a device may load the library's device code (and its
+    # scratch array) lazily; every call after it leaves free memory unchanged.
+    for i, (before, after) in enumerate(free_after[1:], 1):
+        assert before == after, f"call {i}: device free memory changed by {before - after} bytes"
 
 
 def test_noalloc_rejects_merges_beyond_its_scratch():
