@@ -205,24 +205,52 @@ def run_dequant_merge(args, rank, ws, device):
     ctx.synchronize()
     ms = max_over_ranks(start.elapsed_time(end) / (args.steps * ROUNDS * SETS), ws)
     times = [ms]
-    # the same weights without a LoRA: the HBM-bound dequant-only kernel
+    # the same weights without a LoRA: the HBM-bound dequant-only kernel.  A
+    # launch from Python costs more than the ~8 us kernel, so the calls (the
+    # same C-ABI calls) are captured once into a CUDA graph on a context of
+    # their own and the graph is replayed: the device time of back-to-back
+    # dequants.  The eager figure (Python launch per call) is reported beside it.
+    def dq(c, i):
+        c.dequant_merge(qs[i].data_ptr(), ltx_b200.LTX_F8_E4M3, True, scale, 4096, 4096, [], outs[i].data_ptr(),
+                        ltx_b200.LTX_BF16)
+
+    DQ_ROUNDS = 4 * ROUNDS
     for _ in range(args.warmup):
         for i in range(SETS):
-            ctx.dequant_merge(qs[i].data_ptr(), ltx_b200.LTX_F8_E4M3, True, scale, 4096, 4096, [],
-                              outs[i].data_ptr(), ltx_b200.LTX_BF16)
+            dq(ctx, i)
     barrier(ws)
     torch.cuda.synchronize()
-    DQ_ROUNDS = 4 * ROUNDS
     ds, de = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ds.record(stream)
     for _ in range(args.steps * DQ_ROUNDS):
         for i in range(SETS):
-            ctx.dequant_merge(qs[i].data_ptr(), ltx_b200.LTX_F8_E4M3, True, scale, 4096, 4096, [],
-                              outs[i].data_ptr(), ltx_b200.LTX_BF16)
+            dq(ctx, i)
     de.record(stream)
     torch.cuda.synchronize()
     ctx.synchronize()
-    dq_ms = max_over_ranks(ds.elapsed_time(de) / (args.steps * DQ_ROUNDS * SETS), ws)
+    dq_eager_ms = max_over_ranks(ds.elapsed_time(de) / (args.steps * DQ_ROUNDS * SETS), ws)
+    gstream = torch.cuda.Stream()
+    gctx = ltx_b200.Context(device, stream=gstream.cuda_stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=gstream, capture_error_mode="thread_local"):
+        for _ in range(4):
+            for i in range(SETS):
+                dq(gctx, i)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(ws)
+    gs_, ge_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    G_REPLAYS = max(1, DQ_ROUNDS * args.steps // 4)
+    with torch.cuda.stream(gstream):
+        gs_.record(gstream)
+        for _ in range(G_REPLAYS):
+            graph.replay()
+        ge_.record(gstream)
+    torch.cuda.synchronize()
+    dq_ms = max_over_ranks(gs_.elapsed_time(ge_) / (G_REPLAYS * 4 * SETS), ws)
+    del graph
+    gctx.close()
     # e2e through the C ABI with host buffers: pinned H2D of the step's inputs,
     # the kernel, D2H of the result; all inside the timed region.
     qh, ah, bh = q.pin_memory(), a.pin_memory(), b.pin_memory()
@@ -271,7 +299,10 @@ def run_dequant_merge(args, rank, ws, device):
         "dequant_only": {"value": ws * CFG1_DQ_BYTES / (dq_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": dq_ms,
                          "frac": CFG1_DQ_BYTES / (dq_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "peak": peaks["hbm_gbs"],
                          "peak_source": src, "algorithmic_bytes_per_launch": CFG1_DQ_BYTES,
-                         "note": "config 1 without the LoRA (fp8 in, bf16 out): 8 distinct weight sets back to back"},
+                         "eager_ms_per_step": dq_eager_ms,
+                         "note": "config 1 without the LoRA (fp8 in, bf16 out): 8 distinct weight sets back to back "
+                                 "(403 MB > L2), the C-ABI calls replayed from a CUDA graph; eager_ms_per_step is "
+                                 "the same with one Python launch per call"},
         "gpu_launches": 2 * SETS * ROUNDS * args.steps,   # pre-pass + merge kernel per merge
         "merges_timed": SETS * ROUNDS * args.steps,
         "clocks": clk.summary(),
@@ -544,9 +575,14 @@ def run_fp8_step(args, ctx, device, bf16_ref, bf16_ms):
     _log(f"FP8-FFN step: {ms:.1f} ms, latent rel-L2 vs bf16 {err:.2e}, update rel-L2 {upd_err:.2e}")
     # the FP8 FFN-in GEMM alone (e4m3 A and W, per-row / per-tensor scales, GELU)
     M, N, K = 2 * T_TOTAL, FF, D
-    a = torch.randint(0, 126, (M, K), device="cuda", dtype=torch.uint8)   # finite e4m3 bytes
-    sa = torch.ones(M, device="cuda")
-    w = torch.randint(0, 126, (N, K), device="cuda", dtype=torch.uint8)
+    # e4m3 operands as the model quantises them: N(0,1) rows scaled to amax 448, N(0,0.02) weights / (amax/448)
+    x = torch.randn(M, K, device="cuda")
+    sa = x.abs().amax(dim=1) / 448.0
+    a = (x / sa[:, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+    del x
+    w32 = torch.randn(N, K, device="cuda") * 0.02
+    w = (w32 / (w32.abs().max() / 448.0)).to(torch.float8_e4m3fn).view(torch.uint8)
+    del w32
     o = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     for _ in range(3):
         ltx_b200.gemm_e4m3(ctx, a, sa, w, 1.0, o, ltx_b200.EPI_GELU_BF16)

@@ -175,7 +175,7 @@ int ltx_dequant_merge(ltx_ctx *ctx, const void *w_dev, int32_t w_dtype, int32_t 
  * (creating one allocates): `stream` is a cudaStream_t (NULL = default
  * stream) on the current device, and a failure message is written to
  * `errbuf` (may be NULL).  It calls no cudaMalloc/cudaFree: the merge's chain
- * scratch (4 * total rank * (round_up(in,128) + 2*round_up(out,128)) bytes)
+ * scratch (4 * total rank * (round_up(in,128) + round_up(out,128)) bytes)
  * lives in one LTX_NOALLOC_SCRATCH_BYTES file-scope device array that every
  * GPU loading the library holds until exit; larger merges return
  * LTX_ERR_UNSUPPORTED before enqueuing anything.  All calls on a device share

@@ -9,9 +9,8 @@
 //                   f32 FMA chain (rank FMAs per delta, r ascending).  That is
 //                   FP32-pipe-bound, not HBM-bound: 64 FMAs per element at
 //                   rank 64.  The CTA stages coeff*B (rows x r) and A
-//                   (r x cols) in shared memory and each thread keeps a
-//                   16 x 8 register tile, issuing packed FFMA2 (two
-//                   independent IEEE fma.rn per instruction), so the
+//                   (r x cols) in shared memory and each thread keeps an
+//                   8 x 8 register tile of scalar IEEE fma.rn chains, so the
 //                   rounding of every element is the reference's.
 #include <cstdarg>
 #include <cstdio>
@@ -61,43 +60,67 @@ __device__ __forceinline__ void store_out(const MergeParams &p, int64_t idx, flo
 
 // ── no-delta path: HBM-bound streaming kernel ────────────────────────────────
 
+// 16 input elements (one 16-byte FP8 load) -> decode, scale, convert, store.
+template <int WDT, bool OUT_BF16>
+__device__ __forceinline__ void dequant16(const MergeParams &p, int64_t v, uint4 raw) {
+    float f[16];
+    if constexpr (WDT == LTX_F8_E4M3 || WDT == LTX_F8_E5M2) {
+        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const uint32_t byte = (w4[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+            f[j] = WDT == LTX_F8_E4M3 ? dec_e4m3(byte) : dec_e5m2(byte);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) f[j] = load_as_f32(p.w, WDT, v * 16 + j);
+    }
+    if (p.fp8_scaled) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) f[j] = __fmaf_rn(p.scale, f[j], 0.0f);
+    }
+    if constexpr (OUT_BF16) {
+        uint32_t o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+            o[j] = *reinterpret_cast<uint32_t *>(&h);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(p.dst) + v * 2;
+        __stcs(dst, make_uint4(o[0], o[1], o[2], o[3]));
+        __stcs(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
+    } else {
+        float4 *dst = reinterpret_cast<float4 *>(p.dst) + v * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) __stcs(dst + j, make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]));
+    }
+}
+
+// Each thread takes kDqUnroll 16-element vectors a grid-stride apart and
+// issues all their loads before decoding any, so a wave of CTAs keeps the
+// whole input of a 4096 x 4096 weight in flight; the launch sizes the grid
+// for one such round where it fits.
+constexpr int kDqUnroll = 4;
+
 template <int WDT, bool OUT_BF16>
 __global__ void __launch_bounds__(256) dequant_only_kernel(MergeParams p, int64_t n) {
     const int64_t n16 = n / 16;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < n16; v += stride) {
-        float f[16];
+    int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint4 *src = reinterpret_cast<const uint4 *>(p.w);
+    for (; v + (kDqUnroll - 1) * stride < n16; v += kDqUnroll * stride) {
+        uint4 raw[kDqUnroll];
         if constexpr (WDT == LTX_F8_E4M3 || WDT == LTX_F8_E5M2) {
-            const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(p.w) + v);
-            const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const uint32_t byte = (w4[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-                f[j] = WDT == LTX_F8_E4M3 ? dec_e4m3(byte) : dec_e5m2(byte);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) f[j] = load_as_f32(p.w, WDT, v * 16 + j);
+            for (int u = 0; u < kDqUnroll; ++u) raw[u] = __ldcs(src + v + u * stride);
         }
-        if (p.fp8_scaled) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) f[j] = __fmaf_rn(p.scale, f[j], 0.0f);
-        }
-        if constexpr (OUT_BF16) {
-            uint32_t o[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
-                o[j] = *reinterpret_cast<uint32_t *>(&h);
-            }
-            uint4 *dst = reinterpret_cast<uint4 *>(p.dst) + v * 2;
-            __stcs(dst, make_uint4(o[0], o[1], o[2], o[3]));
-            __stcs(dst + 1, make_uint4(o[4], o[5], o[6], o[7]));
-        } else {
-            float4 *dst = reinterpret_cast<float4 *>(p.dst) + v * 4;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) __stcs(dst + j, make_float4(f[4 * j], f[4 * j + 1], f[4 * j + 2], f[4 * j + 3]));
-        }
+        for (int u = 0; u < kDqUnroll; ++u) dequant16<WDT, OUT_BF16>(p, v + u * stride, raw[u]);
+    }
+    for (; v < n16; v += stride) {
+        uint4 raw{};
+        if constexpr (WDT == LTX_F8_E4M3 || WDT == LTX_F8_E5M2) raw = __ldcs(src + v);
+        dequant16<WDT, OUT_BF16>(p, v, raw);
     }
     // tail (n not a multiple of 16)
     for (int64_t i = n16 * 16 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
@@ -113,46 +136,53 @@ __global__ void dequant_only_scalar_kernel(MergeParams p, int64_t n) {
 //
 // All deltas' (c, a) pairs form ONE chain: for delta d, rank step r,
 // v = fma(coeff_d * B_d[o][r], A_d[r][i], v).  A pre-pass writes the chain as
-// f32 into scratch — a32[k][cols_p] and ct[k][rows_p] (ct transposed so a
+// f32 into scratch — a32[k][cols_p] and c32[k][rows_p] (c transposed so a
 // CTA's rows are contiguous for each k) — zero-padded to the tile grid, so
 // the main kernel stages it with unconditional 16-byte cp.async copies.
 
-constexpr int kWarps = 8;
-constexpr int kRowsPerWarp = 16;
-constexpr int kTileRows = kWarps * kRowsPerWarp;  // 128
-constexpr int kTileCols = 128;                     // per lane: 4 columns at lane*4
-constexpr int kRChunk = 32;                        // chain steps per stage
+constexpr int kWarps = 8;       // 2 (rows) x 4 (columns) warps
+constexpr int kTileRows = 128;  // per warp 64 rows; per lane 8 rows (2 x 4)
+constexpr int kTileCols = 128;  // per warp 32 columns; per lane 8 columns (2 x 4)
+constexpr int kRChunk = 32;     // chain steps per stage
 
+// Thread -> element map of the 128 x 128 tile.  Lanes form 8 row groups x 4
+// column groups, so per chain step a warp's shared loads are one contiguous
+// 128-byte piece of coeff*B (2 float4) and one 64-byte piece of A (2 float4):
+// one LSU wavefront each.
+//   rows: wr*64 + 32*j + 4*lr + e   (j < 2, e < 4; register row 4j + e)
+//   cols: wc*32 + 16*k + 4*lc + e   (k < 2, e < 4)
+// Each element's chain runs as scalar IEEE fma.rn (on this B200 scalar FFMA
+// measured 122 FMA/clk/SM against 103-111 for packed FFMA2, and needs no
+// duplicated operand pairs).
 struct MergeSmem {
-    float a[2][kRChunk][kTileCols];    // A chain rows                       32 KB
-    float2 c[2][kRChunk][kTileRows];   // {c, c} = coeff*B, paired for FFMA2  64 KB
-    uint8_t w8[kTileRows][kTileCols];  // FP8 base tile                       16 KB
-};   // 112 KB: two CTAs per SM
+    float a[2][kRChunk][kTileCols];    // A chain rows       32 KB
+    float c[2][kRChunk][kTileRows];    // coeff*B            32 KB
+    uint8_t w8[kTileRows][kTileCols];  // FP8 base tile, 16-byte chunks swizzled by (row >> 2) & 7  16 KB
+};   // 80 KB: two CTAs per SM (registers allow two)
 
 struct ChainMap {
     int n;                      // deltas
     int start[LTX_MAX_DELTAS];  // first chain index of each delta
 };
 
-__global__ void merge_prepass_kernel(MergeParams p, ChainMap cm, int ktot, float *a32, float2 *ct, int64_t cols_p,
+// One chain step k per grid row (blockIdx.y): x < cols_p writes A's row,
+// the next rows_p x write coeff*B's column.
+__global__ void merge_prepass_kernel(MergeParams p, ChainMap cm, float *a32, float *c32, int64_t cols_p,
                                      int64_t rows_p) {
-    const int64_t na = (int64_t)ktot * cols_p, nc = (int64_t)ktot * rows_p;
+    const int k = blockIdx.y;
+    int d = 0;
+#pragma unroll
+    for (int i = 1; i < LTX_MAX_DELTAS; ++i) d += (i < cm.n && k >= cm.start[i]);
+    const DeltaDev dl = p.d[d];
+    const int r = k - cm.start[d];
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nc; i += stride) {
-        const bool is_a = i < na;
-        const int64_t j = is_a ? i : i - na;
-        const int k = (int)(j / (is_a ? cols_p : rows_p));
-        const int64_t x = j % (is_a ? cols_p : rows_p);
-        int d = 0;
-        while (d + 1 < cm.n && k >= cm.start[d + 1]) ++d;
-        const DeltaDev &dl = p.d[d];
-        const int r = k - cm.start[d];
-        if (is_a) {
-            a32[j] = x < p.cols ? load_as_f32(dl.a, dl.a_dt, (int64_t)r * p.cols + x) : 0.f;
+    for (int64_t x = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; x < cols_p + rows_p; x += stride) {
+        if (x < cols_p) {
+            a32[(int64_t)k * cols_p + x] = x < p.cols ? load_as_f32(dl.a, dl.a_dt, (int64_t)r * p.cols + x) : 0.f;
         } else {
+            const int64_t o = x - cols_p;
             // store.rs:786: coeff = self.scale * b_value (one f32 rounding)
-            const float c = x < p.rows ? __fmul_rn(dl.coeff, load_as_f32(dl.b, dl.b_dt, x * dl.rank + r)) : 0.f;
-            ct[j] = make_float2(c, c);
+            c32[(int64_t)k * rows_p + o] = o < p.rows ? __fmul_rn(dl.coeff, load_as_f32(dl.b, dl.b_dt, o * dl.rank + r)) : 0.f;
         }
     }
 }
@@ -170,80 +200,85 @@ __device__ __forceinline__ float base_t(const MergeParams &p, int64_t idx) {
     return p.fp8_scaled ? __fmaf_rn(p.scale, v, 0.0f) : v;
 }
 
-template <int WDT, bool OUT_BF16>
-__global__ void __launch_bounds__(kWarps * 32, 2)
-    dequant_merge_kernel(MergeParams p, const float *__restrict__ a32, const float2 *__restrict__ ct, int ktot,
-                         int64_t cols_p, int64_t rows_p, int base_vec) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    MergeSmem &s = *reinterpret_cast<MergeSmem *>(smem_raw);
-
+// One 128 x 128 tile at (row0, col0).  FULL: the common case, specialised
+// without the ragged paths — an FP8 base staged whole (base_vec), a chain of
+// whole 32-step chunks, every row and column inside the tensor, a 16-byte
+// aligned output.
+template <int WDT, bool OUT_BF16, bool FULL>
+__device__ __forceinline__ void merge_tile(const MergeParams &p, MergeSmem &s, const float *__restrict__ a32,
+                                           const float *__restrict__ c32, int ktot, int64_t cols_p, int64_t rows_p,
+                                           int base_vec, int64_t row0, int64_t col0) {
+    constexpr int TCW = kTileCols;
+    constexpr int NCG = 2;   // 16-column groups per lane
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t row0 = (int64_t)blockIdx.y * kTileRows;
-    const int64_t col0 = (int64_t)blockIdx.x * kTileCols;
+    const int wr = warp >> 2, wc = warp & 3, lr = lane >> 2, lc = lane & 3;
+    const int trow = wr * 64 + 4 * lr;         // + 32j + e
+    const int tcol = wc * 32 + 4 * lc;   // + 16k + e
     const int nchunks = (ktot + kRChunk - 1) / kRChunk;
 
     auto issue = [&](int chunk, int buf) {
         const int k0 = chunk * kRChunk;
-        // A: kRChunk rows x 256 floats = 2048 16-byte pieces; C: kRChunk x 128 = 1024 pieces.
-        for (int q = threadIdx.x; q < kRChunk * kTileCols / 4; q += blockDim.x) {
-            const int r = q / (kTileCols / 4), c4 = q % (kTileCols / 4);
-            const int k = min(k0 + r, ktot - 1);   // rows past the chain end are never read
+        for (int q = threadIdx.x; q < kRChunk * TCW / 4; q += blockDim.x) {
+            const int r = q / (TCW / 4), c4 = q % (TCW / 4);
+            const int k = FULL ? k0 + r : min(k0 + r, ktot - 1);   // rows past the chain end are never read
             cp_async16(&s.a[buf][r][c4 * 4], a32 + (int64_t)k * cols_p + col0 + c4 * 4);
         }
-        for (int q = threadIdx.x; q < kRChunk * kTileRows / 2; q += blockDim.x) {
-            const int r = q / (kTileRows / 2), c2 = q % (kTileRows / 2);
-            const int k = min(k0 + r, ktot - 1);
-            cp_async16(&s.c[buf][r][c2 * 2], ct + (int64_t)k * rows_p + row0 + c2 * 2);
+        for (int q = threadIdx.x; q < kRChunk * kTileRows / 4; q += blockDim.x) {
+            const int r = q / (kTileRows / 4), c4 = q % (kTileRows / 4);
+            const int k = FULL ? k0 + r : min(k0 + r, ktot - 1);
+            cp_async16(&s.c[buf][r][c4 * 4], c32 + (int64_t)k * rows_p + row0 + c4 * 4);
         }
     };
     // Group 0: the FP8 base tile (full, aligned tiles only) and chain chunk 0.
-    if (base_vec) {
-        for (int q = threadIdx.x; q < kTileRows * kTileCols / 16; q += blockDim.x) {
-            const int rr = q / (kTileCols / 16), c16 = q % (kTileCols / 16);
-            cp_async16(&s.w8[rr][c16 * 16],
+    if (FULL || base_vec) {
+        for (int q = threadIdx.x; q < kTileRows * TCW / 16; q += blockDim.x) {
+            const int rr = q / (TCW / 16), c16 = q % (TCW / 16);
+            cp_async16(&s.w8[rr][(c16 ^ ((rr >> 2) & 7)) * 16],
                        static_cast<const uint8_t *>(p.w) + (row0 + rr) * p.cols + col0 + c16 * 16);
         }
     }
     issue(0, 0);
     cp_async_commit();
 
-    float2 acc[kRowsPerWarp][2];
-    const int64_t mycol = col0 + lane * 4;
-    if (base_vec) {
+    float acc[8][4 * NCG];   // [row 4j + e][column 4k + e']
+    if (FULL || base_vec) {
         // FP8 only: decode the staged base tile.
         cp_async_wait<0>();
         __syncthreads();
 #pragma unroll
-        for (int i = 0; i < kRowsPerWarp; ++i) {
-            const int rr = warp * kRowsPerWarp + i;
-            const uint32_t w4 = *reinterpret_cast<const uint32_t *>(&s.w8[rr][lane * 4]);
-            float x[4];
+        for (int i = 0; i < 8; ++i) {
+            const int rr = trow + 32 * (i >> 2) + (i & 3);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const uint32_t b = (w4 >> (8 * e)) & 0xFFu;
-                x[e] = WDT == LTX_F8_E4M3 ? dec_e4m3(b) : dec_e5m2(b);
-                if (p.fp8_scaled) x[e] = __fmaf_rn(p.scale, x[e], 0.0f);
+            for (int k = 0; k < NCG; ++k) {
+                const int cc = tcol + 16 * k;
+                const uint32_t w4 =
+                    *reinterpret_cast<const uint32_t *>(&s.w8[rr][(((cc >> 4) ^ ((rr >> 2) & 7)) << 4) | (cc & 15)]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t b = (w4 >> (8 * e)) & 0xFFu;
+                    float x = WDT == LTX_F8_E4M3 ? dec_e4m3(b) : dec_e5m2(b);
+                    if (p.fp8_scaled) x = __fmaf_rn(p.scale, x, 0.0f);
+                    acc[i][4 * k + e] = x;
+                }
             }
-            acc[i][0] = make_float2(x[0], x[1]);
-            acc[i][1] = make_float2(x[2], x[3]);
         }
-    } else
+    } else if constexpr (!FULL) {
 #pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
-        const int64_t r = row0 + warp * kRowsPerWarp + i;
-        float x[4] = {0.f, 0.f, 0.f, 0.f};
-        if (r < p.rows) {
+        for (int i = 0; i < 8; ++i) {
+            const int64_t r = row0 + trow + 32 * (i >> 2) + (i & 3);
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-                if (mycol + e < p.cols) x[e] = base_t<WDT>(p, r * p.cols + mycol + e);
+            for (int k = 0; k < NCG; ++k) {
+                const int64_t c = col0 + tcol + 16 * k;
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    acc[i][4 * k + e] = (r < p.rows && c + e < p.cols) ? base_t<WDT>(p, r * p.cols + c + e) : 0.f;
+            }
         }
-        acc[i][0] = make_float2(x[0], x[1]);
-        acc[i][1] = make_float2(x[2], x[3]);
     }
 
     for (int ch = 0; ch < nchunks; ++ch) {
         const int buf = ch & 1;
-        if (!base_vec) {
+        if (!FULL && !base_vec) {
             if (ch + 1 < nchunks) {
                 issue(ch + 1, buf ^ 1);
                 cp_async_commit();
@@ -258,55 +293,74 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
         // landed and every thread has finished chunk ch-1, so the other buffer
         // can be refilled with chunk ch+1 under this chunk's FMAs.
         __syncthreads();
-        if (base_vec && ch + 1 < nchunks) {
+        if ((FULL || base_vec) && ch + 1 < nchunks) {
             issue(ch + 1, buf ^ 1);
             cp_async_commit();
         }
-        const int nr = min(kRChunk, ktot - ch * kRChunk);
+        const int nr = FULL ? kRChunk : min(kRChunk, ktot - ch * kRChunk);
+        // Chain step r for this thread's 8 x 4*NCG elements: v = fma(c_row, a_col, v).
         auto step = [&](int r) {
-            const float4 a4 = *reinterpret_cast<const float4 *>(&s.a[buf][r][lane * 4]);
-            const float2 a01 = make_float2(a4.x, a4.y), a23 = make_float2(a4.z, a4.w);
+            float av[4 * NCG], cv[8];
 #pragma unroll
-            for (int q = 0; q < kRowsPerWarp / 2; ++q) {
-                const float4 cc = *reinterpret_cast<const float4 *>(&s.c[buf][r][warp * kRowsPerWarp + 2 * q]);
-                const float2 c0 = make_float2(cc.x, cc.y), c1 = make_float2(cc.z, cc.w);
-                acc[2 * q][0] = __ffma2_rn(c0, a01, acc[2 * q][0]);
-                acc[2 * q][1] = __ffma2_rn(c0, a23, acc[2 * q][1]);
-                acc[2 * q + 1][0] = __ffma2_rn(c1, a01, acc[2 * q + 1][0]);
-                acc[2 * q + 1][1] = __ffma2_rn(c1, a23, acc[2 * q + 1][1]);
+            for (int k = 0; k < NCG; ++k) {
+                const float4 a4 = *reinterpret_cast<const float4 *>(&s.a[buf][r][tcol + 16 * k]);
+                av[4 * k] = a4.x, av[4 * k + 1] = a4.y, av[4 * k + 2] = a4.z, av[4 * k + 3] = a4.w;
             }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const float4 c4 = *reinterpret_cast<const float4 *>(&s.c[buf][r][trow + 32 * j]);
+                cv[4 * j] = c4.x, cv[4 * j + 1] = c4.y, cv[4 * j + 2] = c4.z, cv[4 * j + 3] = c4.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int q = 0; q < 4 * NCG; ++q) acc[i][q] = __fmaf_rn(cv[i], av[q], acc[i][q]);
         };
         if (nr == kRChunk) {
-#pragma unroll 4
+#pragma unroll 2
             for (int r = 0; r < kRChunk; ++r) step(r);
         } else {
             for (int r = 0; r < nr; ++r) step(r);
         }
-        if (!base_vec) __syncthreads();   // buffer `buf` is refilled at the top of the next chunk
+        if (!FULL && !base_vec) __syncthreads();   // buffer `buf` is refilled at the top of the next chunk
     }
 
 #pragma unroll
-    for (int i = 0; i < kRowsPerWarp; ++i) {
-        const int64_t r = row0 + warp * kRowsPerWarp + i;
-        if (r >= p.rows) continue;
-        const int64_t base = r * p.cols + mycol;
-        const float2 v0 = acc[i][0], v1 = acc[i][1];
-        if (p.dst_aligned16 && mycol + 4 <= p.cols && (base & 3) == 0) {
-            if constexpr (OUT_BF16) {
-                __nv_bfloat162 h0 = __floats2bfloat162_rn(v0.x, v0.y), h1 = __floats2bfloat162_rn(v1.x, v1.y);
-                __stcs(reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(p.dst) + base),
-                       make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1)));
-            } else {
-                __stcs(reinterpret_cast<float4 *>(static_cast<float *>(p.dst) + base),
-                       make_float4(v0.x, v0.y, v1.x, v1.y));
-            }
-        } else {
-            const float vv[4] = {v0.x, v0.y, v1.x, v1.y};
+    for (int i = 0; i < 8; ++i) {
+        const int64_t r = row0 + trow + 32 * (i >> 2) + (i & 3);
+        if (!FULL && r >= p.rows) continue;
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-                if (mycol + e < p.cols) store_out(p, base + e, vv[e]);
+        for (int k = 0; k < NCG; ++k) {
+            const int64_t c = col0 + tcol + 16 * k;
+            const int64_t base = r * p.cols + c;
+            const float *v = &acc[i][4 * k];
+            if (FULL || (p.dst_aligned16 && c + 4 <= p.cols && (base & 3) == 0)) {
+                if constexpr (OUT_BF16) {
+                    __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
+                    __stcs(reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(p.dst) + base),
+                           make_uint2(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1)));
+                } else {
+                    __stcs(reinterpret_cast<float4 *>(static_cast<float *>(p.dst) + base),
+                           make_float4(v[0], v[1], v[2], v[3]));
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (c + e < p.cols) store_out(p, base + e, v[e]);
+            }
         }
     }
+}
+
+template <int WDT, bool OUT_BF16, bool FULL>
+__global__ void __launch_bounds__(kWarps * 32, 2)
+    dequant_merge_kernel(MergeParams p, const float *__restrict__ a32, const float *__restrict__ c32, int ktot,
+                         int64_t cols_p, int64_t rows_p, int base_vec, int tiles_x) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    MergeSmem &s = *reinterpret_cast<MergeSmem *>(smem_raw);
+    const int t = blockIdx.x;
+    merge_tile<WDT, OUT_BF16, FULL>(p, s, a32, c32, ktot, cols_p, rows_p, base_vec, (int64_t)(t / tiles_x) * kTileRows,
+                                    (int64_t)(t % tiles_x) * kTileCols);
 }
 
 // Bytes of chain scratch the delta path needs for this call (0 without deltas).
@@ -316,7 +370,7 @@ size_t merge_scratch_bytes(const MergeParams &p) {
     for (int d = 0; d < p.n_deltas; ++d) ktot += p.d[d].rank;
     const int64_t cols_p = (p.cols + kTileCols - 1) / kTileCols * kTileCols;
     const int64_t rows_p = (p.rows + kTileRows - 1) / kTileRows * kTileRows;
-    return (size_t)(ktot * (cols_p + 2 * rows_p)) * sizeof(float);
+    return (size_t)(ktot * (cols_p + rows_p)) * sizeof(float);
 }
 
 template <int WDT>
@@ -330,7 +384,7 @@ cudaError_t launch_merge(const MergeParams &p, cudaStream_t st, int sms, void *s
             dequant_only_scalar_kernel<<<sms * 4, 256, 0, st>>>(p, n);
             return cudaGetLastError();
         }
-        const int64_t work = n / 16 + 1;
+        const int64_t work = (n / 16 + kDqUnroll - 1) / kDqUnroll + 1;   // threads for one unrolled round
         const int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sms * 8);
         if (p.dst_bf16)
             dequant_only_kernel<WDT, true><<<grid, 256, 0, st>>>(p, n);
@@ -338,7 +392,7 @@ cudaError_t launch_merge(const MergeParams &p, cudaStream_t st, int sms, void *s
             dequant_only_kernel<WDT, false><<<grid, 256, 0, st>>>(p, n);
         return cudaGetLastError();
     }
-    // Chain scratch: a32[ktot][cols_p] + ct[ktot][rows_p], f32, zero padded.
+    // Chain scratch: a32[ktot][cols_p] + c32[ktot][rows_p], f32, zero padded.
     ChainMap cm{};
     cm.n = p.n_deltas;
     int ktot = 0;
@@ -349,26 +403,29 @@ cudaError_t launch_merge(const MergeParams &p, cudaStream_t st, int sms, void *s
     const int64_t cols_p = (p.cols + kTileCols - 1) / kTileCols * kTileCols;
     const int64_t rows_p = (p.rows + kTileRows - 1) / kTileRows * kTileRows;
     float *a32 = static_cast<float *>(scratch);
-    float2 *ctp = reinterpret_cast<float2 *>(a32 + (int64_t)ktot * cols_p);
+    float *c32 = a32 + (int64_t)ktot * cols_p;
     const int base_vec = (WDT == LTX_F8_E4M3 || WDT == LTX_F8_E5M2) && p.cols % kTileCols == 0 &&
                          p.rows % kTileRows == 0 && (uintptr_t)p.w % 16 == 0;
+    if (ktot > 65535) return cudaErrorInvalidConfiguration;   // one grid row per chain step
     {
-        const int64_t work = (int64_t)ktot * (cols_p + rows_p);
-        const int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sms * 16);
-        merge_prepass_kernel<<<grid, 256, 0, st>>>(p, cm, ktot, a32, ctp, cols_p, rows_p);
+        const int64_t gx = std::min<int64_t>((cols_p + rows_p + 255) / 256, std::max<int64_t>(1, 8 * sms / ktot));
+        merge_prepass_kernel<<<dim3((unsigned)gx, (unsigned)ktot), 256, 0, st>>>(p, cm, a32, c32, cols_p, rows_p);
     }
-    dim3 grid((unsigned)(cols_p / kTileCols), (unsigned)(rows_p / kTileRows));
-    if (p.dst_bf16) {
-        auto k = dequant_merge_kernel<WDT, true>;
+    const int64_t tiles_x = cols_p / kTileCols, ntiles = tiles_x * (rows_p / kTileRows);
+    if (ntiles > INT32_MAX) return cudaErrorInvalidConfiguration;
+    const bool full = base_vec && ktot % kRChunk == 0 && p.dst_aligned16;
+    auto launch = [&](auto k) -> cudaError_t {
         cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        k<<<grid, kWarps * 32, smem, st>>>(p, a32, ctp, ktot, cols_p, rows_p, base_vec);
-    } else {
-        auto k = dequant_merge_kernel<WDT, false>;
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        k<<<grid, kWarps * 32, smem, st>>>(p, a32, ctp, ktot, cols_p, rows_p, base_vec);
-    }
+        k<<<(unsigned)ntiles, kWarps * 32, smem, st>>>(p, a32, c32, ktot, cols_p, rows_p, base_vec, (int)tiles_x);
+        return cudaSuccess;
+    };
+    cudaError_t e;
+    if (p.dst_bf16)
+        e = full ? launch(dequant_merge_kernel<WDT, true, true>) : launch(dequant_merge_kernel<WDT, true, false>);
+    else
+        e = full ? launch(dequant_merge_kernel<WDT, false, true>) : launch(dequant_merge_kernel<WDT, false, false>);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
@@ -459,9 +516,9 @@ extern "C" int ltx_dequant_merge(ltx_ctx *ctx, const void *w_dev, int32_t w_dtyp
 //
 //   * Size: kNoAllocScratchBytes (16 MiB) on every GPU that loads this
 //     library, held until the process exits.  A call needs
-//       4 * (sum of ranks) * (round_up(in, 128) + 2 * round_up(out, 128)) bytes;
+//       4 * (sum of ranks) * (round_up(in, 128) + round_up(out, 128)) bytes;
 //     rank 64 fits every weight of the 22B DiT (the largest, the 24576 x 4096
-//     adaLN projection, needs 13.6 MB).  Larger calls are rejected with
+//     adaLN projection, needs 7.3 MB).  Larger calls are rejected with
 //     LTX_ERR_UNSUPPORTED before anything is enqueued.
 //   * Sharing: every call on a device uses the same array.  The kernels write
 //     every scratch element they later read, so nothing has to start at zero,
@@ -553,7 +610,7 @@ extern "C" int ltx_dequant_merge_noalloc(void *stream, const void *w_dev, int32_
     if (need > kNoAllocScratchBytes) {
         set_err(errbuf, errbuf_len,
                 "dequant_merge_noalloc: this merge needs %zu bytes of scratch; the allocation-free entry point has "
-                "%zu (4 * total rank * (round_up(in,128) + 2*round_up(out,128)))",
+                "%zu (4 * total rank * (round_up(in,128) + round_up(out,128)))",
                 need, kNoAllocScratchBytes);
         return LTX_ERR_UNSUPPORTED;
     }

@@ -2,7 +2,7 @@
 
     python ltx-rust_b200/ltx_b200/kernel_bench.py attention --B 1 --H 8 --T 4096 [--Tk N] [--iters 3]
     python ltx-rust_b200/ltx_b200/kernel_bench.py gemm --M 4096 --N 4096 --K 4096 [--epi 0..3] [--fp8]
-    python ltx-rust_b200/ltx_b200/kernel_bench.py merge --rows 4096 --cols 4096 --rank 64
+    python ltx-rust_b200/ltx_b200/kernel_bench.py merge --rows 4096 --cols 4096 --rank 64 [--sets 8]
 
 Used for small, self-contained profiler captures of a single kernel and for
 quick shape sweeps; prints one line per run.
@@ -43,6 +43,7 @@ def main():
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--cols", type=int, default=4096)
     ap.add_argument("--rank", type=int, default=64)
+    ap.add_argument("--sets", type=int, default=1, help="merge: distinct weight sets used in turn")
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--iters", type=int, default=3)
     a = ap.parse_args()
@@ -74,13 +75,20 @@ def main():
         flops = 2.0 * a.M * a.N * a.K
         unit = "TFLOP/s"
     else:
-        wq = torch.randint(0, 126, (a.rows * a.cols,), dtype=torch.uint8, device="cuda")
-        A = (torch.randn(a.rank, a.cols, device="cuda", generator=g) * 0.01).to(torch.bfloat16)
-        B = (torch.randn(a.rows, a.rank, device="cuda", generator=g) * 0.01).to(torch.bfloat16)
-        o = torch.empty(a.rows * a.cols, device="cuda", dtype=torch.bfloat16)
-        d = [(A.data_ptr(), B.data_ptr(), a.rank, ltx_b200.LTX_BF16, ltx_b200.LTX_BF16, 1.0)]
-        fn = lambda: ctx.dequant_merge(wq.data_ptr(), ltx_b200.LTX_F8_E4M3, True, 0.01, a.rows, a.cols, d,
-                                       o.data_ptr(), ltx_b200.LTX_BF16)
+        # --sets distinct weight/output pairs merged in turn (more than L2 together: no reuse between
+        # launches); --rank 0 = no LoRA (the dequant-only kernel)
+        wqs = [torch.randint(0, 126, (a.rows * a.cols,), dtype=torch.uint8, device="cuda") for _ in range(a.sets)]
+        A = (torch.randn(max(a.rank, 1), a.cols, device="cuda", generator=g) * 0.01).to(torch.bfloat16)
+        B = (torch.randn(a.rows, max(a.rank, 1), device="cuda", generator=g) * 0.01).to(torch.bfloat16)
+        os_ = [torch.empty(a.rows * a.cols, device="cuda", dtype=torch.bfloat16) for _ in range(a.sets)]
+        d = [(A.data_ptr(), B.data_ptr(), a.rank, ltx_b200.LTX_BF16, ltx_b200.LTX_BF16, 1.0)] if a.rank else []
+        turn = [0]
+
+        def fn():
+            i = turn[0] % a.sets
+            turn[0] += 1
+            ctx.dequant_merge(wqs[i].data_ptr(), ltx_b200.LTX_F8_E4M3, True, 0.01, a.rows, a.cols, d,
+                              os_[i].data_ptr(), ltx_b200.LTX_BF16)
         flops = a.rows * a.cols * (1 + 2) + 2 * a.rank * (a.rows + a.cols)   # algorithmic bytes
         unit = "GB/s"
     for _ in range(a.warmup):

@@ -9,7 +9,7 @@ exactly what ltx_dequant_merge gives (bit-exact: both run the same kernels),
 on calls in a row so that the shared scratch is reused: a config-1 merge, a
 ragged f32 merge with two stacked deltas, a merge with no LoRA at all, and
 the largest 22B DiT weight (the 24576 x 4096 adaLN projection with a rank-64
-LoRA, 13.6 MB of its 16 MiB scratch).  They also check that the device's free
+LoRA, 7.3 MB of its 16 MiB scratch).  They also check that the device's free
 memory does not change across a call once the library is loaded, and that a
 merge too large for the array is refused with a clear error.
 
@@ -84,7 +84,7 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls():
 
 def test_noalloc_rejects_merges_beyond_its_scratch():
     import ltx_b200
-    # 4 * 64 * (16384 + 2 * 65536) bytes of chain scratch > 16 MiB: refused before anything is enqueued,
+    # 4 * 64 * (16384 + 65536) bytes of chain scratch > 16 MiB: refused before anything is enqueued,
     # so small placeholder buffers are enough.
     buf = torch.zeros(64, dtype=torch.uint8, device="cuda")
     d = [(buf.data_ptr(), buf.data_ptr(), 64, ltx_b200.LTX_BF16, ltx_b200.LTX_BF16, 1.0)]
