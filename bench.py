@@ -844,10 +844,11 @@ def launches_per_step(L, tp=False):
     tables, RoPE table, context convert.  Per block 15: 3 norm+modulate, QKV /
     out / cross-q / cross-kv / out / FFN-in / FFN-out GEMMs, fused Q/K
     norm+RoPE, cross q and k norms, 2 attentions.  Split over ranks, per block
-    22: the Q/K norms become 3 sum-of-squares and 4 apply launches, and each of
-    the 3 row-split projections adds a residual add (NCCL's own kernels are
-    not counted).  Output head 2, sampler 2."""
-    return 9 + L * (22 if tp else 15) + 2 + 2
+    40: the Q/K norms become 3 sum-of-squares and 4 apply launches, and each of
+    the 3 row-split projections runs as 4 token slabs of a GEMM plus a
+    residual add (NCCL's own kernels are not counted).  Output head 2, sampler
+    2."""
+    return 9 + L * (40 if tp else 15) + 2 + 2
 
 
 def cpu_model():

@@ -61,34 +61,64 @@ const char *nccl_str(ncclResult_t r) { return nccl().get_error_string ? nccl().g
 
 }  // namespace
 
+int comm_after(ltx_ctx *ctx) {
+    if (!ctx->comm_stream) return LTX_OK;
+    LTX_CUDA_TRY(ctx, cudaEventRecord(ctx->comm_ev[0], ctx->stream));
+    LTX_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->comm_stream, ctx->comm_ev[0], 0));
+    return LTX_OK;
+}
+
+int comm_join(ltx_ctx *ctx) {
+    if (!ctx->comm_stream) return LTX_OK;
+    LTX_CUDA_TRY(ctx, cudaEventRecord(ctx->comm_ev[1], ctx->comm_stream));
+    LTX_CUDA_TRY(ctx, cudaStreamWaitEvent(ctx->stream, ctx->comm_ev[1], 0));
+    return LTX_OK;
+}
+
+static int allreduce_on_comm(ltx_ctx *ctx, void *buf, size_t count, ncclDataType_t dt, const char *what) {
+    if (ctx->tp_size <= 1 || count == 0) return LTX_OK;
+    ncclResult_t r = nccl().all_reduce(buf, buf, count, dt, ncclSum, static_cast<ncclComm_t>(ctx->comm),
+                                       ctx->comm_stream ? ctx->comm_stream : ctx->stream);
+    if (r != ncclSuccess) return fail(ctx, LTX_ERR_NCCL, "allreduce of %zu %s: %s", count, what, nccl_str(r));
+    return LTX_OK;
+}
+
+int allreduce_sum_bf16_async(ltx_ctx *ctx, void *buf, size_t count) {
+    return allreduce_on_comm(ctx, buf, count, ncclBfloat16, "bf16");
+}
+
 int allreduce_sum(ltx_ctx *ctx, float *buf, size_t count) {
     if (ctx->tp_size <= 1 || count == 0) return LTX_OK;
-    const NcclApi &api = nccl();
-    ncclResult_t r = api.all_reduce(buf, buf, count, ncclFloat32, ncclSum, static_cast<ncclComm_t>(ctx->comm),
-                                    ctx->stream);
-    if (r != ncclSuccess) return fail(ctx, LTX_ERR_NCCL, "allreduce of %zu floats: %s", count, nccl_str(r));
-    return LTX_OK;
+    if (int rc = comm_after(ctx)) return rc;
+    if (int rc = allreduce_on_comm(ctx, buf, count, ncclFloat32, "floats")) return rc;
+    return comm_join(ctx);
 }
 
 int allreduce_sum_bf16(ltx_ctx *ctx, void *buf, size_t count) {
     if (ctx->tp_size <= 1 || count == 0) return LTX_OK;
-    const NcclApi &api = nccl();
-    ncclResult_t r = api.all_reduce(buf, buf, count, ncclBfloat16, ncclSum, static_cast<ncclComm_t>(ctx->comm),
-                                    ctx->stream);
-    if (r != ncclSuccess) return fail(ctx, LTX_ERR_NCCL, "allreduce of %zu bf16: %s", count, nccl_str(r));
-    return LTX_OK;
+    if (int rc = comm_after(ctx)) return rc;
+    if (int rc = allreduce_on_comm(ctx, buf, count, ncclBfloat16, "bf16")) return rc;
+    return comm_join(ctx);
 }
 
 void comm_release(ltx_ctx *ctx, bool abort) {
     if (!ctx->comm) return;
     const NcclApi &api = nccl();
-    if (abort)
+    if (abort) {
         api.comm_abort(static_cast<ncclComm_t>(ctx->comm));
-    else
+    } else {
+        if (ctx->comm_stream) cudaStreamSynchronize(ctx->comm_stream);
         api.comm_destroy(static_cast<ncclComm_t>(ctx->comm));
+    }
     ctx->comm = nullptr;
     ctx->tp_size = 1;
     ctx->tp_rank = 0;
+    // Neither call blocks: resources of work still in flight (an aborted
+    // collective's kernels) are released once it completes.
+    if (ctx->comm_stream) cudaStreamDestroy(ctx->comm_stream);
+    ctx->comm_stream = nullptr;
+    for (cudaEvent_t &e : ctx->comm_ev)
+        if (e) cudaEventDestroy(e), e = nullptr;
 }
 
 }  // namespace ltx
@@ -122,6 +152,14 @@ extern "C" int ltx_ctx_init_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, in
     ctx->comm = comm;
     ctx->tp_size = nranks;
     ctx->tp_rank = rank;
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);   // hi: the greatest priority (numerically lowest)
+    if (cudaStreamCreateWithPriority(&ctx->comm_stream, cudaStreamNonBlocking, hi) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->comm_ev[0], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->comm_ev[1], cudaEventDisableTiming) != cudaSuccess) {
+        ltx::comm_release(ctx, false);
+        return ltx::fail(ctx, LTX_ERR_CUDA, "ltx_ctx_init_comm: cannot create the communicator's stream");
+    }
     return LTX_OK;
 }
 

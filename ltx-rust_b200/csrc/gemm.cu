@@ -575,12 +575,13 @@ int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, 
         p.resid_tma = 1;
     }
     cudaError_t e;
+    const int sms = ctx->gemm_sms > 0 ? std::min(ctx->gemm_sms, ctx->sm_count) : ctx->sm_count;
     if (es == 1)
-        e = BN == 128 ? dispatch_epi<128, true>(epi, ta, tb, ta2, tb2, tx, p, ctx->sm_count, st)
-                      : dispatch_epi<256, true>(epi, ta, tb, ta2, tb2, tx, p, ctx->sm_count, st);
+        e = BN == 128 ? dispatch_epi<128, true>(epi, ta, tb, ta2, tb2, tx, p, sms, st)
+                      : dispatch_epi<256, true>(epi, ta, tb, ta2, tb2, tx, p, sms, st);
     else
-        e = BN == 128 ? dispatch_epi<128, false>(epi, ta, tb, ta2, tb2, tx, p, ctx->sm_count, st)
-                      : dispatch_epi<256, false>(epi, ta, tb, ta2, tb2, tx, p, ctx->sm_count, st);
+        e = BN == 128 ? dispatch_epi<128, false>(epi, ta, tb, ta2, tb2, tx, p, sms, st)
+                      : dispatch_epi<256, false>(epi, ta, tb, ta2, tb2, tx, p, sms, st);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm launch");
     return LTX_OK;
 }

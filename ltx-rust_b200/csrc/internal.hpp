@@ -34,6 +34,13 @@ struct ltx_ctx {
     // Tensor-parallel communicator (an ncclComm_t), or null: one GPU.
     void *comm = nullptr;
     int tp_size = 1, tp_rank = 0;
+    // Every collective of the communicator runs on comm_stream (one issue
+    // order for NCCL), ordered against the context's stream by events.
+    cudaStream_t comm_stream = nullptr;
+    cudaEvent_t comm_ev[2] = {nullptr, nullptr};   // [0]: stream -> comm, [1]: comm -> stream
+    // CTAs of the persistent GEMMs (0 = one per SM).  Lowered while
+    // collectives run beside them, so NCCL's kernels find free SMs.
+    int gemm_sms = 0;
 };
 
 namespace ltx {
@@ -60,10 +67,18 @@ int ensure_scratch(ltx_ctx *ctx, size_t bytes);
 // buffer (waits for the previous upload from that buffer to finish first).
 int upload(ltx_ctx *ctx, void *dst_dev, const void *src_host, size_t bytes);
 
-// Sum-allreduce of `count` floats in place over the context's communicator,
-// on its stream (a no-op without one).
+// Sum-allreduce of `count` floats in place over the context's communicator
+// (a no-op without one), ordered after the work enqueued so far on the
+// context's stream and before any work enqueued on it later.
 int allreduce_sum(ltx_ctx *ctx, float *buf, size_t count);
 int allreduce_sum_bf16(ltx_ctx *ctx, void *buf, size_t count);
+// The pieces of that ordering, for callers that overlap a collective with
+// compute: comm_after makes the comm stream wait for the context stream's
+// work so far; allreduce_sum_bf16_async enqueues on the comm stream only;
+// comm_join makes the context stream wait for the comm stream's work so far.
+int comm_after(ltx_ctx *ctx);
+int allreduce_sum_bf16_async(ltx_ctx *ctx, void *buf, size_t count);
+int comm_join(ltx_ctx *ctx);
 // Destroys (or aborts) the context's communicator.
 void comm_release(ltx_ctx *ctx, bool abort);
 

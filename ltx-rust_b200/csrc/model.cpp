@@ -910,19 +910,34 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         return LTX_OK;
     };
     // x += (A . W^T + bias) * gate: fused into the GEMM epilogue on one GPU;
-    // split over ranks, the partial products are summed first.
+    // split over ranks, the partial products are summed first.  The rows go
+    // in kSlabs token slabs: slab i's sum-allreduce and residual add run on
+    // the communicator's stream while the GEMM computes slab i+1 on SMs left
+    // free for the collective; the context stream joins after the last slab.
     auto project_residual = [&](const __nv_bfloat16 *a, int64_t lda, const __nv_bfloat16 *wt, int64_t kdim,
                                 const float *bias, const float *gate) -> int {
         const int *gidx = gate ? w.idx : nullptr;
         if (tp == 1)
             return gemm_bf16(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, LTX_EPI_RESID, bias, w.x, D, gate,
                              gidx, K * D);
-        // the partial products travel as bf16: half the bytes of the allreduce
-        TRY(gemm_bf16(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, LTX_EPI_BF16, nullptr, w.part, D,
-                      nullptr, nullptr, 0));
-        TRY(allreduce_sum_bf16(ctx, w.part, (size_t)rows * D));
-        CU(tp_resid_add(st, sms, w.x, w.part, (int)rows, (int)D, bias, gate, gidx, K * D));
-        return LTX_OK;
+        constexpr int kSlabs = 4, kCommSms = 16;
+        const int64_t slab = rows >= 16 * 128 ? (rows + kSlabs * 128 - 1) / (kSlabs * 128) * 128 : rows;
+        struct GemmSmsGuard {   // restores the GEMM grid on every exit
+            ltx_ctx *c;
+            ~GemmSmsGuard() { c->gemm_sms = 0; }
+        } guard{ctx};
+        if (slab < rows) ctx->gemm_sms = ctx->sm_count - kCommSms;
+        for (int64_t r0 = 0; r0 < rows; r0 += slab) {
+            const int m = (int)std::min<int64_t>(slab, rows - r0);
+            // the partial products travel as bf16: half the bytes of the allreduce
+            TRY(gemm_bf16(ctx, st, a + r0 * lda, lda, wt, kdim, m, (int)D, (int)kdim, LTX_EPI_BF16, nullptr,
+                          w.part + r0 * D, D, nullptr, nullptr, 0));
+            TRY(comm_after(ctx));
+            TRY(allreduce_sum_bf16_async(ctx, w.part + r0 * D, (size_t)m * D));
+            CU(tp_resid_add(ctx->comm_stream ? ctx->comm_stream : st, sms, w.x + r0 * D, w.part + r0 * D, m, (int)D,
+                            bias, gate, gidx ? gidx + r0 : nullptr, K * D));
+        }
+        return comm_join(ctx);
     };
     // RMSNorm(gamma) over the full inner dimension of `nseg` projections that
     // each hold Dl columns per row here (+ RoPE with the tables when given)

@@ -66,6 +66,8 @@ def _leaver(rank, ws, port, q, step1_done):
         q.put(("no error", time.time() - t0))
     except Exception as e:                   # noqa: BLE001 - any error is the detection
         q.put((type(e).__name__, time.time() - t0))
+    q.close()
+    q.join_thread()                          # the result is in the pipe before the process ends
     os._exit(0)
 
 
