@@ -324,7 +324,44 @@ int ltx_model_forward(ltx_model *model, ltx_ctx *ctx, const float *latent_dev, c
                       const float *positions_dev, const float *context_dev, int32_t batch, int32_t tokens,
                       int32_t context_tokens, float *out_dev);
 
+/* TransformerBlock::forward (crates/ltx-dit/src/block.rs:118-126, the
+ * self-attention / cross-attention / feed-forward body :127-153) for block
+ * `block_index` of the model, on the block's own inputs, with context_mask
+ * and self_attn_mask None (as alpha_gen calls it):
+ *   x_dev        f32 [batch*tokens, D], the residual stream, updated in place
+ *   context_dev  f32 [batch*context_tokens, cross_attention_dim]
+ *   timestep_dev f32 [batch*tokens, K*D], the per-token modulation the
+ *                block's ada_values reads (K = 6, or 9 with cross-attention
+ *                adaLN; AdaLayerNormSingle's output, model.rs:196-206)
+ *   pe_cos_dev / pe_sin_dev  the RoPE tables as precompute_freqs_cis returns
+ *                them (rope.rs:118-167): split, f32 (batch, heads, tokens,
+ *                head_dim/2); interleaved, f32 (batch, 1, tokens, D).
+ * For a caller that drives the blocks itself (its own loop, offload or
+ * inspection).  A model loaded with "offload_blocks" > 0 returns
+ * LTX_ERR_UNSUPPORTED here. */
+int ltx_block_forward(ltx_model *model, ltx_ctx *ctx, int32_t block_index, float *x_dev, const float *context_dev,
+                      const float *timestep_dev, const float *pe_cos_dev, const float *pe_sin_dev, int32_t batch,
+                      int32_t tokens, int32_t context_tokens);
+
 /* ── ltx-sampler: one guided Euler step ────────────────────────────────────── */
+
+/* The sampler's update on x0 predictions from any denoiser (a
+ * VideoDenoiserModel that is not this DiT, crates/ltx-sampler/src/model.rs:
+ * 21-51), on the device:
+ *   pred = x0_c + (cfg-1)(x0_c - x0_u), rescaled by
+ *          rescale*std(x0_c)/std(pred) + (1-rescale)     (guidance.rs:149-165,
+ *          std over all tokens*channels values, tensor3_std :178-195)
+ *   x0' = pred*m + clean*(1-m); latent += ((latent - x0')/sigma)(sigma_next - sigma)
+ *                                                        (loop_.rs:37-65)
+ * cond_x0_dev / uncond_x0_dev / clean_dev / latent_dev f32 [tokens, channels],
+ * mask_dev f32 [tokens]; latent_dev is updated in place.  cfg_scale == 1
+ * uses the conditional prediction alone (uncond_x0_dev may be NULL).
+ * Errors: LTX_ERR_SIGMA (sigma not finite or <= 0, sigma_next not finite or
+ * < 0, loop_.rs:126-137), LTX_ERR_NEGATIVE_CONTEXT (cfg_scale != 1 without
+ * an unconditional prediction). */
+int ltx_cfg_euler_step(ltx_ctx *ctx, const float *cond_x0_dev, const float *uncond_x0_dev, float *latent_dev,
+                       const float *clean_dev, const float *mask_dev, int32_t tokens, int32_t channels, float sigma,
+                       float sigma_next, float cfg_scale, float rescale_scale);
 
 /* One iteration of euler_denoising_loop (loop_.rs:93-149) around the DiT:
  *   t = mask * sigma per token (guidance.rs:114)

@@ -297,7 +297,8 @@ __global__ void attn_generic_kernel(const __nv_bfloat16 *q, int64_t ldq, const _
 
 // ── K6: CFG + rescale + post-process + Euler (guidance.rs:149-165, loop_.rs:37-65) ──
 //
-// x0_c = x - t*v_c, x0_u = x - t*v_u  (velocity -> x0 per token, t = mask*sigma)
+// x0_c = x - t*v_c, x0_u = x - t*v_u  (velocity -> x0 per token, t = mask*sigma;
+//                                      tok_t = null: v_c, v_u are x0 predictions)
 // pred = x0_c + (g-1)(x0_c - x0_u);  factor = r*std(x0_c)/std(pred) + (1-r)
 // x0   = pred*factor;  x0' = x0*m + clean*(1-m);  x += ((x - x0')/sigma)*(sigma_next - sigma)
 // Stats: per-block f64 partial sums (sum, sumsq) of x0_c and pred in a fixed
@@ -311,9 +312,15 @@ __global__ void cfg_stats_kernel(const float *x, const float *vc, const float *v
     double s[4] = {0, 0, 0, 0};
     const int64_t n = (int64_t)T * C;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const float t = tok_t[i / C];
-        const float xc = x[i] - t * vc[i];
-        const float xu = x[i] - t * vu[i];
+        float xc, xu;
+        if (tok_t) {
+            const float t = tok_t[i / C];
+            xc = x[i] - t * vc[i];
+            xu = x[i] - t * vu[i];
+        } else {   // the inputs are x0 predictions already
+            xc = vc[i];
+            xu = vu[i];
+        }
         const float pr = xc + (g - 1.0f) * (xc - xu);
         s[0] += xc;
         s[1] += (double)xc * xc;
@@ -359,18 +366,56 @@ __global__ void cfg_euler_apply_kernel(float *x, const float *vc, const float *v
     const int64_t n = (int64_t)T * C;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t tok = i / C;
-        const float t = tok_t[tok];
         const float xi = x[i];
-        const float xc = xi - t * vc[i];
-        float x0 = xc;
-        if (use_cfg) {
-            const float xu = xi - t * vu[i];
-            x0 = (xc + (g - 1.0f) * (xc - xu)) * factor;
+        float x0;
+        if (tok_t) {
+            const float t = tok_t[tok];
+            const float xc = xi - t * vc[i];
+            x0 = xc;
+            if (use_cfg) {
+                const float xu = xi - t * vu[i];
+                x0 = (xc + (g - 1.0f) * (xc - xu)) * factor;
+            }
+        } else {   // the inputs are x0 predictions already
+            const float xc = vc[i];
+            x0 = xc;
+            if (use_cfg) {
+                const float xu = vu[i];
+                x0 = (xc + (g - 1.0f) * (xc - xu)) * factor;
+            }
         }
         const float m = mask[tok];
         const float x0a = x0 * m + clean[i] * (1.0f - m);
         const float vel = (xi - x0a) / sigma;
         x[i] = xi + vel * dt;
+    }
+}
+
+// ── the block seam: TransformerBlock::forward's own inputs ────────────────────
+//
+// tab[row][k][d] = sst[k][d] + mod[row][k*D + d] (ada_values, block.rs:164-198,
+// per token) and idx[row] = row, so the norm and GEMM-epilogue kernels read
+// per-token modulation the way they read the per-timestep tables.
+__global__ void seam_tables_kernel(const float *sst, const float *mod, int64_t rows, int KD, float *tab, int *idx) {
+    const int64_t n = rows * KD;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        tab[i] = sst[i % KD] + mod[i];
+        if (i % KD == 0) idx[i / KD] = (int)(i / KD);
+    }
+}
+
+// Split RoPE tables from the reference's layout (B, H, T, dh) (split_freqs_cis,
+// rope.rs:118-167) to one row per token: out[(b*T + t)*H*dh + h*dh + i].
+__global__ void pe_rows_kernel(const float *cin, const float *sin_, int B, int H, int T, int dh, float *cout,
+                               float *sout) {
+    const int64_t n = (int64_t)B * H * T * dh;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int e = (int)(i % dh);
+        const int64_t r = i / dh;
+        const int t = (int)(r % T), h = (int)((r / T) % H), b = (int)(r / ((int64_t)T * H));
+        const int64_t o = ((int64_t)b * T + t) * H * dh + (int64_t)h * dh + e;
+        cout[o] = cin[i];
+        sout[o] = sin_[i];
     }
 }
 
@@ -682,6 +727,18 @@ cudaError_t attention_generic(cudaStream_t st, const __nv_bfloat16 *q, int64_t l
 }
 
 size_t cfg_scratch_bytes() { return (size_t)kStatBlocks * 4 * sizeof(double); }
+
+cudaError_t seam_tables(cudaStream_t st, int sms, const float *sst, const float *mod, int64_t rows, int KD, float *tab,
+                        int *idx) {
+    seam_tables_kernel<<<grid_for(rows * KD, sms), 256, 0, st>>>(sst, mod, rows, KD, tab, idx);
+    return cudaGetLastError();
+}
+
+cudaError_t pe_rows(cudaStream_t st, int sms, const float *cin, const float *sin_, int B, int H, int T, int dh,
+                    float *cout, float *sout) {
+    pe_rows_kernel<<<grid_for((int64_t)B * H * T * dh, sms), 256, 0, st>>>(cin, sin_, B, H, T, dh, cout, sout);
+    return cudaGetLastError();
+}
 
 cudaError_t cfg_euler(cudaStream_t st, int sms, float *x, const float *vc, const float *vu, const float *tok_t,
                       const float *mask, const float *clean, int T, int C, float g, float rescale, bool use_cfg,

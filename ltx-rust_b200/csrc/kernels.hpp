@@ -65,6 +65,12 @@ bool qk_norm_rope_fused(cudaStream_t st, __nv_bfloat16 *q, __nv_bfloat16 *k, int
                         cudaError_t *err);
 cudaError_t permute_ct(cudaStream_t st, int sms, const float *in, float *out, int B, int C, int64_t T, bool to_tokens);
 size_t cfg_scratch_bytes();
+// Per-token modulation tables tab[row][k][d] = sst[k][d] + mod[row][k*D+d], idx[row] = row (KD = K*D).
+cudaError_t seam_tables(cudaStream_t st, int sms, const float *sst, const float *mod, int64_t rows, int KD, float *tab,
+                        int *idx);
+// Split RoPE (B, H, T, dh) tables -> one row of H*dh values per token.
+cudaError_t pe_rows(cudaStream_t st, int sms, const float *cin, const float *sin_, int B, int H, int T, int dh,
+                    float *cout, float *sout);
 cudaError_t cfg_euler(cudaStream_t st, int sms, float *x, const float *vc, const float *vu, const float *tok_t,
                       const float *mask, const float *clean, int T, int C, float g, float rescale, bool use_cfg,
                       double *partial, float sigma, float sigma_next);

@@ -836,13 +836,27 @@ static int unique_timesteps(const std::vector<float> &ts, std::vector<float> &un
     return (int)uniq.size();
 }
 
+// One block run on TransformerBlock::forward's own inputs (block.rs:118-126)
+// instead of the whole model: the residual x in place, the per-token
+// modulation `timestep` [rows, K*D] and the RoPE tables in the reference's
+// layout (split: cos, sin (B, H, T, d/2); interleaved: (B, 1, T, D)).
+struct BlockSeam {
+    int index;
+    float *x;
+    const float *mod;
+    const float *pe_cos, *pe_sin;
+};
+
 // The full forward on device buffers.  `ts_host` are the per-token timesteps
 // (B*T, host copy) used to build the distinct-timestep index.
 // pos_shared: every batch row has the same positions (the CFG halves of a
 // denoise step), so the RoPE tables are built for T rows instead of B*T.
+// seam: run only block seam->index on the caller's block inputs (no patch
+// embedding, adaLN, RoPE table build or output head).
 static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const std::vector<float> &ts_host,
                         const float *positions, const float *context, int B, int T, int S, float *out,
-                        const Work *given = nullptr, Work *work_out = nullptr, bool pos_shared = false) {
+                        const Work *given = nullptr, Work *work_out = nullptr, bool pos_shared = false,
+                        const BlockSeam *seam = nullptr) {
     const DitConfig &c = m->cfg;
     if (ctx->tp_size != m->tp || ctx->tp_rank != m->tr)
         return fail(ctx, LTX_ERR_INVALID_ARG, "model shard %d of %d run on a context of rank %d of %d", m->tr, m->tp,
@@ -853,9 +867,16 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
     const int sms = ctx->sm_count;
     std::vector<float> uniq;
     std::vector<int> idx;
-    const int U = unique_timesteps(ts_host, uniq, idx);
+    const int U = seam ? 1 : unique_timesteps(ts_host, uniq, idx);
     Work w;
-    if (given) {
+    float *seam_tab = nullptr;   // seam: per-token tables [rows][K][D]
+    if (seam) {
+        const size_t wb = carve_work(nullptr, c, rows, crow, 1, 1, m->tp, m->lora_r64).bytes;
+        TRY(ensure_work(ctx, wb + (size_t)rows * K * D * sizeof(float) + 256));
+        w = carve_work(static_cast<char *>(ctx->work), c, rows, crow, 1, 1, m->tp, m->lora_r64);
+        seam_tab = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(ctx->work) + wb + 255) & ~uintptr_t(255));
+        w.x = seam->x;
+    } else if (given) {
         w = *given;
     } else {
         Work sizing = carve_work(nullptr, c, rows, crow, U, c.layers, m->tp, m->lora_r64);
@@ -863,7 +884,7 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         w = carve_work(static_cast<char *>(ctx->work), c, rows, crow, U, c.layers, m->tp, m->lora_r64);
     }
     if (work_out) *work_out = w;
-    {
+    if (!seam) {
         // one pinned upload: distinct timesteps then the per-token index
         std::vector<char> blob((size_t)U * 4 + (size_t)rows * 4);
         memcpy(blob.data(), uniq.data(), (size_t)U * 4);
@@ -875,26 +896,37 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
                            cudaMemcpyDeviceToDevice, st));
     }
 
-    // patch embedding (model.rs:187): f32 latent -> bf16 -> tensor-core GEMM, f32 out
-    CU(f32_to_bf16(st, sms, latent, rows * c.in_ch, w.latb));
-    TRY(gemm_bf16(ctx, st, w.latb, c.in_ch, m->patch_w, c.in_ch, (int)rows, (int)D, c.in_ch, LTX_EPI_F32, m->patch_b,
-                  w.x, D, nullptr, nullptr, 0));
-    // adaLN-single on the distinct timesteps (adaln.rs:130-142), f32 throughout
-    CU(sinusoid(st, w.ts_u, U, (float)c.ts_mult, m->sin_freq, w.sinus));
-    CU(small_linear(st, w.sinus, U, 256, m->t1_w, m->t1_b, (int)D, false, w.h1));
-    CU(small_linear(st, w.h1, U, (int)D, m->t2_w, m->t2_b, (int)D, true, w.emb));
-    CU(small_linear(st, w.emb, U, (int)D, m->lin_w, m->lin_b, (int)(K * D), true, w.mod));
-    CU(ada_tables(st, sms, m->sst_list, c.layers, (int)K, w.mod, m->sst_out, w.emb, U, (int)D, w.tab, w.otab));
-    // RoPE tables (rope.rs:46-167)
-    const float mp[3] = {(float)c.max_pos[0], (float)c.max_pos[1], (float)c.max_pos[2]};
     const int width = c.interleaved ? (int)D : (int)(D / 2);
-    // Built once per forward, read by every block's Q/K norm.  The fused Q/K
-    // kernel (D 4096, head dim 128, split RoPE, one GPU) indexes the table by
-    // row % tab_rows, so rows that share positions share table rows.
+    // The fused Q/K kernel (D 4096, head dim 128, split RoPE, one GPU) indexes
+    // the RoPE table by row % tab_rows, so rows that share positions share
+    // table rows.
     const bool fused_qk = m->tp == 1 && D == 4096 && d == 128 && !c.interleaved;
-    const int tab_b = fused_qk && pos_shared ? 1 : B;
-    CU(rope_table(st, sms, positions, tab_b, T, m->rope_freq, m->rope_grid, mp, c.use_mid, c.interleaved, width, w.cos,
-                  w.sin));
+    const int tab_b = fused_qk && pos_shared && !seam ? 1 : B;
+    if (!seam) {
+        // patch embedding (model.rs:187): f32 latent -> bf16 -> tensor-core GEMM, f32 out
+        CU(f32_to_bf16(st, sms, latent, rows * c.in_ch, w.latb));
+        TRY(gemm_bf16(ctx, st, w.latb, c.in_ch, m->patch_w, c.in_ch, (int)rows, (int)D, c.in_ch, LTX_EPI_F32,
+                      m->patch_b, w.x, D, nullptr, nullptr, 0));
+        // adaLN-single on the distinct timesteps (adaln.rs:130-142), f32 throughout
+        CU(sinusoid(st, w.ts_u, U, (float)c.ts_mult, m->sin_freq, w.sinus));
+        CU(small_linear(st, w.sinus, U, 256, m->t1_w, m->t1_b, (int)D, false, w.h1));
+        CU(small_linear(st, w.h1, U, (int)D, m->t2_w, m->t2_b, (int)D, true, w.emb));
+        CU(small_linear(st, w.emb, U, (int)D, m->lin_w, m->lin_b, (int)(K * D), true, w.mod));
+        CU(ada_tables(st, sms, m->sst_list, c.layers, (int)K, w.mod, m->sst_out, w.emb, U, (int)D, w.tab, w.otab));
+        // RoPE tables (rope.rs:46-167), built once per forward, read by every block's Q/K norm
+        const float mp[3] = {(float)c.max_pos[0], (float)c.max_pos[1], (float)c.max_pos[2]};
+        CU(rope_table(st, sms, positions, tab_b, T, m->rope_freq, m->rope_grid, mp, c.use_mid, c.interleaved, width,
+                      w.cos, w.sin));
+    } else {
+        // the caller's per-token modulation plus this block's table (ada_values)
+        CU(seam_tables(st, sms, m->blocks[seam->index].sst, seam->mod, rows, (int)(K * D), seam_tab, w.idx));
+        if (c.interleaved) {
+            CU(cudaMemcpyAsync(w.cos, seam->pe_cos, (size_t)rows * D * 4, cudaMemcpyDeviceToDevice, st));
+            CU(cudaMemcpyAsync(w.sin, seam->pe_sin, (size_t)rows * D * 4, cudaMemcpyDeviceToDevice, st));
+        } else {
+            CU(pe_rows(st, sms, seam->pe_cos, seam->pe_sin, B, (int)H, T, (int)(d / 2), w.cos, w.sin));
+        }
+    }
     if (!c.cross_adaln) CU(f32_to_bf16(st, sms, context, crow * Dc, w.ctxb));
 
     // Tensor-parallel split: this rank runs heads [tr*Hl, (tr+1)*Hl) and FFN
@@ -1012,7 +1044,7 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         CU(cudaEventRecord(m->copied[slot], m->copy_stream));
         return LTX_OK;
     };
-    for (int l = 0; n_off && l < std::min(n_off, c.layers); ++l) TRY(prefetch(l));
+    for (int l = 0; n_off && !seam && l < std::min(n_off, c.layers); ++l) TRY(prefetch(l));
     // one block: x updated in place on the compute stream
     auto block_body = [&](const BlockW &b, const float *tab) -> int {
         if (c.fp8_attn && c.fp8_ffn) {
@@ -1086,6 +1118,7 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         TRY(project_residual(w.ffh, Fl, b.ff2, Fl, b.ff2_b, tab + 5 * D));
         return LTX_OK;
     };
+    if (seam) return block_body(m->blocks[seam->index], seam_tab);
     for (int l = 0; l < c.layers; ++l) {
         BlockW bv = m->blocks[l];
         if (n_off) {
@@ -1178,6 +1211,48 @@ extern "C" int ltx_model_forward(ltx_model *m, ltx_ctx *ctx, const float *latent
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "reading timesteps");
     return forward_impl(m, ctx, latent_dev, ts, positions_dev, context_dev, batch, tokens, context_tokens, out_dev);
+}
+
+extern "C" int ltx_block_forward(ltx_model *m, ltx_ctx *ctx, int32_t block_index, float *x_dev,
+                                 const float *context_dev, const float *timestep_dev, const float *pe_cos_dev,
+                                 const float *pe_sin_dev, int32_t batch, int32_t tokens, int32_t context_tokens) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    if (!m || !x_dev || !context_dev || !timestep_dev || !pe_cos_dev || !pe_sin_dev)
+        return fail(ctx, LTX_ERR_INVALID_ARG, "ltx_block_forward: null argument");
+    if (block_index < 0 || block_index >= m->cfg.layers)
+        return fail(ctx, LTX_ERR_INVALID_ARG, "ltx_block_forward: block %d of %d", block_index, m->cfg.layers);
+    if (batch <= 0 || tokens <= 0 || context_tokens <= 0)
+        return fail(ctx, LTX_ERR_SHAPE, "ltx_block_forward: empty batch/tokens/context");
+    if (m->offload_n)
+        return fail(ctx, LTX_ERR_UNSUPPORTED, "ltx_block_forward: the model keeps its blocks in host memory "
+                                              "(offload_blocks); run it through ltx_model_forward");
+    const BlockSeam seam{block_index, x_dev, timestep_dev, pe_cos_dev, pe_sin_dev};
+    return forward_impl(m, ctx, nullptr, {}, nullptr, context_dev, batch, tokens, context_tokens, nullptr, nullptr,
+                        nullptr, false, &seam);
+}
+
+// GuidedDenoiser::apply's combine (guidance.rs:149-165) + post_process and
+// euler_step (loop_.rs:37-65) on x0 predictions from any denoiser.
+extern "C" int ltx_cfg_euler_step(ltx_ctx *ctx, const float *cond_x0_dev, const float *uncond_x0_dev,
+                                  float *latent_dev, const float *clean_dev, const float *mask_dev, int32_t tokens,
+                                  int32_t channels, float sigma, float sigma_next, float cfg_scale,
+                                  float rescale_scale) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    if (!cond_x0_dev || !latent_dev || !clean_dev || !mask_dev)
+        return fail(ctx, LTX_ERR_INVALID_ARG, "ltx_cfg_euler_step: null argument");
+    if (tokens < 0 || channels <= 0) return fail(ctx, LTX_ERR_SHAPE, "ltx_cfg_euler_step: bad shape");
+    if (!std::isfinite(sigma) || sigma <= 0.f) return fail(ctx, LTX_ERR_SIGMA, "invalid sigma %g", (double)sigma);
+    if (!std::isfinite(sigma_next) || sigma_next < 0.f)
+        return fail(ctx, LTX_ERR_SIGMA, "invalid next sigma %g", (double)sigma_next);
+    const bool use_cfg = std::fabs(cfg_scale - 1.0f) > 1e-5f;   // needs_uncond (guidance.rs:58-60)
+    if (use_cfg && !uncond_x0_dev)
+        return fail(ctx, LTX_ERR_NEGATIVE_CONTEXT, "cfg_scale != 1 needs the unconditional prediction");
+    if (tokens == 0) return LTX_OK;
+    TRY(ensure_scratch(ctx, cfg_scratch_bytes()));
+    CU(cfg_euler(ctx->stream, ctx->sm_count, latent_dev, cond_x0_dev, use_cfg ? uncond_x0_dev : cond_x0_dev, nullptr,
+                 mask_dev, clean_dev, tokens, channels, cfg_scale, rescale_scale, use_cfg,
+                 static_cast<double *>(ctx->scratch), sigma, sigma_next));
+    return LTX_OK;
 }
 
 namespace ltx {

@@ -92,6 +92,9 @@ def lib() -> ctypes.CDLL:
         "ltx_model_destroy": (None, [V]),
         "ltx_model_weight_bytes": (I64, [V]),
         "ltx_model_forward": (I, [V, V, P, P, P, P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, P]),
+        "ltx_block_forward": (I, [V, V, ctypes.c_int32, P, P, P, P, P, ctypes.c_int32, ctypes.c_int32,
+                                  ctypes.c_int32]),
+        "ltx_cfg_euler_step": (I, [V, P, P, P, P, P, ctypes.c_int32, ctypes.c_int32, F, F, F, F]),
         "ltx_denoise_step": (I, [V, V, P, P, P, P, P, P, P, ctypes.c_int32, ctypes.c_int32, F, F, F, F]),
         "ltx_denoise_loop": (I, [V, V, P, P, P, P, P, P, P, ctypes.c_int32, ctypes.c_int32, P, ctypes.c_int32, F, F,
                                  ctypes.c_int32, P]),
@@ -330,6 +333,15 @@ class VideoTransformer:
         self.ctx.check(lib().ltx_model_forward(self.h, self.ctx.h, _ptr(latent), _ptr(timesteps), _ptr(positions),
                                                _ptr(context), B, T, S, _ptr(out)), "ltx_model_forward")
 
+    def block_forward(self, index, x, context, timestep, pe_cos, pe_sin):
+        """TransformerBlock::forward of block `index` in place on x [B,T,D] (ltx_block_forward):
+        context [B,S,Dc], timestep [B,T,K*D] (per-token modulation), pe_cos/pe_sin as
+        precompute_freqs_cis returns them (split: [B,H,T,d/2]), all f32 CUDA."""
+        B, T, _ = x.shape
+        S = context.shape[1]
+        self.ctx.check(lib().ltx_block_forward(self.h, self.ctx.h, index, _ptr(x), _ptr(context), _ptr(timestep),
+                                               _ptr(pe_cos), _ptr(pe_sin), B, T, S), "ltx_block_forward")
+
     def denoise_step(self, latent, clean, mask, positions, ctx_cond, ctx_uncond, sigma, sigma_next, cfg_scale=1.0,
                      rescale_scale=0.7, mask_host=None):
         """One guided Euler step in place on latent [T, C] (ltx_denoise_step)."""
@@ -367,6 +379,15 @@ class VideoTransformer:
             self.close()
         except Exception:
             pass
+
+
+def cfg_euler_step(ctx: "Context", cond_x0, uncond_x0, latent, clean, mask, sigma, sigma_next, cfg_scale=1.0,
+                   rescale_scale=0.7):
+    """CFG + rescale + post_process + Euler in place on latent [T, C] from x0 predictions
+    (ltx_cfg_euler_step); uncond_x0 may be None when cfg_scale is 1."""
+    T, C = latent.shape
+    ctx.check(lib().ltx_cfg_euler_step(ctx.h, _ptr(cond_x0), _ptr(uncond_x0), _ptr(latent), _ptr(clean), _ptr(mask),
+                                       T, C, sigma, sigma_next, cfg_scale, rescale_scale), "ltx_cfg_euler_step")
 
 
 def apply_noise(ctx: "Context", latent, noise, clean, mask, noise_scale):
