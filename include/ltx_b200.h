@@ -312,14 +312,19 @@ int ltx_model_load(ltx_ctx *ctx, ltx_store *store, const char *config_json, ltx_
  * tiny random-init fixtures). */
 int ltx_model_init_random(ltx_ctx *ctx, const char *config_json, uint64_t seed, int32_t lora_rank,
                           float lora_strength, ltx_model **out);
+/* Frees the model.  Work that uses it on the callers' streams must have
+ * finished (ltx_ctx_synchronize on each context that ran it). */
 void ltx_model_destroy(ltx_model *model);
 /* Device bytes held by the model's weights. */
 int64_t ltx_model_weight_bytes(const ltx_model *model);
 /* VideoTransformer::forward (model.rs:169-255) with context_mask and
  * self_attn_mask None (as alpha_gen calls it): latent [B,T,in], timesteps
  * [B,T], positions [B,3,T,2], context [B,S,cross_dim] -> out [B,T,out], all
- * f32 device buffers.  Synchronises once to read the timesteps (the adaLN
- * path runs on the distinct values only). */
+ * f32 device buffers.  No host round trip: the adaLN path runs once per
+ * distinct timestep value, deduplicated on the device into at most 8 tables;
+ * a forward with more distinct values is reported as LTX_ERR_UNSUPPORTED by
+ * the next ltx_ctx_synchronize (ltx_denoise_step with mask_host has no such
+ * limit). */
 int ltx_model_forward(ltx_model *model, ltx_ctx *ctx, const float *latent_dev, const float *timesteps_dev,
                       const float *positions_dev, const float *context_dev, int32_t batch, int32_t tokens,
                       int32_t context_tokens, float *out_dev);
@@ -373,9 +378,12 @@ int ltx_cfg_euler_step(ltx_ctx *ctx, const float *cond_x0_dev, const float *unco
  *          rescale*std(x0_c)/std(pred) + (1-rescale)  (guidance.rs:149-165)
  *   x0' = x0*m + clean*(1-m); latent += ((latent - x0')/sigma)(sigma_next - sigma)
  *                                                      (loop_.rs:37-65)
- * latent_dev [T, C] is updated in place.  mask_host (optional, T floats)
- * avoids a device read of mask_dev.  LTX_ERR_SIGMA / LTX_ERR_NEGATIVE_CONTEXT
- * as SamplerError::InvalidSigma / MissingNegativeContext. */
+ * latent_dev [T, C] is updated in place.  mask_host (optional, T floats, the
+ * same values as mask_dev) lets the host size the adaLN tables exactly;
+ * without it the timesteps are formed and deduplicated on the device (no host
+ * round trip; at most 8 distinct mask values, see ltx_model_forward).
+ * LTX_ERR_SIGMA / LTX_ERR_NEGATIVE_CONTEXT as SamplerError::InvalidSigma /
+ * MissingNegativeContext. */
 int ltx_denoise_step(ltx_model *model, ltx_ctx *ctx, float *latent_dev, const float *clean_dev,
                      const float *mask_host, const float *mask_dev, const float *positions_dev,
                      const float *ctx_cond_dev, const float *ctx_uncond_dev, int32_t tokens,

@@ -4,6 +4,7 @@
 #include <new>
 
 #include "internal.hpp"
+#include "kernels.hpp"
 
 namespace ltx {
 
@@ -98,6 +99,10 @@ extern "C" int ltx_ctx_synchronize(ltx_ctx *ctx) {
     if (e != cudaSuccess) return ltx::cuda_fail(ctx, e, "reading the timeout flag");
     if (flag) {
         cudaMemset(ctx->timeout_flag, 0, sizeof(int));
+        if (flag == ltx::kErrTooManyTimesteps)
+            return ltx::fail(ctx, LTX_ERR_UNSUPPORTED,
+                             "a forward had more than %d distinct timesteps on the device (pass them from the host: "
+                             "ltx_denoise_step's mask_host)", ltx::kMaxDistinctTs);
         return ltx::fail(ctx, LTX_ERR_TIMEOUT, "a device-side wait gave up (code %d)", flag);
     }
     return LTX_OK;

@@ -391,6 +391,61 @@ __global__ void cfg_euler_apply_kernel(float *x, const float *vc, const float *v
     }
 }
 
+// ── distinct timesteps on the device ────────────────────────────────────────
+//
+// The adaLN path runs once per distinct timestep value (model.rs:196-206 runs
+// it per token, with the same result).  One CTA collects the distinct f32 bit
+// patterns of ts[rows] (up to umax), sorts them by bit pattern so the table
+// order is deterministic, writes them to ts_u (padded with 0) and each row's
+// index to idx.  More than umax distinct values: `flag` gets `code`.
+__global__ void __launch_bounds__(1024) timestep_set_kernel(const float *ts, int64_t rows, int umax, float *ts_u,
+                                                            int *idx, int *flag, int code) {
+    constexpr uint32_t kEmpty = 0xFFFFFFFFu;   // a NaN pattern: stands for "no value"
+    __shared__ uint32_t vals[kMaxDistinctTs];
+    __shared__ int overflow;
+    for (int k = threadIdx.x; k < kMaxDistinctTs; k += blockDim.x) vals[k] = kEmpty;
+    if (threadIdx.x == 0) overflow = 0;
+    __syncthreads();
+    for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) {
+        const uint32_t b = __float_as_uint(ts[r]);
+        bool placed = false;
+        for (int k = 0; k < umax && !placed; ++k) {
+            uint32_t v = vals[k];
+            if (v == kEmpty) v = atomicCAS(&vals[k], kEmpty, b);
+            placed = v == kEmpty || v == b;
+        }
+        if (!placed) overflow = 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int n = 0;
+        while (n < umax && vals[n] != kEmpty) ++n;
+        for (int i = 1; i < n; ++i)   // insertion sort of at most umax patterns
+            for (int j = i; j > 0 && vals[j - 1] > vals[j]; --j) {
+                const uint32_t t = vals[j];
+                vals[j] = vals[j - 1];
+                vals[j - 1] = t;
+            }
+        for (int k = 0; k < umax; ++k) ts_u[k] = k < n ? __uint_as_float(vals[k]) : 0.0f;
+        if (overflow && flag) atomicExch(flag, code);
+    }
+    __syncthreads();
+    for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) {
+        const uint32_t b = __float_as_uint(ts[r]);
+        int k = 0;
+        while (k + 1 < umax && vals[k] != b) ++k;
+        idx[r] = k;
+    }
+}
+
+// Per-token timesteps of a denoise step, t = mask * sigma (guidance.rs:114),
+// for each of the `halves` batch rows of the CFG batch.
+__global__ void mask_timesteps_kernel(const float *mask, float sigma, int T, int halves, float *ts) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)T * halves;
+         i += (int64_t)gridDim.x * blockDim.x)
+        ts[i] = mask[i % T] * sigma;
+}
+
 // ── the block seam: TransformerBlock::forward's own inputs ────────────────────
 //
 // tab[row][k][d] = sst[k][d] + mod[row][k*D + d] (ada_values, block.rs:164-198,
@@ -727,6 +782,18 @@ cudaError_t attention_generic(cudaStream_t st, const __nv_bfloat16 *q, int64_t l
 }
 
 size_t cfg_scratch_bytes() { return (size_t)kStatBlocks * 4 * sizeof(double); }
+
+cudaError_t timestep_set(cudaStream_t st, const float *ts, int64_t rows, int umax, float *ts_u, int *idx, int *flag,
+                         int code) {
+    if (umax < 1 || umax > kMaxDistinctTs) return cudaErrorInvalidValue;
+    timestep_set_kernel<<<1, 1024, 0, st>>>(ts, rows, umax, ts_u, idx, flag, code);
+    return cudaGetLastError();
+}
+
+cudaError_t mask_timesteps(cudaStream_t st, int sms, const float *mask, float sigma, int T, int halves, float *ts) {
+    mask_timesteps_kernel<<<grid_for((int64_t)T * halves, sms), 256, 0, st>>>(mask, sigma, T, halves, ts);
+    return cudaGetLastError();
+}
 
 cudaError_t seam_tables(cudaStream_t st, int sms, const float *sst, const float *mod, int64_t rows, int KD, float *tab,
                         int *idx) {

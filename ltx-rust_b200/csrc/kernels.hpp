@@ -65,6 +65,15 @@ bool qk_norm_rope_fused(cudaStream_t st, __nv_bfloat16 *q, __nv_bfloat16 *k, int
                         cudaError_t *err);
 cudaError_t permute_ct(cudaStream_t st, int sms, const float *in, float *out, int B, int C, int64_t T, bool to_tokens);
 size_t cfg_scratch_bytes();
+// Distinct per-token timesteps on the device: at most kMaxDistinctTs values,
+// sorted by bit pattern into ts_u[umax] (padded with 0), idx[row] = the row's
+// table; more than umax distinct values set *flag = code.
+constexpr int kMaxDistinctTs = 8;
+constexpr int kErrTooManyTimesteps = 1001;   // device error code: more distinct timesteps than kMaxDistinctTs
+cudaError_t timestep_set(cudaStream_t st, const float *ts, int64_t rows, int umax, float *ts_u, int *idx, int *flag,
+                         int code);
+// ts[h*T + t] = mask[t] * sigma for h < halves.
+cudaError_t mask_timesteps(cudaStream_t st, int sms, const float *mask, float sigma, int T, int halves, float *ts);
 // Per-token modulation tables tab[row][k][d] = sst[k][d] + mod[row][k*D+d], idx[row] = row (KD = K*D).
 cudaError_t seam_tables(cudaStream_t st, int sms, const float *sst, const float *mod, int64_t rows, int KD, float *tab,
                         int *idx);

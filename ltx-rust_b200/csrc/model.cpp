@@ -853,10 +853,12 @@ struct BlockSeam {
 // denoise step), so the RoPE tables are built for T rows instead of B*T.
 // seam: run only block seam->index on the caller's block inputs (no patch
 // embedding, adaLN, RoPE table build or output head).
+// ts_dev: the per-token timesteps on the device instead (ts_host empty): they
+// are deduplicated there into kMaxDistinctTs tables, with no host round trip.
 static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const std::vector<float> &ts_host,
                         const float *positions, const float *context, int B, int T, int S, float *out,
                         const Work *given = nullptr, Work *work_out = nullptr, bool pos_shared = false,
-                        const BlockSeam *seam = nullptr) {
+                        const BlockSeam *seam = nullptr, const float *ts_dev = nullptr) {
     const DitConfig &c = m->cfg;
     if (ctx->tp_size != m->tp || ctx->tp_rank != m->tr)
         return fail(ctx, LTX_ERR_INVALID_ARG, "model shard %d of %d run on a context of rank %d of %d", m->tr, m->tp,
@@ -867,7 +869,7 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
     const int sms = ctx->sm_count;
     std::vector<float> uniq;
     std::vector<int> idx;
-    const int U = seam ? 1 : unique_timesteps(ts_host, uniq, idx);
+    const int U = seam ? 1 : ts_dev ? kMaxDistinctTs : unique_timesteps(ts_host, uniq, idx);
     Work w;
     float *seam_tab = nullptr;   // seam: per-token tables [rows][K][D]
     if (seam) {
@@ -884,7 +886,9 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         w = carve_work(static_cast<char *>(ctx->work), c, rows, crow, U, c.layers, m->tp, m->lora_r64);
     }
     if (work_out) *work_out = w;
-    if (!seam) {
+    if (!seam && ts_dev) {
+        CU(timestep_set(st, ts_dev, rows, U, w.ts_u, w.idx, ctx->timeout_flag, kErrTooManyTimesteps));
+    } else if (!seam) {
         // one pinned upload: distinct timesteps then the per-token index
         std::vector<char> blob((size_t)U * 4 + (size_t)rows * 4);
         memcpy(blob.data(), uniq.data(), (size_t)U * 4);
@@ -1193,7 +1197,9 @@ extern "C" int ltx_model_init_random(ltx_ctx *ctx, const char *config_json, uint
 extern "C" void ltx_model_destroy(ltx_model *m) {
     if (!m) return;
     cudaSetDevice(m->device);
-    cudaDeviceSynchronize();
+    // The model's own copy stream (streamed offload); work on the callers'
+    // streams is theirs to finish first (ltx_ctx_synchronize).
+    if (m->copy_stream) cudaStreamSynchronize(m->copy_stream);
     free_model(m);
 }
 
@@ -1206,11 +1212,8 @@ extern "C" int ltx_model_forward(ltx_model *m, ltx_ctx *ctx, const float *latent
         return ctx ? fail(ctx, LTX_ERR_INVALID_ARG, "ltx_model_forward: null argument") : LTX_ERR_INVALID_ARG;
     if (batch <= 0 || tokens <= 0 || context_tokens <= 0)
         return fail(ctx, LTX_ERR_SHAPE, "ltx_model_forward: empty batch/tokens/context");
-    std::vector<float> ts((size_t)batch * tokens);
-    cudaError_t e = cudaMemcpyAsync(ts.data(), timesteps_dev, ts.size() * 4, cudaMemcpyDeviceToHost, ctx->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "reading timesteps");
-    return forward_impl(m, ctx, latent_dev, ts, positions_dev, context_dev, batch, tokens, context_tokens, out_dev);
+    return forward_impl(m, ctx, latent_dev, {}, positions_dev, context_dev, batch, tokens, context_tokens, out_dev,
+                        nullptr, nullptr, false, nullptr, timesteps_dev);
 }
 
 extern "C" int ltx_block_forward(ltx_model *m, ltx_ctx *ctx, int32_t block_index, float *x_dev,
@@ -1310,13 +1313,18 @@ static int denoise_step_core(ltx_model *m, ltx_ctx *ctx, float *latent_dev, cons
     const bool use_cfg = std::fabs(cfg_scale - 1.0f) > 1e-5f;   // needs_uncond (guidance.rs:58-60)
     const int B = use_cfg ? 2 : 1, C = c.in_ch;
     cudaStream_t st = ctx->stream;
-    // per-token timesteps = mask * sigma (guidance.rs:114), both CFG halves
-    std::vector<float> ts((size_t)B * T);
-    for (int b = 0; b < B; ++b)
-        for (int t = 0; t < T; ++t) ts[(size_t)b * T + t] = mask_host[t] * sigma;
-    std::vector<float> uq;
-    std::vector<int> ix;
-    const int U = unique_timesteps(ts, uq, ix);
+    // per-token timesteps = mask * sigma (guidance.rs:114), both CFG halves:
+    // on the host when the caller has the mask there, else on the device
+    std::vector<float> ts;
+    int U = kMaxDistinctTs;
+    if (mask_host) {
+        ts.resize((size_t)B * T);
+        for (int b = 0; b < B; ++b)
+            for (int t = 0; t < T; ++t) ts[(size_t)b * T + t] = mask_host[t] * sigma;
+        std::vector<float> uq;
+        std::vector<int> ix;
+        U = unique_timesteps(ts, uq, ix);
+    }
     TRY(ensure_work(ctx, step_work_bytes(m, B, T, S, U)));   // grow-only: a no-op inside a loop
     char *base = static_cast<char *>(ctx->work);
     const StepBufs sb = carve_step(base, c, B, T, S);
@@ -1324,9 +1332,14 @@ static int denoise_step_core(ltx_model *m, ltx_ctx *ctx, float *latent_dev, cons
     if (!static_ready) TRY(stage_static(ctx, sb, positions_dev, cc, cu, B, T, S, c.cross_dim));
     for (int b = 0; b < B; ++b)
         CU(cudaMemcpyAsync(sb.lat2 + (int64_t)b * T * C, latent_dev, (size_t)T * C * 4, cudaMemcpyDeviceToDevice, st));
-    TRY(forward_impl(m, ctx, sb.lat2, ts, sb.pos2, sb.ctx2, B, T, S, sb.vel, &w, nullptr, true));
-    // per-token t for the velocity -> x0 adapter: x0 = x - t * v
-    TRY(upload(ctx, w.tok_t, ts.data(), (size_t)T * 4));
+    if (mask_host) {
+        TRY(forward_impl(m, ctx, sb.lat2, ts, sb.pos2, sb.ctx2, B, T, S, sb.vel, &w, nullptr, true));
+        // per-token t for the velocity -> x0 adapter: x0 = x - t * v
+        TRY(upload(ctx, w.tok_t, ts.data(), (size_t)T * 4));
+    } else {
+        CU(mask_timesteps(st, ctx->sm_count, mask_dev, sigma, T, B, w.tok_t));
+        TRY(forward_impl(m, ctx, sb.lat2, {}, sb.pos2, sb.ctx2, B, T, S, sb.vel, &w, nullptr, true, nullptr, w.tok_t));
+    }
     CU(cfg_euler(st, ctx->sm_count, latent_dev, sb.vel, use_cfg ? sb.vel + (int64_t)T * C : sb.vel, w.tok_t, mask_dev,
                  clean_dev, T, C, cfg_scale, rescale_scale, use_cfg, w.partial, sigma, sigma_next));
     return LTX_OK;
@@ -1358,13 +1371,6 @@ extern "C" int ltx_denoise_step(ltx_model *m, ltx_ctx *ctx, float *latent_dev, c
     if (!std::isfinite(sigma) || sigma <= 0.f) return fail(ctx, LTX_ERR_SIGMA, "invalid sigma %g", (double)sigma);
     if (!std::isfinite(sigma_next) || sigma_next < 0.f)
         return fail(ctx, LTX_ERR_SIGMA, "invalid next sigma %g", (double)sigma_next);
-    std::vector<float> mask_copy;
-    if (!mask_host) {
-        mask_copy.resize(tokens);
-        CU(cudaMemcpyAsync(mask_copy.data(), mask_dev, (size_t)tokens * 4, cudaMemcpyDeviceToHost, ctx->stream));
-        CU(cudaStreamSynchronize(ctx->stream));
-        mask_host = mask_copy.data();
-    }
     return denoise_step_core(m, ctx, latent_dev, clean_dev, mask_host, mask_dev, positions_dev, ctx_cond_dev,
                              ctx_uncond_dev, tokens, context_tokens, sigma, sigma_next, cfg_scale, rescale_scale, false);
 }
@@ -1397,21 +1403,19 @@ extern "C" int ltx_denoise_loop(ltx_model *m, ltx_ctx *ctx, float *latent_dev, c
     const DitConfig &c = m->cfg;
     const bool use_cfg = std::fabs(cfg_scale - 1.0f) > 1e-5f;
     const int B = use_cfg ? 2 : 1, T = tokens, S = context_tokens;
-    std::vector<float> mask_copy;
-    if (!mask_host) {
-        mask_copy.resize(T);
-        CU(cudaMemcpyAsync(mask_copy.data(), mask_dev, (size_t)T * 4, cudaMemcpyDeviceToHost, ctx->stream));
-        CU(cudaStreamSynchronize(ctx->stream));
-        mask_host = mask_copy.data();
+    // distinct mask values bound the distinct timesteps of every step (the
+    // device path sizes for kMaxDistinctTs)
+    int U = kMaxDistinctTs;
+    if (mask_host) {
+        std::set<uint32_t> mvals;
+        for (int t = 0; t < T; ++t) {
+            uint32_t bits;
+            memcpy(&bits, &mask_host[t], 4);
+            mvals.insert(bits);
+        }
+        U = (int)mvals.size();
     }
-    // distinct mask values bound the distinct timesteps of every step
-    std::set<uint32_t> mvals;
-    for (int t = 0; t < T; ++t) {
-        uint32_t bits;
-        memcpy(&bits, &mask_host[t], 4);
-        mvals.insert(bits);
-    }
-    TRY(ensure_work(ctx, step_work_bytes(m, B, T, S, (int)mvals.size())));
+    TRY(ensure_work(ctx, step_work_bytes(m, B, T, S, U)));
     const StepBufs sb = carve_step(static_cast<char *>(ctx->work), c, B, T, S);
     TRY(stage_static(ctx, sb, positions_dev, ctx_cond_dev, ctx_uncond_dev, B, T, S, c.cross_dim));
     for (int i = 0; i + 1 < n_sigmas; ++i)

@@ -470,3 +470,52 @@ def test_offload_stream_load_matches_resident(ctx, mid_ckpt):
         model.close()
         st.close()
     assert np.array_equal(got[1].view(np.uint32), got[0].view(np.uint32))
+
+
+def test_device_mask_path_matches_host_mask_path(ctx, mid_ckpt):
+    """Without mask_host the step and the loop take the per-token timesteps from the device
+    mask (deduplicated on the device, no host round trip); the result is bit-identical to
+    the host-mask path, with three distinct mask values (target, keyframe strength 0.6,
+    IC reference)."""
+    import ltx_b200
+    cfg, ck, lo, params = mid_ckpt
+    st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    state, cc, cu, Tt = _loop_state(cfg)
+    mask_h = np.ascontiguousarray(state.denoise_mask[0, :, 0], np.float32)
+    mask_h[: Tt // 4] = 0.4   # a conditioned stretch: strength 0.6
+    sig = [float(x) for x in sampler.scheduler_execute(8, Tt)[:3]]
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+    clean, pos, mask = dev(state.clean_latent[0]), dev(state.positions), dev(mask_h)
+    outs = []
+    for mh in (mask_h, None):
+        lat = dev(state.latent[0])
+        model.denoise_step(lat, clean, mask, pos, dev(cc[0]), dev(cu[0]), sig[0], sig[1], 3.0, 0.7, mask_host=mh)
+        loop_lat = dev(state.latent[0])
+        model.denoise_loop(loop_lat, clean, mask, pos, dev(cc[0]), dev(cu[0]), sig, 3.0, 0.7, mask_host=mh)
+        ctx.synchronize()
+        outs.append((lat.cpu().numpy(), loop_lat.cpu().numpy()))
+    for a, b in zip(outs[0], outs[1]):
+        assert np.isfinite(a).all() and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    model.close()
+    st.close()
+
+
+def test_forward_with_too_many_distinct_timesteps_is_reported(ctx, mid_ckpt):
+    """Device timesteps are deduplicated into at most 8 tables; a forward with more distinct
+    values is reported as UNSUPPORTED by the next synchronize (the host-timestep path of
+    ltx_denoise_step has no such limit)."""
+    import ltx_b200
+    cfg, ck, lo, _ = mid_ckpt
+    st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    lat, ts, pos, ctxt = make_inputs(cfg)
+    ts = (np.arange(ts.size, dtype=np.float32) % 9 / 10.0).reshape(ts.shape)   # 9 distinct values
+    out = torch.empty(lat.shape, dtype=torch.float32, device="cuda")
+    model.forward(*(torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (lat, ts, pos, ctxt)), out)
+    with pytest.raises(ltx_b200.LtxError) as e:
+        ctx.synchronize()
+    assert e.value.kind == "UNSUPPORTED" and "distinct timesteps" in str(e.value)
+    ctx.synchronize()   # the flag is cleared: the context stays usable
+    model.close()
+    st.close()
