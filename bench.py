@@ -412,8 +412,9 @@ class StepRunner:
         self.ctx.synchronize()
         return self.lat.double().cpu()
 
-    def timed(self, steps, warmup, ws, device, clocks=True):
-        """ms per step over `steps` steps after `warmup` (CUDA events on the stream, max over ranks)."""
+    def timed(self, steps, warmup, ws, device, clocks=True, label="denoise_timed"):
+        """ms per step over `steps` steps after `warmup` (CUDA events on the stream, max over ranks).
+        The timed launches sit in an NVTX range named `label` (a profiler can capture just them)."""
         import torch
         for i in range(warmup):
             self.step(i)
@@ -425,7 +426,7 @@ class StepRunner:
         clk = ClockSampler(device) if clocks else None
         if clk:
             clk.__enter__()
-        torch.cuda.nvtx.range_push("denoise_timed")   # lets a profiler capture just these launches
+        torch.cuda.nvtx.range_push(label)
         start.record(stream)
         for i in range(steps):
             self.step(i)
@@ -566,7 +567,7 @@ def run_fp8_step(args, ctx, device, bf16_ref, bf16_ms):
     import ltx_b200
     run = StepRunner(ctx, 7, 100, precision="e4m3_ffn")
     steps = max(3, min(args.steps, 10))
-    ms, clocks = run.timed(steps, 3, 1, device)
+    ms, clocks = run.timed(steps, 3, 1, device, label="denoise_timed_fp8")
     got = run.reference_step()
     lat0 = torch.from_numpy(np.ascontiguousarray(run.lat0, np.float64))
     run.close()
@@ -615,7 +616,7 @@ def run_replicas(args, rank, ws, device):
     ctx = ltx_b200.Context(device)
     run = StepRunner(ctx, 7 + rank, 100 + rank)
     steps = max(3, min(args.steps, 5))
-    ms, clocks = run.timed(steps, 3, ws, device, clocks=False)
+    ms, clocks = run.timed(steps, 3, ws, device, clocks=False, label="denoise_timed_replicas")
     run.close()
     ctx.close()
     return {"value": ws * T_TOTAL / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,

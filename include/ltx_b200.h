@@ -53,7 +53,8 @@ typedef enum {
     LTX_ERR_MISSING_CONFIG = 18,  /* WeightError::MissingConfig                             */
     LTX_ERR_NEGATIVE_CONTEXT = 19, /* SamplerError::MissingNegativeContext                  */
     LTX_ERR_CHUNK_PLAN = 20,      /* ChunkError (crates/ltx-chunk/src/error.rs)             */
-    LTX_ERR_TARGET_TOKENS = 21    /* SamplerError::TargetTokensTooLarge (loop_.rs:162-185)  */
+    LTX_ERR_TARGET_TOKENS = 21,   /* SamplerError::TargetTokensTooLarge (loop_.rs:162-185)  */
+    LTX_ERR_STRENGTH = 22         /* SamplerError::InvalidStrength (conditioning.rs:150-152) */
 } ltx_status;
 
 /* Element types, named after the safetensors dtype strings. */
@@ -415,6 +416,19 @@ int ltx_denoise_loop(ltx_model *model, ltx_ctx *ctx, float *latent_dev, const fl
 int ltx_apply_noise(ltx_ctx *ctx, float *latent_dev, const float *noise_dev, const float *clean_dev,
                     const float *mask_dev, int32_t tokens, int32_t channels, float noise_scale);
 
+/* ImageKeyframeCondition::apply_to (crates/ltx-sampler/src/conditioning.rs:
+ * 127-205) on the device, bit-exact: the tokens of latent frame
+ * `latent_frame_index` (tokens_per_frame tokens from latent_frame_index *
+ * tokens_per_frame) take the keyframe's tokens in clean_dev [tokens, channels]
+ * and 1 - strength in mask_dev [tokens]; every other token keeps its values
+ * (each as the reference's clean*keep + image*frame and mask*keep +
+ * frame*(1-strength), f32).  image_dev is the one-frame latent
+ * [channels, 1, H, W] with H*W = tokens_per_frame, as the reference takes it
+ * (patchified inside).  LTX_ERR_STRENGTH for a strength outside [0, 1] (or
+ * NaN), LTX_ERR_SHAPE when the frame lies beyond the tokens. */
+int ltx_apply_keyframe(ltx_ctx *ctx, float *clean_dev, float *mask_dev, int32_t tokens, int32_t channels,
+                       const float *image_dev, int32_t latent_frame_index, int32_t tokens_per_frame, float strength);
+
 /* LTX2Scheduler::execute (crates/ltx-sampler/src/scheduler.rs:67-125): writes
  * steps + 1 sigmas with the reference's f32 operations (bit-exact).  Defaults
  * of SchedulerConfig: max_shift 2.05, base_shift 0.95, stretch 1, terminal 0.1.
@@ -459,6 +473,12 @@ typedef struct {
  * names the variant.  Host-only. */
 int ltx_chunk_plan(uint32_t total, uint32_t chunk_len, uint32_t overlap, ltx_chunk *chunks_out,
                    int32_t max_chunks, int32_t *n_chunks);
+/* seam_cond_plan (crates/ltx-chunk/src/seam.rs:110-125): the keyframe
+ * conditioning chunk n > 0 takes from chunk n-1's output at the seam: one
+ * frame at chunk-local index 0 with strength 0.95 (DEFAULT_KEYFRAME_STRENGTH),
+ * and overlap - 1 frames left to the blend.  LTX_ERR_CHUNK_PLAN
+ * (ZeroOverlapForSeam) when overlap is 0.  Host-only. */
+int ltx_seam_cond_plan(uint32_t overlap, uint32_t *chunk_local_idx, float *strength, uint32_t *blend_tail_len);
 /* crossfade_weight (crates/ltx-chunk/src/blend.rs:49-56): f32 of the f64
  * smoothstep(offset / overlap_len); 1 when overlap_len is 0.  Host-only. */
 float ltx_crossfade_weight(uint32_t offset, uint32_t overlap_len);

@@ -100,6 +100,20 @@ cudaError_t launch_seam_blend(cudaStream_t st, int sms, const float *outgoing, c
 
 extern "C" float ltx_crossfade_weight(uint32_t offset, uint32_t overlap_len) { return crossfade(offset, overlap_len); }
 
+// seam_cond_plan (crates/ltx-chunk/src/seam.rs:110-125): one keyframe at the
+// seam (chunk-local 0, latent-aligned), strength DEFAULT_KEYFRAME_STRENGTH.
+extern "C" int ltx_seam_cond_plan(uint32_t overlap, uint32_t *chunk_local_idx, float *strength,
+                                  uint32_t *blend_tail_len) {
+    if (!chunk_local_idx || !strength || !blend_tail_len)
+        return ltx::host_fail(LTX_ERR_INVALID_ARG, "ltx_seam_cond_plan: null output");
+    if (overlap == 0)
+        return ltx::host_fail(LTX_ERR_CHUNK_PLAN, "ZeroOverlapForSeam: overlap must be non-zero for a seam conditioning plan");
+    *chunk_local_idx = 0;
+    *strength = 0.95f;   // DEFAULT_KEYFRAME_STRENGTH (seam.rs:60)
+    *blend_tail_len = overlap - 1;
+    return LTX_OK;
+}
+
 extern "C" int ltx_chunk_plan(uint32_t total, uint32_t chunk_len, uint32_t overlap, ltx_chunk *chunks_out,
                               int32_t max_chunks, int32_t *n_chunks) {
     using ltx::host_fail;

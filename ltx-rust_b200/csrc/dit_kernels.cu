@@ -845,6 +845,44 @@ extern "C" int ltx_unpatchify(ltx_ctx *ctx, const float *tokens_dev, int32_t bat
     return e == cudaSuccess ? LTX_OK : ltx::cuda_fail(ctx, e, "ltx_unpatchify");
 }
 
+// ImageKeyframeCondition::apply_to (crates/ltx-sampler/src/conditioning.rs:
+// 127-205): per value, clean*keep + img*frame, and per token mask*keep +
+// frame*(1-strength), each Burn op one f32 rounding (keep = 1 - frame).
+namespace {
+__global__ void apply_keyframe_kernel(float *clean, float *mask, int64_t tokens, int C, const float *image,
+                                      int64_t start, int64_t tpf, float one_minus_s) {
+    const int64_t n = tokens * C;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / C;
+        const int c = (int)(i % C);
+        const bool in = t >= start && t < start + tpf;
+        const float frame = in ? 1.0f : 0.0f, keep = in ? 0.0f : 1.0f;
+        const float img = in ? image[(int64_t)c * tpf + (t - start)] : 0.0f;   // patchify of [C, 1, H, W]
+        clean[i] = __fadd_rn(__fmul_rn(clean[i], keep), __fmul_rn(img, frame));
+        if (c == 0) mask[t] = __fadd_rn(__fmul_rn(mask[t], keep), __fmul_rn(frame, one_minus_s));
+    }
+}
+}  // namespace
+
+extern "C" int ltx_apply_keyframe(ltx_ctx *ctx, float *clean_dev, float *mask_dev, int32_t tokens, int32_t channels,
+                                  const float *image_dev, int32_t latent_frame_index, int32_t tokens_per_frame,
+                                  float strength) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    if (!(strength >= 0.0f && strength <= 1.0f))
+        return ltx::fail(ctx, LTX_ERR_STRENGTH, "InvalidStrength: keyframe strength %g outside [0, 1]", (double)strength);
+    if (!clean_dev || !mask_dev || !image_dev || tokens < 0 || channels <= 0 || latent_frame_index < 0 ||
+        tokens_per_frame <= 0)
+        return ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_apply_keyframe: bad arguments");
+    const int64_t start = (int64_t)latent_frame_index * tokens_per_frame;
+    if (start + tokens_per_frame > tokens)
+        return ltx::fail(ctx, LTX_ERR_SHAPE, "image keyframe index exceeds latent frame count");
+    const int64_t n = (int64_t)tokens * channels;
+    apply_keyframe_kernel<<<ltx::grid_for(n, ctx->sm_count), 256, 0, ctx->stream>>>(
+        clean_dev, mask_dev, tokens, channels, image_dev, start, tokens_per_frame, 1.0f - strength);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? LTX_OK : ltx::cuda_fail(ctx, e, "ltx_apply_keyframe");
+}
+
 // GaussianNoiser::apply_with_noise (crates/ltx-sampler/src/noiser.rs:91-106):
 // lerp(latent, noise, s) then lerp(clean, noised, mask), each Burn op one f32
 // rounding (mul_scalar, add, ones - mask, mul, add), bit-exact.

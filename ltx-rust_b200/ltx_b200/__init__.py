@@ -23,7 +23,7 @@ STATUS = {
     6: "LORA_RANK", 7: "NO_LORA_MATCHES", 8: "IO", 9: "FORMAT", 10: "CONFIG", 11: "SIGMA",
     12: "SCHEDULE", 13: "CUDA", 14: "NCCL", 15: "TIMEOUT", 16: "OOM", 17: "UNSUPPORTED",
     18: "MISSING_CONFIG", 19: "NEGATIVE_CONTEXT", 20: "CHUNK_PLAN",
-    21: "TARGET_TOKENS",
+    21: "TARGET_TOKENS", 22: "STRENGTH",
 }
 
 
@@ -99,6 +99,9 @@ def lib() -> ctypes.CDLL:
         "ltx_denoise_loop": (I, [V, V, P, P, P, P, P, P, P, ctypes.c_int32, ctypes.c_int32, P, ctypes.c_int32, F, F,
                                  ctypes.c_int32, P]),
         "ltx_apply_noise": (I, [V, P, P, P, P, ctypes.c_int32, ctypes.c_int32, F]),
+        "ltx_apply_keyframe": (I, [V, P, P, ctypes.c_int32, ctypes.c_int32, P, ctypes.c_int32, ctypes.c_int32, F]),
+        "ltx_seam_cond_plan": (I, [ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_float),
+                                   ctypes.POINTER(ctypes.c_uint32)]),
         "ltx_scheduler_execute": (I, [ctypes.c_int32, ctypes.c_uint64, F, F, ctypes.c_int32, F, P]),
         "ltx_target_positions": (I, [ctypes.c_uint32] * 7 + [F, P]),
         "ltx_reference_positions": (I, [ctypes.c_uint32] * 8 + [F, ctypes.c_uint32, ctypes.c_uint32, P]),
@@ -395,6 +398,24 @@ def apply_noise(ctx: "Context", latent, noise, clean, mask, noise_scale):
     T, C = latent.shape
     ctx.check(lib().ltx_apply_noise(ctx.h, _ptr(latent), _ptr(noise), _ptr(clean), _ptr(mask), T, C, noise_scale),
               "ltx_apply_noise")
+
+
+def apply_keyframe(ctx: "Context", clean, mask, image, latent_frame_index, strength):
+    """ImageKeyframeCondition::apply_to in place on clean [T, C] and mask [T] (ltx_apply_keyframe):
+    image is the one-frame latent [C, 1, H, W] (or [C, H*W]); f32 CUDA tensors."""
+    T, C = clean.shape
+    tpf = image.numel() // C
+    ctx.check(lib().ltx_apply_keyframe(ctx.h, _ptr(clean), _ptr(mask), T, C, _ptr(image), latent_frame_index, tpf,
+                                       strength), "ltx_apply_keyframe")
+
+
+def seam_cond_plan(overlap):
+    """seam_cond_plan -> (chunk_local_idx, strength, blend_tail_len) (host, no GPU needed)."""
+    idx, st, tail = ctypes.c_uint32(), ctypes.c_float(), ctypes.c_uint32()
+    rc = lib().ltx_seam_cond_plan(overlap, ctypes.byref(idx), ctypes.byref(st), ctypes.byref(tail))
+    if rc:
+        raise LtxError(rc, lib().ltx_host_last_error().decode())
+    return idx.value, st.value, tail.value
 
 
 def scheduler_execute(steps, num_tokens, max_shift=2.05, base_shift=0.95, stretch=True, terminal=0.1):

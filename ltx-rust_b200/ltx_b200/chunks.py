@@ -19,6 +19,9 @@ last chunk), as Blender::finish_chunk emits them (blend.rs:151-182).
 Collectives: one point-to-point send/recv per seam whose two chunks sit on
 different ranks (NCCL on device tensors, gloo on CPU tensors); every rank
 takes the same steps in the same order.
+
+With seam keyframes on (the reference's default) chunk n depends on chunk
+n-1's output, so the chunks run one after another: denoise_sequential.
 """
 from __future__ import annotations
 
@@ -114,3 +117,42 @@ def gather_clip(chunks, assignment, rank: int, chunk_data: dict, total_shape, ro
         for w in dist.batch_isend_irecv(ops):
             w.wait()
     return clip
+
+
+def denoise_sequential(ctx, model, states, latent_plan, tokens_per_frame, sigmas, cfg_scale=3.0, rescale_scale=0.7,
+                       target_tokens=None, seam_keyframes=True):
+    """The reference's default chunk loop (PipelineConfig::seam_keyframes = true,
+    crates/ltx-pipeline/src/lib.rs:28-39, 300-311): before chunk n > 0 is
+    denoised it is conditioned on chunk n-1's output at the seam
+    (keyframes_from_previous, lib.rs:493-548): seam_cond_plan (crates/ltx-chunk/
+    src/seam.rs:110-125) names one frame at chunk-local index 0 with strength
+    0.95, applied as ImageKeyframeCondition (crates/ltx-sampler/src/
+    conditioning.rs:127-205).  The reference encodes chunk n-1's decoded pixel
+    frame with the VAE; here the keyframe is chunk n-1's final latent frame at
+    the same clip position, applied in latent space (ltx_apply_keyframe), so
+    no VAE is needed.
+
+    states: one dict per chunk of device tensors latent [T, C], clean [T, C],
+    mask [T], positions, ctx_cond, ctx_uncond (the chunk's sampler state;
+    clean and mask are modified); latent_plan: [(start, end, real_overlap)] in
+    latent frames.  Returns each chunk's final target tokens [target_tokens, C]."""
+    import torch
+    from . import apply_keyframe, seam_cond_plan, unpatchify
+    outs = []
+    for n, st in enumerate(states):
+        T, C = st["latent"].shape
+        tt = T if target_tokens is None else target_tokens
+        ro = latent_plan[n][2]
+        if seam_keyframes and n > 0 and ro > 0:
+            idx, strength, _ = seam_cond_plan(8 * ro)          # pixel overlap: 8 frames per latent frame
+            src = latent_plan[n][0] - latent_plan[n - 1][0] + idx // 8   # that clip frame in chunk n-1
+            tok = outs[n - 1][src * tokens_per_frame:(src + 1) * tokens_per_frame]
+            image = torch.empty(C, tokens_per_frame, dtype=tok.dtype, device=tok.device)
+            unpatchify(ctx, tok.contiguous(), image.view(1, C, 1, 1, tokens_per_frame))   # [tpf, C] -> [C, 1, 1, tpf]
+            apply_keyframe(ctx, st["clean"], st["mask"], image, idx // 8, strength)
+        out = torch.empty(tt, C, dtype=st["latent"].dtype, device=st["latent"].device)
+        lat = st["latent"].clone()
+        model.denoise_loop(lat, st["clean"], st["mask"], st["positions"], st["ctx_cond"], st["ctx_uncond"], sigmas,
+                           cfg_scale, rescale_scale, target_tokens=tt, out=out)
+        outs.append(out)
+    return outs

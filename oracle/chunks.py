@@ -11,6 +11,7 @@ Follows, line by line:
   Blender                   blend.rs:67-298 (new, push_frame, finish_chunk, drain, flush)
   the pipeline's driving    crates/ltx-pipeline/src/lib.rs:270-353 (push every frame,
                             finish_chunk(len, next.real_overlap), drain, flush at the end)
+  seam_cond_plan            crates/ltx-chunk/src/seam.rs:110-125 (one keyframe at the seam)
 
 Pinned against the known answers in plan.rs / blend.rs's own tests
 (tests/test_chunks_host.py).
@@ -24,6 +25,16 @@ class ChunkError(ValueError):
     def __init__(self, kind, msg=""):
         super().__init__(f"{kind}: {msg}")
         self.kind = kind
+
+
+DEFAULT_KEYFRAME_STRENGTH = np.float32(0.95)   # seam.rs:60
+
+
+def seam_cond_plan(overlap):
+    """seam_cond_plan (seam.rs:110-125): ([(chunk_local_idx, strength)], blend_tail_len)."""
+    if overlap == 0:
+        raise ChunkError("ZeroOverlapForSeam", "overlap must be non-zero for a seam conditioning plan")
+    return [(0, DEFAULT_KEYFRAME_STRENGTH)], overlap - 1
 
 
 def _sat_sub(a, b):

@@ -7,6 +7,7 @@ host loop; never imported by the product library).
   patchify / unpatchify        crates/ltx-sampler/src/patchifier.rs:50-89
   target / reference positions patchifier.rs:101-161, 183-332
   VideoReferenceCondition      crates/ltx-sampler/src/conditioning.rs:63-106
+  ImageKeyframeCondition       conditioning.rs:127-205
   apply_noise                  crates/ltx-sampler/src/noiser.rs:91-106
   GuidedDenoiser::apply        crates/ltx-sampler/src/guidance.rs:102-195
   post_process / euler_step    crates/ltx-sampler/src/loop_.rs:37-65
@@ -146,6 +147,31 @@ def apply_reference(state: LatentState, ref_latent5, strength=1.0, fps=24.0,
                        np.concatenate([state.denoise_mask, mask], 1),
                        np.concatenate([state.positions, pos], 2),
                        np.concatenate([state.clean_latent, ref_tok], 1))
+
+
+def apply_keyframe(state: LatentState, image_latent, latent_frame_index, tokens_per_frame, strength):
+    """ImageKeyframeCondition::apply_to (conditioning.rs:127-205): image_latent [B, C, 1, H, W];
+    clean[span] <- its tokens, mask[span] <- 1 - strength, every value as Burn computes it
+    (clean*keep + img*frame, mask*keep + frame*(1-strength), f32 mul then add)."""
+    s = f32(strength)
+    if not (f32(0) <= s <= f32(1)):
+        raise SamplerError("InvalidStrength", str(strength))
+    B, C, F1, H, W = image_latent.shape
+    if H * W != tokens_per_frame:
+        raise SamplerError("Shape", "image_latent H*W does not match tokens_per_frame")
+    img_tok = patchify(image_latent)
+    T = state.latent.shape[1]
+    start, end = latent_frame_index * tokens_per_frame, (latent_frame_index + 1) * tokens_per_frame
+    if end > T:
+        raise SamplerError("Shape", "image keyframe index exceeds latent frame count")
+    img_clean = np.zeros(state.clean_latent.shape, np.float32)
+    img_clean[:, start:end] = img_tok
+    frame = np.zeros((B, T, 1), np.float32)
+    frame[:, start:end] = 1.0
+    keep = (np.float32(1.0) - frame).astype(np.float32)
+    clean = (state.clean_latent * keep).astype(np.float32) + (img_clean * frame).astype(np.float32)
+    mask = (state.denoise_mask * keep).astype(np.float32) + (frame * f32(f32(1.0) - s)).astype(np.float32)
+    return LatentState(state.latent, mask.astype(np.float32), state.positions, clean.astype(np.float32))
 
 
 def apply_noise(state: LatentState, noise, noise_scale):

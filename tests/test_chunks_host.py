@@ -191,3 +191,46 @@ def test_assign_contiguous():
     assert cp.assign(1, 2) == [[0], []]
     p = oc.plan(100, 17, 8)
     assert [cp.emitted_range(p, n) for n in range(len(p))][0] == (0, p[1][0])
+
+
+# ── seam keyframes (crates/ltx-chunk/src/seam.rs, ltx-sampler conditioning.rs) ──
+
+def test_seam_cond_plan_oracle_matches_reference_tests():
+    """seam.rs's own tests: one conditioning at chunk-local 0 (latent-aligned), strength 0.95,
+    blend tail overlap - 1 (so conditioning + tail == overlap), ZeroOverlapForSeam at 0."""
+    from oracle import chunks as oc
+    for overlap in (8, 16, 24, 32):
+        conds, tail = oc.seam_cond_plan(overlap)
+        assert conds == [(0, np.float32(0.95))] and tail == overlap - 1 and len(conds) + tail == overlap
+        assert all(i % 8 == 0 for i, _ in conds)
+    with pytest.raises(oc.ChunkError) as e:
+        oc.seam_cond_plan(0)
+    assert e.value.kind == "ZeroOverlapForSeam"
+
+
+def test_seam_cond_plan_c_abi_matches_oracle():
+    import ltx_b200
+    from oracle import chunks as oc
+    for overlap in (1, 8, 16, 40):
+        idx, strength, tail = ltx_b200.seam_cond_plan(overlap)
+        (o_idx, o_s), = oc.seam_cond_plan(overlap)[0]
+        assert (idx, np.float32(strength), tail) == (o_idx, o_s, oc.seam_cond_plan(overlap)[1])
+    with pytest.raises(ltx_b200.LtxError) as e:
+        ltx_b200.seam_cond_plan(0)
+    assert e.value.kind == "CHUNK_PLAN" and "ZeroOverlapForSeam" in str(e.value)
+
+
+def test_keyframe_oracle_matches_reference_tests():
+    """conditioning.rs keyframe_condition_writes_only_its_frame and
+    keyframe_condition_rejects_strength_outside_unit_range."""
+    from oracle import sampler as os_
+    st = os_.LatentState(np.zeros((1, 6, 2), np.float32), np.ones((1, 6, 1), np.float32),
+                         np.zeros((1, 3, 6, 2), np.float32), np.full((1, 6, 2), -1.0, np.float32))
+    img = np.array([1.0, 3.0, 2.0, 4.0], np.float32).reshape(1, 2, 1, 1, 2)
+    out = os_.apply_keyframe(st, img, 1, 2, 0.95)
+    assert out.clean_latent.reshape(-1).tolist() == [-1, -1, -1, -1, 1, 2, 3, 4, -1, -1, -1, -1]
+    np.testing.assert_allclose(out.denoise_mask.reshape(-1), [1, 1, 0.05, 0.05, 1, 1], atol=1e-6)
+    for s in (-0.1, 1.5, float("nan")):
+        with pytest.raises(os_.SamplerError) as e:
+            os_.apply_keyframe(st, np.zeros((1, 2, 1, 1, 2), np.float32), 0, 2, s)
+        assert e.value.kind == "InvalidStrength"

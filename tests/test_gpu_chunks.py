@@ -118,3 +118,99 @@ def test_chunk_parallel_nccl_two_gpus():
         p.join(180)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert q.get(timeout=5) is True
+
+
+# ── seam keyframes: ImageKeyframeCondition on the device, the sequential chunk loop ──
+
+def test_apply_keyframe_bit_exact():
+    """ltx_apply_keyframe against oracle/sampler.apply_keyframe (Burn's clean*keep + img*frame,
+    mask*keep + frame*(1-strength)): bit-exact, -0.0 values included."""
+    import ltx_b200
+    from oracle import sampler as osam
+    ctx = ltx_b200.Context(0)
+    rng = np.random.default_rng(4)
+    T, C, tpf = 6 * 20, 7, 20
+    for frame, strength in ((0, 0.95), (3, 0.3), (5, 1.0), (2, 0.0)):
+        clean = rng.standard_normal((1, T, C)).astype(np.float32)
+        clean[0, :3, 0] = -0.0
+        mask = rng.choice(np.array([0.0, 1.0, -0.0, 0.25], np.float32), size=(1, T, 1))
+        img = rng.standard_normal((1, C, 1, 4, 5)).astype(np.float32)
+        img[0, 0, 0, 0, :2] = -0.0
+        st = osam.LatentState(np.zeros((1, T, C), np.float32), mask, None, clean)
+        exp = osam.apply_keyframe(st, img, frame, tpf, strength)
+        cd, md = torch.from_numpy(clean[0].copy()).cuda(), torch.from_numpy(mask[0, :, 0].copy()).cuda()
+        ltx_b200.apply_keyframe(ctx, cd, md, torch.from_numpy(img[0]).cuda(), frame, strength)
+        ctx.synchronize()
+        assert np.array_equal(cd.cpu().numpy().view(np.uint32), exp.clean_latent[0].view(np.uint32))
+        assert np.array_equal(md.cpu().numpy().view(np.uint32), exp.denoise_mask[0, :, 0].view(np.uint32))
+    z = torch.zeros(T, C, device="cuda")
+    m = torch.zeros(T, device="cuda")
+    for frame, strength, kind in ((0, 1.5, "STRENGTH"), (0, float("nan"), "STRENGTH"), (6, 0.9, "SHAPE")):
+        with pytest.raises(ltx_b200.LtxError) as e:
+            ltx_b200.apply_keyframe(ctx, z, m, torch.zeros(C, tpf, device="cuda"), frame, strength)
+        assert e.value.kind == kind
+    ctx.close()
+
+
+def test_sequential_chunks_with_seam_keyframes_match_oracle(tmp_path):
+    """Two overlapping chunks (4 latent frames each, 1 shared) through denoise_sequential:
+    chunk 1's first latent frame is conditioned (strength 0.95) on chunk 0's final latent at
+    that clip frame, then denoised.  Against the oracle running the same loop on its own
+    chunk-0 output: rel-L2 <= 1e-2 per chunk."""
+    import ltx_b200
+    from ltx_b200 import chunks as lc
+    from dit_checkpoint import small_config, write_checkpoint
+    from oracle import dit, sampler as osam
+    from oracle.weight_store import KeyMap, WeightStore as OracleStore
+    cfg = small_config(heads=2, head_dim=128, layers=2)
+    ck = str(tmp_path / "seq.safetensors")
+    write_checkpoint(ck, cfg, seed=17)
+    ctx = ltx_b200.Context(0)
+    st = ltx_b200.WeightStore(ctx, [ck], ltx_b200.KEYMAP_TRANSFORMER)
+    model = ltx_b200.VideoTransformer.load(ctx, st)
+    o = OracleStore([ck], KeyMap.transformer())
+    params = dit.load_params({k: o.read(k) for k in o.keys()})
+    c = dit.DiTConfig.from_json(cfg)
+    F, Hh, W, S, C = 4, 4, 8, 24, 128
+    tpf, Tt = Hh * W, F * Hh * W
+    plan = [(0, 4, 0), (3, 7, 1)]
+    sig = [float(x) for x in osam.scheduler_execute(8, Tt)[:3]]
+    rng = np.random.default_rng(8)
+    o_states, d_states = [], []
+    for n in range(2):
+        init = osam.LatentState(rng.standard_normal((1, Tt, C)).astype(np.float32), np.ones((1, Tt, 1), np.float32),
+                                osam.target_positions(F, Hh, W), np.zeros((1, Tt, C), np.float32))
+        s = osam.apply_reference(init, rng.standard_normal((1, C, F, Hh, W)).astype(np.float32), strength=1.0)
+        cc = rng.standard_normal((1, S, cfg["cross_attention_dim"])).astype(np.float32)
+        cu = rng.standard_normal((1, S, cfg["cross_attention_dim"])).astype(np.float32)
+        o_states.append((s, cc, cu))
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+        d_states.append({"latent": dev(s.latent[0]), "clean": dev(s.clean_latent[0]), "mask": dev(s.denoise_mask[0, :, 0]),
+                         "positions": dev(s.positions), "ctx_cond": dev(cc[0]), "ctx_uncond": dev(cu[0])})
+    got = lc.denoise_sequential(ctx, model, d_states, plan, tpf, sig, 3.0, 0.7, target_tokens=Tt)
+    ctx.synchronize()
+    got = [g.cpu().numpy() for g in got]
+
+    def model_x0(latent, ts, pos, ctx_):
+        with torch.no_grad():
+            v = dit.model_forward(params, c, torch.from_numpy(latent), torch.from_numpy(ts), torch.from_numpy(pos),
+                                  torch.from_numpy(ctx_)).numpy()
+        return osam.velocity_to_x0(latent, ts, v)
+
+    exp = []
+    for n, (s, cc, cu) in enumerate(o_states):
+        if n > 0:
+            (idx, strength), = oc.seam_cond_plan(8 * plan[n][2])[0]
+            src = plan[n][0] - plan[n - 1][0] + idx // 8
+            tok = exp[n - 1][src * tpf:(src + 1) * tpf]                      # [tpf, C]
+            image = osam.unpatchify(tok[None], 1, 1, tpf)                  # [1, C, 1, 1, tpf]
+            s = osam.apply_keyframe(s, image, idx // 8, tpf, strength)
+        exp.append(osam.euler_loop(sig, s, Tt, model_x0, cc, cu, cfg_scale=3.0, rescale_scale=0.7).latent[0])
+    for n in range(2):
+        err = float(np.linalg.norm(got[n] - exp[n]) / np.linalg.norm(exp[n]))
+        print(f"\nchunk {n} with seam keyframes: rel-L2 {err:.2e}")
+        assert np.isfinite(got[n]).all() and err < 1e-2
+    # the keyframe moved chunk 1's first latent frame toward chunk 0's output there
+    model.close()
+    st.close()
+    ctx.close()
