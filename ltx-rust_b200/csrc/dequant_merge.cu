@@ -60,17 +60,35 @@ __device__ __forceinline__ void store_out(const MergeParams &p, int64_t idx, flo
 
 // ── no-delta path: HBM-bound streaming kernel ────────────────────────────────
 
+// Four FP8 bytes (byte j = element j) -> f32, exact: the hardware converts
+// e4m3/e5m2 pairs to f16 (both formats are subsets of f16, NaN stays NaN,
+// e5m2 infinities stay infinite), and f16 -> f32 is exact.
+template <int WDT>
+__device__ __forceinline__ void fp8x4_to_f32(uint32_t w, float *f) {
+    uint32_t h01, h23;
+    if constexpr (WDT == LTX_F8_E4M3)
+        asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+            "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+            : "=r"(h01), "=r"(h23) : "r"(w));
+    else
+        asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+            "cvt.rn.f16x2.e5m2x2 %0, lo;\n\tcvt.rn.f16x2.e5m2x2 %1, hi;\n\t}"
+            : "=r"(h01), "=r"(h23) : "r"(w));
+    f[0] = __half2float(__ushort_as_half((unsigned short)(h01 & 0xFFFFu)));
+    f[1] = __half2float(__ushort_as_half((unsigned short)(h01 >> 16)));
+    f[2] = __half2float(__ushort_as_half((unsigned short)(h23 & 0xFFFFu)));
+    f[3] = __half2float(__ushort_as_half((unsigned short)(h23 >> 16)));
+}
+
 // 16 input elements (one 16-byte FP8 load) -> decode, scale, convert, store.
 template <int WDT, bool OUT_BF16>
 __device__ __forceinline__ void dequant16(const MergeParams &p, int64_t v, uint4 raw) {
     float f[16];
     if constexpr (WDT == LTX_F8_E4M3 || WDT == LTX_F8_E5M2) {
-        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const uint32_t byte = (w4[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-            f[j] = WDT == LTX_F8_E4M3 ? dec_e4m3(byte) : dec_e5m2(byte);
-        }
+        fp8x4_to_f32<WDT>(raw.x, f);
+        fp8x4_to_f32<WDT>(raw.y, f + 4);
+        fp8x4_to_f32<WDT>(raw.z, f + 8);
+        fp8x4_to_f32<WDT>(raw.w, f + 12);
     } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) f[j] = load_as_f32(p.w, WDT, v * 16 + j);
@@ -108,19 +126,16 @@ __global__ void __launch_bounds__(256) dequant_only_kernel(MergeParams p, int64_
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint4 *src = reinterpret_cast<const uint4 *>(p.w);
-    for (; v + (kDqUnroll - 1) * stride < n16; v += kDqUnroll * stride) {
+    for (; v < n16; v += kDqUnroll * stride) {
         uint4 raw[kDqUnroll];
         if constexpr (WDT == LTX_F8_E4M3 || WDT == LTX_F8_E5M2) {
 #pragma unroll
-            for (int u = 0; u < kDqUnroll; ++u) raw[u] = __ldcs(src + v + u * stride);
+            for (int u = 0; u < kDqUnroll; ++u)
+                if (v + u * stride < n16) raw[u] = __ldcs(src + v + u * stride);
         }
 #pragma unroll
-        for (int u = 0; u < kDqUnroll; ++u) dequant16<WDT, OUT_BF16>(p, v + u * stride, raw[u]);
-    }
-    for (; v < n16; v += stride) {
-        uint4 raw{};
-        if constexpr (WDT == LTX_F8_E4M3 || WDT == LTX_F8_E5M2) raw = __ldcs(src + v);
-        dequant16<WDT, OUT_BF16>(p, v, raw);
+        for (int u = 0; u < kDqUnroll; ++u)
+            if (v + u * stride < n16) dequant16<WDT, OUT_BF16>(p, v + u * stride, raw[u]);
     }
     // tail (n not a multiple of 16)
     for (int64_t i = n16 * 16 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
@@ -384,8 +399,17 @@ cudaError_t launch_merge(const MergeParams &p, cudaStream_t st, int sms, void *s
             dequant_only_scalar_kernel<<<sms * 4, 256, 0, st>>>(p, n);
             return cudaGetLastError();
         }
+        // one unrolled round per thread where it fits in one wave of resident CTAs
+        static int per_sm[2][2] = {{0, 0}, {0, 0}};   // [e5m2][bf16 out], filled once
+        int &resident = per_sm[WDT == LTX_F8_E5M2][p.dst_bf16 ? 1 : 0];
+        if (!resident) {
+            int nb = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &nb, p.dst_bf16 ? dequant_only_kernel<WDT, true> : dequant_only_kernel<WDT, false>, 256, 0);
+            resident = std::max(nb, 1);
+        }
         const int64_t work = (n / 16 + kDqUnroll - 1) / kDqUnroll + 1;   // threads for one unrolled round
-        const int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sms * 8);
+        const int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)sms * resident);
         if (p.dst_bf16)
             dequant_only_kernel<WDT, true><<<grid, 256, 0, st>>>(p, n);
         else
