@@ -17,7 +17,9 @@ Workloads:
                  states: heads and FFN units per rank, NCCL allreduce after
                  each row-split projection; strong scaling, value = 12288/t).
                  The N > 1 line also carries `replicas` (one independent
-                 sequence per GPU, no collective: weak scaling) and
+                 sequence per GPU, no collective: weak scaling), at even N
+                 `cfg_tp` (the cond and uncond passes on two halves of the
+                 GPUs, each half tensor-parallel; strong scaling) and
                  `chunk_pipeline` (config 5 on the N GPUs).  --parallel chunk
                  makes the replica figure the headline instead.  The N = 1
                  line carries `step_fp8` (the same step with FP8 FFN GEMMs).
@@ -623,6 +625,26 @@ def run_replicas(args, rank, ws, device):
             "scaling": "weak", "parallelism": f"replicas x{ws}: one independent sequence per GPU"}
 
 
+def run_cfg_tp(args, rank, ws, device):
+    """Config 4 on an even number of GPUs as CFG-parallel x tensor-parallel: ranks
+    [0, N/2) run the conditional pass, [N/2, N) the unconditional one, each half
+    one tensor-parallel group of N/2 (none at N = 2); one velocity all-gather per
+    step between the halves.  Same sequence, same metric as the headline."""
+    import torch
+    import ltx_b200
+    torch.cuda.set_device(device)
+    ctx = ltx_b200.Context(device)
+    cfg_rank, half, _ = ltx_b200.init_cfg_tensor_parallel(ctx)
+    run = StepRunner(ctx, 7, 100)
+    steps = max(3, min(args.steps, 5))
+    ms, _ = run.timed(steps, 3, ws, device, clocks=False, label="denoise_timed_cfg_tp")
+    run.close()
+    ctx.close()
+    return {"value": T_TOTAL / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "scaling": "strong",
+            "parallelism": f"cfg2 x tp{half}: cond/uncond pass on two groups of {half} GPU(s), velocity all-gather"}
+
+
 def run_chunk_pipeline(args, rank, ws, device):
     """Config 5: 8 overlapping temporal chunks (pixel chunk_len 121 -> 16 latent
     frames, overlap 16 pixel frames -> 2 latent frames), each a config-4 state
@@ -1083,6 +1105,10 @@ def main():
                 rep = run_replicas(args, rank, ws, local)
                 _log(f"replicas: {rep['ms_per_step']:.1f} ms/step, {rep['value']:.0f} tokens/s")
                 res["replicas"] = rep
+                if ws % 2 == 0:
+                    ct = run_cfg_tp(args, rank, ws, local)
+                    _log(f"cfg x tp: {ct['ms_per_step']:.1f} ms/step, {ct['value']:.0f} tokens/s")
+                    res["cfg_tp"] = ct
             pl_args = argparse.Namespace(warmup=3)
             pl = run_chunk_pipeline(pl_args, rank, ws, local)
             _log(f"config-5 pipeline: {pl['ms_per_step'] / 1e3:.2f} s, {pl['speedup_vs_serial_chunks']:.2f}x the "

@@ -107,6 +107,19 @@ int ltx_ctx_synchronize(ltx_ctx *ctx);
 int ltx_comm_unique_id(uint8_t *id_out, size_t len);
 /* Collective over the nranks contexts: binds this context to rank `rank`. */
 int ltx_ctx_init_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t nranks, int32_t rank);
+/* CFG-parallel pair: the conditional and unconditional passes of the CFG
+ * batch (guidance.rs:126, :147) run on two contexts (two GPUs, or two
+ * tensor-parallel groups of equal size) instead of as one batch-2 forward.
+ * Collective over the 2 ranks of the pair, with an id made by
+ * ltx_comm_unique_id: cfg_rank 0 computes the conditional pass, 1 the
+ * unconditional one.  ltx_denoise_step / ltx_denoise_loop on such a context
+ * run their own pass (batch 1), all-gather the two velocities over the pair
+ * once per step, and every rank computes the same CFG/Euler update, so the
+ * latents stay identical on all ranks.  Combined with ltx_ctx_init_comm,
+ * ranks r and r + n/2 of n GPUs form the pairs and each half is one
+ * tensor-parallel group of n/2.  No reference counterpart (the reference runs
+ * one device). */
+int ltx_ctx_init_cfg_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t cfg_rank);
 /* LTX_ERR_NCCL if the communicator has recorded an asynchronous error. */
 int ltx_ctx_comm_check(ltx_ctx *ctx);
 /* Aborts the communicator (after a peer failed); the context falls back to

@@ -27,6 +27,7 @@ struct NcclApi {
     ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
     ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                                cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t *) = nullptr;
     const char *(*get_error_string)(ncclResult_t) = nullptr;
 };
@@ -48,10 +49,11 @@ const NcclApi &nccl() {
         api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
         api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
         api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
+        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
         api.comm_get_async_error = reinterpret_cast<decltype(api.comm_get_async_error)>(sym("ncclCommGetAsyncError"));
         api.get_error_string = reinterpret_cast<decltype(api.get_error_string)>(sym("ncclGetErrorString"));
         api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.comm_abort && api.all_reduce &&
-                 api.comm_get_async_error && api.get_error_string;
+                 api.all_gather && api.comm_get_async_error && api.get_error_string;
         if (!api.ok) api.why = "libnccl.so.2 lacks an expected entry point";
     });
     return api;
@@ -101,7 +103,23 @@ int allreduce_sum_bf16(ltx_ctx *ctx, void *buf, size_t count) {
     return comm_join(ctx);
 }
 
+int cfg_allgather(ltx_ctx *ctx, float *buf, size_t count) {
+    if (!ctx->cfg_comm || count == 0) return LTX_OK;
+    ncclResult_t r = nccl().all_gather(buf + (size_t)ctx->cfg_rank * count, buf, count, ncclFloat32,
+                                       static_cast<ncclComm_t>(ctx->cfg_comm), ctx->stream);
+    if (r != ncclSuccess) return fail(ctx, LTX_ERR_NCCL, "CFG all-gather of %zu floats: %s", count, nccl_str(r));
+    return LTX_OK;
+}
+
 void comm_release(ltx_ctx *ctx, bool abort) {
+    if (ctx->cfg_comm) {
+        if (abort)
+            nccl().comm_abort(static_cast<ncclComm_t>(ctx->cfg_comm));
+        else
+            nccl().comm_destroy(static_cast<ncclComm_t>(ctx->cfg_comm));
+        ctx->cfg_comm = nullptr;
+        ctx->cfg_rank = 0;
+    }
     if (!ctx->comm) return;
     const NcclApi &api = nccl();
     if (abort) {
@@ -163,13 +181,33 @@ extern "C" int ltx_ctx_init_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, in
     return LTX_OK;
 }
 
+extern "C" int ltx_ctx_init_cfg_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t cfg_rank) {
+    if (!ctx) return LTX_ERR_INVALID_ARG;
+    if (!id || len < LTX_COMM_ID_BYTES || cfg_rank < 0 || cfg_rank > 1)
+        return ltx::fail(ctx, LTX_ERR_INVALID_ARG, "ltx_ctx_init_cfg_comm: bad id or CFG rank %d", cfg_rank);
+    if (ctx->cfg_comm) return ltx::fail(ctx, LTX_ERR_INVALID_ARG, "context already has a CFG pair");
+    const auto &api = ltx::nccl();
+    if (!api.ok) return ltx::fail(ctx, LTX_ERR_NCCL, "%s", api.why.c_str());
+    cudaSetDevice(ctx->device);
+    ncclUniqueId uid;
+    memcpy(uid.internal, id, LTX_COMM_ID_BYTES);
+    ncclComm_t comm = nullptr;
+    ncclResult_t r = api.comm_init_rank(&comm, 2, uid, cfg_rank);
+    if (r != ncclSuccess) return ltx::fail(ctx, LTX_ERR_NCCL, "ncclCommInitRank (CFG pair): %s", ltx::nccl_str(r));
+    ctx->cfg_comm = comm;
+    ctx->cfg_rank = cfg_rank;
+    return LTX_OK;
+}
+
 extern "C" int ltx_ctx_comm_check(ltx_ctx *ctx) {
     if (!ctx) return LTX_ERR_INVALID_ARG;
-    if (!ctx->comm) return LTX_OK;
-    ncclResult_t async = ncclSuccess;
-    ncclResult_t r = ltx::nccl().comm_get_async_error(static_cast<ncclComm_t>(ctx->comm), &async);
-    if (r != ncclSuccess || async != ncclSuccess)
-        return ltx::fail(ctx, LTX_ERR_NCCL, "communicator error: %s", ltx::nccl_str(r != ncclSuccess ? r : async));
+    for (void *c : {ctx->comm, ctx->cfg_comm}) {
+        if (!c) continue;
+        ncclResult_t async = ncclSuccess;
+        ncclResult_t r = ltx::nccl().comm_get_async_error(static_cast<ncclComm_t>(c), &async);
+        if (r != ncclSuccess || async != ncclSuccess)
+            return ltx::fail(ctx, LTX_ERR_NCCL, "communicator error: %s", ltx::nccl_str(r != ncclSuccess ? r : async));
+    }
     return LTX_OK;
 }
 

@@ -41,6 +41,12 @@ struct ltx_ctx {
     // CTAs of the persistent GEMMs (0 = one per SM).  Lowered while
     // collectives run beside them, so NCCL's kernels find free SMs.
     int gemm_sms = 0;
+    // CFG-parallel pair (an ncclComm_t over 2 ranks), or null: this context
+    // runs both passes of the CFG batch.  With it, cfg_rank 0 computes the
+    // conditional pass and 1 the unconditional one, and the two velocities
+    // are all-gathered once per step.
+    void *cfg_comm = nullptr;
+    int cfg_rank = 0;
 };
 
 namespace ltx {
@@ -81,6 +87,10 @@ int allreduce_sum_bf16_async(ltx_ctx *ctx, void *buf, size_t count);
 int comm_join(ltx_ctx *ctx);
 // Destroys (or aborts) the context's communicator.
 void comm_release(ltx_ctx *ctx, bool abort);
+// All-gather of `count` floats per rank over the CFG pair, on the context's
+// stream: rank r's block goes to buf + r*count; the rank's own block is
+// already in place.
+int cfg_allgather(ltx_ctx *ctx, float *buf, size_t count);
 
 // Message of the last failed host-only call (no context) on this thread.
 inline std::string &host_error() {

@@ -1273,7 +1273,7 @@ static StepBufs carve_step(char *base, const DitConfig &c, int B, int T, int S) 
     a.base = base;
     StepBufs b{};
     b.lat2 = a.take<float>((int64_t)B * T * c.in_ch);
-    b.vel = a.take<float>((int64_t)B * T * c.out_ch);
+    b.vel = a.take<float>((int64_t)2 * T * c.out_ch);   // both CFG passes (a pair rank gathers the other's)
     b.pos2 = a.take<float>((int64_t)B * 3 * T * 2);
     b.ctx2 = a.take<float>((int64_t)B * S * c.cross_dim);
     b.bytes = (a.off + 255) & ~size_t(255);
@@ -1300,20 +1300,36 @@ static int stage_static(ltx_ctx *ctx, const StepBufs &sb, const float *positions
     return LTX_OK;
 }
 
+// Rows of the CFG batch this context's forward computes: both passes (2),
+// one when CFG is off, or one when the context is half of a CFG pair.
+static int forward_batch(const ltx_ctx *ctx, bool use_cfg) { return use_cfg && !ctx->cfg_comm ? 2 : 1; }
+
+// Positions and the context(s) of this context's forward into the step
+// buffers: cond then uncond, or the pair rank's own (0: cond, 1: uncond).
+static int stage_for_step(ltx_ctx *ctx, const StepBufs &sb, const float *positions_dev, const float *cc,
+                          const float *cu, bool use_cfg, int T, int S, int64_t Dc) {
+    if (use_cfg && ctx->cfg_comm)
+        return stage_static(ctx, sb, positions_dev, ctx->cfg_rank == 0 ? cc : cu, nullptr, 1, T, S, Dc);
+    return stage_static(ctx, sb, positions_dev, cc, cu, forward_batch(ctx, use_cfg), T, S, Dc);
+}
+
 // One Euler step of euler_denoising_loop (loop_.rs:93-149) with GuidedDenoiser::apply
 // (guidance.rs:102-166): the cond and uncond passes run as ONE batch-2 forward,
 // then the CFG/rescale combine, post_process and the Euler update in one kernel.
-// Arguments are validated by the callers.  static_ready: positions/contexts are
-// already in the step buffers (the loop stages them once).
+// On a CFG pair each rank runs its own pass (batch 1) and the two velocities
+// are all-gathered before the update, which every rank then computes from the
+// same inputs.  Arguments are validated by the callers.  static_ready:
+// positions/contexts are already in the step buffers (the loop stages them once).
 static int denoise_step_core(ltx_model *m, ltx_ctx *ctx, float *latent_dev, const float *clean_dev,
                              const float *mask_host, const float *mask_dev, const float *positions_dev,
                              const float *cc, const float *cu, int T, int S, float sigma, float sigma_next,
                              float cfg_scale, float rescale_scale, bool static_ready) {
     const DitConfig &c = m->cfg;
     const bool use_cfg = std::fabs(cfg_scale - 1.0f) > 1e-5f;   // needs_uncond (guidance.rs:58-60)
-    const int B = use_cfg ? 2 : 1, C = c.in_ch;
+    const bool pair = use_cfg && ctx->cfg_comm;                 // this rank runs one pass of the CFG batch
+    const int B = forward_batch(ctx, use_cfg), C = c.in_ch;
     cudaStream_t st = ctx->stream;
-    // per-token timesteps = mask * sigma (guidance.rs:114), both CFG halves:
+    // per-token timesteps = mask * sigma (guidance.rs:114), each CFG row:
     // on the host when the caller has the mask there, else on the device
     std::vector<float> ts;
     int U = kMaxDistinctTs;
@@ -1329,17 +1345,20 @@ static int denoise_step_core(ltx_model *m, ltx_ctx *ctx, float *latent_dev, cons
     char *base = static_cast<char *>(ctx->work);
     const StepBufs sb = carve_step(base, c, B, T, S);
     Work w = carve_work(base + sb.bytes, c, (int64_t)B * T, (int64_t)B * S, U, c.layers, m->tp, m->lora_r64);
-    if (!static_ready) TRY(stage_static(ctx, sb, positions_dev, cc, cu, B, T, S, c.cross_dim));
+    if (!static_ready) TRY(stage_for_step(ctx, sb, positions_dev, cc, cu, use_cfg, T, S, c.cross_dim));
     for (int b = 0; b < B; ++b)
         CU(cudaMemcpyAsync(sb.lat2 + (int64_t)b * T * C, latent_dev, (size_t)T * C * 4, cudaMemcpyDeviceToDevice, st));
+    // a pair rank's velocity goes to its own slot: cond [0, T*C), uncond [T*C, 2*T*C)
+    float *vel = pair ? sb.vel + (int64_t)ctx->cfg_rank * T * C : sb.vel;
     if (mask_host) {
-        TRY(forward_impl(m, ctx, sb.lat2, ts, sb.pos2, sb.ctx2, B, T, S, sb.vel, &w, nullptr, true));
+        TRY(forward_impl(m, ctx, sb.lat2, ts, sb.pos2, sb.ctx2, B, T, S, vel, &w, nullptr, true));
         // per-token t for the velocity -> x0 adapter: x0 = x - t * v
         TRY(upload(ctx, w.tok_t, ts.data(), (size_t)T * 4));
     } else {
         CU(mask_timesteps(st, ctx->sm_count, mask_dev, sigma, T, B, w.tok_t));
-        TRY(forward_impl(m, ctx, sb.lat2, {}, sb.pos2, sb.ctx2, B, T, S, sb.vel, &w, nullptr, true, nullptr, w.tok_t));
+        TRY(forward_impl(m, ctx, sb.lat2, {}, sb.pos2, sb.ctx2, B, T, S, vel, &w, nullptr, true, nullptr, w.tok_t));
     }
+    if (pair) TRY(cfg_allgather(ctx, sb.vel, (size_t)T * C));
     CU(cfg_euler(st, ctx->sm_count, latent_dev, sb.vel, use_cfg ? sb.vel + (int64_t)T * C : sb.vel, w.tok_t, mask_dev,
                  clean_dev, T, C, cfg_scale, rescale_scale, use_cfg, w.partial, sigma, sigma_next));
     return LTX_OK;
@@ -1402,7 +1421,7 @@ extern "C" int ltx_denoise_loop(ltx_model *m, ltx_ctx *ctx, float *latent_dev, c
                     tokens);
     const DitConfig &c = m->cfg;
     const bool use_cfg = std::fabs(cfg_scale - 1.0f) > 1e-5f;
-    const int B = use_cfg ? 2 : 1, T = tokens, S = context_tokens;
+    const int B = forward_batch(ctx, use_cfg), T = tokens, S = context_tokens;
     // distinct mask values bound the distinct timesteps of every step (the
     // device path sizes for kMaxDistinctTs)
     int U = kMaxDistinctTs;
@@ -1417,7 +1436,7 @@ extern "C" int ltx_denoise_loop(ltx_model *m, ltx_ctx *ctx, float *latent_dev, c
     }
     TRY(ensure_work(ctx, step_work_bytes(m, B, T, S, U)));
     const StepBufs sb = carve_step(static_cast<char *>(ctx->work), c, B, T, S);
-    TRY(stage_static(ctx, sb, positions_dev, ctx_cond_dev, ctx_uncond_dev, B, T, S, c.cross_dim));
+    TRY(stage_for_step(ctx, sb, positions_dev, ctx_cond_dev, ctx_uncond_dev, use_cfg, T, S, c.cross_dim));
     for (int i = 0; i + 1 < n_sigmas; ++i)
         TRY(denoise_step_core(m, ctx, latent_dev, clean_dev, mask_host, mask_dev, positions_dev, ctx_cond_dev,
                               ctx_uncond_dev, T, S, sigmas_host[i], sigmas_host[i + 1], cfg_scale, rescale_scale, true));

@@ -111,6 +111,7 @@ def lib() -> ctypes.CDLL:
         "ltx_comm_unique_id": (I, [P, ctypes.c_size_t]),
         "ltx_ctx_init_comm": (I, [V, P, ctypes.c_size_t, ctypes.c_int32, ctypes.c_int32]),
         "ltx_ctx_comm_check": (I, [V]),
+        "ltx_ctx_init_cfg_comm": (I, [V, P, ctypes.c_size_t, ctypes.c_int32]),
         "ltx_ctx_abort_comm": (None, [V]),
         "ltx_wait_flag": (I, [V, P, ctypes.c_int32, ctypes.c_uint32]),
         "ltx_set_flag": (I, [V, P, ctypes.c_int32]),
@@ -155,6 +156,11 @@ class Context:
         """Binds this context to rank `rank` of a tensor-parallel group (collective)."""
         buf = ctypes.create_string_buffer(bytes(comm_id), COMM_ID_BYTES)
         self.check(lib().ltx_ctx_init_comm(self.h, buf, COMM_ID_BYTES, nranks, rank), "ltx_ctx_init_comm")
+
+    def init_cfg_comm(self, comm_id: bytes, cfg_rank: int):
+        """Makes this context half of a CFG-parallel pair (ltx_ctx_init_cfg_comm)."""
+        buf = ctypes.create_string_buffer(comm_id, len(comm_id))
+        self.check(lib().ltx_ctx_init_cfg_comm(self.h, buf, len(comm_id), cfg_rank), "ltx_ctx_init_cfg_comm")
 
     def comm_check(self):
         self.check(lib().ltx_ctx_comm_check(self.h), "ltx_ctx_comm_check")
@@ -542,3 +548,37 @@ def init_tensor_parallel(ctx: "Context", group=None):
     rank, ws = dist.get_rank(group), dist.get_world_size(group)
     if ws > 1:
         ctx.init_comm(share_comm_id(group), ws, rank)
+
+
+def cfg_tp_layout(world_size: int, rank: int):
+    """CFG-parallel x tensor-parallel placement of `rank` among `world_size` (even)
+    GPUs: ranks [0, n/2) run the conditional pass, [n/2, n) the unconditional one,
+    each half one tensor-parallel group; rank r pairs with r + n/2.
+    Returns (cfg_rank, tp_size, tp_rank, tp_group_ranks, pair_ranks)."""
+    if world_size < 2 or world_size % 2:
+        raise ValueError(f"CFG-parallel needs an even number of ranks, not {world_size}")
+    half = world_size // 2
+    cfg_rank, tp_rank = divmod(rank, half)
+    return (cfg_rank, half, tp_rank, list(range(cfg_rank * half, cfg_rank * half + half)),
+            [tp_rank, tp_rank + half])
+
+
+def init_cfg_tensor_parallel(ctx: "Context"):
+    """Binds ctx to its CFG pair and (for more than 2 ranks) its tensor-parallel group,
+    over the default torch.distributed group; the ids travel over torch.distributed.
+    Every rank creates every subgroup in the same order (new_group is collective)."""
+    import torch.distributed as dist
+    ws, rank = dist.get_world_size(), dist.get_rank()
+    cfg_rank, half, tp_rank, tp_ranks, pair = cfg_tp_layout(ws, rank)
+    tp_groups = [dist.new_group(list(range(g * half, g * half + half))) for g in range(2)]
+    pair_groups = [dist.new_group([r, r + half]) for r in range(half)]
+    if half > 1:
+        g = tp_groups[cfg_rank]
+        obj = [comm_unique_id() if rank == tp_ranks[0] else None]
+        dist.broadcast_object_list(obj, src=tp_ranks[0], group=g)
+        ctx.init_comm(obj[0], half, tp_rank)
+    g = pair_groups[tp_rank]
+    obj = [comm_unique_id() if rank == pair[0] else None]
+    dist.broadcast_object_list(obj, src=pair[0], group=g)
+    ctx.init_cfg_comm(obj[0], cfg_rank)
+    return cfg_rank, half, tp_rank

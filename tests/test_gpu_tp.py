@@ -103,3 +103,87 @@ def test_tensor_parallel_two_gpus_matches_one(heads, head_dim, layers, frames):
     print(f"\nTP x2 ({heads} heads, {layers} layers): forward rel-L2 {err_f:.2e}, step update rel-L2 {err_s:.2e}")
     assert same, "ranks disagree on the replicated output"
     assert err_f < 1e-2 and err_s < 1e-2
+
+
+def _cfg_pair_worker(rank, ws, port, cfg, q):
+    """CFG-parallel pair: rank 0 runs the conditional pass, rank 1 the unconditional
+    one; every step all-gathers the two velocities and both ranks update the latent."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    import ltx_b200
+    from oracle import sampler
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=timedelta(seconds=90))
+    try:
+        ctx = ltx_b200.Context(rank)
+        assert ltx_b200.init_cfg_tensor_parallel(ctx) == (rank, 1, 0)
+        cj = json.dumps(cfg)
+        model = ltx_b200.VideoTransformer.init_random(ctx, cj, seed=23, lora_rank=8, lora_strength=0.8)
+        F, Hh, W, S = 2, 8, 8, 40
+        rng = np.random.default_rng(6)
+        Tt = F * Hh * W
+        T = 2 * Tt
+        C, Dc = cfg["in_channels"], cfg["cross_attention_dim"]
+        lat = rng.standard_normal((T, C)).astype(np.float32)
+        pos = np.concatenate([sampler.target_positions(F, Hh, W), sampler.reference_positions(F, Hh, W)], axis=2)
+        ctxt = rng.standard_normal((S, Dc)).astype(np.float32)
+        unc = rng.standard_normal((S, Dc)).astype(np.float32)
+        clean = np.concatenate([np.zeros((Tt, C), np.float32), rng.standard_normal((Tt, C)).astype(np.float32)])
+        mask = np.concatenate([np.ones(Tt, np.float32), np.zeros(Tt, np.float32)])
+        sig = np.array([1.0, 0.9, 0.7, 0.4], np.float32)
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+        def run(m):
+            step = dev(lat)
+            m.denoise_step(step, dev(clean), dev(mask), dev(pos), dev(ctxt), dev(unc), 0.8, 0.6, 3.0, 0.7)
+            loop = dev(lat)
+            m.denoise_loop(loop, dev(clean), dev(mask), dev(pos), dev(ctxt), dev(unc), sig, 3.0, 0.7)
+            return step, loop
+
+        step, loop = run(model)
+        ctx.synchronize()
+        ctx.comm_check()
+        got = (step.cpu().numpy(), loop.cpu().numpy())
+        outs = [None] * ws
+        dist.all_gather_object(outs, got)
+        if rank == 0:
+            ctx1 = ltx_b200.Context(0)   # both passes as one batch-2 forward, no communicator
+            m1 = ltx_b200.VideoTransformer.init_random(ctx1, cj, seed=23, lora_rank=8, lora_strength=0.8)
+            r_step, r_loop = run(m1)
+            ctx1.synchronize()
+            ref = (r_step.cpu().numpy(), r_loop.cpu().numpy())
+            same_ranks = all(np.array_equal(o[i], outs[0][i]) for o in outs for i in range(2))
+            bits = all(np.array_equal(got[i], ref[i]) for i in range(2))
+            q.put((same_ranks, bits, _rel_l2(got[0] - lat, ref[0] - lat), _rel_l2(got[1] - lat, ref[1] - lat)))
+            m1.close()
+            ctx1.close()
+        model.close()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_cfg_pair_two_gpus_matches_batch2():
+    """The pair's two batch-1 passes and the single GPU's batch-2 forward compute the
+    same rows (every kernel is row-wise or per batch row), so the step and a 3-step
+    loop match the single GPU's; the bar is rel-L2 <= 1e-5 of the update, and the run
+    reports whether the bits agree."""
+    import socket
+    import torch.multiprocessing as mp
+    cfg = _cfg(4, 128, 2)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mctx = mp.get_context("spawn")
+    q = mctx.Queue()
+    procs = [mctx.Process(target=_cfg_pair_worker, args=(r, 2, port, cfg, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    same, bits, err_step, err_loop = q.get(timeout=5)
+    print(f"\nCFG pair x2: step update rel-L2 {err_step:.2e}, 3-step loop rel-L2 {err_loop:.2e}, bit-identical {bits}")
+    assert same, "the pair's ranks disagree on the latent"
+    assert err_step < 1e-5 and err_loop < 1e-5

@@ -87,3 +87,15 @@ def test_lost_rank_is_detected_by_the_next_collective():
         p.join(60)
     kind, waited = q.get(timeout=5)
     assert kind != "no error" and waited < 30, (kind, waited)
+
+
+def test_cfg_tp_layout():
+    """Ranks [0, n/2) run the conditional pass, [n/2, n) the unconditional one; rank r
+    pairs with r + n/2 and each half is one tensor-parallel group."""
+    import ltx_b200
+    assert ltx_b200.cfg_tp_layout(2, 1) == (1, 1, 0, [1], [0, 1])
+    assert ltx_b200.cfg_tp_layout(8, 5) == (1, 4, 1, [4, 5, 6, 7], [1, 5])
+    assert ltx_b200.cfg_tp_layout(4, 0) == (0, 2, 0, [0, 1], [0, 2])
+    for n in (1, 3):
+        with pytest.raises(ValueError):
+            ltx_b200.cfg_tp_layout(n, 0)
