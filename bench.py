@@ -13,14 +13,17 @@ Workloads:
                  cond / uncond contexts), rescale 0.7.  Random-init FP8 e4m3
                  weights merged with a rank-64 LoRA on the device at load.
                  metric tokens/s = 12288 / step time.  At N > 1 the N ranks
-                 split ONE sequence's model (tensor parallel, as config 4
-                 states: heads and FFN units per rank, NCCL allreduce after
-                 each row-split projection; strong scaling, value = 12288/t).
-                 The N > 1 line also carries `replicas` (one independent
-                 sequence per GPU, no collective: weak scaling), at even N
-                 `cfg_tp` (the cond and uncond passes on two halves of the
-                 GPUs, each half tensor-parallel; strong scaling) and
-                 `chunk_pipeline` (config 5 on the N GPUs).  --parallel chunk
+                 run ONE sequence (strong scaling, value = 12288/t): at even
+                 N the CFG batch's conditional and unconditional passes run
+                 on two halves of the GPUs and each half is tensor-parallel
+                 as config 4 states (heads and FFN units per rank, NCCL
+                 allreduce after each row-split projection), with one
+                 all-gather of the two velocities per step (`--parallel
+                 cfg_tp`, the default); `--parallel tp` splits the model over
+                 all N for both passes.  The N > 1 line also carries the
+                 other of those two layouts (`tp` or `cfg_tp`), `replicas`
+                 (one independent sequence per GPU, no collective: weak
+                 scaling) and `chunk_pipeline` (config 5 on the N GPUs).  --parallel chunk
                  makes the replica figure the headline instead.  The N = 1
                  line carries `step_fp8` (the same step with FP8 FFN GEMMs).
   dequant_merge  config 1: FP8 e4m3 [4096,4096] (+scale) + rank-64 bf16 LoRA
@@ -361,17 +364,47 @@ def make_step_inputs(F, H, W, S, Dc, seed):
             "sigmas": ltx_b200.scheduler_execute(8, Tt)}
 
 
-def step_config(ws, tp):
+def step_mode(ws, parallel):
+    """How config 4 uses `ws` GPUs: "single" (one GPU), "cfg_tp" (even N: the CFG
+    batch's two passes on two halves, each half tensor-parallel), "tp" (every GPU
+    one shard of the model, both passes) or "replicas" (one sequence per GPU)."""
+    if ws == 1:
+        return "single"
+    if parallel == "chunk":
+        return "replicas"
+    return "cfg_tp" if parallel == "cfg_tp" and ws % 2 == 0 else "tp"
+
+
+def step_config(ws, mode):
     """The config-4 workload as both arms' lines name it (identical dicts)."""
+    half = ws // 2
+    par = {"single": "one GPU, one sequence",
+           "tp": f"tp{ws}: one sequence, heads and FFN units split over {ws} GPUs, NCCL allreduce",
+           "cfg_tp": (f"cfg2 x tp{half}: one sequence; the conditional and unconditional passes of the CFG batch "
+                      f"on two halves of {half} GPU(s)" + (", heads and FFN units split inside a half (NCCL "
+                                                            "allreduce)" if half > 1 else "") +
+                      "; one NCCL all-gather of the two velocities per step"),
+           "replicas": f"replicas x{ws}: one independent sequence per GPU"}[mode]
     return {"workload": "denoise_step_config4", "layers": 48, "hidden": D, "heads": 32, "head_dim": 128,
             "ffn": FF, "tokens": T_TOTAL, "latent": [1, 128, LAT_F, LAT_H, LAT_W], "ic_reference": True,
             "context_tokens": S_CTX, "cfg_batch": 2, "guidance": 3.0, "rescale": 0.7,
             "weights": "random-init fp8 e4m3 per-tensor scale + rank-64 LoRA merged on device",
-            "parallelism": (f"tp{ws}: one sequence, heads and FFN units split over {ws} GPUs, NCCL allreduce"
-                            if tp else (f"replicas x{ws}: one independent sequence per GPU" if ws > 1 else
-                                        "one GPU, one sequence")),
+            "parallelism": par,
             "l2": "inputs and weights exceed L2 (25.8 GB bf16 weights streamed per step)",
             "step_tflop": step_flops()[0] / 1e12}
+
+
+def init_step_mode(ctx, mode):
+    """Binds the context for `mode`; returns (seed offset of this rank's model and
+    inputs, whether the model is split over ranks)."""
+    import ltx_b200
+    if mode == "tp":
+        ltx_b200.init_tensor_parallel(ctx)   # this rank's shard of one model
+        return 0, True
+    if mode == "cfg_tp":
+        _, half, _ = ltx_b200.init_cfg_tensor_parallel(ctx)   # one pass, this rank's shard of it
+        return 0, half > 1
+    return (dist_env()[1] if mode == "replicas" else 0), False
 
 
 class StepRunner:
@@ -469,11 +502,10 @@ def run_denoise_step(args, rank, ws, device):
     import ltx_b200
     torch.cuda.set_device(device)
     ctx = ltx_b200.Context(device)
-    tp = args.parallel == "tp" and ws > 1
-    if tp:
-        ltx_b200.init_tensor_parallel(ctx)   # this rank's shard of one model
-    # one sequence split over the ranks: every rank holds the same weights and inputs
-    run = StepRunner(ctx, 7 if tp else 7 + rank, 100 if tp else 100 + rank, offload_blocks=args.offload_blocks)
+    mode = step_mode(ws, args.parallel)
+    one_seq = mode != "replicas"   # every rank holds the same weights and inputs
+    off, split = init_step_mode(ctx, mode)
+    run = StepRunner(ctx, 7 + off, 100 + off, offload_blocks=args.offload_blocks)
     _log(f"model initialised in {run.load_s:.1f}s")
     ms, clocks = run.timed(args.steps, args.warmup, ws, device)
     _log(f"{args.steps} timed steps: {ms:.1f} ms/step")
@@ -525,13 +557,13 @@ def run_denoise_step(args, rank, ws, device):
     gemm_tf = 2.0 * M * N * K / (gemm_ms * 1e-3) / 1e12
     res = {
         "metric": "DiT denoise-step tokens/s (config 4: 48 blocks, T=12288, CFG batch 2 + Euler)",
-        "value": (1 if tp else ws) * T_TOTAL / (ms * 1e-3),
+        "value": (1 if one_seq else ws) * T_TOTAL / (ms * 1e-3),
         "unit": "tokens/s",
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "strong" if tp else "weak",
+        "scaling": "strong" if one_seq and ws > 1 else "weak",
         "dtype": "bf16 (tensor-core GEMM/attention inputs; f32 accumulate, residual and sampler)",
-        "config": step_config(ws, tp),
+        "config": step_config(ws, mode),
         "model_load_s": load_s,
         **({"offload_blocks": args.offload_blocks, "device_weight_bytes": weight_bytes}
            if args.offload_blocks else {}),
@@ -540,16 +572,16 @@ def run_denoise_step(args, rank, ws, device):
                      "unit": "TFLOP/s", "frac": attn_flop / (attn_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
                      "traffic": ATTN_NCU_TRAFFIC, "peak_source": src, "algorithmic_flops_per_launch": attn_flop,
                      "traffic_note": "ncu DRAM bytes of a B=1, T=8192 launch scaled by Q/K/V/O bytes",
-                     "step_tflops_per_gpu": (total / ws if tp else total) / (ms * 1e-3) / 1e12,
-                     "step_frac_of_sustained": (total / ws if tp else total) / (ms * 1e-3) / 1e12 /
+                     "step_tflops_per_gpu": (total / ws if one_seq else total) / (ms * 1e-3) / 1e12,
+                     "step_frac_of_sustained": (total / ws if one_seq else total) / (ms * 1e-3) / 1e12 /
                      peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])},
         "roofline_gemm": {"bound": "tensor", "kernel": "tcgen05 GEMM, FFN-in + GELU (M=24576, N=16384, K=4096)",
                           "achieved": gemm_tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                           "frac": gemm_tf / peaks["bf16_tflops"], "traffic": FFN_IN_NCU_TRAFFIC, "peak_source": src,
                           "algorithmic_flops_per_launch": 2.0 * M * N * K},
-        "e2e": {"value": (1 if tp else ws) * T_TOTAL / (e2e_ms * 1e-3), "unit": "tokens/s",
+        "e2e": {"value": (1 if one_seq else ws) * T_TOTAL / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps * launches_per_step(48, tp),
+        "gpu_launches": args.steps * launches_per_step(48, split),
         "clocks": clocks,
         "finite_output": ok,
     }
@@ -625,24 +657,21 @@ def run_replicas(args, rank, ws, device):
             "scaling": "weak", "parallelism": f"replicas x{ws}: one independent sequence per GPU"}
 
 
-def run_cfg_tp(args, rank, ws, device):
-    """Config 4 on an even number of GPUs as CFG-parallel x tensor-parallel: ranks
-    [0, N/2) run the conditional pass, [N/2, N) the unconditional one, each half
-    one tensor-parallel group of N/2 (none at N = 2); one velocity all-gather per
-    step between the halves.  Same sequence, same metric as the headline."""
+def run_parallel_step(args, rank, ws, device, mode):
+    """Config 4's one sequence on the N GPUs in another layout than the line's
+    headline ("tp" or "cfg_tp"), timed like it (max over ranks, a few steps)."""
     import torch
     import ltx_b200
     torch.cuda.set_device(device)
     ctx = ltx_b200.Context(device)
-    cfg_rank, half, _ = ltx_b200.init_cfg_tensor_parallel(ctx)
+    init_step_mode(ctx, mode)
     run = StepRunner(ctx, 7, 100)
     steps = max(3, min(args.steps, 5))
-    ms, _ = run.timed(steps, 3, ws, device, clocks=False, label="denoise_timed_cfg_tp")
+    ms, _ = run.timed(steps, 3, ws, device, clocks=False, label=f"denoise_timed_{mode}")
     run.close()
     ctx.close()
     return {"value": T_TOTAL / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
-            "scaling": "strong",
-            "parallelism": f"cfg2 x tp{half}: cond/uncond pass on two groups of {half} GPU(s), velocity all-gather"}
+            "scaling": "strong", "parallelism": step_config(ws, mode)["parallelism"]}
 
 
 def run_chunk_pipeline(args, rank, ws, device):
@@ -1014,9 +1043,10 @@ def main():
     ap.add_argument("--workload", default="denoise_step", choices=["denoise_step", "dequant_merge", "chunk_pipeline"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=5.0)
-    ap.add_argument("--parallel", default="tp", choices=["tp", "chunk"],
-                    help="denoise_step at N>1: one sequence split over the GPUs (default, config 4's tensor "
-                         "parallel) or one independent sequence per GPU")
+    ap.add_argument("--parallel", default="cfg_tp", choices=["cfg_tp", "tp", "chunk"],
+                    help="denoise_step at N>1: one sequence with the CFG batch's two passes on two halves of the "
+                         "GPUs, each half tensor-parallel (default; plain tp at odd N), one sequence with every "
+                         "GPU a tensor-parallel shard of both passes, or one independent sequence per GPU")
     ap.add_argument("--offload-blocks", type=int, default=0,
                     help="denoise_step: keep the blocks in pinned host memory with this many on the device")
     args = ap.parse_args()
@@ -1038,11 +1068,12 @@ def main():
                # what ran: one extrapolated step from one timed block, the head and the sampler
                "steps": 1, "warmup": 0, "blocks_timed": base["blocks_timed"], "extrapolated": True,
                "ms_per_step": (64 if pipe else 1) * T_TOTAL / base["value"] * 1e3,
-               "higher_is_better": True, "scaling": "strong" if pipe else ("strong" if args.gpus > 1 else "weak"),
+               "higher_is_better": True,
+               "scaling": "strong" if pipe or step_mode(args.gpus, args.parallel) in ("tp", "cfg_tp") else "weak",
                "vs_baseline": None,
                "dtype": "f32", "data": "synthetic (random-init weights, N(0,1) activations)",
                "config": ({"workload": "chunk_pipeline_config5"} if pipe else
-                          step_config(args.gpus, args.gpus > 1 and args.parallel == "tp")),
+                          step_config(args.gpus, step_mode(args.gpus, args.parallel))),
                "cpu_baseline": base,
                "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                "note": "CPU restatement of the reference (oracle/dit.py + oracle/sampler.py, torch/numpy f32): the "
@@ -1101,14 +1132,17 @@ def main():
                  f"(rel-L2 {blk['e4m3_ffn']['rel_l2_vs_bf16']:.2e}), e4m3 {blk['e4m3']['ms']:.2f} ms "
                  f"(rel-L2 {blk['e4m3']['rel_l2_vs_bf16']:.2e})")
         if ws > 1:
-            if args.parallel == "tp":
+            mode = step_mode(ws, args.parallel)
+            if mode != "replicas":
                 rep = run_replicas(args, rank, ws, local)
                 _log(f"replicas: {rep['ms_per_step']:.1f} ms/step, {rep['value']:.0f} tokens/s")
                 res["replicas"] = rep
-                if ws % 2 == 0:
-                    ct = run_cfg_tp(args, rank, ws, local)
-                    _log(f"cfg x tp: {ct['ms_per_step']:.1f} ms/step, {ct['value']:.0f} tokens/s")
-                    res["cfg_tp"] = ct
+            # the other single-sequence layout beside the headline's
+            other = "tp" if mode == "cfg_tp" else ("cfg_tp" if mode == "tp" and ws % 2 == 0 else None)
+            if other:
+                o = run_parallel_step(args, rank, ws, local, other)
+                _log(f"{other}: {o['ms_per_step']:.1f} ms/step, {o['value']:.0f} tokens/s")
+                res[other] = o
             pl_args = argparse.Namespace(warmup=3)
             pl = run_chunk_pipeline(pl_args, rank, ws, local)
             _log(f"config-5 pipeline: {pl['ms_per_step'] / 1e3:.2f} s, {pl['speedup_vs_serial_chunks']:.2f}x the "

@@ -48,11 +48,11 @@ def test_reference_arm_names_what_it_ran_with_the_same_config(monkeypatch, capsy
     canned = {"value": 10.0, "unit": "tokens/s", "cores": 4, "cpu_model": "x", "kind": "port",
               "blocks_timed": 1, "extrapolated": True, "sample": "canned"}
     monkeypatch.setattr(bench, "cpu_baseline_step", lambda blocks=1: dict(canned))
-    for gpus, tp in ((1, False), (8, True)):
+    for gpus, mode in ((1, "single"), (8, "cfg_tp")):
         monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--gpus", str(gpus), "--steps", "20",
                                           "--warmup", "5"])
         bench.main()
         d = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
         assert d["impl"] == "reference" and d["steps"] == 1 and d["blocks_timed"] == 1 and d["extrapolated"]
-        assert d["config"] == bench.step_config(gpus, tp)
+        assert d["config"] == bench.step_config(gpus, mode)
         assert d["cpu_baseline"]["cpu_model"] == "x"

@@ -99,3 +99,58 @@ def test_cfg_tp_layout():
     for n in (1, 3):
         with pytest.raises(ValueError):
             ltx_b200.cfg_tp_layout(n, 0)
+
+
+class _FakeCtx:
+    """Records the communicator calls init_cfg_tensor_parallel makes."""
+    def __init__(self):
+        self.calls = []
+
+    def init_comm(self, cid, n, r):
+        self.calls.append(("tp", cid, n, r))
+
+    def init_cfg_comm(self, cid, cfg_rank):
+        self.calls.append(("cfg", cid, cfg_rank))
+
+
+def _cfg_layout_worker(rank, ws, port, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+    import ltx_b200
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=timedelta(seconds=60))
+    try:
+        ctx = _FakeCtx()
+        got = ltx_b200.init_cfg_tensor_parallel(ctx)
+        allc = [None] * ws
+        dist.all_gather_object(allc, (got, ctx.calls))
+        if rank == 0:
+            q.put(allc)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_cfg_tensor_parallel_groups_over_four_gloo_ranks():
+    """Four ranks: two tensor-parallel halves {0,1} and {2,3}, CFG pairs {0,2} and
+    {1,3}; every member of a group receives the same fresh id, the groups' ids differ."""
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_cfg_layout_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    allc = q.get(timeout=5)
+    assert [a[0] for a in allc] == [(0, 2, 0), (0, 2, 1), (1, 2, 0), (1, 2, 1)]
+    tp = [c[0] for c in (a[1] for a in allc)]
+    cfg = [c[1] for c in (a[1] for a in allc)]
+    assert [(t[0], t[2], t[3]) for t in tp] == [("tp", 2, 0), ("tp", 2, 1), ("tp", 2, 0), ("tp", 2, 1)]
+    assert tp[0][1] == tp[1][1] and tp[2][1] == tp[3][1] and tp[0][1] != tp[2][1]
+    assert [(c[0], c[2]) for c in cfg] == [("cfg", 0), ("cfg", 0), ("cfg", 1), ("cfg", 1)]
+    assert cfg[0][1] == cfg[2][1] and cfg[1][1] == cfg[3][1] and cfg[0][1] != cfg[1][1]
