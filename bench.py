@@ -585,6 +585,8 @@ def run_denoise_step(args, rank, ws, device):
         "clocks": clocks,
         "finite_output": ok,
     }
+    if ws > 1:
+        res["tp_exchange"] = ctx.tp_exchange()
     if ws == 1:
         res["step_fp8"] = run_fp8_step(args, ctx, device, bf16_ref, ms)
     ctx.close()
@@ -657,21 +659,32 @@ def run_replicas(args, rank, ws, device):
             "scaling": "weak", "parallelism": f"replicas x{ws}: one independent sequence per GPU"}
 
 
-def run_parallel_step(args, rank, ws, device, mode):
+def run_parallel_step(args, rank, ws, device, mode, exchange="peer"):
     """Config 4's one sequence on the N GPUs in another layout than the line's
-    headline ("tp" or "cfg_tp"), timed like it (max over ranks, a few steps)."""
+    headline ("tp" or "cfg_tp"), timed like it (max over ranks, a few steps).
+    exchange "nccl" sums the tensor-parallel projections with NCCL instead of
+    inside the GEMM over peer memory."""
     import torch
     import ltx_b200
     torch.cuda.set_device(device)
-    ctx = ltx_b200.Context(device)
-    init_step_mode(ctx, mode)
-    run = StepRunner(ctx, 7, 100)
-    steps = max(3, min(args.steps, 5))
-    ms, _ = run.timed(steps, 3, ws, device, clocks=False, label=f"denoise_timed_{mode}")
-    run.close()
-    ctx.close()
+    old = os.environ.get("LTX_TP_EXCHANGE")
+    os.environ["LTX_TP_EXCHANGE"] = exchange
+    try:
+        ctx = ltx_b200.Context(device)
+        init_step_mode(ctx, mode)
+        run = StepRunner(ctx, 7, 100)
+        steps = max(3, min(args.steps, 5))
+        ms, _ = run.timed(steps, 3, ws, device, clocks=False, label=f"denoise_timed_{mode}_{exchange}")
+        used = ctx.tp_exchange()
+        run.close()
+        ctx.close()
+    finally:
+        if old is None:
+            os.environ.pop("LTX_TP_EXCHANGE", None)
+        else:
+            os.environ["LTX_TP_EXCHANGE"] = old
     return {"value": T_TOTAL / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
-            "scaling": "strong", "parallelism": step_config(ws, mode)["parallelism"]}
+            "scaling": "strong", "parallelism": step_config(ws, mode)["parallelism"], "tp_exchange": used}
 
 
 def run_chunk_pipeline(args, rank, ws, device):
@@ -1141,8 +1154,14 @@ def main():
             other = "tp" if mode == "cfg_tp" else ("cfg_tp" if mode == "tp" and ws % 2 == 0 else None)
             if other:
                 o = run_parallel_step(args, rank, ws, local, other)
-                _log(f"{other}: {o['ms_per_step']:.1f} ms/step, {o['value']:.0f} tokens/s")
+                _log(f"{other}: {o['ms_per_step']:.1f} ms/step, {o['value']:.0f} tokens/s ({o['tp_exchange']})")
                 res[other] = o
+            # the tensor-parallel sums by NCCL allreduce instead of inside the GEMM
+            tp_mode = "tp" if mode in ("tp", "cfg_tp") else None
+            if tp_mode:
+                o = run_parallel_step(args, rank, ws, local, tp_mode, exchange="nccl")
+                _log(f"{tp_mode} (NCCL exchange): {o['ms_per_step']:.1f} ms/step, {o['value']:.0f} tokens/s")
+                res[f"{tp_mode}_nccl"] = o
             pl_args = argparse.Namespace(warmup=3)
             pl = run_chunk_pipeline(pl_args, rank, ws, local)
             _log(f"config-5 pipeline: {pl['ms_per_step'] / 1e3:.2f} s, {pl['speedup_vs_serial_chunks']:.2f}x the "

@@ -120,10 +120,20 @@ int ltx_ctx_init_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t nrank
  * tensor-parallel group of n/2.  No reference counterpart (the reference runs
  * one device). */
 int ltx_ctx_init_cfg_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t cfg_rank);
+/* How the tensor-parallel ranks sum each row-split projection, as set up by
+ * the first forward on the context: 0 not yet (or one rank), 1 inside the
+ * GEMM over NVLink peer memory (each rank's residual lives in memory the other
+ * ranks map through CUDA IPC; the GEMM's epilogue pushes partial products to
+ * the rows' owner, which adds them and writes the updated rows into every
+ * rank's copy), 2 NCCL allreduce (when a rank cannot map its peers, more than
+ * 8 ranks, or LTX_TP_EXCHANGE=nccl in every rank's environment). */
+int ltx_ctx_tp_exchange(const ltx_ctx *ctx);
 /* LTX_ERR_NCCL if the communicator has recorded an asynchronous error. */
 int ltx_ctx_comm_check(ltx_ctx *ctx);
 /* Aborts the communicator (after a peer failed); the context falls back to
- * one rank and models built on it can no longer run. */
+ * one rank and models built on it can no longer run.  (ltx_ctx_destroy of a
+ * context whose ranks share peer memory, ltx_ctx_tp_exchange() == 1, waits
+ * for every rank to destroy theirs; after a failure abort first.) */
 void ltx_ctx_abort_comm(ltx_ctx *ctx);
 
 /* ── device-side signalling ───────────────────────────────────────────────── */

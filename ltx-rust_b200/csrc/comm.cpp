@@ -9,8 +9,10 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "internal.hpp"
 
@@ -111,7 +113,153 @@ int cfg_allgather(ltx_ctx *ctx, float *buf, size_t count) {
     return LTX_OK;
 }
 
+// ── peer memory of the tensor-parallel ranks ────────────────────────────────
+
+namespace {
+
+size_t up256(size_t b) { return (b + 255) & ~size_t(255); }
+
+// Every rank's `n` bytes, in rank order, over the communicator (through the
+// context's scratch; returns once the bytes are on the host).
+int allgather_host_bytes(ltx_ctx *ctx, const void *mine, size_t n, std::vector<char> &all) {
+    const int R = ctx->tp_size;
+    if (int rc = ensure_scratch(ctx, up256(n * R))) return rc;
+    char *d = static_cast<char *>(ctx->scratch);
+    LTX_CUDA_TRY(ctx, cudaMemcpyAsync(d + (size_t)ctx->tp_rank * n, mine, n, cudaMemcpyHostToDevice, ctx->stream));
+    if (int rc = comm_after(ctx)) return rc;
+    ncclResult_t r = nccl().all_gather(d + (size_t)ctx->tp_rank * n, d, n, ncclUint8, static_cast<ncclComm_t>(ctx->comm),
+                                       ctx->comm_stream ? ctx->comm_stream : ctx->stream);
+    if (r != ncclSuccess) return fail(ctx, LTX_ERR_NCCL, "all-gather of %zu bytes: %s", n, nccl_str(r));
+    if (int rc = comm_join(ctx)) return rc;
+    all.resize(n * R);
+    LTX_CUDA_TRY(ctx, cudaMemcpyAsync(all.data(), d, n * R, cudaMemcpyDeviceToHost, ctx->stream));
+    LTX_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+    return LTX_OK;
+}
+
+void unmap_peers(TpPeerMem &pm) {
+    for (int r = 0; r < kMaxTpPeers; ++r) {
+        if (pm.peer[r] && pm.peer[r] != pm.base) cudaIpcCloseMemHandle(pm.peer[r]);
+        pm.peer[r] = nullptr;
+    }
+}
+
+}  // namespace
+
+void tp_peer_release(ltx_ctx *ctx) {
+    TpPeerMem &pm = ctx->pm;
+    unmap_peers(pm);
+    if (pm.base) cudaFree(pm.base);
+    const uint32_t epoch = pm.epoch;
+    pm = TpPeerMem{};
+    pm.epoch = epoch;
+}
+
+int tp_peer_ensure(ltx_ctx *ctx, int64_t rows, int64_t D, bool *on) {
+    *on = false;
+    TpPeerMem &pm = ctx->pm;
+    const int n = ctx->tp_size;
+    if (!ctx->comm || n < 2 || n > kMaxTpPeers || pm.state == -1) return LTX_OK;
+    if (pm.state == 1 && rows <= pm.rows_cap && D == pm.D) {
+        *on = true;
+        return LTX_OK;
+    }
+    // (Re)allocation, collective: every rank gets here at the same call.
+    // Nothing may still write into the old memory when it goes: each rank
+    // drains its work, then all unmap, then all free.
+    std::vector<char> sync;
+    const char one = 1;
+    if (pm.base) {
+        LTX_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+        if (int rc = allgather_host_bytes(ctx, &one, 1, sync)) return rc;
+        unmap_peers(pm);
+        if (int rc = allgather_host_bytes(ctx, &one, 1, sync)) return rc;
+        tp_peer_release(ctx);
+    }
+    const char *env = getenv("LTX_TP_EXCHANGE");
+    bool ok = !(env && strcmp(env, "nccl") == 0);
+    TpPeerMem nm;
+    nm.epoch = pm.epoch;
+    nm.rows_cap = rows;
+    nm.D = D;
+    nm.tiles_cap = ((rows + 127) / 128) * ((D + 127) / 128);   // any tile width >= 128
+    size_t off = up256((size_t)rows * D * 4);
+    nm.recv_off = off;
+    off += up256((size_t)(n - 1) * rows * D * 2);
+    nm.tstamp_off = off;
+    off += up256((size_t)(n - 1) * nm.tiles_cap * 4 * 4);
+    nm.dstamp_off = off;
+    off += 256;
+    nm.count_off = off;
+    off += 256;
+    nm.bytes = off;
+    cudaIpcMemHandle_t h{};
+    if (ok && cudaMalloc(reinterpret_cast<void **>(&nm.base), nm.bytes) != cudaSuccess) {
+        cudaGetLastError();
+        nm.base = nullptr;
+        ok = false;
+    }
+    if (ok && (cudaMemsetAsync(nm.base, 0, nm.bytes, ctx->stream) != cudaSuccess ||
+               cudaIpcGetMemHandle(&h, nm.base) != cudaSuccess)) {
+        cudaGetLastError();
+        ok = false;
+    }
+    std::vector<char> handles;
+    if (int rc = allgather_host_bytes(ctx, &h, sizeof h, handles)) {
+        if (nm.base) cudaFree(nm.base);
+        return rc;
+    }
+    nm.peer[ctx->tp_rank] = nm.base;
+    for (int r = 0; r < n && ok; ++r) {
+        if (r == ctx->tp_rank) continue;
+        cudaIpcMemHandle_t hr;
+        memcpy(&hr, handles.data() + (size_t)r * sizeof hr, sizeof hr);
+        void *mapped = nullptr;
+        if (cudaIpcOpenMemHandle(&mapped, hr, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+        } else {
+            nm.peer[r] = static_cast<char *>(mapped);
+        }
+    }
+    // the ranks vote: the fused path runs only if every rank mapped every peer
+    const char mine = ok ? 1 : 0;
+    std::vector<char> votes;
+    if (int rc = allgather_host_bytes(ctx, &mine, 1, votes)) {
+        unmap_peers(nm);
+        if (nm.base) cudaFree(nm.base);
+        return rc;
+    }
+    bool all_ok = true;
+    for (char v : votes) all_ok = all_ok && v == 1;
+    if (!all_ok) {
+        unmap_peers(nm);
+        if (nm.base) cudaFree(nm.base);
+        pm = TpPeerMem{};
+        pm.epoch = nm.epoch;
+        pm.state = -1;
+        return LTX_OK;
+    }
+    nm.state = 1;
+    pm = nm;
+    *on = true;
+    return LTX_OK;
+}
+
 void comm_release(ltx_ctx *ctx, bool abort) {
+    if (ctx->pm.base && ctx->comm && !abort) {
+        // Every rank stops using the others' memory before any of it goes:
+        // drain, unmap, then free (an exporter must not free before the
+        // importers have unmapped).
+        cudaStreamSynchronize(ctx->stream);
+        std::vector<char> sync;
+        const char one = 1;
+        if (allgather_host_bytes(ctx, &one, 1, sync) == LTX_OK) {
+            unmap_peers(ctx->pm);
+            allgather_host_bytes(ctx, &one, 1, sync);
+        }
+    }
+    tp_peer_release(ctx);
     if (ctx->cfg_comm) {
         if (abort)
             nccl().comm_abort(static_cast<ncclComm_t>(ctx->cfg_comm));
@@ -197,6 +345,11 @@ extern "C" int ltx_ctx_init_cfg_comm(ltx_ctx *ctx, const uint8_t *id, size_t len
     ctx->cfg_comm = comm;
     ctx->cfg_rank = cfg_rank;
     return LTX_OK;
+}
+
+extern "C" int ltx_ctx_tp_exchange(const ltx_ctx *ctx) {
+    if (!ctx || !ctx->comm || ctx->tp_size < 2) return 0;
+    return ctx->pm.state == 1 ? 1 : ctx->pm.state == -1 ? 2 : 0;
 }
 
 extern "C" int ltx_ctx_comm_check(ltx_ctx *ctx) {

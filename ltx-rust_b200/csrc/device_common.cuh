@@ -59,6 +59,19 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
+// System-scope acquire load / release store of a 32-bit stamp (a word another
+// GPU writes or reads over NVLink).
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Stamps hold launch epochs that only grow: "reached" tolerates wrap-around.
+__device__ __forceinline__ bool stamp_reached(uint32_t stamp, uint32_t epoch) { return (int32_t)(stamp - epoch) >= 0; }
+
 // ── shared-memory barriers (mbarrier) ───────────────────────────────────────
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

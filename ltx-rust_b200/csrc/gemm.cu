@@ -27,6 +27,7 @@ enum GemmEpilogue : int {
     EPI_GELU_BF16 = 1,   // out_bf16 = gelu_tanh(acc + bias)
     EPI_F32 = 2,         // out_f32 = acc + bias
     EPI_RESID = 3,       // x_f32 += (acc + bias) * gate[gidx[row]][col]   (gate optional)
+    EPI_TP_RESID = 4,    // EPI_RESID with acc summed over the tensor-parallel ranks (gemm_tp_resid)
 };
 
 struct GemmParams {
@@ -46,6 +47,14 @@ struct GemmParams {
                             // (A2 [M, 64*k2] . B2 [N, 64*k2]^T, same accumulator)
     const float *w_col_scale;   // FP8 only: per-column weight scale [N] (null = w_scale)
     int resid_tma;          // EPI_RESID: the residual moves by TMA through shared memory (tmX)
+    int m_rot;              // M-blocks are walked from this one on, wrapping (0: natural order)
+    // EPI_TP_RESID: this rank, the ranks, this launch's epoch and the peer
+    // memory (every rank's base as mapped here; the offsets of ltx::TpPeerMem)
+    int tp_rank, tp_size;
+    uint32_t epoch;
+    int64_t rows_cap, tiles_cap;
+    size_t recv_off, tstamp_off, dstamp_off, count_off;
+    char *peer[kMaxTpPeers];
 };
 
 namespace {
@@ -57,6 +66,8 @@ constexpr int kThreads = 192;
 // 128-byte swizzled, filled and drained by TMA.
 constexpr int kXChunkBytes = BM * 32 * 4;
 constexpr int kXStageBytes = 2 * kXChunkBytes;
+// EPI_TP_RESID staging: per epilogue warp, its 32 rows x 32 columns of f32.
+constexpr int kTpStageBytes = 4 * 32 * 32 * 4;
 
 // F8: e4m3 operands (kind::f8f6f4), 128 elements of K per stage; otherwise
 // bf16 (kind::f16), 64 per stage.  Either way a stage row is one 128-byte
@@ -82,14 +93,27 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 // Tile t -> (M-block, N-block): groups of group_m M-blocks, M fastest inside a
 // group, so the ~148 tiles in flight share a few W panels and one A panel, and
 // W is streamed from DRAM once per group.
-__device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, int group_m, int &mb, int &nb) {
+// m_rot rotates the M-block order (the tensor-parallel exchange walks the
+// other ranks' rows first and its own last).
+__device__ __forceinline__ void tile_coords(int t, int m_blocks, int n_blocks, int group_m, int m_rot, int &mb,
+                                            int &nb) {
     const int per_group = group_m * n_blocks;
     const int g = t / per_group;
     const int first_m = g * group_m;
     const int gm = min(group_m, m_blocks - first_m);
     const int r = t - g * per_group;
-    mb = first_m + r % gm;
+    mb = first_m + r % gm + m_rot;
+    if (mb >= m_blocks) mb -= m_blocks;
     nb = r / gm;
+}
+
+// Tensor-parallel row ownership: rank r owns M-blocks [lo(r), lo(r+1)),
+// lo(r) = r * m_blocks / n.
+__host__ __device__ __forceinline__ int tp_lo(int r, int m_blocks, int n) { return (int)((int64_t)r * m_blocks / n); }
+__device__ __forceinline__ int tp_owner(int mb, int m_blocks, int n) {
+    int o = 0;
+    while (o + 1 < n && mb >= tp_lo(o + 1, m_blocks, n)) ++o;
+    return o;
 }
 
 __device__ __forceinline__ void tma_store_2d(const void *tmap, const void *smem_src, int x, int y) {
@@ -108,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                 const __grid_constant__ CUtensorMap tmX, GemmParams p) {
     using C = GemmCfg<BN, F8>;
-    constexpr int XS = EPI == EPI_RESID ? kXStageBytes : 0;
+    constexpr int XS = EPI == EPI_RESID ? kXStageBytes : EPI == EPI_TP_RESID ? kTpStageBytes : 0;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *sA = smem;
@@ -163,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t it = 0;
             for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
                 int mb, nb;
-                tile_coords(t, m_blocks, n_blocks, p.group_m, mb, nb);
+                tile_coords(t, m_blocks, n_blocks, p.group_m, p.m_rot, mb, nb);
                 for (int kb = 0; kb < k_total; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     const uint32_t ph = (it / C::STAGES) & 1;
@@ -244,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t tile_i = 0;
         for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tile_i) {
             int mb, nb;
-            tile_coords(t, m_blocks, n_blocks, p.group_m, mb, nb);
+            tile_coords(t, m_blocks, n_blocks, p.group_m, p.m_rot, mb, nb);
             const uint32_t acc = tile_i & 1, aph = (tile_i >> 1) & 1;
             if (elected) load_chunk(u, mb, nb, 0);   // under this tile's mainloop
             __syncwarp();
@@ -324,13 +348,137 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t uu = u; uu < issued; ++uu) mbar_wait(&xfull[uu & 1], (uu >> 1) & 1, nullptr, 0, &quiet);
             bulk_wait_all();
         }
+    } else if (EPI == EPI_TP_RESID) {
+        // Row-split projection of a model split over n ranks, with the sum over
+        // ranks fused in: every rank computes a partial product of every tile.
+        // Rank r owns the rows of M-blocks [lo(r), lo(r+1)) and walks them last.
+        //  - a tile it does not own: the partial goes, as bf16, straight into
+        //    the owner's receive area over NVLink (its slot among the owner's
+        //    n-1 sources), then a per-warp stamp (this launch's epoch) tells the
+        //    owner those 32 rows have landed;
+        //  - a tile it owns: once the other ranks' stamps for these rows are in
+        //    (bounded wait), acc + their partials (in slot order) + bias, gated,
+        //    update the residual x here and in every other rank's x, so the
+        //    replicas stay identical bit for bit.
+        // Each warp moves its 32 rows through shared memory so that global
+        // and NVLink traffic is row-contiguous (8 lanes per 128-byte row).
+        const int quad = warp & 3;
+        float *stg = xs + quad * 32 * 32;
+        const int n = p.tp_size, me = p.tp_rank;
+        float *x_loc = static_cast<float *>(p.out);
+        uint32_t tile_i = 0;
+        for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tile_i) {
+            int mb, nb;
+            tile_coords(t, m_blocks, n_blocks, p.group_m, p.m_rot, mb, nb);
+            const uint32_t acc = tile_i & 1, aph = (tile_i >> 1) & 1;
+            if (!warp_wait(&tfull[acc], aph, p.timeout_flag, 104, &aborted)) break;
+            tc_fence_after();
+            const int owner = tp_owner(mb, m_blocks, n);
+            const int64_t tile = (int64_t)mb * n_blocks + nb;
+            const int row_base = mb * BM + quad * 32;
+            if (owner == me) {
+                bool ok = true;
+                const uint32_t *ts = reinterpret_cast<const uint32_t *>(p.peer[me] + p.tstamp_off);
+                const uint64_t t0 = global_ns();
+                for (int sl = 0; sl < n - 1 && ok; ++sl) {
+                    const uint32_t *f = ts + ((int64_t)sl * p.tiles_cap + tile) * 4 + quad;
+                    while (!stamp_reached(ld_acquire_sys(f), p.epoch)) {
+                        if (global_ns() - t0 > kWaitLimitNs) {
+                            ok = false;
+                            break;
+                        }
+                        __nanosleep(32);
+                    }
+                }
+                if (!__all_sync(0xffffffffu, ok)) {
+                    if (lane == 0) atomicExch(p.timeout_flag, 108);
+                    aborted = true;
+                    break;
+                }
+            }
+            const int slot = me < owner ? me : me - 1;   // this rank among the owner's sources
+            const int q = lane & 7;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + c * 32, r);
+                tmem_ld_wait();
+                // lane = row: 16-byte piece j of the row sits at j ^ (row % 8)
+                float4 *srow = reinterpret_cast<float4 *>(stg + lane * 32);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    srow[j ^ (lane & 7)] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                       __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+                __syncwarp();
+                const int col = nb * BN + c * 32 + 4 * q;
+#pragma unroll 2
+                for (int i = 0; i < 8; ++i) {
+                    const int rl = i * 4 + (lane >> 3);
+                    const int row = row_base + rl;
+                    float4 v = reinterpret_cast<const float4 *>(stg + rl * 32)[q ^ (rl & 7)];
+                    if (row >= p.M) continue;
+                    if (owner == me) {
+                        const __nv_bfloat16 *rcv = reinterpret_cast<const __nv_bfloat16 *>(p.peer[me] + p.recv_off);
+                        for (int sl = 0; sl < n - 1; ++sl) {
+                            const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(
+                                rcv + ((int64_t)sl * p.rows_cap + row) * p.N + col));
+                            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
+                            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
+                            v.x += a.x;
+                            v.y += a.y;
+                            v.z += b.x;
+                            v.w += b.y;
+                        }
+                        if (p.bias) {
+                            const float4 b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + col));
+                            v.x += b4.x;
+                            v.y += b4.y;
+                            v.z += b4.z;
+                            v.w += b4.w;
+                        }
+                        float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
+                        if (p.gate)
+                            g = __ldg(reinterpret_cast<const float4 *>(
+                                p.gate + (int64_t)(p.gate_idx ? p.gate_idx[row] : 0) * p.ld_gate + col));
+                        const int64_t xo = (int64_t)row * p.ldo + col;
+                        float4 x = *reinterpret_cast<const float4 *>(x_loc + xo);
+                        x.x += v.x * g.x;
+                        x.y += v.y * g.y;
+                        x.z += v.z * g.z;
+                        x.w += v.w * g.w;
+                        *reinterpret_cast<float4 *>(x_loc + xo) = x;
+                        for (int pr = 0; pr < n; ++pr)
+                            if (pr != me) *reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.peer[pr]) + xo) = x;
+                    } else {
+                        __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.peer[owner] + p.recv_off) +
+                                             ((int64_t)slot * p.rows_cap + row) * p.N + col;
+                        const __nv_bfloat162 lo2 = __floats2bfloat162_rn(v.x, v.y), hi2 = __floats2bfloat162_rn(v.z, v.w);
+                        *reinterpret_cast<uint2 *>(dst) =
+                            make_uint2(*reinterpret_cast<const uint32_t *>(&lo2), *reinterpret_cast<const uint32_t *>(&hi2));
+                    }
+                }
+                __syncwarp();
+            }
+            if (owner != me) {
+                __threadfence_system();   // these rows' pushes, before their stamp
+                __syncwarp();
+                if (lane == 0)
+                    st_release_sys(reinterpret_cast<uint32_t *>(p.peer[owner] + p.tstamp_off) +
+                                       ((int64_t)slot * p.tiles_cap + tile) * 4 + quad,
+                                   p.epoch);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        __threadfence_system();   // every push of this warp, before the CTA reports done
     } else {
         // Epilogue warps 2..5 own TMEM lane quadrant (warp % 4).
         const int quad = warp & 3;
         uint32_t tile_i = 0;
         for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x, ++tile_i) {
             int mb, nb;
-            tile_coords(t, m_blocks, n_blocks, p.group_m, mb, nb);
+            tile_coords(t, m_blocks, n_blocks, p.group_m, p.m_rot, mb, nb);
             const uint32_t acc = tile_i & 1, aph = (tile_i >> 1) & 1;
             // warp-uniform outcome: the tcgen05.ld below are warp-collective
             if (!warp_wait(&tfull[acc], aph, p.timeout_flag, 104, &aborted)) break;
@@ -446,6 +594,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem_base, C::TMEM_COLS);
     }
+    if constexpr (EPI == EPI_TP_RESID) {
+        // The last CTA to finish tells every other rank that all of this
+        // rank's pushes of this launch have landed (its done stamp there).
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            uint32_t *count = reinterpret_cast<uint32_t *>(p.peer[p.tp_rank] + p.count_off);
+            if (atomicAdd(count, 1u) + 1 == gridDim.x) {
+                atomicExch(count, 0u);
+                __threadfence_system();
+                for (int pr = 0; pr < p.tp_size; ++pr)
+                    if (pr != p.tp_rank)
+                        st_release_sys(reinterpret_cast<uint32_t *>(p.peer[pr] + p.dstamp_off) +
+                                           (p.tp_rank < pr ? p.tp_rank : p.tp_rank - 1),
+                                       p.epoch);
+            }
+        }
+    }
+}
+
+// Holds the stream until every other rank's fused projection of this epoch
+// has finished pushing into this rank's memory (bounded; code 109 on timeout).
+__global__ void tp_wait_kernel(const uint32_t *dstamp, int slots, uint32_t epoch, int *timeout_flag) {
+    const int s = threadIdx.x;
+    if (blockIdx.x != 0 || s >= slots) return;
+    const uint64_t t0 = global_ns();
+    while (!stamp_reached(ld_acquire_sys(dstamp + s), epoch)) {
+        if (global_ns() - t0 > kWaitLimitNs) {
+            atomicExch(timeout_flag, 109);
+            return;
+        }
+        __nanosleep(64);
+    }
 }
 
 // ── host side ────────────────────────────────────────────────────────────────
@@ -500,13 +680,29 @@ template <int BN, int EPI, bool F8>
 cudaError_t launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &ta2, const CUtensorMap &tb2,
                         const CUtensorMap &tx, const GemmParams &p, int sms, cudaStream_t st) {
     using C = GemmCfg<BN, F8>;
-    constexpr size_t smem = C::SMEM + (EPI == EPI_RESID ? kXStageBytes : 0);
+    constexpr size_t smem =
+        C::SMEM + (EPI == EPI_RESID ? kXStageBytes : EPI == EPI_TP_RESID ? kTpStageBytes : 0);
     static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
     auto k = gemm_kernel<BN, EPI, F8>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
     const int grid = std::min(tiles, sms);
+    if constexpr (EPI == EPI_TP_RESID) {
+        // Its CTAs wait on other GPUs' CTAs, which wait on this GPU's: every CTA
+        // must be resident at once, which a cooperative launch guarantees (or refuses).
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, k, ta, tb, ta2, tb2, tx, p);
+    }
     k<<<grid, kThreads, smem, st>>>(ta, tb, ta2, tb2, tx, p);
     return cudaGetLastError();
 }
@@ -587,6 +783,54 @@ int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, 
 }
 
 }  // namespace
+
+// x += (sum over ranks of A_r . W_r^T + bias) * gate on every rank of the
+// communicator, in one launch per rank plus a wait: the row-split projection
+// of a model split over ranks with the reduction and the replication of the
+// result fused into the GEMM's epilogue (EPI_TP_RESID), moving over NVLink
+// into the peer memory of ctx->pm (x is its residual).  Collective: every
+// rank enqueues the same sequence of these calls with the same shapes.
+int gemm_tp_resid(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
+                  int K, const float *bias, const float *gate, const int *gate_idx, int64_t ld_gate) {
+    TpPeerMem &pm = ctx->pm;
+    const int n = ctx->tp_size;
+    constexpr int BN = 256;
+    if (pm.state != 1 || n < 2 || n > kMaxTpPeers)
+        return fail(ctx, LTX_ERR_INVALID_ARG, "gemm_tp_resid: no peer memory");
+    if (!A || !W || M <= 0 || K <= 0 || N != pm.D || N % BN || M > pm.rows_cap)
+        return fail(ctx, LTX_ERR_SHAPE, "gemm_tp_resid: %d x %d x %d does not fit the peer memory (%lld x %lld)", M, N,
+                    K, (long long)pm.rows_cap, (long long)pm.D);
+    if (lda % 8 || ldw % 8 || lda < K || ldw < K || ((uintptr_t)A & 15) || ((uintptr_t)W & 15) ||
+        ((uintptr_t)bias & 15) || ((uintptr_t)gate & 15) || (gate && ld_gate % 4))
+        return fail(ctx, LTX_ERR_SHAPE, "gemm_tp_resid: operands need 16-byte aligned rows");
+    const int m_blocks = (M + BM - 1) / BM, n_blocks = N / BN;
+    if ((int64_t)m_blocks * n_blocks > pm.tiles_cap) return fail(ctx, LTX_ERR_SHAPE, "gemm_tp_resid: too many tiles");
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, A, M, K, lda, BM, 2) || !make_tmap_2d(&tb, W, N, K, ldw, BN, 2))
+        return fail(ctx, LTX_ERR_CUDA, "gemm_tp_resid: cuTensorMapEncodeTiled failed");
+    const size_t panel = (size_t)BM * K * 2, w_bytes = (size_t)N * K * 2;
+    const int group_m = w_bytes <= kGroupPanelBytes
+                            ? 1
+                            : (int)std::max<size_t>(1, std::min<size_t>((size_t)m_blocks, kGroupPanelBytes / panel));
+    GemmParams p{M, N, K, nullptr, 1.0f, bias, pm.base, pm.D, gate, gate_idx, ld_gate, ctx->timeout_flag, N, group_m};
+    p.m_rot = tp_lo(ctx->tp_rank + 1, m_blocks, n) % m_blocks;   // the other ranks' rows first, this rank's last
+    p.tp_rank = ctx->tp_rank;
+    p.tp_size = n;
+    p.epoch = ++pm.epoch;
+    p.rows_cap = pm.rows_cap;
+    p.tiles_cap = pm.tiles_cap;
+    p.recv_off = pm.recv_off;
+    p.tstamp_off = pm.tstamp_off;
+    p.dstamp_off = pm.dstamp_off;
+    p.count_off = pm.count_off;
+    for (int r = 0; r < n; ++r) p.peer[r] = pm.peer[r];
+    cudaError_t e = launch_gemm<BN, EPI_TP_RESID, false>(ta, tb, ta, tb, ta, p, ctx->sm_count, st);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "gemm_tp_resid launch");
+    tp_wait_kernel<<<1, 32, 0, st>>>(reinterpret_cast<const uint32_t *>(pm.base + pm.dstamp_off), n - 1, p.epoch,
+                                     ctx->timeout_flag);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? LTX_OK : cuda_fail(ctx, e, "tp wait launch");
+}
 
 // Enqueues out = epilogue(A[M,K] . W[N,K]^T).  A and W are bf16 row-major
 // with leading dimensions lda/ldw (elements, multiples of 8, 16-byte aligned bases).

@@ -12,6 +12,29 @@
 
 #include "../../include/ltx_b200.h"
 
+namespace ltx {
+// Tensor-parallel peer memory: one cudaMalloc per rank, mapped into every
+// other rank of the communicator (CUDA IPC over NVLink), laid out alike on
+// every rank so one offset names the same object everywhere:
+//   x      f32  [rows_cap][D]                 the replicated residual stream
+//   recv   bf16 [tp-1][rows_cap][D]           partial products other ranks pushed
+//   tstamp u32  [tp-1][tiles_cap][4]          per-tile, per-warp arrival stamps
+//   dstamp u32  [tp-1]                        "all my pushes landed" stamps
+//   count  u32                                CTAs of the current launch done
+// Stamps hold the launch epoch that wrote them; epochs only grow, so nothing
+// is ever reset between launches.
+constexpr int kMaxTpPeers = 8;
+struct TpPeerMem {
+    char *base = nullptr;            // this rank's allocation
+    size_t bytes = 0;
+    int64_t rows_cap = 0, D = 0, tiles_cap = 0;
+    size_t recv_off = 0, tstamp_off = 0, dstamp_off = 0, count_off = 0;
+    char *peer[kMaxTpPeers] = {};    // every rank's allocation as mapped here (own = base)
+    uint32_t epoch = 0;              // fused launches so far (the same sequence on every rank)
+    int state = 0;                   // 0 not set up, 1 on, -1 off (the NCCL path runs)
+};
+}  // namespace ltx
+
 struct ltx_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
@@ -47,6 +70,8 @@ struct ltx_ctx {
     // are all-gathered once per step.
     void *cfg_comm = nullptr;
     int cfg_rank = 0;
+    // Peer memory of the tensor-parallel ranks (fused projection + exchange).
+    ltx::TpPeerMem pm;
 };
 
 namespace ltx {
@@ -91,6 +116,14 @@ void comm_release(ltx_ctx *ctx, bool abort);
 // stream: rank r's block goes to buf + r*count; the rank's own block is
 // already in place.
 int cfg_allgather(ltx_ctx *ctx, float *buf, size_t count);
+
+// Tensor-parallel peer memory for `rows` x D residual rows (collective over
+// the communicator when it (re)allocates; every rank calls it with the same
+// shape).  *on = false when the fused path is off: one rank, more than
+// kMaxTpPeers ranks, LTX_TP_EXCHANGE=nccl in the environment, or a rank that
+// could not map its peers' memory (the ranks vote, so all agree).
+int tp_peer_ensure(ltx_ctx *ctx, int64_t rows, int64_t D, bool *on);
+void tp_peer_release(ltx_ctx *ctx);
 
 // Message of the last failed host-only call (no context) on this thread.
 inline std::string &host_error() {

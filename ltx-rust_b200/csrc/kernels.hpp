@@ -16,6 +16,11 @@ int dequant_merge(ltx_ctx *ctx, cudaStream_t stream, const void *w, int w_dt, in
 int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
               int K, int epi, const float *bias, void *out, int64_t ldo, const float *gate, const int *gate_idx,
               int64_t ld_gate, int f16_from_col = 1 << 30);
+// Row-split projection of a model split over ranks, the sum over ranks and
+// the residual update fused (x = ctx->pm's residual; N = pm.D, a multiple of
+// 256): x += (sum_r A_r . W_r^T + bias) * gate[gate_idx[row]] on every rank.
+int gemm_tp_resid(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
+                  int K, const float *bias, const float *gate, const int *gate_idx, int64_t ld_gate);
 // A bf16 block appended to an e4m3 GEMM's K loop, accumulated into the same
 // TMEM accumulator before the scales: acc += A2[M, k2] . B2[N, k2]^T
 // (k2 a multiple of 64; leading dimensions in elements).

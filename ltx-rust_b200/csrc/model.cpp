@@ -867,6 +867,11 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
     const int64_t rows = (int64_t)B * T, crow = (int64_t)B * S;
     cudaStream_t st = ctx->stream;
     const int sms = ctx->sm_count;
+    // Split over ranks: the residual lives in the ranks' shared peer memory,
+    // where the fused row-split projections update every rank's copy.  Set up
+    // first (it is collective and uses the scratch buffer).
+    bool peer_x = false;
+    if (m->tp > 1 && !seam) TRY(tp_peer_ensure(ctx, rows, D, &peer_x));
     std::vector<float> uniq;
     std::vector<int> idx;
     const int U = seam ? 1 : ts_dev ? kMaxDistinctTs : unique_timesteps(ts_host, uniq, idx);
@@ -885,6 +890,7 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         TRY(ensure_work(ctx, sizing.bytes));
         w = carve_work(static_cast<char *>(ctx->work), c, rows, crow, U, c.layers, m->tp, m->lora_r64);
     }
+    if (peer_x) w.x = reinterpret_cast<float *>(ctx->pm.base);
     if (work_out) *work_out = w;
     if (!seam && ts_dev) {
         CU(timestep_set(st, ts_dev, rows, U, w.ts_u, w.idx, ctx->timeout_flag, kErrTooManyTimesteps));
@@ -946,16 +952,22 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         return LTX_OK;
     };
     // x += (A . W^T + bias) * gate: fused into the GEMM epilogue on one GPU;
-    // split over ranks, the partial products are summed first.  The rows go
-    // in kSlabs token slabs: slab i's sum-allreduce and residual add run on
-    // the communicator's stream while the GEMM computes slab i+1 on SMs left
-    // free for the collective; the context stream joins after the last slab.
+    // split over ranks, the partial products are summed first: inside the
+    // GEMM over NVLink peer memory (gemm_tp_resid) when the ranks share it,
+    // else by NCCL.  The NCCL path runs the rows in kSlabs token slabs: slab
+    // i's sum-allreduce and residual add run on the communicator's stream
+    // while the GEMM computes slab i+1 on SMs left free for the collective;
+    // the context stream joins after the last slab.
     auto project_residual = [&](const __nv_bfloat16 *a, int64_t lda, const __nv_bfloat16 *wt, int64_t kdim,
                                 const float *bias, const float *gate) -> int {
         const int *gidx = gate ? w.idx : nullptr;
         if (tp == 1)
             return gemm_bf16(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, LTX_EPI_RESID, bias, w.x, D, gate,
                              gidx, K * D);
+        // the sum over ranks fused into the GEMM, over NVLink peer memory
+        if (peer_x && D % 256 == 0)
+            return gemm_tp_resid(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, bias, gate, gidx, K * D);
+        // otherwise NCCL:
         constexpr int kSlabs = 4, kCommSms = 16;
         const int64_t slab = rows >= 16 * 128 ? (rows + kSlabs * 128 - 1) / (kSlabs * 128) * 128 : rows;
         struct GemmSmsGuard {   // restores the GEMM grid on every exit

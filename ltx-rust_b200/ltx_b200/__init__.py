@@ -112,6 +112,7 @@ def lib() -> ctypes.CDLL:
         "ltx_ctx_init_comm": (I, [V, P, ctypes.c_size_t, ctypes.c_int32, ctypes.c_int32]),
         "ltx_ctx_comm_check": (I, [V]),
         "ltx_ctx_init_cfg_comm": (I, [V, P, ctypes.c_size_t, ctypes.c_int32]),
+        "ltx_ctx_tp_exchange": (I, [V]),
         "ltx_ctx_abort_comm": (None, [V]),
         "ltx_wait_flag": (I, [V, P, ctypes.c_int32, ctypes.c_uint32]),
         "ltx_set_flag": (I, [V, P, ctypes.c_int32]),
@@ -156,6 +157,10 @@ class Context:
         """Binds this context to rank `rank` of a tensor-parallel group (collective)."""
         buf = ctypes.create_string_buffer(bytes(comm_id), COMM_ID_BYTES)
         self.check(lib().ltx_ctx_init_comm(self.h, buf, COMM_ID_BYTES, nranks, rank), "ltx_ctx_init_comm")
+
+    def tp_exchange(self) -> str:
+        """How tensor-parallel sums run on this context (ltx_ctx_tp_exchange)."""
+        return {0: "none", 1: "peer", 2: "nccl"}[lib().ltx_ctx_tp_exchange(self.h)]
 
     def init_cfg_comm(self, comm_id: bytes, cfg_rank: int):
         """Makes this context half of a CFG-parallel pair (ltx_ctx_init_cfg_comm)."""

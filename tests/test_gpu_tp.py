@@ -1,5 +1,7 @@
-"""Tensor-parallel model (heads and FFN units split over two GPUs, allreduce
-after each row-split projection) against the same model on one GPU.
+"""Tensor-parallel model (heads and FFN units split over two GPUs, a sum over
+ranks after each row-split projection) against the same model on one GPU.
+The sum runs both ways the library has: fused into the GEMM over NVLink peer
+memory (the default) and as an NCCL allreduce (LTX_TP_EXCHANGE=nccl).
 
 Needs two GPUs; each rank is a spawned process.  The whole model on one GPU
 is the reference: same seed, same synthetic FP8 + LoRA weights (every shard
@@ -27,12 +29,14 @@ def _cfg(heads, head_dim, layers):
     return small_config(heads=heads, head_dim=head_dim, layers=layers)
 
 
-def _worker(rank, ws, port, cfg, T_frames, q):
+def _worker(rank, ws, port, cfg, T_frames, q, exchange="peer"):
     import torch.distributed as dist
     from datetime import timedelta
     import ltx_b200
     from oracle import sampler
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    if exchange == "nccl":
+        os.environ["LTX_TP_EXCHANGE"] = "nccl"
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=timedelta(seconds=90))
     try:
@@ -60,6 +64,7 @@ def _worker(rank, ws, port, cfg, T_frames, q):
         model.denoise_step(lat_s, dev(clean), dev(mask), dev(pos), dev(ctxt[0]), dev(unc), 0.8, 0.6, 3.0, 0.7)
         ctx.synchronize()
         ctx.comm_check()
+        used = ctx.tp_exchange()
         got_f, got_s = out.cpu().numpy(), lat_s.cpu().numpy()
         outs = [None] * ws
         dist.all_gather_object(outs, (got_f, got_s))
@@ -74,7 +79,7 @@ def _worker(rank, ws, port, cfg, T_frames, q):
             ctx1.synchronize()
             ref_f, ref_s = ref.cpu().numpy(), lat1.cpu().numpy()
             same_ranks = all(np.array_equal(o[0], outs[0][0]) and np.array_equal(o[1], outs[0][1]) for o in outs)
-            q.put((same_ranks, _rel_l2(got_f, ref_f), _rel_l2(got_s - lat[0], ref_s - lat[0])))
+            q.put((same_ranks, used, _rel_l2(got_f, ref_f), _rel_l2(got_s - lat[0], ref_s - lat[0])))
             m1.close()
             ctx1.close()
         model.close()
@@ -83,8 +88,9 @@ def _worker(rank, ws, port, cfg, T_frames, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("heads,head_dim,layers,frames", [(4, 128, 2, 2), (32, 128, 1, 1)])
-def test_tensor_parallel_two_gpus_matches_one(heads, head_dim, layers, frames):
+@pytest.mark.parametrize("heads,head_dim,layers,frames,exchange",
+                         [(4, 128, 2, 2, "peer"), (32, 128, 1, 1, "peer"), (4, 128, 2, 2, "nccl")])
+def test_tensor_parallel_two_gpus_matches_one(heads, head_dim, layers, frames, exchange):
     import socket
     import torch.multiprocessing as mp
     cfg = _cfg(heads, head_dim, layers)
@@ -93,14 +99,16 @@ def test_tensor_parallel_two_gpus_matches_one(heads, head_dim, layers, frames):
         port = s.getsockname()[1]
     mctx = mp.get_context("spawn")
     q = mctx.Queue()
-    procs = [mctx.Process(target=_worker, args=(r, 2, port, cfg, frames, q)) for r in range(2)]
+    procs = [mctx.Process(target=_worker, args=(r, 2, port, cfg, frames, q, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    same, err_f, err_s = q.get(timeout=5)
-    print(f"\nTP x2 ({heads} heads, {layers} layers): forward rel-L2 {err_f:.2e}, step update rel-L2 {err_s:.2e}")
+    same, used, err_f, err_s = q.get(timeout=5)
+    print(f"\nTP x2 ({heads} heads, {layers} layers, {used}): forward rel-L2 {err_f:.2e}, "
+          f"step update rel-L2 {err_s:.2e}")
+    assert used == exchange
     assert same, "ranks disagree on the replicated output"
     assert err_f < 1e-2 and err_s < 1e-2
 
