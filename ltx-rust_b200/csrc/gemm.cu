@@ -398,6 +398,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const int slot = me < owner ? me : me - 1;   // this rank among the owner's sources
             const int q = lane & 7;
+            // owned rows: lane l holds the gate table row of this warp's row l
+            const int gidx_lane =
+                owner == me && p.gate && p.gate_idx && row_base + lane < p.M ? p.gate_idx[row_base + lane] : 0;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
@@ -411,49 +414,81 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                        __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
                 __syncwarp();
                 const int col = nb * BN + c * 32 + 4 * q;
-#pragma unroll 2
+                // lane -> rows i*4 + lane/8 (i < 8) of this warp's 32, columns col..col+3
+                float4 v[8];
+#pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int rl = i * 4 + (lane >> 3);
-                    const int row = row_base + rl;
-                    float4 v = reinterpret_cast<const float4 *>(stg + rl * 32)[q ^ (rl & 7)];
-                    if (row >= p.M) continue;
-                    if (owner == me) {
-                        const __nv_bfloat16 *rcv = reinterpret_cast<const __nv_bfloat16 *>(p.peer[me] + p.recv_off);
-                        for (int sl = 0; sl < n - 1; ++sl) {
-                            const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(
-                                rcv + ((int64_t)sl * p.rows_cap + row) * p.N + col));
-                            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.x));
-                            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u.y));
-                            v.x += a.x;
-                            v.y += a.y;
-                            v.z += b.x;
-                            v.w += b.y;
+                    v[i] = reinterpret_cast<const float4 *>(stg + rl * 32)[q ^ (rl & 7)];
+                }
+                if (owner == me) {
+                    // every load of the chunk is issued before the first use
+                    float4 xv[8], g[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int rl = i * 4 + (lane >> 3);
+                        const int row = row_base + rl;
+                        const int gi = __shfl_sync(0xffffffffu, gidx_lane, rl);
+                        xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        g[i] = make_float4(1.f, 1.f, 1.f, 1.f);
+                        if (row < p.M) {
+                            xv[i] = *reinterpret_cast<const float4 *>(x_loc + (int64_t)row * p.ldo + col);
+                            if (p.gate)
+                                g[i] = __ldg(reinterpret_cast<const float4 *>(p.gate + (int64_t)gi * p.ld_gate + col));
                         }
+                    }
+                    const __nv_bfloat16 *rcv = reinterpret_cast<const __nv_bfloat16 *>(p.peer[me] + p.recv_off);
+                    for (int sl = 0; sl < n - 1; ++sl) {   // partials added in slot (rank) order
+                        uint2 u[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int row = row_base + i * 4 + (lane >> 3);
+                            u[i] = row < p.M ? __ldcg(reinterpret_cast<const uint2 *>(
+                                                   rcv + ((int64_t)sl * p.rows_cap + row) * p.N + col))
+                                             : make_uint2(0u, 0u);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u[i].x));
+                            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&u[i].y));
+                            v[i].x += a.x;
+                            v[i].y += a.y;
+                            v[i].z += b.x;
+                            v[i].w += b.y;
+                        }
+                    }
+                    const float4 b4 =
+                        p.bias ? __ldg(reinterpret_cast<const float4 *>(p.bias + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int row = row_base + i * 4 + (lane >> 3);
+                        if (row >= p.M) continue;
                         if (p.bias) {
-                            const float4 b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + col));
-                            v.x += b4.x;
-                            v.y += b4.y;
-                            v.z += b4.z;
-                            v.w += b4.w;
+                            v[i].x += b4.x;
+                            v[i].y += b4.y;
+                            v[i].z += b4.z;
+                            v[i].w += b4.w;
                         }
-                        float4 g = make_float4(1.f, 1.f, 1.f, 1.f);
-                        if (p.gate)
-                            g = __ldg(reinterpret_cast<const float4 *>(
-                                p.gate + (int64_t)(p.gate_idx ? p.gate_idx[row] : 0) * p.ld_gate + col));
+                        float4 x = xv[i];
+                        x.x += v[i].x * g[i].x;
+                        x.y += v[i].y * g[i].y;
+                        x.z += v[i].z * g[i].z;
+                        x.w += v[i].w * g[i].w;
                         const int64_t xo = (int64_t)row * p.ldo + col;
-                        float4 x = *reinterpret_cast<const float4 *>(x_loc + xo);
-                        x.x += v.x * g.x;
-                        x.y += v.y * g.y;
-                        x.z += v.z * g.z;
-                        x.w += v.w * g.w;
                         *reinterpret_cast<float4 *>(x_loc + xo) = x;
                         for (int pr = 0; pr < n; ++pr)
                             if (pr != me) *reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.peer[pr]) + xo) = x;
-                    } else {
-                        __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(p.peer[owner] + p.recv_off) +
-                                             ((int64_t)slot * p.rows_cap + row) * p.N + col;
-                        const __nv_bfloat162 lo2 = __floats2bfloat162_rn(v.x, v.y), hi2 = __floats2bfloat162_rn(v.z, v.w);
-                        *reinterpret_cast<uint2 *>(dst) =
+                    }
+                } else {
+                    __nv_bfloat16 *dst0 = reinterpret_cast<__nv_bfloat16 *>(p.peer[owner] + p.recv_off) +
+                                          (int64_t)slot * p.rows_cap * p.N + col;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int row = row_base + i * 4 + (lane >> 3);
+                        if (row >= p.M) continue;
+                        const __nv_bfloat162 lo2 = __floats2bfloat162_rn(v[i].x, v[i].y),
+                                             hi2 = __floats2bfloat162_rn(v[i].z, v[i].w);
+                        *reinterpret_cast<uint2 *>(dst0 + (int64_t)row * p.N) =
                             make_uint2(*reinterpret_cast<const uint32_t *>(&lo2), *reinterpret_cast<const uint32_t *>(&hi2));
                     }
                 }

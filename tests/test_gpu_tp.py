@@ -195,3 +195,85 @@ def test_cfg_pair_two_gpus_matches_batch2():
     print(f"\nCFG pair x2: step update rel-L2 {err_step:.2e}, 3-step loop rel-L2 {err_loop:.2e}, bit-identical {bits}")
     assert same, "the pair's ranks disagree on the latent"
     assert err_step < 1e-5 and err_loop < 1e-5
+
+
+def _cfg_tp_worker(rank, ws, port, cfg, q):
+    """CFG-parallel x tensor-parallel on four GPUs: ranks {0,1} run the conditional
+    pass split over two GPUs, {2,3} the unconditional one; the pairs {0,2}, {1,3}
+    all-gather the velocities."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    import ltx_b200
+    from oracle import sampler
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=timedelta(seconds=90))
+    try:
+        ctx = ltx_b200.Context(rank)
+        layout = ltx_b200.init_cfg_tensor_parallel(ctx)
+        cj = json.dumps(cfg)
+        model = ltx_b200.VideoTransformer.init_random(ctx, cj, seed=29, lora_rank=8, lora_strength=0.8)
+        F, Hh, W, S = 2, 8, 8, 40
+        rng = np.random.default_rng(8)
+        Tt = F * Hh * W
+        T = 2 * Tt
+        C, Dc = cfg["in_channels"], cfg["cross_attention_dim"]
+        lat = rng.standard_normal((T, C)).astype(np.float32)
+        pos = np.concatenate([sampler.target_positions(F, Hh, W), sampler.reference_positions(F, Hh, W)], axis=2)
+        ctxt = rng.standard_normal((S, Dc)).astype(np.float32)
+        unc = rng.standard_normal((S, Dc)).astype(np.float32)
+        clean = np.concatenate([np.zeros((Tt, C), np.float32), rng.standard_normal((Tt, C)).astype(np.float32)])
+        mask = np.concatenate([np.ones(Tt, np.float32), np.zeros(Tt, np.float32)])
+        sig = np.array([1.0, 0.8, 0.5], np.float32)
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+        def run(m):
+            loop = dev(lat)
+            m.denoise_loop(loop, dev(clean), dev(mask), dev(pos), dev(ctxt), dev(unc), sig, 3.0, 0.7)
+            return loop
+
+        got = run(model)
+        ctx.synchronize()
+        ctx.comm_check()
+        used = ctx.tp_exchange()
+        got = got.cpu().numpy()
+        outs = [None] * ws
+        dist.all_gather_object(outs, (layout, used, got))
+        if rank == 0:
+            ctx1 = ltx_b200.Context(0)
+            m1 = ltx_b200.VideoTransformer.init_random(ctx1, cj, seed=29, lora_rank=8, lora_strength=0.8)
+            ref = run(m1)
+            ctx1.synchronize()
+            ref = ref.cpu().numpy()
+            same = all(np.array_equal(o[2], outs[0][2]) for o in outs)
+            q.put(([o[0] for o in outs], [o[1] for o in outs], same, _rel_l2(got - lat, ref - lat)))
+            m1.close()
+            ctx1.close()
+        model.close()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
+def test_cfg_x_tensor_parallel_four_gpus_matches_one():
+    import socket
+    import torch.multiprocessing as mp
+    cfg = _cfg(4, 128, 2)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mctx = mp.get_context("spawn")
+    q = mctx.Queue()
+    procs = [mctx.Process(target=_cfg_tp_worker, args=(r, 4, port, cfg, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    layouts, used, same, err = q.get(timeout=5)
+    print(f"\nCFG x TP (2 x 2): 2-step loop update rel-L2 {err:.2e}, exchanges {used}")
+    assert layouts == [(0, 2, 0), (0, 2, 1), (1, 2, 0), (1, 2, 1)]
+    assert used == ["peer"] * 4
+    assert same, "the four ranks disagree on the latent"
+    assert err < 1e-2
