@@ -150,9 +150,11 @@ void tp_peer_release(ltx_ctx *ctx) {
     TpPeerMem &pm = ctx->pm;
     unmap_peers(pm);
     if (pm.base) cudaFree(pm.base);
-    const uint32_t epoch = pm.epoch;
+    const uint32_t epoch = pm.epoch, gepoch = pm.gepoch, bepoch = pm.bepoch;
     pm = TpPeerMem{};
     pm.epoch = epoch;
+    pm.gepoch = gepoch;
+    pm.bepoch = bepoch;
 }
 
 int tp_peer_ensure(ltx_ctx *ctx, int64_t rows, int64_t D, bool *on) {
@@ -180,6 +182,8 @@ int tp_peer_ensure(ltx_ctx *ctx, int64_t rows, int64_t D, bool *on) {
     bool ok = !(env && strcmp(env, "nccl") == 0);
     TpPeerMem nm;
     nm.epoch = pm.epoch;
+    nm.gepoch = pm.gepoch;
+    nm.bepoch = pm.bepoch;
     nm.rows_cap = rows;
     nm.D = D;
     nm.tiles_cap = ((rows + 127) / 128) * ((D + 127) / 128);   // any tile width >= 128
@@ -192,6 +196,13 @@ int tp_peer_ensure(ltx_ctx *ctx, int64_t rows, int64_t D, bool *on) {
     off += 256;
     nm.count_off = off;
     off += 256;
+    nm.mblocks_cap = (rows + 127) / 128;
+    nm.xn_off = off;
+    off += up256((size_t)rows * D * 2);
+    nm.gstamp_off = off;
+    off += up256((size_t)(n - 1) * nm.mblocks_cap * 4);
+    nm.gcount_off = off;
+    off += up256((size_t)nm.mblocks_cap * 4);
     nm.bytes = off;
     cudaIpcMemHandle_t h{};
     if (ok && cudaMalloc(reinterpret_cast<void **>(&nm.base), nm.bytes) != cudaSuccess) {
@@ -237,6 +248,8 @@ int tp_peer_ensure(ltx_ctx *ctx, int64_t rows, int64_t D, bool *on) {
         if (nm.base) cudaFree(nm.base);
         pm = TpPeerMem{};
         pm.epoch = nm.epoch;
+        pm.gepoch = nm.gepoch;
+        pm.bepoch = nm.bepoch;
         pm.state = -1;
         return LTX_OK;
     }

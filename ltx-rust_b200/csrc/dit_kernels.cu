@@ -502,10 +502,14 @@ __device__ __forceinline__ float warp_sum_all(float v) {
 // owns float4 columns w*D/SPLIT + l*4 + 128*i): the row stays in registers
 // with a per-thread state small enough for 2 blocks (16 warps) per SM.  The partial sums
 // meet in shared memory.  Same modes and results as norm_mod_kernel.
-template <int SPLIT>
+// PUSH (a model split over ranks, sequence-parallel norms): every row also
+// goes into every other rank's copy of `out`, and the last block of each
+// 128-row M-block stamps that M-block on every other rank.
+template <int SPLIT, bool PUSH = false>
 __global__ void __launch_bounds__(256) norm_mod_split_kernel(const float *x, int64_t ldx, int rows, float eps, int mode,
                                                              const float *tab, int tab_coeff, const int *idx,
-                                                             int k_shift, __nv_bfloat16 *out, int64_t ldo) {
+                                                             int k_shift, __nv_bfloat16 *out, int64_t ldo,
+                                                             TpNormPush push = TpNormPush{}) {
     constexpr int D = 4096, NV = D / 128 / SPLIT, RPB = 8 / SPLIT;   // float4 per lane, rows per block
     __shared__ float part[2][8];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -547,10 +551,10 @@ __global__ void __launch_bounds__(256) norm_mod_split_kernel(const float *x, int
     float tot = 0.f;
 #pragma unroll
     for (int q = 0; q < SPLIT; ++q) tot += part[1][rib * SPLIT + q];
-    if (!live) return;
+    if (!PUSH && !live) return;
     const float denom = sqrtf(tot / (float)D + eps);
     const float4 *sh = nullptr, *sc = nullptr;
-    if (mode != 0) {
+    if (mode != 0 && live) {
         const int u = idx ? idx[row] : 0;
         const float *shift = tab + ((int64_t)u * tab_coeff + k_shift) * D + col0;
         sh = reinterpret_cast<const float4 *>(shift);
@@ -559,6 +563,7 @@ __global__ void __launch_bounds__(256) norm_mod_split_kernel(const float *x, int
     uint2 *o = reinterpret_cast<uint2 *>(out + (int64_t)row * ldo + col0);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
+        if (!live) break;   // PUSH only (a dead row's block still reaches the report below)
         float a = v[i].x / denom, b = v[i].y / denom, c = v[i].z / denom, d = v[i].w / denom;
         if (mode != 0) {
             const float4 s4 = __ldg(sc + lane + 32 * i), h4 = __ldg(sh + lane + 32 * i);
@@ -568,7 +573,34 @@ __global__ void __launch_bounds__(256) norm_mod_split_kernel(const float *x, int
             d = d * (s4.w + 1.0f) + h4.w;
         }
         __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
-        o[lane + 32 * i] = make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+        const uint2 val = make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+        o[lane + 32 * i] = val;
+        if constexpr (PUSH) {
+            for (int q = 0; q < push.n; ++q)
+                if (q != push.me)
+                    reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(push.peer_out[q]) + (int64_t)row * ldo +
+                                              col0)[lane + 32 * i] = val;
+        }
+    }
+    if constexpr (PUSH) {
+        // Rows of one 128-row M-block: the launch's rows start at a multiple
+        // of 128 and a block holds RPB consecutive rows, so no block spans two.
+        __threadfence_system();   // this thread's pushes, before the block reports
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const int r_first = blockIdx.x * RPB;
+            const int mb = (push.row0 + r_first) / 128;
+            const int in_mb = min(128, push.row0 + rows - mb * 128);
+            const unsigned blocks_in_mb = (unsigned)((in_mb + RPB - 1) / RPB);
+            if (atomicAdd(push.count + mb, 1u) + 1 == blocks_in_mb) {
+                atomicExch(push.count + mb, 0u);
+                __threadfence_system();
+                for (int q = 0; q < push.n; ++q)
+                    if (q != push.me)
+                        st_release_sys(push.peer_stamp[q] + (int64_t)(push.me < q ? push.me : push.me - 1) * push.mcap + mb,
+                                       push.epoch);
+            }
+        }
     }
 }
 
@@ -708,6 +740,18 @@ cudaError_t norm_mod(cudaStream_t st, const float *x, int64_t ldx, int rows, int
         return cudaGetLastError();
     }
     norm_mod_kernel<<<rows, 256, 0, st>>>(x, ldx, rows, D, eps, mode, tab, tab_coeff, idx, k_shift, out, ldo);
+    return cudaGetLastError();
+}
+
+cudaError_t norm_mod_push(cudaStream_t st, const float *x, int64_t ldx, int rows, float eps, int mode, const float *tab,
+                          int tab_coeff, const int *idx, int k_shift, __nv_bfloat16 *out, int64_t ldo,
+                          const TpNormPush &push) {
+    if (rows <= 0) return cudaSuccess;
+    if (push.row0 % 128 || ldx % 4 || ldo % 4 || ((uintptr_t)x & 15) || ((uintptr_t)out & 7) ||
+        (tab && ((uintptr_t)tab & 15)))
+        return cudaErrorInvalidValue;
+    norm_mod_split_kernel<2, true><<<(rows + 3) / 4, 256, 0, st>>>(x, ldx, rows, eps, mode, tab, tab_coeff, idx, k_shift,
+                                                                    out, ldo, push);
     return cudaGetLastError();
 }
 

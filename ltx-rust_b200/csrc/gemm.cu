@@ -48,6 +48,12 @@ struct GemmParams {
     const float *w_col_scale;   // FP8 only: per-column weight scale [N] (null = w_scale)
     int resid_tma;          // EPI_RESID: the residual moves by TMA through shared memory (tmX)
     int m_rot;              // M-blocks are walked from this one on, wrapping (0: natural order)
+    // A rows gathered from other ranks (TpGather): the producer waits for the
+    // owner's stamp of an M-block before loading its A tiles (ag_stamp null: no wait)
+    const uint32_t *ag_stamp;
+    uint32_t ag_epoch;
+    int ag_n, ag_me, ag_mcap;
+    int tp_bcast;           // EPI_TP_RESID: 1 = write finished rows into every other rank's x too
     // EPI_TP_RESID: this rank, the ranks, this launch's epoch and the peer
     // memory (every rank's base as mapped here; the offsets of ltx::TpPeerMem)
     int tp_rank, tp_size;
@@ -185,9 +191,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_prefetch_desc(&tmB2);
             }
             uint32_t it = 0;
+            int ag_ready = -1;   // the last M-block whose gathered rows are known to be here
             for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
                 int mb, nb;
                 tile_coords(t, m_blocks, n_blocks, p.group_m, p.m_rot, mb, nb);
+                if (p.ag_stamp && mb != ag_ready) {
+                    const int o = tp_owner(mb, m_blocks, p.ag_n);
+                    if (o != p.ag_me) {
+                        const uint32_t *f = p.ag_stamp + (int64_t)(o < p.ag_me ? o : o - 1) * p.ag_mcap + mb;
+                        const uint64_t t0 = global_ns();
+                        while (!stamp_reached(ld_acquire_sys(f), p.ag_epoch)) {
+                            if (global_ns() - t0 > kWaitLimitNs) {
+                                atomicExch(p.timeout_flag, 110);
+                                aborted = true;
+                                break;
+                            }
+                            __nanosleep(64);
+                        }
+                        if (aborted) break;
+                        // rows another GPU wrote (generic proxy), read next by TMA (async proxy)
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                    }
+                    ag_ready = mb;
+                }
                 for (int kb = 0; kb < k_total; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     const uint32_t ph = (it / C::STAGES) & 1;
@@ -476,8 +502,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         x.w += v[i].w * g[i].w;
                         const int64_t xo = (int64_t)row * p.ldo + col;
                         *reinterpret_cast<float4 *>(x_loc + xo) = x;
-                        for (int pr = 0; pr < n; ++pr)
-                            if (pr != me) *reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.peer[pr]) + xo) = x;
+                        if (p.tp_bcast)
+                            for (int pr = 0; pr < n; ++pr)
+                                if (pr != me) *reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.peer[pr]) + xo) = x;
                     }
                 } else {
                     __nv_bfloat16 *dst0 = reinterpret_cast<__nv_bfloat16 *>(p.peer[owner] + p.recv_off) +
@@ -648,6 +675,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Rank barrier on the stream: stamps `epoch` into every other rank's slot for
+// this rank, then waits (bounded; code 111) for every other rank's stamp here.
+struct TpBarrierArgs {
+    uint32_t *peer_bstamp[kMaxTpPeers];   // every rank's barrier stamps [n-1]
+    int n, me;
+    uint32_t epoch;
+    int *timeout_flag;
+};
+__global__ void tp_barrier_kernel(TpBarrierArgs a) {
+    const int s = threadIdx.x;
+    if (blockIdx.x != 0) return;
+    if (s < a.n && s != a.me) st_release_sys(a.peer_bstamp[s] + (a.me < s ? a.me : a.me - 1), a.epoch);
+    if (s >= a.n - 1) return;
+    const uint32_t *own = a.peer_bstamp[a.me] + s;
+    const uint64_t t0 = global_ns();
+    while (!stamp_reached(ld_acquire_sys(own), a.epoch)) {
+        if (global_ns() - t0 > kWaitLimitNs) {
+            atomicExch(a.timeout_flag, 111);
+            return;
+        }
+        __nanosleep(64);
+    }
+}
+
 // Holds the stream until every other rank's fused projection of this epoch
 // has finished pushing into this rank's memory (bounded; code 109 on timeout).
 __global__ void tp_wait_kernel(const uint32_t *dstamp, int slots, uint32_t epoch, int *timeout_flag) {
@@ -758,7 +809,7 @@ cudaError_t dispatch_epi(int epi, const CUtensorMap &ta, const CUtensorMap &tb, 
 int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, const float *a_scale, const void *W,
              int64_t ldw, float w_scale, int M, int N, int K, int epi, const float *bias, void *out, int64_t ldo,
              const float *gate, const int *gate_idx, int64_t ld_gate, int f16_from_col, const GemmLowRank *lr = nullptr,
-             const float *w_col_scale = nullptr) {
+             const float *w_col_scale = nullptr, const TpGather *ag = nullptr) {
     if (!A || !W || !out) return fail(ctx, LTX_ERR_INVALID_ARG, "gemm: null pointer");
     if (M <= 0 || N <= 0 || K <= 0) return fail(ctx, LTX_ERR_SHAPE, "gemm: empty shape %d x %d x %d", M, N, K);
     const int align = 16 / es;   // elements per 16 bytes (TMA strides and the innermost coordinate)
@@ -797,6 +848,16 @@ int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, 
                             : (int)std::max<size_t>(1, std::min<size_t>((size_t)m_blocks, kGroupPanelBytes / panel));
     GemmParams p{M,   N,    K,        a_scale, w_scale,           bias,         out,     ldo,       gate,
                  gate_idx, ld_gate, ctx->timeout_flag, f16_from_col, group_m, k2_blocks, w_col_scale};
+    if (ag && ag->stamp && ag->n > 1) {
+        // gathered A rows: this rank's own rows first, the others' as they arrive
+        p.ag_stamp = ag->stamp;
+        p.ag_epoch = ag->epoch;
+        p.ag_n = ag->n;
+        p.ag_me = ag->me;
+        p.ag_mcap = ag->mcap;
+        if (m_blocks > ag->mcap) return fail(ctx, LTX_ERR_SHAPE, "gemm: more M-blocks than the gather stamps");
+        p.m_rot = tp_lo(ag->me, m_blocks, ag->n);
+    }
     // EPI_RESID: the residual x [M, ldo] f32 as a TMA map with 128 x 32 boxes
     // (rows 16-byte aligned); otherwise the epilogue updates it with plain loads.
     CUtensorMap tx = ta;
@@ -826,7 +887,7 @@ int gemm_any(ltx_ctx *ctx, cudaStream_t st, int es, const void *A, int64_t lda, 
 // into the peer memory of ctx->pm (x is its residual).  Collective: every
 // rank enqueues the same sequence of these calls with the same shapes.
 int gemm_tp_resid(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
-                  int K, const float *bias, const float *gate, const int *gate_idx, int64_t ld_gate) {
+                  int K, const float *bias, const float *gate, const int *gate_idx, int64_t ld_gate, bool bcast) {
     TpPeerMem &pm = ctx->pm;
     const int n = ctx->tp_size;
     constexpr int BN = 256;
@@ -851,6 +912,7 @@ int gemm_tp_resid(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, con
     p.m_rot = tp_lo(ctx->tp_rank + 1, m_blocks, n) % m_blocks;   // the other ranks' rows first, this rank's last
     p.tp_rank = ctx->tp_rank;
     p.tp_size = n;
+    p.tp_bcast = bcast ? 1 : 0;
     p.epoch = ++pm.epoch;
     p.rows_cap = pm.rows_cap;
     p.tiles_cap = pm.tiles_cap;
@@ -867,13 +929,30 @@ int gemm_tp_resid(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, con
     return e == cudaSuccess ? LTX_OK : cuda_fail(ctx, e, "tp wait launch");
 }
 
+// Every rank of the communicator reaches this point of its stream before any
+// goes on (so the ranks' peer memory may be rewritten after it).  Collective.
+int tp_peer_barrier(ltx_ctx *ctx, cudaStream_t st) {
+    TpPeerMem &pm = ctx->pm;
+    const int n = ctx->tp_size;
+    if (pm.state != 1 || n < 2) return LTX_OK;
+    TpBarrierArgs a{};
+    for (int q = 0; q < n; ++q) a.peer_bstamp[q] = reinterpret_cast<uint32_t *>(pm.peer[q] + pm.dstamp_off + 128);
+    a.n = n;
+    a.me = ctx->tp_rank;
+    a.epoch = ++pm.bepoch;
+    a.timeout_flag = ctx->timeout_flag;
+    tp_barrier_kernel<<<1, 32, 0, st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? LTX_OK : cuda_fail(ctx, e, "tp barrier launch");
+}
+
 // Enqueues out = epilogue(A[M,K] . W[N,K]^T).  A and W are bf16 row-major
 // with leading dimensions lda/ldw (elements, multiples of 8, 16-byte aligned bases).
 int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
               int K, int epi, const float *bias, void *out, int64_t ldo, const float *gate, const int *gate_idx,
-              int64_t ld_gate, int f16_from_col) {
+              int64_t ld_gate, int f16_from_col, const TpGather *ag) {
     return gemm_any(ctx, st, 2, A, lda, nullptr, W, ldw, 1.0f, M, N, K, epi, bias, out, ldo, gate, gate_idx, ld_gate,
-                    f16_from_col);
+                    f16_from_col, nullptr, nullptr, ag);
 }
 
 // The same with e4m3 A and W (leading dimensions multiples of 16): the

@@ -20,7 +20,11 @@ namespace ltx {
 //   recv   bf16 [tp-1][rows_cap][D]           partial products other ranks pushed
 //   tstamp u32  [tp-1][tiles_cap][4]          per-tile, per-warp arrival stamps
 //   dstamp u32  [tp-1]                        "all my pushes landed" stamps
+//          (+128 bytes: u32 [tp-1] rank-barrier stamps)
 //   count  u32                                CTAs of the current launch done
+//   xn     bf16 [rows_cap][D]                 normalised rows, gathered from their owners
+//   gstamp u32  [tp-1][mblocks_cap]           per-M-block "my rows of xn landed" stamps
+//   gcount u32  [mblocks_cap]                 norm blocks done per M-block (current launch)
 // Stamps hold the launch epoch that wrote them; epochs only grow, so nothing
 // is ever reset between launches.
 constexpr int kMaxTpPeers = 8;
@@ -29,6 +33,10 @@ struct TpPeerMem {
     size_t bytes = 0;
     int64_t rows_cap = 0, D = 0, tiles_cap = 0;
     size_t recv_off = 0, tstamp_off = 0, dstamp_off = 0, count_off = 0;
+    size_t xn_off = 0, gstamp_off = 0, gcount_off = 0;
+    int64_t mblocks_cap = 0;
+    uint32_t gepoch = 0;             // gathers of normalised rows so far (same sequence on every rank)
+    uint32_t bepoch = 0;             // rank barriers so far
     char *peer[kMaxTpPeers] = {};    // every rank's allocation as mapped here (own = base)
     uint32_t epoch = 0;              // fused launches so far (the same sequence on every rank)
     int state = 0;                   // 0 not set up, 1 on, -1 off (the NCCL path runs)

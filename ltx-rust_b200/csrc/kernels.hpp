@@ -13,14 +13,38 @@ int dequant_merge(ltx_ctx *ctx, cudaStream_t stream, const void *w, int w_dt, in
                   int64_t cols, const ltx_lora_delta *deltas, int n_deltas, void *dst, int dst_dt);
 
 // gemm.cu (epilogue codes = ltx_epilogue)
+struct TpGather;
 int gemm_bf16(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
               int K, int epi, const float *bias, void *out, int64_t ldo, const float *gate, const int *gate_idx,
-              int64_t ld_gate, int f16_from_col = 1 << 30);
+              int64_t ld_gate, int f16_from_col = 1 << 30, const TpGather *ag = nullptr);
+// Sequence-parallel gather of normalised rows over the tensor-parallel ranks:
+// a GEMM whose A rows of other ranks' M-blocks arrive from their owners waits
+// (in its TMA producer, bounded) for the owner's stamp of that M-block.
+struct TpGather {
+    const uint32_t *stamp;   // this rank's stamps [n-1][mcap]
+    uint32_t epoch;
+    int n, me, mcap;
+};
+// Where a norm kernel of the split model also sends its rows: every rank's
+// copy of the normalised rows (at the launch's first row), every rank's
+// stamps, and this rank's per-M-block block counters.
+struct TpNormPush {
+    char *peer_out[kMaxTpPeers];
+    uint32_t *peer_stamp[kMaxTpPeers];
+    uint32_t *count;
+    int n, me, mcap, row0;   // row0: the launch's first row, a multiple of 128
+    uint32_t epoch;
+};
 // Row-split projection of a model split over ranks, the sum over ranks and
 // the residual update fused (x = ctx->pm's residual; N = pm.D, a multiple of
 // 256): x += (sum_r A_r . W_r^T + bias) * gate[gate_idx[row]] on every rank.
+// Every rank of the communicator reaches this point of its stream before any
+// goes on (collective; bounded wait).
+int tp_peer_barrier(ltx_ctx *ctx, cudaStream_t st);
+// bcast: also write the finished rows into every other rank's x (false: each
+// rank keeps only its own rows current, the sequence-parallel layout).
 int gemm_tp_resid(ltx_ctx *ctx, cudaStream_t st, const void *A, int64_t lda, const void *W, int64_t ldw, int M, int N,
-                  int K, const float *bias, const float *gate, const int *gate_idx, int64_t ld_gate);
+                  int K, const float *bias, const float *gate, const int *gate_idx, int64_t ld_gate, bool bcast = true);
 // A bf16 block appended to an e4m3 GEMM's K loop, accumulated into the same
 // TMEM accumulator before the scales: acc += A2[M, k2] . B2[N, k2]^T
 // (k2 a multiple of 64; leading dimensions in elements).
@@ -48,6 +72,12 @@ cudaError_t rope_table(cudaStream_t st, int sms, const float *pos, int B, int T,
                        float *sin_out);
 cudaError_t norm_mod(cudaStream_t st, const float *x, int64_t ldx, int rows, int D, float eps, int mode,
                      const float *tab, int tab_coeff, const int *idx, int k_shift, __nv_bfloat16 *out, int64_t ldo);
+// norm_mod of `rows` rows (D 4096, 16-byte aligned) that also writes each row
+// into every other rank's copy and stamps each finished M-block there.
+struct TpNormPush;
+cudaError_t norm_mod_push(cudaStream_t st, const float *x, int64_t ldx, int rows, float eps, int mode, const float *tab,
+                          int tab_coeff, const int *idx, int k_shift, __nv_bfloat16 *out, int64_t ldo,
+                          const TpNormPush &push);
 cudaError_t ada_tables(cudaStream_t st, int sms, const float *const *sst_dev, int L, int coeff, const float *mod,
                        const float *sst_out, const float *emb, int U, int D, float *tab, float *otab);
 cudaError_t qk_norm_rope(cudaStream_t st, __nv_bfloat16 *buf, int64_t ld, int rows, int D, int H, float eps,

@@ -890,7 +890,13 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         TRY(ensure_work(ctx, sizing.bytes));
         w = carve_work(static_cast<char *>(ctx->work), c, rows, crow, U, c.layers, m->tp, m->lora_r64);
     }
+    // Sequence-parallel norms on top (D 4096, the vectorised norm kernel): each
+    // rank keeps only its own rows of x current (M-blocks [lo(r), lo(r+1)),
+    // lo(r) = r * blocks / n), normalises those and sends them into every
+    // rank's copy of the normalised rows, which the next GEMMs gather.
+    const bool sp = peer_x && D == 4096;
     if (peer_x) w.x = reinterpret_cast<float *>(ctx->pm.base);
+    if (sp) w.xn = reinterpret_cast<__nv_bfloat16 *>(ctx->pm.base + ctx->pm.xn_off);
     if (work_out) *work_out = w;
     if (!seam && ts_dev) {
         CU(timestep_set(st, ts_dev, rows, U, w.ts_u, w.idx, ctx->timeout_flag, kErrTooManyTimesteps));
@@ -964,9 +970,10 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         if (tp == 1)
             return gemm_bf16(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, LTX_EPI_RESID, bias, w.x, D, gate,
                              gidx, K * D);
-        // the sum over ranks fused into the GEMM, over NVLink peer memory
+        // the sum over ranks fused into the GEMM, over NVLink peer memory (the
+        // finished rows also go to every rank unless the norms are sequence-parallel)
         if (peer_x && D % 256 == 0)
-            return gemm_tp_resid(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, bias, gate, gidx, K * D);
+            return gemm_tp_resid(ctx, st, a, lda, wt, kdim, (int)rows, (int)D, (int)kdim, bias, gate, gidx, K * D, !sp);
         // otherwise NCCL:
         constexpr int kSlabs = 4, kCommSms = 16;
         const int64_t slab = rows >= 16 * 128 ? (rows + kSlabs * 128 - 1) / (kSlabs * 128) * 128 : rows;
@@ -986,6 +993,38 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
                             bias, gate, gidx ? gidx + r0 : nullptr, K * D));
         }
         return comm_join(ctx);
+    };
+    // x -> w.xn = mod(norm(x)) in `mode`: every row, or with sequence-parallel
+    // norms this rank's rows, also written into every other rank's w.xn; the
+    // GEMMs that read w.xn next gather the other ranks' rows (agp).
+    TpGather ag{};
+    const TpGather *agp = sp ? &ag : nullptr;
+    auto norm_x = [&](int mode, const float *tabp, int coeff, int k_shift) -> int {
+        if (!sp) {
+            CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, mode, tabp, coeff, w.idx, k_shift, w.xn, D));
+            return LTX_OK;
+        }
+        TpPeerMem &pm = ctx->pm;
+        const int n = ctx->tp_size, me = ctx->tp_rank;
+        const int64_t mblk = (rows + 127) / 128;
+        const int64_t r0 = (int64_t)me * mblk / n * 128;
+        const int64_t r1 = std::min<int64_t>(rows, (int64_t)(me + 1) * mblk / n * 128);
+        TpNormPush push{};
+        push.n = n;
+        push.me = me;
+        push.mcap = (int)pm.mblocks_cap;
+        push.row0 = (int)r0;
+        push.epoch = ++pm.gepoch;
+        for (int q = 0; q < n; ++q) {
+            push.peer_out[q] = pm.peer[q] + pm.xn_off + (size_t)r0 * D * 2;
+            push.peer_stamp[q] = reinterpret_cast<uint32_t *>(pm.peer[q] + pm.gstamp_off);
+        }
+        push.count = reinterpret_cast<uint32_t *>(pm.base + pm.gcount_off);
+        if (r1 > r0)
+            CU(norm_mod_push(st, w.x + r0 * D, D, (int)(r1 - r0), c.eps, mode, tabp, coeff, w.idx ? w.idx + r0 : nullptr,
+                             k_shift, w.xn + r0 * D, D, push));
+        ag = TpGather{reinterpret_cast<const uint32_t *>(pm.base + pm.gstamp_off), pm.gepoch, n, me, (int)pm.mblocks_cap};
+        return LTX_OK;
     };
     // RMSNorm(gamma) over the full inner dimension of `nseg` projections that
     // each hold Dl columns per row here (+ RoPE with the tables when given)
@@ -1069,11 +1108,11 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
             return LTX_OK;
         }
         // self-attention: x += attn(mod(rms(x))) * gate_msa
-        CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 0, w.xn, D));
+        TRY(norm_x(1, tab, (int)K, 0));
         // V columns come out as f16: the attention keeps P in f16 for the P.V MMA
         const int vcol = d == 128 ? (int)(2 * Dl) : (int)(3 * Dl);
         TRY(gemm_bf16(ctx, st, w.xn, D, b.qkv, D, (int)rows, (int)(3 * Dl), (int)D, LTX_EPI_BF16, b.qkv_b, w.qkv,
-                      3 * Dl, nullptr, nullptr, 0, vcol));
+                      3 * Dl, nullptr, nullptr, 0, vcol, agp));
         if (tp > 1) {
             CU(tp_sumsq_rows(st, w.qkv, 3 * Dl, (int)rows, (int)Dl, 2, Dl, w.ss));
             TRY(allreduce_sum(ctx, w.ss, (size_t)2 * rows));
@@ -1092,17 +1131,17 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         TRY(attend(w.qkv, 3 * Dl, w.qkv + Dl, 3 * Dl, w.qkv + 2 * Dl, 3 * Dl, T));
         if (c.gated) {
             TRY(gemm_bf16(ctx, st, w.xn, D, b.g1, D, (int)rows, (int)Hl, (int)D, LTX_EPI_F32, b.g1_b, w.glog, Hl,
-                          nullptr, nullptr, 0));
+                          nullptr, nullptr, 0, 1 << 30, agp));
             CU(head_gate(st, sms, w.att, Dl, w.glog, Hl, (int)rows, (int)Hl, (int)d));
         }
         TRY(project_residual(w.att, Dl, b.o, Dl, b.o_b, tab + 2 * D));
         // cross-attention: x += attn(rms(x), ctx)   [flag path: modulated q, gated, modulated ctx]
         if (c.cross_adaln)
-            CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 6, w.xn, D));
+            TRY(norm_x(1, tab, (int)K, 6));
         else
-            CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 0, nullptr, 0, nullptr, 0, w.xn, D));
+            TRY(norm_x(0, nullptr, 0, 0));
         TRY(gemm_bf16(ctx, st, w.xn, D, b.q2, D, (int)rows, (int)Dl, (int)D, LTX_EPI_BF16, b.q2_b, w.q2, Dl, nullptr,
-                      nullptr, 0));
+                      nullptr, 0, 1 << 30, agp));
         if (c.cross_adaln) CU(ctx_mod(st, sms, context, crow * Dc, (int)Dc, b.pst, w.ctxb));
         TRY(gemm_bf16(ctx, st, w.ctxb, Dc, b.kv2, Dc, (int)crow, (int)(2 * Dl), (int)Dc, LTX_EPI_BF16, b.kv2_b, w.kv2,
                       2 * Dl, nullptr, nullptr, 0, d == 128 ? (int)Dl : (int)(2 * Dl)));
@@ -1119,7 +1158,7 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         TRY(attend(w.q2, Dl, w.kv2, 2 * Dl, w.kv2 + Dl, 2 * Dl, S));
         if (c.gated) {
             TRY(gemm_bf16(ctx, st, w.xn, D, b.g2, D, (int)rows, (int)Hl, (int)D, LTX_EPI_F32, b.g2_b, w.glog, Hl,
-                          nullptr, nullptr, 0));
+                          nullptr, nullptr, 0, 1 << 30, agp));
             CU(head_gate(st, sms, w.att, Dl, w.glog, Hl, (int)rows, (int)Hl, (int)d));
         }
         TRY(project_residual(w.att, Dl, b.o2, Dl, b.o2_b, c.cross_adaln ? tab + 8 * D : nullptr));
@@ -1128,9 +1167,9 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
             TRY(ffn_f8(b, tab));
             return LTX_OK;
         }
-        CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 1, tab, (int)K, w.idx, 3, w.xn, D));
+        TRY(norm_x(1, tab, (int)K, 3));
         TRY(gemm_bf16(ctx, st, w.xn, D, b.ff1, D, (int)rows, (int)Fl, (int)D, LTX_EPI_GELU_BF16, b.ff1_b, w.ffh, Fl,
-                      nullptr, nullptr, 0));
+                      nullptr, nullptr, 0, 1 << 30, agp));
         TRY(project_residual(w.ffh, Fl, b.ff2, Fl, b.ff2_b, tab + 5 * D));
         return LTX_OK;
     };
@@ -1152,9 +1191,12 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
         }
     }
     // output head: LN(x) * (1 + scale) + shift -> proj_out (model.rs:237-254)
-    CU(norm_mod(st, w.x, D, (int)rows, (int)D, c.eps, 2, w.otab, 2, w.idx, 0, w.xn, D));
+    TRY(norm_x(2, w.otab, 2, 0));
     TRY(gemm_bf16(ctx, st, w.xn, D, m->out_w, D, (int)rows, c.out_ch, (int)D, LTX_EPI_F32, m->out_b, out, c.out_ch,
-                  nullptr, nullptr, 0));
+                  nullptr, nullptr, 0, 1 << 30, agp));
+    // the next forward's first norm rewrites every rank's gathered rows: no
+    // rank may get there while another still reads them here
+    if (sp) TRY(tp_peer_barrier(ctx, st));
     return LTX_OK;
 }
 
