@@ -122,11 +122,14 @@ int ltx_ctx_init_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t nrank
 int ltx_ctx_init_cfg_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t cfg_rank);
 /* How the tensor-parallel ranks sum each row-split projection, as set up by
  * the first forward on the context: 0 not yet (or one rank), 1 inside the
- * GEMM over NVLink peer memory (each rank's residual lives in memory the other
- * ranks map through CUDA IPC; the GEMM's epilogue pushes partial products to
- * the rows' owner, which adds them and writes the updated rows into every
- * rank's copy), 2 NCCL allreduce (when a rank cannot map its peers, more than
- * 8 ranks, or LTX_TP_EXCHANGE=nccl in every rank's environment). */
+ * GEMM over NVLink peer memory (the ranks map each other's memory through
+ * CUDA IPC; each rank owns a contiguous range of rows, and the GEMM's
+ * epilogue pushes partial products to the rows' owner, which adds them and
+ * updates its residual rows; at inner dimension 4096 every norm then runs on
+ * the owner's rows only and the normalised rows are gathered into every rank,
+ * else the owner writes its updated rows into every rank's residual), 2 NCCL
+ * allreduce (when a rank cannot map its peers, more than 8 ranks, or
+ * LTX_TP_EXCHANGE=nccl in every rank's environment). */
 int ltx_ctx_tp_exchange(const ltx_ctx *ctx);
 /* LTX_ERR_NCCL if the communicator has recorded an asynchronous error. */
 int ltx_ctx_comm_check(ltx_ctx *ctx);
