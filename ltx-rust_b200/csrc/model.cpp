@@ -11,6 +11,7 @@
 //   modulation tables  [L][U][coeff][D] f32 for the U distinct timesteps.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <set>
@@ -894,7 +895,10 @@ static int forward_impl(ltx_model *m, ltx_ctx *ctx, const float *latent, const s
     // rank keeps only its own rows of x current (M-blocks [lo(r), lo(r+1)),
     // lo(r) = r * blocks / n), normalises those and sends them into every
     // rank's copy of the normalised rows, which the next GEMMs gather.
-    const bool sp = peer_x && D == 4096;
+    // Opt-in (LTX_TP_SEQ_NORMS=1 in every rank's environment): measured no
+    // faster than the broadcast layout at 2 ranks.
+    const char *sp_env = getenv("LTX_TP_SEQ_NORMS");
+    const bool sp = peer_x && D == 4096 && sp_env && strcmp(sp_env, "1") == 0;
     if (peer_x) w.x = reinterpret_cast<float *>(ctx->pm.base);
     if (sp) w.xn = reinterpret_cast<__nv_bfloat16 *>(ctx->pm.base + ctx->pm.xn_off);
     if (work_out) *work_out = w;

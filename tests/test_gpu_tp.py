@@ -1,7 +1,8 @@
 """Tensor-parallel model (heads and FFN units split over two GPUs, a sum over
 ranks after each row-split projection) against the same model on one GPU.
-The sum runs both ways the library has: fused into the GEMM over NVLink peer
-memory (the default) and as an NCCL allreduce (LTX_TP_EXCHANGE=nccl).
+The sum runs every way the library has: fused into the GEMM over NVLink peer
+memory (the default), the same with sequence-parallel norms
+(LTX_TP_SEQ_NORMS=1), and as an NCCL allreduce (LTX_TP_EXCHANGE=nccl).
 
 Needs two GPUs; each rank is a spawned process.  The whole model on one GPU
 is the reference: same seed, same synthetic FP8 + LoRA weights (every shard
@@ -37,6 +38,8 @@ def _worker(rank, ws, port, cfg, T_frames, q, exchange="peer"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     if exchange == "nccl":
         os.environ["LTX_TP_EXCHANGE"] = "nccl"
+    if exchange == "peer_sp":   # sequence-parallel norms (inner dimension 4096)
+        os.environ["LTX_TP_SEQ_NORMS"] = "1"
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=ws, timeout=timedelta(seconds=90))
     try:
@@ -89,7 +92,8 @@ def _worker(rank, ws, port, cfg, T_frames, q, exchange="peer"):
 
 
 @pytest.mark.parametrize("heads,head_dim,layers,frames,exchange",
-                         [(4, 128, 2, 2, "peer"), (32, 128, 1, 1, "peer"), (4, 128, 2, 2, "nccl")])
+                         [(4, 128, 2, 2, "peer"), (32, 128, 1, 1, "peer"), (4, 128, 2, 2, "nccl"),
+                          (32, 128, 2, 1, "peer_sp")])
 def test_tensor_parallel_two_gpus_matches_one(heads, head_dim, layers, frames, exchange):
     import socket
     import torch.multiprocessing as mp
@@ -108,7 +112,7 @@ def test_tensor_parallel_two_gpus_matches_one(heads, head_dim, layers, frames, e
     same, used, err_f, err_s = q.get(timeout=5)
     print(f"\nTP x2 ({heads} heads, {layers} layers, {used}): forward rel-L2 {err_f:.2e}, "
           f"step update rel-L2 {err_s:.2e}")
-    assert used == exchange
+    assert used == exchange.split("_")[0]
     assert same, "ranks disagree on the replicated output"
     assert err_f < 1e-2 and err_s < 1e-2
 
