@@ -43,6 +43,7 @@ struct MergeParams {
     void *dst;
     int dst_bf16;
     int dst_aligned16;  // dst is 16-byte aligned: vector stores allowed
+    int *timeout_flag;  // where a bounded wait records that it gave up (null: nowhere)
 };
 
 __device__ __forceinline__ float base_value(const MergeParams &p, int64_t idx) {
@@ -140,6 +141,115 @@ __global__ void __launch_bounds__(256) dequant_only_kernel(MergeParams p, int64_
     // tail (n not a multiple of 16)
     for (int64_t i = n16 * 16 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
         store_out(p, i, base_value(p, i));
+}
+
+// Streaming through shared memory with bulk copies: each CTA walks chunks of
+// kBulkElems elements (grid-stride).  Thread 0 keeps kBulkStages chunk loads
+// in flight (cp.async.bulk global -> shared, completion counted on an
+// mbarrier); every thread decodes its 32 elements of the chunk from shared
+// memory into an output buffer there, and thread 0 writes the buffer back
+// with one bulk store.  A few large copies in flight per SM keep HBM busy
+// with far fewer instructions per byte than per-thread 16-byte loads.
+constexpr int kBulkElems = 8192, kBulkStages = 4;
+
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(smem_dst)),
+                 "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_store(void *gdst, const void *smem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(smem_src)),
+                 "r"(bytes)
+                 : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+
+template <bool OUT_BF16>
+constexpr size_t bulk_smem_bytes() {
+    return (size_t)kBulkStages * kBulkElems * (1 + (OUT_BF16 ? 2 : 4)) + 64;
+}
+
+template <int WDT, bool OUT_BF16>
+__global__ void __launch_bounds__(256) dequant_bulk_kernel(MergeParams p, int64_t nchunks, int *timeout_flag) {
+    constexpr int OUT_ES = OUT_BF16 ? 2 : 4;
+    constexpr uint32_t IN_BYTES = kBulkElems, OUT_BYTES = kBulkElems * OUT_ES;
+    static_assert(kBulkElems == 32 * 256, "one chunk is 32 elements per thread");
+    extern __shared__ __align__(128) unsigned char smem[];
+    unsigned char *in = smem;                              // [stages][IN_BYTES]
+    unsigned char *out = smem + kBulkStages * IN_BYTES;    // [stages][OUT_BYTES]
+    uint64_t *full = reinterpret_cast<uint64_t *>(out + kBulkStages * OUT_BYTES);
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int s = 0; s < kBulkStages; ++s) mbar_init(&full[s], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const int64_t first = blockIdx.x, step = gridDim.x;
+    const int64_t mine = first < nchunks ? (nchunks - 1 - first) / step + 1 : 0;   // this CTA's chunks
+    int64_t issued = 0;
+    auto issue = [&](int64_t i) {   // thread 0: the load of this CTA's i-th chunk
+        const int s = (int)(i % kBulkStages);
+        mbar_arrive_expect_tx(&full[s], IN_BYTES);
+        bulk_load(in + s * IN_BYTES, static_cast<const uint8_t *>(p.w) + (first + i * step) * IN_BYTES, IN_BYTES,
+                  &full[s]);
+        issued = i + 1;
+    };
+    if (tid == 0)
+        for (int64_t i = 0; i < mine && i < kBulkStages; ++i) issue(i);
+    bool aborted = false;
+    int64_t i = 0;
+    for (; i < mine; ++i) {
+        const int s = (int)(i % kBulkStages);
+        const uint32_t ph = (uint32_t)((i / kBulkStages) & 1);
+        if (tid == 0) bulk_wait_read<kBulkStages - 1>();   // the store that last used out[s] has read it
+        // every thread's wait has one outcome for the block (bounded)
+        if (!__syncthreads_and(mbar_wait(&full[s], ph, timeout_flag, 120, &aborted))) break;
+        const uint4 *src = reinterpret_cast<const uint4 *>(in + s * IN_BYTES) + tid * 2;
+        const uint4 r0 = src[0], r1 = src[1];
+        const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) fp8x4_to_f32<WDT>(w[j], f + 4 * j);
+        if (p.fp8_scaled) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = __fmaf_rn(p.scale, f[j], 0.0f);
+        }
+        if constexpr (OUT_BF16) {
+            uint4 *dst = reinterpret_cast<uint4 *>(out + s * OUT_BYTES) + tid * 4;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint32_t o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    __nv_bfloat162 h = __floats2bfloat162_rn(f[8 * q + 2 * e], f[8 * q + 2 * e + 1]);
+                    o[e] = *reinterpret_cast<uint32_t *>(&h);
+                }
+                dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        } else {
+            float4 *dst = reinterpret_cast<float4 *>(out + s * OUT_BYTES) + tid * 8;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dst[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the bulk store
+        __syncthreads();
+        if (tid == 0) {
+            bulk_store(static_cast<unsigned char *>(p.dst) + (first + i * step) * OUT_BYTES, out + s * OUT_BYTES,
+                       OUT_BYTES);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            if (i + kBulkStages < mine) issue(i + kBulkStages);   // in[s] is free: every thread has read it
+        }
+    }
+    if (tid == 0) {
+        // loads an abort left unconsumed land (bounded waits) before the CTA
+        // exits, and every store completes
+        bool quiet = false;
+        for (int64_t j = i; j < issued; ++j)
+            mbar_wait(&full[j % kBulkStages], (uint32_t)((j / kBulkStages) & 1), nullptr, 0, &quiet);
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    }
 }
 
 __global__ void dequant_only_scalar_kernel(MergeParams p, int64_t n) {
@@ -400,6 +510,17 @@ cudaError_t launch_merge(const MergeParams &p, cudaStream_t st, int sms, void *s
             return cudaGetLastError();
         }
         // one unrolled round per thread where it fits in one wave of resident CTAs
+        if ((WDT == LTX_F8_E4M3 || WDT == LTX_F8_E5M2) && n % kBulkElems == 0) {
+            const int64_t nchunks = n / kBulkElems;
+            auto k = p.dst_bf16 ? dequant_bulk_kernel<WDT, true> : dequant_bulk_kernel<WDT, false>;
+            const size_t bsm = p.dst_bf16 ? bulk_smem_bytes<true>() : bulk_smem_bytes<false>();
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm);
+            if (e != cudaSuccess) return e;
+            const int per_sm = p.dst_bf16 ? 2 : 1;   // CTAs that fit one SM's shared memory
+            const int grid = (int)std::min<int64_t>(nchunks, (int64_t)sms * per_sm);
+            k<<<grid, 256, bsm, st>>>(p, nchunks, p.timeout_flag);
+            return cudaGetLastError();
+        }
         static int per_sm[2][2] = {{0, 0}, {0, 0}};   // [e5m2][bf16 out], filled once
         int &resident = per_sm[WDT == LTX_F8_E5M2][p.dst_bf16 ? 1 : 0];
         if (!resident) {
@@ -477,6 +598,7 @@ int dequant_merge(ltx_ctx *ctx, cudaStream_t stream, const void *w, int w_dt, in
         return fail(ctx, LTX_ERR_INVALID_ARG, "dequant_merge: bad delta count %d", n_deltas);
     if (rows * cols == 0) return LTX_OK;
     MergeParams p{};
+    p.timeout_flag = ctx->timeout_flag;
     p.w = w;
     p.w_dt = w_dt;
     p.fp8_scaled = (w_dt == LTX_F8_E4M3 || w_dt == LTX_F8_E5M2) && has_scale;
