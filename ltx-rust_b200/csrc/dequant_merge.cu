@@ -185,6 +185,12 @@ __global__ void __launch_bounds__(256) dequant_bulk_kernel(MergeParams p, int64_
         for (int s = 0; s < kBulkStages; ++s) mbar_init(&full[s], 1);
         fence_barrier_init();
     }
+    // Launched as a programmatic dependent of the previous kernel on the
+    // stream: the set-up above overlaps that kernel's tail; no global memory
+    // is touched before it has completed.  The next such launch (another
+    // weight's dequant) may likewise start setting up as this one's CTAs drain.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     __syncthreads();
     const int64_t first = blockIdx.x, step = gridDim.x;
     const int64_t mine = first < nchunks ? (nchunks - 1 - first) / step + 1 : 0;   // this CTA's chunks
@@ -518,8 +524,17 @@ cudaError_t launch_merge(const MergeParams &p, cudaStream_t st, int sms, void *s
             if (e != cudaSuccess) return e;
             const int per_sm = p.dst_bf16 ? 2 : 1;   // CTAs that fit one SM's shared memory
             const int grid = (int)std::min<int64_t>(nchunks, (int64_t)sms * per_sm);
-            k<<<grid, 256, bsm, st>>>(p, nchunks, p.timeout_flag);
-            return cudaGetLastError();
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(grid);
+            cfg.blockDim = dim3(256);
+            cfg.dynamicSmemBytes = bsm;
+            cfg.stream = st;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            return cudaLaunchKernelEx(&cfg, k, p, nchunks, p.timeout_flag);
         }
         static int per_sm[2][2] = {{0, 0}, {0, 0}};   // [e5m2][bf16 out], filled once
         int &resident = per_sm[WDT == LTX_F8_E5M2][p.dst_bf16 ? 1 : 0];
