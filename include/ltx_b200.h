@@ -130,7 +130,10 @@ int ltx_ctx_init_cfg_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t c
  * every norm instead runs on the owner's rows only and the normalised rows
  * are gathered into every rank), 2 NCCL
  * allreduce (when a rank cannot map its peers, more than 8 ranks, or
- * LTX_TP_EXCHANGE=nccl in every rank's environment). */
+ * LTX_TP_EXCHANGE=nccl in every rank's environment).  With 1, a rank's
+ * kernels wait on the other ranks' kernels on the device for at most 2 s each
+ * (then LTX_ERR_TIMEOUT at the next ltx_ctx_synchronize): every rank must
+ * enqueue the same calls within about a second of the others. */
 int ltx_ctx_tp_exchange(const ltx_ctx *ctx);
 /* LTX_ERR_NCCL if the communicator has recorded an asynchronous error. */
 int ltx_ctx_comm_check(ltx_ctx *ctx);
