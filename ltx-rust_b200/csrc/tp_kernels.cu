@@ -85,6 +85,76 @@ __global__ void __launch_bounds__(256) norm_apply_rope_kernel(__nv_bfloat16 *x, 
     }
 }
 
+// The same for head dim 128 with split RoPE (or none), one warp per row and
+// 16-byte accesses: per iteration the warp takes 4 heads, lane group k (8
+// lanes) the pairs 8k'..8k'+7 of its head (x1 at j, x2 at j + 64).  Without
+// RoPE each lane takes 8 consecutive columns.  Same arithmetic per element.
+__device__ __forceinline__ void bf16x8_to_f32(uint4 u, float *f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[e]));
+        f[2 * e] = t.x;
+        f[2 * e + 1] = t.y;
+    }
+}
+__device__ __forceinline__ uint4 f32_to_bf16x8(const float *f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+        w[e] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+__global__ void __launch_bounds__(256) norm_apply_rope_d128_kernel(__nv_bfloat16 *x, int64_t ld, int rows, int cols,
+                                                                   int D, int head0, float eps, const float *gamma,
+                                                                   const float *ss, const float *cos_t,
+                                                                   const float *sin_t) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + warp;
+    if (row >= rows) return;
+    __nv_bfloat16 *xr = x + (int64_t)row * ld;
+    const float denom = sqrtf(ss[row] / (float)D + eps);
+    if (!cos_t) {
+        for (int c = lane * 8; c < cols; c += 256) {
+            float f[8], g[8];
+            bf16x8_to_f32(*reinterpret_cast<const uint4 *>(xr + c), f);
+            *reinterpret_cast<float4 *>(g) = __ldg(reinterpret_cast<const float4 *>(gamma + c));
+            *reinterpret_cast<float4 *>(g + 4) = __ldg(reinterpret_cast<const float4 *>(gamma + c + 4));
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = f[e] / denom * g[e];
+            *reinterpret_cast<uint4 *>(xr + c) = f32_to_bf16x8(f);
+        }
+        return;
+    }
+    const float *cr = cos_t + (int64_t)row * (D / 2) + (int64_t)head0 * 64;
+    const float *sr = sin_t + (int64_t)row * (D / 2) + (int64_t)head0 * 64;
+    const int k = lane & 7;
+    for (int h = lane >> 3; h < cols / 128; h += 4) {
+        const int c1 = h * 128 + 8 * k, c2 = c1 + 64, t = h * 64 + 8 * k;
+        float x1[8], x2[8], g1[8], g2[8], cs[8], sn[8];
+        bf16x8_to_f32(*reinterpret_cast<const uint4 *>(xr + c1), x1);
+        bf16x8_to_f32(*reinterpret_cast<const uint4 *>(xr + c2), x2);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            *reinterpret_cast<float4 *>(g1 + 4 * q) = __ldg(reinterpret_cast<const float4 *>(gamma + c1 + 4 * q));
+            *reinterpret_cast<float4 *>(g2 + 4 * q) = __ldg(reinterpret_cast<const float4 *>(gamma + c2 + 4 * q));
+            *reinterpret_cast<float4 *>(cs + 4 * q) = *reinterpret_cast<const float4 *>(cr + t + 4 * q);
+            *reinterpret_cast<float4 *>(sn + 4 * q) = *reinterpret_cast<const float4 *>(sr + t + 4 * q);
+        }
+        float o1[8], o2[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float a = x1[e] / denom * g1[e], b = x2[e] / denom * g2[e];
+            o1[e] = cs[e] * a - sn[e] * b;
+            o2[e] = sn[e] * a + cs[e] * b;
+        }
+        *reinterpret_cast<uint4 *>(xr + c1) = f32_to_bf16x8(o1);
+        *reinterpret_cast<uint4 *>(xr + c2) = f32_to_bf16x8(o2);
+    }
+}
+
 // x[row][c] += (p[row][c] + bias[c]) * gate[idx[row]][c]: the single-GPU
 // EPI_RESID epilogue, applied after the partial products (bf16) were summed.
 __global__ void __launch_bounds__(256) resid_add_kernel(float *x, const __nv_bfloat16 *p, int rows, int D,
@@ -135,6 +205,13 @@ cudaError_t tp_norm_apply_rope(cudaStream_t st, __nv_bfloat16 *x, int64_t ld, in
                                int head0, float eps, const float *gamma, const float *ss, const float *cos_t,
                                const float *sin_t, bool interleaved) {
     if (rows == 0) return cudaSuccess;
+    const bool aligned = ld % 8 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)gamma & 15) == 0 &&
+                         (!cos_t || (((uintptr_t)cos_t & 15) == 0 && ((uintptr_t)sin_t & 15) == 0 && D % 8 == 0));
+    if (d == 128 && !interleaved && cols % 512 == 0 && aligned) {
+        norm_apply_rope_d128_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, ld, rows, cols, D, head0, eps, gamma, ss, cos_t,
+                                                                    sin_t);
+        return cudaGetLastError();
+    }
     const size_t smem = (size_t)cols * sizeof(float);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(norm_apply_rope_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
