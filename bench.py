@@ -1151,7 +1151,11 @@ def main():
                 _log(f"replicas: {rep['ms_per_step']:.1f} ms/step, {rep['value']:.0f} tokens/s")
                 res["replicas"] = rep
             # the other single-sequence layout beside the headline's
-            other = "tp" if mode == "cfg_tp" else ("cfg_tp" if mode == "tp" and ws % 2 == 0 else None)
+            # (plain TP with the fused exchange is not run past 4 GPUs: that
+            # path has not been exercised on 8; the NCCL-exchange TP line below
+            # covers plain TP there)
+            other = ("tp" if ws <= 4 else None) if mode == "cfg_tp" else \
+                ("cfg_tp" if mode == "tp" and ws % 2 == 0 else None)
             if other:
                 o = run_parallel_step(args, rank, ws, local, other)
                 _log(f"{other}: {o['ms_per_step']:.1f} ms/step, {o['value']:.0f} tokens/s ({o['tp_exchange']})")

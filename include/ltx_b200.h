@@ -125,10 +125,10 @@ int ltx_ctx_init_cfg_comm(ltx_ctx *ctx, const uint8_t *id, size_t len, int32_t c
  * GEMM over NVLink peer memory (the ranks map each other's memory through
  * CUDA IPC; each rank owns a contiguous range of rows, and the GEMM's
  * epilogue pushes partial products to the rows' owner, which adds them and
- * updates its residual rows and writes them into every rank's residual; with
- * LTX_TP_SEQ_NORMS=1 in every rank's environment and inner dimension 4096,
- * every norm instead runs on the owner's rows only and the normalised rows
- * are gathered into every rank), 2 NCCL
+ * updates its residual rows and writes them into every rank's residual; from
+ * 4 ranks at inner dimension 4096 every norm instead runs on the owner's rows
+ * only and the normalised rows are gathered into every rank, which
+ * LTX_TP_SEQ_NORMS=1 / =0 in every rank's environment forces on / off), 2 NCCL
  * allreduce (when a rank cannot map its peers, more than 8 ranks, or
  * LTX_TP_EXCHANGE=nccl in every rank's environment).  With 1, a rank's
  * kernels wait on the other ranks' kernels on the device for at most 2 s each
