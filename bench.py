@@ -21,7 +21,8 @@ Workloads:
                  all-gather of the two velocities per step (`--parallel
                  cfg_tp`, the default); `--parallel tp` splits the model over
                  all N for both passes.  The N > 1 line also carries the
-                 other of those two layouts (`tp` or `cfg_tp`), `replicas`
+                 other of those two layouts (`tp` or `cfg_tp`; `tp` only up
+                 to 4 GPUs), `tp_nccl` (plain TP with the NCCL exchange), `replicas`
                  (one independent sequence per GPU, no collective: weak
                  scaling) and `chunk_pipeline` (config 5 on the N GPUs).  --parallel chunk
                  makes the replica figure the headline instead.  The N = 1
