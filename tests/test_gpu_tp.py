@@ -281,3 +281,28 @@ def test_cfg_x_tensor_parallel_four_gpus_matches_one():
     assert used == ["peer"] * 4
     assert same, "the four ranks disagree on the latent"
     assert err < 1e-2
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
+def test_tensor_parallel_four_gpus_matches_one():
+    """Heads and FFN units split four ways (inner dimension 4096: the fused exchange
+    with sequence-parallel norms, the default from 4 ranks) against one GPU."""
+    import socket
+    import torch.multiprocessing as mp
+    cfg = _cfg(32, 128, 1)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mctx = mp.get_context("spawn")
+    q = mctx.Queue()
+    procs = [mctx.Process(target=_worker, args=(r, 4, port, cfg, 1, q, "peer")) for r in range(4)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    same, used, err_f, err_s = q.get(timeout=5)
+    print(f"\nTP x4 (32 heads, 1 layer, {used}): forward rel-L2 {err_f:.2e}, step update rel-L2 {err_s:.2e}")
+    assert used == "peer"
+    assert same, "ranks disagree on the replicated output"
+    assert err_f < 1e-2 and err_s < 1e-2
