@@ -56,3 +56,20 @@ def test_reference_arm_names_what_it_ran_with_the_same_config(monkeypatch, capsy
         assert d["impl"] == "reference" and d["steps"] == 1 and d["blocks_timed"] == 1 and d["extrapolated"]
         assert d["config"] == bench.step_config(gpus, mode)
         assert d["cpu_baseline"]["cpu_model"] == "x"
+
+
+def test_step_layouts():
+    """How config 4 uses N GPUs: one GPU; at even N the CFG pair over two
+    tensor-parallel halves (the default); plain TP at odd N or on request; one
+    sequence per GPU with --parallel chunk.  The config names the layout."""
+    import bench
+    assert bench.step_mode(1, "cfg_tp") == "single"
+    assert bench.step_mode(2, "cfg_tp") == "cfg_tp"
+    assert bench.step_mode(3, "cfg_tp") == "tp"
+    assert bench.step_mode(8, "tp") == "tp"
+    assert bench.step_mode(8, "chunk") == "replicas"
+    par = bench.step_config(8, "cfg_tp")["parallelism"]
+    assert par.startswith("cfg2 x tp4") and "allreduce" in par
+    assert "allreduce" not in bench.step_config(2, "cfg_tp")["parallelism"]
+    assert bench.step_config(4, "tp")["parallelism"].startswith("tp4")
+    assert bench.step_config(1, "single")["workload"] == "denoise_step_config4"
