@@ -514,6 +514,13 @@ def run_denoise_step(args, rank, ws, device):
     _log(f"e2e: {e2e_ms:.1f} ms/step")
     bf16_ref = run.reference_step() if ws == 1 else None
     weight_bytes = run.model.weight_bytes()
+    # how the split model's sums ran (for the launch count): fused or NCCL, and
+    # whether the norms were sequence-parallel (the library's rule: from 4
+    # ranks per tensor-parallel group, unless LTX_TP_SEQ_NORMS says otherwise)
+    exchange = ctx.tp_exchange()
+    tp_group = ws if mode == "tp" else (ws // 2 if mode == "cfg_tp" else 1)
+    sp_env = os.environ.get("LTX_TP_SEQ_NORMS", "")
+    seq_norms = exchange == "peer" and (sp_env == "1" if sp_env else tp_group >= 4)
     load_s = run.load_s
     run.close()
     # dominant kernels timed alone at the step's shapes
@@ -582,7 +589,8 @@ def run_denoise_step(args, rank, ws, device):
                           "algorithmic_flops_per_launch": 2.0 * M * N * K},
         "e2e": {"value": (1 if one_seq else ws) * T_TOTAL / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps * launches_per_step(48, split),
+        "gpu_launches": args.steps * launches_per_step(48, split, fused=split and exchange == "peer",
+                                                       seq_norms=seq_norms),
         "clocks": clocks,
         "finite_output": ok,
     }
@@ -904,17 +912,20 @@ def run_block_forward(device, iters=5):
     return res
 
 
-def launches_per_step(L, tp=False):
+def launches_per_step(L, tp=False, fused=False, seq_norms=False):
     """Kernels one ltx_denoise_step enqueues, counted from model.cpp's forward.
     Head 9: latent convert, patchify GEMM, sinusoid, 3 small linears, adaLN
     tables, RoPE table, context convert.  Per block 15: 3 norm+modulate, QKV /
     out / cross-q / cross-kv / out / FFN-in / FFN-out GEMMs, fused Q/K
-    norm+RoPE, cross q and k norms, 2 attentions.  Split over ranks, per block
-    40: the Q/K norms become 3 sum-of-squares and 4 apply launches, and each of
-    the 3 row-split projections runs as 4 token slabs of a GEMM plus a
-    residual add (NCCL's own kernels are not counted).  Output head 2, sampler
-    2."""
-    return 9 + L * (40 if tp else 15) + 2 + 2
+    norm+RoPE, cross q and k norms, 2 attentions.  Split over ranks (tp), the
+    Q/K norms become 3 sum-of-squares and 4 apply launches, and each of the 3
+    row-split projections runs either (NCCL exchange) as 4 token slabs of a
+    GEMM plus a residual add, 40 per block, or (fused exchange) as one GEMM
+    plus its wait kernel, 22 per block; sequence-parallel norms add one rank
+    barrier after the head.  NCCL's own kernels are not counted.  Output head
+    2, sampler 2."""
+    per_block = (22 if fused else 40) if tp else 15
+    return 9 + L * per_block + 2 + 2 + (1 if tp and fused and seq_norms else 0)
 
 
 def cpu_model():
